@@ -1,0 +1,590 @@
+#!/usr/bin/env python
+"""Benchmark of the attention hot path on B200 (one JSON line on rank 0).
+
+Headline workload (`--config c3`, the default): BASELINE config 3, one batched GQA decode step of
+64 independent sequences (32 query / 8 KV heads, head_dim 128, RoPE base 1e6, Mask::Causal,
+cache lengths drawn uniform in [512, 8192] from a seed), f32 cache. A step is one pass of the
+hot path over the batch: RoPE + keep of each sequence's new row, then attention of every row
+over its cache. `value` is tokens/s of the whole job (64 tokens per step); with N GPUs the
+sequences are split across ranks by total length with no collective (total work fixed).
+
+Other configurations (`--config c1|c2|c3bf16|c4`) run the same way; at N=1 the default run adds
+c1, c2, c3bf16 and c4 under "configs" in the same line.
+
+`--impl reference` times the reference's CPU path (the oracle's C++ restatement of fusor-ai's
+f32 attention, split over the host's threads as its thread team splits heads) on the same
+workload and prints the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "fusor-ai_b200"))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+
+C3_SEQS, C3_HEADS, C3_KV, C3_D = 64, 32, 8, 128
+L2_BYTES = 126 * 1024 * 1024
+
+
+def c3_lengths():
+    return np.random.default_rng(301).integers(512, 8193, size=C3_SEQS)
+
+
+def shard_sequences(lengths, world):
+    """Greedy longest-first split of sequences over ranks by total keys."""
+    order = sorted(range(len(lengths)), key=lambda i: -int(lengths[i]))
+    loads = [0] * world
+    parts = [[] for _ in range(world)]
+    for i in order:
+        r = min(range(world), key=lambda k: loads[k])
+        parts[r].append(i)
+        loads[r] += int(lengths[i]) + 1
+    return [sorted(p) for p in parts]
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def profile_traffic(kernel_key: str):
+    """DRAM bytes per launch of `kernel_key` from the committed ncu summary, or None."""
+    path = os.path.join(ROOT, "profiles", "ncu_summary.md")
+    try:
+        for line in open(path):
+            if line.startswith(f"traffic_bytes_per_launch[{kernel_key}]"):
+                return float(line.split("=")[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """SM clocks and clock-event reasons of this rank's GPU, sampled by NVML while running."""
+
+    REASONS = {
+        "hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+        "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4,
+    }
+
+    def __init__(self, torch, device: int):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+            self._h = pynvml.nvmlDeviceGetHandleByUUID(uuid.encode())
+            self._nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # noqa: BLE001 - clocks are reported as unavailable
+            self._nv = None
+            self.error = str(e)
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for name, bit in self.REASONS.items():
+                    if bits & bit:
+                        self.reasons.add(name)
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(0.005)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def report(self):
+        if self._nv is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": "NVML unavailable"}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------------------------
+
+class Workload:
+    """One configuration on this rank: `step()` enqueues one pass; `kernel()` the dominant
+    kernel alone; `e2e_step()` a pass through the public API from pinned host memory."""
+
+    name = ""
+    tokens = 0             # tokens of the whole job per step
+    bound = "hbm"
+    launches_per_step = 0
+    flush_l2 = False
+
+    def algorithmic(self) -> float:
+        """Bytes (hbm) or FLOPs (tensor) of one launch of the dominant kernel on this rank."""
+        raise NotImplementedError
+
+
+class C3Decode(Workload):
+    def __init__(self, torch, fa, rank, world, dtype):
+        self.torch, self.fa = torch, fa
+        self.dtype = dtype
+        self.name = "c3" if dtype == fa.F32 else "c3bf16"
+        lengths = c3_lengths()
+        mine = shard_sequences(lengths, world)[rank]
+        self.tokens = C3_SEQS
+        self.lengths = [int(lengths[i]) for i in mine]
+        shape = fa.Shape(1, C3_HEADS, C3_KV, C3_D)
+        self.shape = shape
+        gen = torch.Generator("cuda").manual_seed(1000 + rank)
+        tdt = torch.float32 if dtype == fa.F32 else torch.bfloat16
+        self.caches = []
+        for n in self.lengths:
+            c = fa.KvCache(shape, n + 1, dtype)
+            k = torch.randn((1, C3_KV, n, C3_D), device="cuda", generator=gen).to(tdt)
+            v = torch.randn((1, C3_KV, n, C3_D), device="cuda", generator=gen).to(tdt)
+            c.put_rows(k, v)
+            del k, v
+            self.caches.append(c)
+        spans = [fa.Span(1, n, fa.Mask.causal()) for n in self.lengths]
+        self.batch = fa.Batch(self.caches, spans)
+        b = len(self.caches)
+        self.qkv = torch.randn((b, shape.qkv), device="cuda", generator=gen)
+        self.angles = torch.from_numpy(
+            fa.rotary_angles(fa.Rotation(base=1e6), C3_D, self.lengths)).cuda()
+        self.q = torch.zeros((b, shape.width), device="cuda")
+        self.out = torch.zeros((b, shape.width), device="cuda")
+        self.launches_per_step = 2 * ((b + 255) // 256)
+        # e2e: pinned host inputs and outputs
+        self.h_qkv = self.qkv.cpu().pin_memory()
+        self.h_angles = self.angles.cpu().pin_memory()
+        self.h_out = torch.zeros_like(self.out, device="cpu").pin_memory()
+        self.d_qkv = torch.empty_like(self.qkv)
+        self.d_angles = torch.empty_like(self.angles)
+        self.h2d = self.h_qkv.numel() * 4 + self.h_angles.numel() * 4
+        self.d2h = self.h_out.numel() * 4
+        esize = 4 if dtype == fa.F32 else 2
+        keys = sum(n + 1 for n in self.lengths)
+        self.bytes = keys * C3_KV * C3_D * 2 * esize + 2 * b * shape.width * 4
+
+    def step(self, mid=None):
+        self.batch.attention_input(0, self.qkv, self.q, self.angles, self.fa.ROPE_HALF)
+        if mid is not None:
+            mid.record()
+        self.batch.attend(0, self.q, self.out)
+
+    def e2e_step(self):
+        self.d_qkv.copy_(self.h_qkv, non_blocking=True)
+        self.d_angles.copy_(self.h_angles, non_blocking=True)
+        self.batch.attention(0, self.d_qkv, self.out, self.d_angles, self.fa.ROPE_HALF)
+        self.h_out.copy_(self.out, non_blocking=True)
+
+    def algorithmic(self):
+        return float(self.bytes)
+
+
+class SingleDecode(Workload):
+    """C1 (14/2, d64, position 1024) and C4 (16/8, d128, position 131072) on one GPU."""
+
+    def __init__(self, torch, fa, name, heads, kv, d, position):
+        self.torch, self.fa, self.name = torch, fa, name
+        shape = fa.Shape(1, heads, kv, d)
+        self.shape = shape
+        self.cache = fa.KvCache(shape, position + 1)
+        gen = torch.Generator("cuda").manual_seed(7)
+        k = torch.randn((1, kv, position, d), device="cuda", generator=gen)
+        v = torch.randn((1, kv, position, d), device="cuda", generator=gen)
+        self.cache.put_rows(k, v)
+        del k, v
+        self.span = fa.Span(1, position, fa.Mask.causal())
+        self.qkv = torch.randn((1, shape.qkv), device="cuda", generator=gen)
+        self.angles = torch.from_numpy(fa.rotary_angles(fa.Rotation(base=1e6), d, [position])).cuda()
+        self.q = torch.zeros((1, shape.width), device="cuda")
+        self.out = torch.zeros((1, shape.width), device="cuda")
+        self.tokens = 1
+        self.launches_per_step = 2
+        self.flush_l2 = (position + 1) * kv * d * 8 < L2_BYTES
+        self.h_qkv = self.qkv.cpu().pin_memory()
+        self.h_angles = self.angles.cpu().pin_memory()
+        self.h_out = torch.zeros_like(self.out, device="cpu").pin_memory()
+        self.d_qkv = torch.empty_like(self.qkv)
+        self.d_angles = torch.empty_like(self.angles)
+        self.h2d = (self.h_qkv.numel() + self.h_angles.numel()) * 4
+        self.d2h = self.h_out.numel() * 4
+        self.bytes = (position + 1) * kv * d * 2 * 4 + 2 * shape.width * 4
+
+    def step(self, mid=None):
+        self.cache.attention_input(0, self.span, self.qkv, self.angles, self.fa.ROPE_HALF, q_out=self.q)
+        if mid is not None:
+            mid.record()
+        self.cache.attend(0, self.span, self.q, self.out)
+
+    def e2e_step(self):
+        self.d_qkv.copy_(self.h_qkv, non_blocking=True)
+        self.d_angles.copy_(self.h_angles, non_blocking=True)
+        self.cache.attention(0, self.span, self.d_qkv, self.out, self.d_angles, self.fa.ROPE_HALF)
+        self.h_out.copy_(self.out, non_blocking=True)
+
+    def algorithmic(self):
+        return float(self.bytes)
+
+
+class C2Prefill(Workload):
+    """C2: 512 rows from position 0, causal, 14/2 heads, d64; the cache written by the pass."""
+
+    def __init__(self, torch, fa):
+        self.torch, self.fa, self.name = torch, fa, "c2"
+        shape = fa.Shape(1, 14, 2, 64)
+        self.shape = shape
+        self.cache = fa.KvCache(shape, 512)
+        gen = torch.Generator("cuda").manual_seed(9)
+        self.span = fa.Span(512, 0, fa.Mask.causal())
+        self.qkv = torch.randn((512, shape.qkv), device="cuda", generator=gen)
+        self.angles = torch.from_numpy(fa.rotary_angles(fa.Rotation(base=1e6), 64, range(512))).cuda()
+        self.q = torch.zeros((512, shape.width), device="cuda")
+        self.out = torch.zeros((512, shape.width), device="cuda")
+        self.tokens = 512
+        self.bound = "tensor"
+        self.launches_per_step = 2
+        self.flush_l2 = True
+        self.h_qkv = self.qkv.cpu().pin_memory()
+        self.h_angles = self.angles.cpu().pin_memory()
+        self.h_out = torch.zeros_like(self.out, device="cpu").pin_memory()
+        self.d_qkv = torch.empty_like(self.qkv)
+        self.d_angles = torch.empty_like(self.angles)
+        self.h2d = (self.h_qkv.numel() + self.h_angles.numel()) * 4
+        self.d2h = self.h_out.numel() * 4
+        self.flops = 4.0 * 14 * 64 * sum(i + 1 for i in range(512))
+
+    def step(self, mid=None):
+        self.cache.attention_input(0, self.span, self.qkv, self.angles, self.fa.ROPE_HALF, q_out=self.q)
+        if mid is not None:
+            mid.record()
+        self.cache.attend(0, self.span, self.q, self.out)
+
+    def e2e_step(self):
+        self.d_qkv.copy_(self.h_qkv, non_blocking=True)
+        self.d_angles.copy_(self.h_angles, non_blocking=True)
+        self.cache.attention(0, self.span, self.d_qkv, self.out, self.d_angles, self.fa.ROPE_HALF)
+        self.h_out.copy_(self.out, non_blocking=True)
+
+    def algorithmic(self):
+        return self.flops
+
+
+def time_workload(torch, dist, w: Workload, steps: int, warmup: int, sampler=None):
+    """W untimed steps, then exactly K timed steps between barrier + synchronize, CUDA events
+    per step around the pass and around the dominant kernel; the max over ranks."""
+    flush = torch.empty(L2_BYTES * 2 // 4, dtype=torch.float32, device="cuda") if w.flush_l2 else None
+    for _ in range(warmup):
+        w.step()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    mids = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ctx = sampler if sampler is not None else _null()
+    with ctx:
+        for i in range(steps):
+            if flush is not None:
+                flush.fill_(float(i))  # evicts L2 between steps, outside the timed events
+            starts[i].record()
+            w.step(mids[i])
+            ends[i].record()
+        torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    step_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    kern_ms = sum(m.elapsed_time(e) for m, e in zip(mids, ends))
+    t = torch.tensor([step_ms, kern_ms], device="cuda", dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t[0]) / steps, float(t[1]) / steps
+
+
+def time_e2e(torch, dist, w: Workload, steps: int, warmup: int):
+    """Wall clock per step through the public API: H2D of the step's inputs from pinned host
+    memory, the attention, D2H of the output, synchronized; the max over ranks."""
+    for _ in range(warmup):
+        w.e2e_step()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        w.e2e_step()
+        torch.cuda.current_stream().synchronize()
+    ms = (time.perf_counter() - t0) * 1e3 / steps
+    t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t[0])
+
+
+class _null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+
+def roofline(w: Workload, kern_ms: float, peaks):
+    hbm, tflops, kind = peaks
+    if w.bound == "hbm":
+        achieved = w.algorithmic() / (kern_ms * 1e-3) / 1e9
+        peak, unit = hbm, "GB/s"
+    else:
+        achieved = w.algorithmic() / (kern_ms * 1e-3) / 1e12
+        peak, unit = tflops, "TFLOP/s"
+    return {"bound": w.bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
+            "frac": round(achieved / peak, 4), "peak_source": kind,
+            "traffic": profile_traffic(w.name), "kernel": "attend_kernel",
+            "algorithmic_per_launch": w.algorithmic()}
+
+
+def cpu_baseline_c3(threads: int, budget_s: float = 20.0):
+    """The oracle's team-split decode of C3 sequences on the host (the reference's CPU path),
+    on a bounded sample: 8 of the 64 sequences, evenly spaced by length."""
+    import oracle
+    lengths = c3_lengths()
+    order = np.argsort(lengths)
+    sample = [int(i) for i in order[4::8]]
+    rng = np.random.default_rng(5)
+    caches, firsts = [], []
+    for i in sample:
+        n = int(lengths[i])
+        c = oracle.Cache(1, C3_HEADS, C3_KV, C3_D, n + 1)
+        c.keys[:] = rng.standard_normal(c.keys.shape, dtype=np.float32)
+        c.values[:] = rng.standard_normal(c.values.shape, dtype=np.float32)
+        caches.append(c)
+        firsts.append(n)
+    qkv = rng.standard_normal((len(sample), (C3_HEADS + 2 * C3_KV) * C3_D), dtype=np.float32)
+    mask = oracle.Mask.causal()
+
+    def one_pass():
+        for j, c in enumerate(caches):
+            c.attend(0, 1, firsts[j], mask, qkv[j:j + 1], qkv.shape[1], threads=threads)
+
+    one_pass()  # warm-up (harness::bench::time's one warm-up call)
+    t0 = time.perf_counter()
+    passes = 0
+    while True:
+        one_pass()
+        passes += 1
+        if time.perf_counter() - t0 > budget_s / 4 or passes >= 20:
+            break
+    dt = (time.perf_counter() - t0) / passes
+    oracle.release()
+    return len(sample) / dt, {
+        "sample": f"{len(sample)} of the 64 C3 sequences (every 8th by length, mean "
+                  f"{np.mean([lengths[i] for i in sample]):.0f} keys vs {np.mean(lengths):.0f}), "
+                  f"one forward call each, heads split over the thread team; mean of {passes} passes"}
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as distmod
+
+    import fusor_attn as fa
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        distmod.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                   device_id=torch.device("cuda", local))
+        dist = distmod
+    fa.lib()
+    peaks = measured_peaks()
+    steps, warmup = args.steps, max(args.warmup, 3)
+
+    def build(name):
+        if name in ("c3", "c3bf16"):
+            return C3Decode(torch, fa, rank, world, fa.F32 if name == "c3" else fa.BF16)
+        if name == "c1":
+            return SingleDecode(torch, fa, "c1", 14, 2, 64, 1024)
+        if name == "c4":
+            return SingleDecode(torch, fa, "c4", 16, 8, 128, 131072)
+        if name == "c2":
+            return C2Prefill(torch, fa)
+        raise SystemExit(f"unknown config {name}")
+
+    w = build(args.config)
+    sampler = ClockSampler(torch, local)
+    ms, kern_ms = time_workload(torch, dist, w, steps, warmup, sampler)
+    fa.device_status()
+    e2e_ms = time_e2e(torch, dist, w, min(steps, 200), warmup)
+    value = w.tokens / (ms * 1e-3) if args.config.startswith("c3") else w.tokens * world / (ms * 1e-3)
+    line = {
+        "metric": f"{args.config} attention tokens/s (decode attn HBM GB/s & prefill TFLOP/s as roofline)",
+        "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": steps,
+        "warmup": warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+        "scaling": "strong" if args.config.startswith("c3") else "weak", "vs_baseline": None,
+        "dtype": "f32" if args.config != "c3bf16" else "bf16-kv/f32",
+        "data": "synthetic N(0,1) (seeded), random keys/values of the config's shape",
+        "config": config_of(args.config, world),
+        "roofline": roofline(w, kern_ms, peaks),
+        "e2e": {"value": round((w.tokens if args.config.startswith("c3") else w.tokens * world) / (e2e_ms * 1e-3), 2),
+                "unit": "tokens/s", "ms_per_step": round(e2e_ms, 4),
+                "h2d_bytes_per_step": w.h2d, "d2h_bytes_per_step": w.d2h,
+                "path": "pinned host rows -> fa_attention_batch / fa_attention -> pinned host output"},
+        "gpu_launches": w.launches_per_step * steps,
+        "clocks": sampler.report(),
+    }
+    del w
+    torch.cuda.empty_cache()
+    if world == 1 and args.config == "c3" and not args.no_extras:
+        extras = {}
+        for name in ("c1", "c2", "c3bf16", "c4"):
+            x = build(name)
+            xs = min(steps, 200)
+            ms_x, kern_x = time_workload(torch, dist, x, xs, warmup)
+            extras[name] = {"tokens_per_s": round(x.tokens / (ms_x * 1e-3), 2),
+                            "ms_per_step": round(ms_x, 5), "steps": xs,
+                            "config": config_of(name, 1), "roofline": roofline(x, kern_x, peaks),
+                            "l2": "flushed between steps" if x.flush_l2 else "inputs larger than L2"}
+            del x
+            torch.cuda.empty_cache()
+        line["configs"] = extras
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config.startswith("c3"):
+        threads = min(host_threads(), C3_HEADS)
+        v, meta = cpu_baseline_c3(threads)
+        line["cpu_baseline"] = {"value": round(v, 3), "unit": "tokens/s", "cores": threads,
+                                "kind": "port", **meta}
+    fa.device_status()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def config_of(name, world):
+    cfgs = {
+        "c3": {"workload": "C3 batched GQA decode", "sequences": 64, "heads": 32, "kv_heads": 8,
+               "head_dim": 128, "cache_lengths": "U[512, 8192] seed 301", "mask": "causal",
+               "kv_dtype": "f32", "rope_base": 1e6},
+        "c3bf16": {"workload": "C3 batched GQA decode, bf16 cache", "sequences": 64, "heads": 32,
+                   "kv_heads": 8, "head_dim": 128, "kv_dtype": "bf16"},
+        "c1": {"workload": "C1 Qwen2-0.5B decode", "heads": 14, "kv_heads": 2, "head_dim": 64,
+               "position": 1024, "mask": "causal"},
+        "c2": {"workload": "C2 Qwen2-0.5B prefill", "rows": 512, "heads": 14, "kv_heads": 2,
+               "head_dim": 64, "mask": "causal"},
+        "c4": {"workload": "C4 long-context decode", "keys": 131073, "heads": 16, "kv_heads": 8,
+               "head_dim": 128},
+    }
+    c = dict(cfgs[name])
+    c["parallelism"] = f"sequences over {world} GPU(s), no collective" if name.startswith("c3") else f"replicas x{world}"
+    c["l2"] = "inputs larger than L2" if name.startswith("c3") or name == "c4" else "L2 flushed between steps"
+    return c
+
+
+# ---------------------------------------------------------------------------------------------
+# reference arm
+# ---------------------------------------------------------------------------------------------
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    if not args.config.startswith("c3"):
+        print(json.dumps({"impl": "reference", "unavailable": "reference arm implemented for c3"}))
+        return
+    import oracle
+    threads = min(host_threads(), C3_HEADS)
+    lengths = c3_lengths()
+    order = np.argsort(lengths)
+    sample = [int(i) for i in order[4::8]]
+    rng = np.random.default_rng(5)
+    caches = []
+    for i in sample:
+        n = int(lengths[i])
+        c = oracle.Cache(1, C3_HEADS, C3_KV, C3_D, n + 1)
+        c.keys[:] = rng.standard_normal(c.keys.shape, dtype=np.float32)
+        c.values[:] = rng.standard_normal(c.values.shape, dtype=np.float32)
+        caches.append((c, n))
+    qkv = rng.standard_normal((len(sample), (C3_HEADS + 2 * C3_KV) * C3_D), dtype=np.float32)
+    mask = oracle.Mask.causal()
+
+    def step():
+        for j, (c, n) in enumerate(caches):
+            c.attend(0, 1, n, mask, qkv[j:j + 1], qkv.shape[1], threads=threads)
+
+    for _ in range(max(args.warmup, 1)):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    ms = (time.perf_counter() - t0) * 1e3 / args.steps
+    oracle.release()
+    value = len(sample) / (ms * 1e-3)
+    sample_desc = (f"each step {len(sample)} of the 64 C3 sequences (every 8th by length), one "
+                   f"forward call each, heads split over {threads} threads")
+    print(json.dumps({
+        "impl": "reference", "metric": "c3 attention tokens/s (decode attn HBM GB/s & prefill TFLOP/s as roofline)",
+        "value": round(value, 3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1)",
+        "config": config_of("c3", 1),
+        "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads,
+                         "kind": "port", "sample": sample_desc},
+        "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": "fusor-ai is Rust and no Rust toolchain exists here: the oracle's C++ restatement "
+                "of its Scalar-backend f32 attention is timed",
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", default="c3", choices=["c1", "c2", "c3", "c3bf16", "c4"])
+    ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

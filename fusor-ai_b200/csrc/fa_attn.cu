@@ -1,0 +1,1045 @@
+// The C ABI of include/fa_attn.h: KvCache objects in HBM, argument checks that turn the
+// reference's panics into status codes, the per-call plan (chunks per row, work units) and the
+// kernel launches. There is no CPU fallback: without a CUDA device every compute entry point
+// returns FA_ERR_CUDA.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <climits>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "fa_attn.h"
+#include "fa_launch.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(FA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define FA_CUDA(call, what)                     \
+  do {                                          \
+    cudaError_t e_ = (call);                    \
+    if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+  } while (0)
+
+bool supported_head_dim(int d) { return d == 16 || d == 32 || d == 64 || d == 128 || d == 256; }
+
+// Per-device state: the SM count and the device error word.
+struct Device {
+  int sms = 0;
+  unsigned* err = nullptr;
+  std::atomic<int> epoch{0};  // bumped when a timeout is seen: caches re-zero their counters
+};
+
+std::mutex g_devices_mutex;
+Device g_devices[64];
+
+int device_state(int device, Device** out) {
+  if (device < 0 || device >= 64) return fail(FA_ERR_ARG, "device %d out of range", device);
+  std::lock_guard<std::mutex> lock(g_devices_mutex);
+  Device& d = g_devices[device];
+  if (d.err == nullptr) {
+    int prev = 0;
+    FA_CUDA(cudaGetDevice(&prev), "cudaGetDevice");
+    FA_CUDA(cudaSetDevice(device), "cudaSetDevice");
+    FA_CUDA(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, device),
+            "cudaDeviceGetAttribute");
+    FA_CUDA(cudaMalloc(&d.err, sizeof(unsigned)), "cudaMalloc(error word)");
+    FA_CUDA(cudaMemset(d.err, 0, sizeof(unsigned)), "cudaMemset(error word)");
+    cudaSetDevice(prev);
+  }
+  *out = &d;
+  return FA_OK;
+}
+
+// Restores the caller's current device on scope exit.
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int device) {
+    if (cudaGetDevice(&prev) == cudaSuccess && prev != device) cudaSetDevice(device);
+    else prev = -1;
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+// A grow-only device buffer.
+struct Buffer {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+  int ensure(size_t want, cudaStream_t stream) {
+    if (want <= bytes) return FA_OK;
+    if (ptr != nullptr) {
+      FA_CUDA(cudaStreamSynchronize(stream), "cudaStreamSynchronize(workspace growth)");
+      cudaFree(ptr);
+      ptr = nullptr;
+      bytes = 0;
+    }
+    const size_t size = std::max<size_t>(want + want / 2, 1 << 16);
+    FA_CUDA(cudaMalloc(&ptr, size), "cudaMalloc(workspace)");
+    bytes = size;
+    return FA_OK;
+  }
+  void release() {
+    if (ptr != nullptr) cudaFree(ptr);
+    ptr = nullptr;
+    bytes = 0;
+  }
+};
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+}  // namespace
+
+struct fa_kvcache {
+  int layers, heads, kv_heads, head_dim, capacity, dtype, device;
+  void* keys = nullptr;
+  void* values = nullptr;
+  Device* dev = nullptr;
+  Buffer work;       // queries and partials
+  Buffer staging;    // fa_attention_host's device copies of the host rows
+  Buffer counters;   // arrival counters (kept zero between launches)
+  int counters_epoch = 0;
+  size_t elem() const { return dtype == FA_F32 ? 4 : 2; }
+  int64_t layer_elems() const { return int64_t(kv_heads) * capacity * head_dim; }
+};
+
+namespace {
+
+int check_cache(const fa_kvcache* cache) {
+  if (cache == nullptr) return fail(FA_ERR_ARG, "null cache");
+  return FA_OK;
+}
+
+int ensure_counters(fa_kvcache* c, size_t n, cudaStream_t stream) {
+  const size_t want = n * sizeof(int);
+  const int epoch = c->dev->epoch.load();
+  if (want <= c->counters.bytes && epoch == c->counters_epoch) return FA_OK;
+  if (int rc = c->counters.ensure(want, stream)) return rc;
+  FA_CUDA(cudaMemsetAsync(c->counters.ptr, 0, c->counters.bytes, stream), "cudaMemsetAsync(counters)");
+  c->counters_epoch = epoch;
+  return FA_OK;
+}
+
+// Checks a span against the cache (Transformer::run, transformer.rs:329-341; Mask::Groups's
+// ends, transformer.rs:107-110) and copies its Groups ends.
+int check_span(const fa_kvcache* c, const fa_span* span, std::vector<int>* ends) {
+  if (span == nullptr) return fail(FA_ERR_ARG, "null span");
+  if (span->rows < 0 || span->first < 0) return fail(FA_ERR_ARG, "negative span");
+  const fa_mask& m = span->mask;
+  if (m.kind < FA_MASK_CAUSAL || m.kind > FA_MASK_GROUPS)
+    return fail(FA_ERR_ARG, "mask kind %d", m.kind);
+  const int64_t end = int64_t(span->first) + span->rows;
+  if (m.kind == FA_MASK_WINDOW && m.window < 1) return fail(FA_ERR_ARG, "window %d", m.window);
+  const int64_t reach = m.kind == FA_MASK_WINDOW ? int64_t(m.window) + span->rows : end;
+  if (reach > c->capacity)
+    return fail(FA_ERR_CAPACITY, "the cache holds every key the span sees: %lld > capacity %d",
+                (long long)reach, c->capacity);
+  ends->clear();
+  if (m.kind == FA_MASK_GROUPS) {
+    if (m.n_ends < 1 || m.ends == nullptr || m.n_ends > fa::kMaxEnds)
+      return fail(FA_ERR_ARG, "Groups needs 1..%d ends", fa::kMaxEnds);
+    if (m.state < 0 || m.state > end) return fail(FA_ERR_ARG, "Groups state %d", m.state);
+    for (int i = 0; i < m.n_ends; ++i) {
+      if (m.ends[i] <= (i == 0 ? m.state - 1 : m.ends[i - 1]) || m.ends[i] > end)
+        return fail(FA_ERR_ARG, "Groups ends must rise after the state and end by the call's end");
+      ends->push_back(m.ends[i]);
+    }
+    if (ends->back() != end) return fail(FA_ERR_ARG, "the last group ends with the call");
+  }
+  return FA_OK;
+}
+
+float query_scale(int head_dim) {
+  return float((1.0 / std::sqrt(double(head_dim))) * 1.4426950408889634);
+}
+
+int heads_per_cta(int group) {
+  if (group >= 8) return 8;
+  if (group >= 4) return group == 4 ? 4 : 8;
+  return group;  // 1, 2 or 3 -> 1, 2, 4
+}
+
+int pow2_heads(int group) {
+  const int g = heads_per_cta(group);
+  return g == 3 ? 4 : g;
+}
+
+// Work units wanted per launch: four waves of two CTAs per SM.
+int target_units(const Device* dev) { return std::max(dev->sms, 1) * 2 * 4; }
+
+struct Plan {
+  int g = 1, hgroups = 1, kv_groups = 1, chunks = 1;
+};
+
+Plan plan_span(const fa_kvcache* c, int rows, int max_keys) {
+  Plan p;
+  const int group = c->heads / c->kv_heads;
+  p.g = pow2_heads(group);
+  p.hgroups = (group + p.g - 1) / p.g;
+  p.kv_groups = c->kv_heads * p.hgroups;
+  const int tile = fa::tile_keys(c->head_dim, c->dtype == FA_F32 ? fa::kKtF32 : fa::kKtBf16);
+  const int max_chunks = std::max(1, (max_keys + tile - 1) / tile);
+  const int want = (target_units(c->dev) + rows * p.kv_groups - 1) / std::max(rows * p.kv_groups, 1);
+  p.chunks = std::min(max_chunks, std::max(1, want));
+  return p;
+}
+
+// Workspace layout of one call: rotated queries, chunk partials (o then max/sum).
+struct Work {
+  float* q = nullptr;
+  float* part_o = nullptr;
+  float* part_ml = nullptr;
+};
+
+int ensure_work(fa_kvcache* c, size_t q_floats, size_t part_slots, size_t unused,
+                cudaStream_t stream, Work* w) {
+  (void)unused;
+  const size_t q_bytes = align_up(q_floats * 4, 256);
+  const size_t o_bytes = align_up(part_slots * c->head_dim * 4, 256);
+  const size_t ml_bytes = align_up(part_slots * 2 * 4, 256);
+  if (int rc = c->work.ensure(q_bytes + o_bytes + ml_bytes, stream)) return rc;
+  unsigned char* base = static_cast<unsigned char*>(c->work.ptr);
+  w->q = reinterpret_cast<float*>(base);
+  w->part_o = reinterpret_cast<float*>(base + q_bytes);
+  w->part_ml = reinterpret_cast<float*>(base + q_bytes + o_bytes);
+  return FA_OK;
+}
+
+void fill_common(fa::AttendCommon* a, const fa_kvcache* c, const Plan& p) {
+  a->heads = c->heads;
+  a->kv_heads = c->kv_heads;
+  a->group = c->heads / c->kv_heads;
+  a->hgroups = p.hgroups;
+  a->kv_stride = int64_t(c->capacity) * c->head_dim;
+  a->key_stride = c->head_dim;
+  a->q_scale = query_scale(c->head_dim);
+  a->err = c->dev->err;
+}
+
+cudaError_t launch_attend_d(int head_dim, const fa::AttendLaunch& l, cudaStream_t stream) {
+  switch (head_dim) {
+    case 16: return fa::launch_attend<16>(l, stream);
+    case 32: return fa::launch_attend<32>(l, stream);
+    case 64: return fa::launch_attend<64>(l, stream);
+    case 128: return fa::launch_attend<128>(l, stream);
+    case 256: return fa::launch_attend<256>(l, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+const unsigned char* layer_ptr(const fa_kvcache* c, const void* base, int layer) {
+  return static_cast<const unsigned char*>(base) + size_t(layer) * c->layer_elems() * c->elem();
+}
+
+// The plan of a span over a cache: the largest key count of its rows decides the chunks.
+Plan plan_for_span(const fa_kvcache* c, const fa_span* span, const std::vector<int>& ends) {
+  int max_keys = 0;
+  for (int r = 0; r < span->rows; ++r) {
+    fa::Runs runs = fa::mask_runs(span->mask.kind, span->mask.window, span->mask.state,
+                                  int(ends.size()), ends.data(), span->first + r,
+                                  span->first + span->rows);
+    max_keys = std::max(max_keys, runs.n0 + runs.n1);
+  }
+  return plan_span(c, std::max(span->rows, 1), max_keys);
+}
+
+// The attention of a span's rows over the cache, queries already rotated and scaled in q;
+// `w` holds the partials of `p`.
+int attend_rows(fa_kvcache* c, int layer, const fa_span* span, const std::vector<int>& ends,
+                const Plan& p, const Work& w, const float* q, int64_t q_stride, float* out,
+                int64_t out_stride, float* partial_out, cudaStream_t stream) {
+  const int rows = span->rows;
+  if (rows == 0) return FA_OK;
+  if (int rc = ensure_counters(c, size_t(rows) * p.kv_groups, stream)) return rc;
+  fa::SpanArgs args{};
+  fill_common(&args.c, c, p);
+  args.c.q = q;
+  args.c.q_stride = q_stride;
+  args.c.out = out;
+  args.c.out_stride = out_stride;
+  args.c.partial_out = partial_out;
+  args.c.part_o = w.part_o;
+  args.c.part_ml = w.part_ml;
+  args.c.counters = static_cast<int*>(c->counters.ptr);
+  args.k = layer_ptr(c, c->keys, layer);
+  args.v = layer_ptr(c, c->values, layer);
+  args.capacity = c->capacity;
+  args.rows = rows;
+  args.first = span->first;
+  args.end = span->first + rows;
+  args.kind = span->mask.kind;
+  args.window = span->mask.window;
+  args.state = span->mask.state;
+  args.n_ends = int(ends.size());
+  args.chunks = p.chunks;
+  args.rows_per_image = rows;
+  args.keys_per_image = 0;
+  for (size_t i = 0; i < ends.size(); ++i) args.ends[i] = ends[i];
+  fa::AttendLaunch l{c->dtype == FA_F32 ? fa::kKtF32 : fa::kKtBf16, p.g, false, &args, nullptr,
+                     rows * p.kv_groups * p.chunks};
+  cudaError_t e = launch_attend_d(c->head_dim, l, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "attend launch");
+  return FA_OK;
+}
+
+int rope_rows(fa_kvcache* c, int layer, const fa_span* span, int rope, const float* angles,
+              const fa_head_norm* norm, const float* qkv, int64_t qkv_stride, float* q_out,
+              int64_t q_out_stride, float q_scale, bool keep, cudaStream_t stream) {
+  if (span->rows == 0) return FA_OK;
+  fa::RopeArgs a{};
+  a.heads = c->heads;
+  a.kv_heads = c->kv_heads;
+  a.head_dim = c->head_dim;
+  a.rope = rope;
+  a.n_rows = span->rows;
+  a.qkv = qkv;
+  a.qkv_stride = qkv_stride;
+  a.angles = angles;
+  a.q_norm = norm ? norm->q_norm : nullptr;
+  a.k_norm = norm ? norm->k_norm : nullptr;
+  a.eps = norm ? norm->eps : 0.0f;
+  a.q_out = q_out;
+  a.q_out_stride = q_out_stride;
+  a.q_scale = q_scale;
+  a.kv_stride = int64_t(c->capacity) * c->head_dim;
+  a.keep = keep ? 1 : 0;
+  a.batch = 0;
+  a.first = span->first;
+  a.keep_rows[0].k = const_cast<unsigned char*>(layer_ptr(c, c->keys, layer));
+  a.keep_rows[0].v = const_cast<unsigned char*>(layer_ptr(c, c->values, layer));
+  a.keep_rows[0].capacity = c->capacity;
+  cudaError_t e = fa::launch_rope(c->dtype == FA_F32 ? fa::kKtF32 : fa::kKtBf16, a, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "rope launch");
+  return FA_OK;
+}
+
+int check_layer(const fa_kvcache* c, int layer) {
+  if (layer < 0 || layer >= c->layers)
+    return fail(FA_ERR_SHAPE, "layer %d of a %d-layer cache", layer, c->layers);
+  return FA_OK;
+}
+
+int check_rope(int rope, const float* angles) {
+  if (rope < FA_ROPE_NONE || rope > FA_ROPE_INTERLEAVED) return fail(FA_ERR_ARG, "rope %d", rope);
+  if (rope != FA_ROPE_NONE && angles == nullptr) return fail(FA_ERR_ARG, "RoPE without angles");
+  return FA_OK;
+}
+
+// Rotary::new + spatially_scaled (rotary.rs:117-168): the frequencies and the axis of each.
+int rotary_frequencies(const fa_rotation* r, int head_dim, std::vector<float>* inv_freq,
+                       std::vector<int>* axes) {
+  const int half = head_dim / 2;
+  auto inv = [&](int dims, std::vector<float>* out) {
+    out->resize(dims / 2);
+    for (int i = 0; i < dims / 2; ++i)
+      (*out)[i] = 1.0f / std::pow(r->base, float(2 * i) / float(dims));
+  };
+  auto sections = [&](const int32_t* s) {
+    if (s[0] < 0 || s[1] < 0 || s[2] < 0 || s[0] + s[1] + s[2] != half) return false;
+    axes->clear();
+    for (int a = 0; a < 3; ++a) axes->insert(axes->end(), s[a], a);
+    return true;
+  };
+  axes->assign(half, 0);
+  switch (r->kind) {
+    case FA_ROT_SEQUENCE:
+      inv(head_dim, inv_freq);
+      break;
+    case FA_ROT_LINEAR:
+      if (r->params[0] <= 0) return fail(FA_ERR_ARG, "Linear factor %d", r->params[0]);
+      inv(head_dim, inv_freq);
+      for (auto& f : *inv_freq) f = f / float(r->params[0]);
+      break;
+    case FA_ROT_PARTIAL:
+      inv(head_dim, inv_freq);
+      for (int i = std::max(0, r->params[0]); i < half; ++i) (*inv_freq)[i] = 0.0f;
+      break;
+    case FA_ROT_MULTIMODAL:
+      inv(head_dim, inv_freq);
+      if (!sections(r->params)) return fail(FA_ERR_ARG, "sections do not cover half a head");
+      break;
+    case FA_ROT_AXES:
+    case FA_ROT_GRID: {
+      const int32_t grid[3] = {0, half / 2, half / 2};
+      const int32_t* s = r->kind == FA_ROT_GRID ? grid : r->params;
+      if (!sections(s)) return fail(FA_ERR_ARG, "sections do not cover half a head");
+      inv_freq->clear();
+      for (int a = 0; a < 3; ++a) {
+        std::vector<float> part;
+        inv(2 * s[a], &part);
+        inv_freq->insert(inv_freq->end(), part.begin(), part.end());
+      }
+      break;
+    }
+    case FA_ROT_MULTIMODAL_INTERLEAVED:
+      inv(head_dim, inv_freq);
+      for (int i = 0; i < half; ++i) {
+        const int m = i % 3;
+        (*axes)[i] = (m == 1 && i < 3 * r->params[1]) ? 1 : (m == 2 && i < 3 * r->params[2]) ? 2 : 0;
+      }
+      break;
+    default:
+      return fail(FA_ERR_ARG, "rotation kind %d", r->kind);
+  }
+  for (int i = 0; i < half; ++i)
+    if ((*axes)[i] != 0) (*inv_freq)[i] = (*inv_freq)[i] * r->spatial_scale;
+  return FA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* fa_last_error(void) { return g_last_error.c_str(); }
+
+int fa_capabilities(int32_t* flags, int32_t* head_dims, int32_t max_head_dims,
+                    int32_t* n_head_dims) {
+  static const int32_t dims[] = {16, 32, 64, 128, 256};
+  if (flags) *flags = 1 | 2;
+  const int n = int(sizeof dims / sizeof dims[0]);
+  if (head_dims)
+    for (int i = 0; i < n && i < max_head_dims; ++i) head_dims[i] = dims[i];
+  if (n_head_dims) *n_head_dims = n;
+  return FA_OK;
+}
+
+int fa_kvcache_create(int32_t layers, int32_t heads, int32_t kv_heads, int32_t head_dim,
+                      int32_t capacity, int32_t dtype, int32_t device, fa_kvcache** out) {
+  if (out == nullptr) return fail(FA_ERR_ARG, "null out");
+  *out = nullptr;
+  if (layers < 1 || heads < 1 || kv_heads < 1 || capacity < 1)
+    return fail(FA_ERR_ARG, "a cache of %d layers, %d heads, %d kv heads, capacity %d", layers,
+                heads, kv_heads, capacity);
+  if (heads % kv_heads != 0)
+    return fail(FA_ERR_SHAPE, "%d heads over %d KV heads", heads, kv_heads);
+  if (!supported_head_dim(head_dim)) return fail(FA_ERR_UNSUPPORTED, "head_dim %d", head_dim);
+  if (dtype != FA_F32 && dtype != FA_BF16) return fail(FA_ERR_ARG, "dtype %d", dtype);
+  Device* dev = nullptr;
+  if (int rc = device_state(device, &dev)) return rc;
+  DeviceGuard guard(device);
+  auto* c = new fa_kvcache();
+  c->layers = layers;
+  c->heads = heads;
+  c->kv_heads = kv_heads;
+  c->head_dim = head_dim;
+  c->capacity = capacity;
+  c->dtype = dtype;
+  c->device = device;
+  c->dev = dev;
+  const size_t bytes = size_t(layers) * c->layer_elems() * c->elem();
+  cudaError_t e = cudaMalloc(&c->keys, bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&c->values, bytes);
+  if (e == cudaSuccess) e = cudaMemset(c->keys, 0, bytes);
+  if (e == cudaSuccess) e = cudaMemset(c->values, 0, bytes);
+  if (e != cudaSuccess) {
+    fa_kvcache_destroy(c);
+    return cuda_fail(e, "cache allocation");
+  }
+  *out = c;
+  return FA_OK;
+}
+
+int fa_kvcache_destroy(fa_kvcache* cache) {
+  if (cache == nullptr) return FA_OK;
+  DeviceGuard guard(cache->device);
+  if (cache->keys) cudaFree(cache->keys);
+  if (cache->values) cudaFree(cache->values);
+  cache->work.release();
+  cache->staging.release();
+  cache->counters.release();
+  delete cache;
+  return FA_OK;
+}
+
+int fa_kvcache_data(const fa_kvcache* cache, void** keys, void** values, int32_t* shape5,
+                    int32_t* dtype) {
+  if (int rc = check_cache(cache)) return rc;
+  if (keys) *keys = cache->keys;
+  if (values) *values = cache->values;
+  if (shape5) {
+    shape5[0] = cache->layers;
+    shape5[1] = cache->heads;
+    shape5[2] = cache->kv_heads;
+    shape5[3] = cache->head_dim;
+    shape5[4] = cache->capacity;
+  }
+  if (dtype) *dtype = cache->dtype;
+  return FA_OK;
+}
+
+int fa_kvcache_reserve(fa_kvcache* cache, int32_t rows) {
+  if (int rc = check_cache(cache)) return rc;
+  if (rows < 1) return fail(FA_ERR_ARG, "rows %d", rows);
+  DeviceGuard guard(cache->device);
+  const Plan p = plan_span(cache, rows, cache->capacity);
+  Work w;
+  const size_t staging = size_t(rows) * (cache->heads + 2 * cache->kv_heads) * cache->head_dim * 4 +
+                         size_t(rows) * cache->head_dim * 4 + size_t(rows) * cache->heads * cache->head_dim * 4;
+  if (int rc = ensure_work(cache, size_t(rows) * cache->heads * cache->head_dim,
+                           size_t(rows) * p.chunks * cache->heads, 0, nullptr, &w))
+    return rc;
+  if (int rc = cache->staging.ensure(staging, nullptr)) return rc;
+  if (int rc = ensure_counters(cache, size_t(rows) * p.kv_groups, nullptr)) return rc;
+  FA_CUDA(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+  return FA_OK;
+}
+
+int fa_kvcache_copy_rows(const fa_kvcache* cache, int32_t rows, void* keys_out,
+                         void* values_out, void* stream) {
+  if (int rc = check_cache(cache)) return rc;
+  if (rows < 0 || rows > cache->capacity)
+    return fail(FA_ERR_CAPACITY, "%d rows don't fit a cache of %d", rows, cache->capacity);
+  if (keys_out == nullptr || values_out == nullptr) return fail(FA_ERR_ARG, "null output");
+  DeviceGuard guard(cache->device);
+  const size_t width = size_t(rows) * cache->head_dim * cache->elem();
+  const size_t pitch = size_t(cache->capacity) * cache->head_dim * cache->elem();
+  const size_t blocks = size_t(cache->layers) * cache->kv_heads;
+  if (width == 0) return FA_OK;
+  auto s = static_cast<cudaStream_t>(stream);
+  FA_CUDA(cudaMemcpy2DAsync(keys_out, width, cache->keys, pitch, width, blocks,
+                            cudaMemcpyDeviceToDevice, s), "copy_rows keys");
+  FA_CUDA(cudaMemcpy2DAsync(values_out, width, cache->values, pitch, width, blocks,
+                            cudaMemcpyDeviceToDevice, s), "copy_rows values");
+  return FA_OK;
+}
+
+int fa_kvcache_put_rows(fa_kvcache* cache, int32_t rows, const void* keys, const void* values,
+                        void* stream) {
+  if (int rc = check_cache(cache)) return rc;
+  if (rows < 0 || rows > cache->capacity)
+    return fail(FA_ERR_CAPACITY, "%d rows don't fit a cache of %d", rows, cache->capacity);
+  if (keys == nullptr || values == nullptr) return fail(FA_ERR_ARG, "null input");
+  DeviceGuard guard(cache->device);
+  const size_t width = size_t(rows) * cache->head_dim * cache->elem();
+  const size_t pitch = size_t(cache->capacity) * cache->head_dim * cache->elem();
+  const size_t blocks = size_t(cache->layers) * cache->kv_heads;
+  if (width == 0) return FA_OK;
+  auto s = static_cast<cudaStream_t>(stream);
+  FA_CUDA(cudaMemcpy2DAsync(cache->keys, pitch, keys, width, width, blocks,
+                            cudaMemcpyDeviceToDevice, s), "put_rows keys");
+  FA_CUDA(cudaMemcpy2DAsync(cache->values, pitch, values, width, width, blocks,
+                            cudaMemcpyDeviceToDevice, s), "put_rows values");
+  return FA_OK;
+}
+
+int fa_rotary_angles(const fa_rotation* rotation, int32_t head_dim, const fa_position* positions,
+                     int32_t rows, float* angles_out) {
+  if (rotation == nullptr || (rows > 0 && (positions == nullptr || angles_out == nullptr)))
+    return fail(FA_ERR_ARG, "null argument");
+  if (head_dim < 2 || head_dim % 2 != 0) return fail(FA_ERR_ARG, "head_dim %d", head_dim);
+  std::vector<float> inv_freq;
+  std::vector<int> axes;
+  if (int rc = rotary_frequencies(rotation, head_dim, &inv_freq, &axes)) return rc;
+  const int half = head_dim / 2;
+  for (int r = 0; r < rows; ++r) {
+    const int32_t along[3] = {positions[r].temporal, positions[r].height, positions[r].width};
+    float* cos = angles_out + size_t(r) * head_dim;
+    float* sin = cos + half;
+    for (int i = 0; i < half; ++i) {
+      const float angle = float(along[axes[i]]) * inv_freq[i];
+      cos[i] = std::cos(angle);
+      sin[i] = std::sin(angle);
+    }
+  }
+  return FA_OK;
+}
+
+int fa_attention_input(fa_kvcache* cache, int32_t layer, const fa_span* span, int32_t rope,
+                       const float* angles, const fa_head_norm* norm, const float* qkv,
+                       int64_t qkv_stride, float* q_out, void* stream) {
+  if (int rc = check_cache(cache)) return rc;
+  if (int rc = check_layer(cache, layer)) return rc;
+  std::vector<int> ends;
+  if (int rc = check_span(cache, span, &ends)) return rc;
+  if (int rc = check_rope(rope, angles)) return rc;
+  if (qkv == nullptr && span->rows > 0) return fail(FA_ERR_ARG, "null qkv");
+  if (qkv_stride < int64_t(cache->heads + 2 * cache->kv_heads) * cache->head_dim)
+    return fail(FA_ERR_SHAPE, "qkv rows of %lld values hold fewer than the heads",
+                (long long)qkv_stride);
+  DeviceGuard guard(cache->device);
+  return rope_rows(cache, layer, span, rope, angles, norm, qkv, qkv_stride, q_out,
+                   int64_t(cache->heads) * cache->head_dim, 1.0f, true,
+                   static_cast<cudaStream_t>(stream));
+}
+
+int fa_attend(fa_kvcache* cache, int32_t layer, const fa_span* span, const float* q,
+              int64_t q_stride, float* out, int64_t out_stride, void* stream) {
+  if (int rc = check_cache(cache)) return rc;
+  if (int rc = check_layer(cache, layer)) return rc;
+  std::vector<int> ends;
+  if (int rc = check_span(cache, span, &ends)) return rc;
+  const int64_t width = int64_t(cache->heads) * cache->head_dim;
+  if (span->rows > 0 && (q == nullptr || out == nullptr)) return fail(FA_ERR_ARG, "null q or out");
+  if (q_stride < width || out_stride < width) return fail(FA_ERR_SHAPE, "row strides below heads x head_dim");
+  DeviceGuard guard(cache->device);
+  auto s = static_cast<cudaStream_t>(stream);
+  if (span->rows == 0) return FA_OK;
+  Work w;
+  const Plan p = plan_for_span(cache, span, ends);
+  if (int rc = ensure_work(cache, 0, size_t(span->rows) * p.chunks * cache->heads, 0, s, &w))
+    return rc;
+  return attend_rows(cache, layer, span, ends, p, w, q, q_stride, out, out_stride, nullptr, s);
+}
+
+int fa_attention(fa_kvcache* cache, int32_t layer, const fa_span* span, int32_t rope,
+                 const float* angles, const fa_head_norm* norm, const float* qkv,
+                 int64_t qkv_stride, float* out, int64_t out_stride, void* stream) {
+  if (int rc = check_cache(cache)) return rc;
+  if (int rc = check_layer(cache, layer)) return rc;
+  std::vector<int> ends;
+  if (int rc = check_span(cache, span, &ends)) return rc;
+  if (int rc = check_rope(rope, angles)) return rc;
+  const int64_t width = int64_t(cache->heads) * cache->head_dim;
+  if (span->rows > 0 && (qkv == nullptr || out == nullptr)) return fail(FA_ERR_ARG, "null qkv or out");
+  if (qkv_stride < int64_t(cache->heads + 2 * cache->kv_heads) * cache->head_dim || out_stride < width)
+    return fail(FA_ERR_SHAPE, "row strides below the heads' widths");
+  if (span->rows == 0) return FA_OK;
+  DeviceGuard guard(cache->device);
+  auto s = static_cast<cudaStream_t>(stream);
+  Work w;
+  const Plan p = plan_for_span(cache, span, ends);
+  if (int rc = ensure_work(cache, size_t(span->rows) * width,
+                           size_t(span->rows) * p.chunks * cache->heads, 0, s, &w))
+    return rc;
+  if (int rc = rope_rows(cache, layer, span, rope, angles, norm, qkv, qkv_stride, w.q, width,
+                         1.0f, true, s))
+    return rc;
+  return attend_rows(cache, layer, span, ends, p, w, w.q, width, out, out_stride, nullptr, s);
+}
+
+int fa_attention_host(fa_kvcache* cache, int32_t layer, const fa_span* span, int32_t rope,
+                      const float* angles_host, const fa_head_norm* norm, const float* qkv_host,
+                      int64_t qkv_stride, float* out_host, int64_t out_stride, void* stream) {
+  if (int rc = check_cache(cache)) return rc;
+  if (span == nullptr) return fail(FA_ERR_ARG, "null span");
+  if (span->rows == 0) return FA_OK;
+  if (qkv_host == nullptr || out_host == nullptr) return fail(FA_ERR_ARG, "null qkv or out");
+  if (int rc = check_rope(rope, angles_host)) return rc;
+  if (qkv_stride < int64_t(cache->heads + 2 * cache->kv_heads) * cache->head_dim ||
+      out_stride < int64_t(cache->heads) * cache->head_dim)
+    return fail(FA_ERR_SHAPE, "row strides below the heads' widths");
+  DeviceGuard guard(cache->device);
+  auto s = static_cast<cudaStream_t>(stream);
+  const int rows = span->rows;
+  const int64_t width = int64_t(cache->heads) * cache->head_dim;
+  const int64_t units = int64_t(cache->heads + 2 * cache->kv_heads) * cache->head_dim;
+  // Staging: the rows' qkv (packed to the units' width), their angles and outputs.
+  const size_t staging = size_t(rows) * units * 4 + size_t(rows) * cache->head_dim * 4 +
+                         size_t(rows) * width * 4;
+  if (int rc = cache->staging.ensure(staging, s)) return rc;
+  float* qkv_dev = static_cast<float*>(cache->staging.ptr);
+  float* angles_dev = qkv_dev + size_t(rows) * units;
+  float* out_dev = angles_dev + size_t(rows) * cache->head_dim;
+  FA_CUDA(cudaMemcpy2DAsync(qkv_dev, units * 4, qkv_host, qkv_stride * 4, units * 4, rows,
+                            cudaMemcpyHostToDevice, s), "qkv to device");
+  if (rope != FA_ROPE_NONE)
+    FA_CUDA(cudaMemcpyAsync(angles_dev, angles_host, size_t(rows) * cache->head_dim * 4,
+                            cudaMemcpyHostToDevice, s), "angles to device");
+  if (int rc = fa_attention(cache, layer, span, rope, rope != FA_ROPE_NONE ? angles_dev : nullptr,
+                            norm, qkv_dev, units, out_dev, width, stream))
+    return rc;
+  FA_CUDA(cudaMemcpy2DAsync(out_host, out_stride * 4, out_dev, width * 4, width * 4, rows,
+                            cudaMemcpyDeviceToHost, s), "out to host");
+  FA_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+  return FA_OK;
+}
+
+namespace {
+
+// The checks and the per-row key runs of a batch of one-row spans over caches of one shape.
+int check_batch(fa_kvcache* const* caches, const fa_span* spans, int32_t batch, int32_t layer,
+                std::vector<fa::Runs>* runs, int64_t* total_keys) {
+  if (caches == nullptr || spans == nullptr) return fail(FA_ERR_ARG, "null caches or spans");
+  if (batch < 0 || batch > 1024) return fail(FA_ERR_ARG, "batch %d (1..1024)", batch);
+  if (batch == 0) return FA_OK;
+  const fa_kvcache* c0 = caches[0];
+  if (int rc = check_cache(c0)) return rc;
+  if (int rc = check_layer(c0, layer)) return rc;
+  runs->assign(batch, fa::Runs{0, 0, 0, 0});
+  std::vector<int> ends;
+  *total_keys = 0;
+  for (int i = 0; i < batch; ++i) {
+    const fa_kvcache* c = caches[i];
+    if (int rc = check_cache(c)) return rc;
+    if (c->heads != c0->heads || c->kv_heads != c0->kv_heads || c->head_dim != c0->head_dim ||
+        c->layers != c0->layers || c->dtype != c0->dtype || c->device != c0->device ||
+        c->capacity != c0->capacity)
+      return fail(FA_ERR_SHAPE, "sequence %d's cache differs in shape from the first", i);
+    if (spans[i].rows != 1) return fail(FA_ERR_ARG, "batched spans are one row (decode)");
+    if (spans[i].mask.kind == FA_MASK_GROUPS)
+      return fail(FA_ERR_UNSUPPORTED, "Groups masks in a batched decode");
+    if (int rc = check_span(c, &spans[i], &ends)) return rc;
+    (*runs)[i] = fa::mask_runs(spans[i].mask.kind, spans[i].mask.window, 0, 0, nullptr,
+                               spans[i].first, spans[i].first + 1);
+    *total_keys += (*runs)[i].n0 + (*runs)[i].n1;
+  }
+  return FA_OK;
+}
+
+}  // namespace
+
+int fa_attention_input_batch(fa_kvcache* const* caches, const fa_span* spans, int32_t batch,
+                             int32_t layer, int32_t rope, const float* angles,
+                             const fa_head_norm* norm, const float* qkv, int64_t qkv_stride,
+                             float* q_out, int64_t q_out_stride, void* stream) {
+  std::vector<fa::Runs> runs;
+  int64_t total_keys = 0;
+  if (int rc = check_batch(caches, spans, batch, layer, &runs, &total_keys)) return rc;
+  if (batch == 0) return FA_OK;
+  if (int rc = check_rope(rope, angles)) return rc;
+  fa_kvcache* c0 = caches[0];
+  const int64_t width = int64_t(c0->heads) * c0->head_dim;
+  if (qkv == nullptr) return fail(FA_ERR_ARG, "null qkv");
+  if (qkv_stride < int64_t(c0->heads + 2 * c0->kv_heads) * c0->head_dim ||
+      (q_out != nullptr && q_out_stride < width))
+    return fail(FA_ERR_SHAPE, "row strides below the heads' widths");
+  DeviceGuard guard(c0->device);
+  auto s = static_cast<cudaStream_t>(stream);
+  const int kt = c0->dtype == FA_F32 ? fa::kKtF32 : fa::kKtBf16;
+  for (int first = 0; first < batch; first += fa::kMaxBatchRows) {
+    const int n = std::min(batch - first, fa::kMaxBatchRows);
+    fa::RopeArgs ra{};
+    ra.heads = c0->heads;
+    ra.kv_heads = c0->kv_heads;
+    ra.head_dim = c0->head_dim;
+    ra.rope = rope;
+    ra.n_rows = n;
+    ra.qkv = qkv + int64_t(first) * qkv_stride;
+    ra.qkv_stride = qkv_stride;
+    ra.angles = angles ? angles + int64_t(first) * c0->head_dim : nullptr;
+    ra.q_norm = norm ? norm->q_norm : nullptr;
+    ra.k_norm = norm ? norm->k_norm : nullptr;
+    ra.eps = norm ? norm->eps : 0.0f;
+    ra.q_out = q_out ? q_out + int64_t(first) * q_out_stride : nullptr;
+    ra.q_out_stride = q_out_stride;
+    ra.q_scale = 1.0f;
+    ra.kv_stride = int64_t(c0->capacity) * c0->head_dim;
+    ra.keep = 1;
+    ra.batch = 1;
+    for (int i = 0; i < n; ++i) {
+      const fa_kvcache* c = caches[first + i];
+      ra.keep_rows[i].k = const_cast<unsigned char*>(layer_ptr(c, c->keys, layer));
+      ra.keep_rows[i].v = const_cast<unsigned char*>(layer_ptr(c, c->values, layer));
+      ra.keep_rows[i].capacity = c->capacity;
+      ra.keep_rows[i].position = spans[first + i].first;
+    }
+    cudaError_t e = fa::launch_rope(kt, ra, s);
+    if (e != cudaSuccess) return cuda_fail(e, "rope launch");
+  }
+  return FA_OK;
+}
+
+int fa_attend_batch(fa_kvcache* const* caches, const fa_span* spans, int32_t batch,
+                    int32_t layer, const float* q, int64_t q_stride, float* out,
+                    int64_t out_stride, void* stream) {
+  std::vector<fa::Runs> runs;
+  int64_t total_keys = 0;
+  if (int rc = check_batch(caches, spans, batch, layer, &runs, &total_keys)) return rc;
+  if (batch == 0) return FA_OK;
+  fa_kvcache* c0 = caches[0];
+  const int64_t width = int64_t(c0->heads) * c0->head_dim;
+  if (q == nullptr || out == nullptr) return fail(FA_ERR_ARG, "null q or out");
+  if (q_stride < width || out_stride < width) return fail(FA_ERR_SHAPE, "row strides below heads x head_dim");
+  DeviceGuard guard(c0->device);
+  auto s = static_cast<cudaStream_t>(stream);
+  const Plan base = plan_span(c0, 1, 1);
+  const int tile = fa::tile_keys(c0->head_dim, c0->dtype == FA_F32 ? fa::kKtF32 : fa::kKtBf16);
+  const int64_t want = target_units(c0->dev);
+  int64_t chunk_keys = (total_keys * base.kv_groups + want - 1) / want;
+  chunk_keys = std::max<int64_t>(tile, (chunk_keys + tile - 1) / tile * tile);
+  // Chunks and partial slots of every row, then one launch per kMaxBatchRows rows.
+  std::vector<int> chunks(batch), part_base(batch);
+  int64_t slots = 0;
+  for (int i = 0; i < batch; ++i) {
+    const int64_t n = runs[i].n0 + runs[i].n1;
+    chunks[i] = int(std::max<int64_t>(1, (n + chunk_keys - 1) / chunk_keys));
+    part_base[i] = int(slots);
+    slots += chunks[i];
+  }
+  Work w;
+  if (int rc = ensure_work(c0, 0, size_t(slots) * c0->heads, 0, s, &w)) return rc;
+  if (int rc = ensure_counters(c0, size_t(batch) * base.kv_groups, s)) return rc;
+  const int kt = c0->dtype == FA_F32 ? fa::kKtF32 : fa::kKtBf16;
+  for (int first = 0; first < batch; first += fa::kMaxBatchRows) {
+    const int n = std::min(batch - first, fa::kMaxBatchRows);
+    fa::BatchArgs ba{};
+    fill_common(&ba.c, c0, base);
+    ba.c.q = q + int64_t(first) * q_stride;
+    ba.c.q_stride = q_stride;
+    ba.c.out = out + int64_t(first) * out_stride;
+    ba.c.out_stride = out_stride;
+    ba.c.partial_out = nullptr;
+    ba.c.part_o = w.part_o;
+    ba.c.part_ml = w.part_ml;
+    ba.c.counters = static_cast<int*>(c0->counters.ptr) + int64_t(first) * base.kv_groups;
+    ba.n = n;
+    int units = 0;
+    for (int i = 0; i < n; ++i) {
+      const fa_kvcache* c = caches[first + i];
+      fa::BatchRow& br = ba.rows[i];
+      br.k = layer_ptr(c, c->keys, layer);
+      br.v = layer_ptr(c, c->values, layer);
+      br.capacity = c->capacity;
+      br.runs = runs[first + i];
+      br.chunks = chunks[first + i];
+      br.unit_begin = units;
+      br.part_base = part_base[first + i];
+      units += base.kv_groups * br.chunks;
+    }
+    fa::AttendLaunch l{kt, base.g, true, nullptr, &ba, units};
+    cudaError_t e = launch_attend_d(c0->head_dim, l, s);
+    if (e != cudaSuccess) return cuda_fail(e, "attend launch");
+  }
+  return FA_OK;
+}
+
+int fa_attention_batch(fa_kvcache* const* caches, const fa_span* spans, int32_t batch,
+                       int32_t layer, int32_t rope, const float* angles,
+                       const fa_head_norm* norm, const float* qkv, int64_t qkv_stride,
+                       float* out, int64_t out_stride, void* stream) {
+  std::vector<fa::Runs> runs;
+  int64_t total_keys = 0;
+  if (int rc = check_batch(caches, spans, batch, layer, &runs, &total_keys)) return rc;
+  if (batch == 0) return FA_OK;
+  fa_kvcache* c0 = caches[0];
+  const int64_t width = int64_t(c0->heads) * c0->head_dim;
+  DeviceGuard guard(c0->device);
+  auto s = static_cast<cudaStream_t>(stream);
+  // The rotated queries go to the first cache's staging buffer (its workspace holds partials).
+  if (int rc = c0->staging.ensure(size_t(batch) * width * 4, s)) return rc;
+  float* q = static_cast<float*>(c0->staging.ptr);
+  if (int rc = fa_attention_input_batch(caches, spans, batch, layer, rope, angles, norm, qkv,
+                                        qkv_stride, q, width, stream))
+    return rc;
+  return fa_attend_batch(caches, spans, batch, layer, q, width, out, out_stride, stream);
+}
+
+int fa_attend_partial(fa_kvcache* cache, int32_t layer, const float* q, int32_t key_begin,
+                      int32_t key_end, float* partials, void* stream) {
+  if (int rc = check_cache(cache)) return rc;
+  if (int rc = check_layer(cache, layer)) return rc;
+  if (q == nullptr || partials == nullptr) return fail(FA_ERR_ARG, "null q or partials");
+  if (key_begin < 0 || key_end < key_begin) return fail(FA_ERR_ARG, "key range");
+  if (key_end - key_begin > cache->capacity)
+    return fail(FA_ERR_CAPACITY, "%d keys in a cache of %d", key_end - key_begin, cache->capacity);
+  DeviceGuard guard(cache->device);
+  auto s = static_cast<cudaStream_t>(stream);
+  const int64_t width = int64_t(cache->heads) * cache->head_dim;
+  const int n = key_end - key_begin;
+  const Plan p = plan_span(cache, 1, std::max(n, 1));
+  Work w;
+  if (int rc = ensure_work(cache, 0, size_t(p.chunks) * cache->heads, 0, s, &w)) return rc;
+  if (int rc = ensure_counters(cache, size_t(p.kv_groups), s)) return rc;
+  if (n == 0) {
+    // No keys: max -inf, sum 0, o 0 for every head.
+    std::vector<float> empty(size_t(cache->heads) * (cache->head_dim + 2), 0.0f);
+    for (int h = 0; h < cache->heads; ++h) empty[size_t(h) * (cache->head_dim + 2)] = -INFINITY;
+    FA_CUDA(cudaMemcpyAsync(partials, empty.data(), empty.size() * 4, cudaMemcpyHostToDevice, s),
+            "empty partials");
+    FA_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+    return FA_OK;
+  }
+  // The range is the key run of one row at position key_end - 1 under Window(n): positions
+  // key_begin .. key_end - 1, every one visible.
+  fa::SpanArgs args{};
+  fill_common(&args.c, cache, p);
+  args.c.q = q;
+  args.c.q_stride = width;
+  args.c.out = nullptr;
+  args.c.partial_out = partials;
+  args.c.part_o = w.part_o;
+  args.c.part_ml = w.part_ml;
+  args.c.counters = static_cast<int*>(cache->counters.ptr);
+  args.k = layer_ptr(cache, cache->keys, layer);
+  args.v = layer_ptr(cache, cache->values, layer);
+  args.capacity = cache->capacity;
+  args.rows = 1;
+  args.first = key_end - 1;
+  args.end = key_end;
+  args.kind = FA_MASK_WINDOW;
+  args.window = n;
+  args.chunks = p.chunks;
+  args.rows_per_image = 1;
+  args.keys_per_image = 0;
+  fa::AttendLaunch l{cache->dtype == FA_F32 ? fa::kKtF32 : fa::kKtBf16, p.g, false, &args, nullptr,
+                     p.kv_groups * p.chunks};
+  cudaError_t e = launch_attend_d(cache->head_dim, l, s);
+  if (e != cudaSuccess) return cuda_fail(e, "attend launch");
+  return FA_OK;
+}
+
+int fa_merge_partials(const float* partials, int32_t shards, int32_t heads, int32_t head_dim,
+                      float* out, void* stream) {
+  if (partials == nullptr || out == nullptr) return fail(FA_ERR_ARG, "null argument");
+  if (shards < 1 || heads < 1 || head_dim < 1 || head_dim > 1024)
+    return fail(FA_ERR_ARG, "shards %d heads %d head_dim %d", shards, heads, head_dim);
+  cudaError_t e = fa::launch_merge_partials(partials, shards, heads, head_dim, out,
+                                            static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "merge launch");
+  return FA_OK;
+}
+
+int fa_attend_full(const fa_call* call, void* out, int64_t out_stride, void* stream) {
+  if (call == nullptr || out == nullptr) return fail(FA_ERR_ARG, "null argument");
+  const fa_call& k = *call;
+  if (k.heads < 1 || k.kv_heads < 1 || k.images < 0 || k.queries < 0 || k.keys < 0)
+    return fail(FA_ERR_ARG, "call sizes");
+  if (k.heads % k.kv_heads != 0) return fail(FA_ERR_SHAPE, "%d heads over %d KV heads", k.heads, k.kv_heads);
+  if (!supported_head_dim(k.head_dim)) return fail(FA_ERR_UNSUPPORTED, "head_dim %d", k.head_dim);
+  if (k.dtype != FA_F32 && k.dtype != FA_BF16) return fail(FA_ERR_ARG, "dtype %d", k.dtype);
+  if (k.out_dtype != FA_F32) return fail(FA_ERR_UNSUPPORTED, "full-mask output dtype %d", k.out_dtype);
+  if (k.images == 0 || k.queries == 0) return FA_OK;
+  if (k.keys == 0) return fail(FA_ERR_ARG, "a full-mask call without keys");
+  if (k.query.values == nullptr || k.key.values == nullptr || k.value.values == nullptr)
+    return fail(FA_ERR_ARG, "null operand");
+  const int64_t width = int64_t(k.heads) * k.head_dim;
+  if (out_stride < width) return fail(FA_ERR_SHAPE, "output rows narrower than heads x head_dim");
+  const size_t esize = k.dtype == FA_F32 ? 4 : 2;
+  const int64_t align = 16 / int64_t(esize);
+  if (k.key.stride % align || k.key.offset % align || k.value.stride % align ||
+      k.value.offset % align || k.key.stride != k.value.stride ||
+      reinterpret_cast<uintptr_t>(k.key.values) % 16 || reinterpret_cast<uintptr_t>(k.value.values) % 16)
+    return fail(FA_ERR_UNSUPPORTED, "key/value rows must start on 16-byte boundaries with one stride");
+  int device = 0;
+  FA_CUDA(cudaGetDevice(&device), "cudaGetDevice");
+  Device* dev = nullptr;
+  if (int rc = device_state(device, &dev)) return rc;
+  auto s = static_cast<cudaStream_t>(stream);
+  // A call-local workspace, kept per device and grown on demand.
+  static Buffer work[64];
+  static Buffer counters[64];
+  static int counters_epoch[64];
+  const int rows = k.images * k.queries;
+  fa_kvcache view;  // the call viewed as a cache for the planner
+  view.layers = 1;
+  view.heads = k.heads;
+  view.kv_heads = k.kv_heads;
+  view.head_dim = k.head_dim;
+  view.capacity = k.images * k.keys;
+  view.dtype = k.dtype;
+  view.device = device;
+  view.dev = dev;
+  const Plan p = plan_span(&view, rows, k.keys);
+  const size_t q_bytes = align_up(size_t(rows) * width * 4, 256);
+  const size_t o_bytes = align_up(size_t(rows) * p.chunks * k.heads * k.head_dim * 4, 256);
+  const size_t ml_bytes = align_up(size_t(rows) * p.chunks * k.heads * 2 * 4, 256);
+  if (int rc = work[device].ensure(q_bytes + o_bytes + ml_bytes, s)) return rc;
+  const size_t counter_bytes = size_t(rows) * p.kv_groups * sizeof(int);
+  if (counter_bytes > counters[device].bytes || counters_epoch[device] != dev->epoch.load()) {
+    if (int rc = counters[device].ensure(counter_bytes, s)) return rc;
+    FA_CUDA(cudaMemsetAsync(counters[device].ptr, 0, counters[device].bytes, s), "counters");
+    counters_epoch[device] = dev->epoch.load();
+  }
+  unsigned char* base = static_cast<unsigned char*>(work[device].ptr);
+  float* q = reinterpret_cast<float*>(base);
+  cudaError_t e = fa::launch_prepare_queries(k.dtype, k.query.values, k.query.stride, k.query.offset,
+                                             rows, k.heads, k.head_dim, query_scale(k.head_dim), q, s);
+  if (e != cudaSuccess) return cuda_fail(e, "query scaling");
+  fa::SpanArgs args{};
+  args.c.heads = k.heads;
+  args.c.kv_heads = k.kv_heads;
+  args.c.group = k.heads / k.kv_heads;
+  args.c.hgroups = p.hgroups;
+  args.c.kv_stride = k.head_dim;  // KV head h at h * head_dim within a row
+  args.c.key_stride = k.key.stride;
+  args.c.q_scale = 1.0f;  // prepare_queries scaled them
+  args.c.err = dev->err;
+  args.c.q = q;
+  args.c.q_stride = width;
+  args.c.out = static_cast<float*>(out);
+  args.c.out_stride = out_stride;
+  args.c.part_o = reinterpret_cast<float*>(base + q_bytes);
+  args.c.part_ml = reinterpret_cast<float*>(base + q_bytes + o_bytes);
+  args.c.counters = static_cast<int*>(counters[device].ptr);
+  args.k = static_cast<const unsigned char*>(k.key.values) + k.key.offset * esize;
+  args.v = static_cast<const unsigned char*>(k.value.values) + k.value.offset * esize;
+  args.capacity = INT_MAX;
+  args.rows = rows;
+  args.first = 0;
+  args.end = k.keys;
+  args.kind = FA_MASK_FULL;
+  args.chunks = p.chunks;
+  args.rows_per_image = k.queries;
+  args.keys_per_image = k.keys;
+  fa::AttendLaunch l{k.dtype == FA_F32 ? fa::kKtF32 : fa::kKtBf16, p.g, false, &args, nullptr,
+                     rows * p.kv_groups * p.chunks};
+  e = launch_attend_d(k.head_dim, l, s);
+  if (e != cudaSuccess) return cuda_fail(e, "attend launch");
+  return FA_OK;
+}
+
+int fa_device_status(void* stream) {
+  int device = 0;
+  FA_CUDA(cudaGetDevice(&device), "cudaGetDevice");
+  Device* dev = nullptr;
+  if (int rc = device_state(device, &dev)) return rc;
+  FA_CUDA(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), "cudaStreamSynchronize");
+  unsigned word = 0;
+  FA_CUDA(cudaMemcpy(&word, dev->err, sizeof word, cudaMemcpyDeviceToHost), "read error word");
+  if (word != 0) {
+    FA_CUDA(cudaMemset(dev->err, 0, sizeof word), "clear error word");
+    dev->epoch.fetch_add(1);
+    return fail(FA_ERR_TIMEOUT, "a device-side wait gave up (error word 0x%x)", word);
+  }
+  return FA_OK;
+}
+
+int fa_rng_fill_normal(uint64_t seed, float* out, int64_t n) {
+  if (n < 0 || (n > 0 && out == nullptr)) return fail(FA_ERR_ARG, "bad output");
+  // SplitMix64 seeding of xoshiro256** (rng.rs:10-35).
+  uint64_t mixed = seed;
+  auto next_seed = [&]() {
+    mixed += 0x9E3779B97F4A7C15ull;
+    uint64_t z = mixed;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+  };
+  uint64_t st[4] = {next_seed(), next_seed(), next_seed(), next_seed()};
+  auto rotl = [](uint64_t x, int k) { return (x << k) | (x >> (64 - k)); };
+  auto next = [&]() {
+    const uint64_t result = rotl(st[1] * 5, 7) * 9;
+    const uint64_t t = st[1] << 17;
+    st[2] ^= st[0];
+    st[3] ^= st[1];
+    st[1] ^= st[2];
+    st[0] ^= st[3];
+    st[2] ^= t;
+    st[3] = rotl(st[3], 45);
+    return result;
+  };
+  // Uniform in (0, 1] (rng.rs:37-40); Box-Muller pairs (rng.rs:42-52).
+  auto uniform = [&]() { return double((next() >> 11) + 1) / double(1ull << 53); };
+  const double tau = 6.283185307179586476925286766559;
+  for (int64_t i = 0; i < n; i += 2) {
+    const double radius = std::sqrt(-2.0 * std::log(uniform()));
+    const double angle = tau * uniform();
+    out[i] = float(radius * std::cos(angle));
+    if (i + 1 < n) out[i + 1] = float(radius * std::sin(angle));
+  }
+  return FA_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,450 @@
+// The memory-bound half of the hot path: RoPE + keep (Stack::attention_input, layer.rs:175-234;
+// KvCache::keep, transformer.rs:164-180) and flash-decoding attention over the KvCache
+// (KvCache::attend, transformer.rs:182-219, with ops::attend's arithmetic, ops.rs:310-342).
+//
+// attend_kernel: one CTA per (query row, KV head and up to G of its query heads, chunk of keys).
+//  - A producer warp streams the chunk's key and value rows from HBM into a ring of shared-memory
+//    stages with 1-D bulk copies (cp.async.bulk, completion counted on an mbarrier). The cache
+//    keeps the reference's layout [layer][kv_head][slot][head_dim], so a run of positions is one
+//    contiguous copy; a run that wraps a window ring, or crosses into Mask::Groups's second run,
+//    is split into pieces.
+//  - Four consumer warps score each key against the G query heads that share it (GQA reuse the
+//    CPU path lacks: it re-reads the KV head once per query head), LPK lanes per key with 8
+//    elements each, warp-shuffle reductions and an online softmax in base 2 (the queries are
+//    scaled by log2(e)/sqrt(head_dim) as they are loaded).
+//  - The warps' (max, sum, output) states merge in shared memory; a single-chunk row writes its
+//    output, otherwise the chunk's partial goes to the workspace and the last CTA of the row
+//    (an arrival counter, reset by that CTA) merges the partials by log-sum-exp.
+#pragma once
+
+#include "fa_ptx.cuh"
+
+namespace fa {
+
+constexpr int kConsumerWarps = 4;
+constexpr int kDecodeThreads = (kConsumerWarps + 1) * 32;
+constexpr int kStages = 3;
+constexpr int kTileBytes = 16384;  // bytes of one K (or V) tile of a stage
+
+// Mask::keys (transformer.rs:116-128): the key positions of a row as two runs.
+struct Runs {
+  int b0, n0, b1, n1;
+};
+
+__host__ __device__ inline Runs mask_runs(int kind, int window, int state, int n_ends,
+                                          const int* ends, int position, int end) {
+  Runs r{0, 0, 0, 0};
+  if (kind == 0) {  // Causal
+    r.n0 = position + 1;
+  } else if (kind == 1) {  // Window
+    int lo = position + 1 - window;
+    if (lo < 0) lo = 0;
+    r.b0 = lo;
+    r.n0 = position + 1 - lo;
+  } else if (kind == 2 || position < state) {  // Full, or Groups before the state
+    r.n0 = end;
+  } else {  // Groups: the state, then the row's own group
+    int g = 0;
+    while (g < n_ends && ends[g] <= position) ++g;
+    const int start = g == 0 ? state : ends[g - 1];
+    r.n0 = state;
+    r.b1 = start;
+    r.n1 = (g < n_ends ? ends[g] : end) - start;
+  }
+  return r;
+}
+
+template <typename KT>
+struct KvElem;
+template <>
+struct KvElem<float> {
+  static constexpr int kBytes = 4;
+};
+template <>
+struct KvElem<__nv_bfloat16> {
+  static constexpr int kBytes = 2;
+};
+
+template <int D, typename KT>
+struct DecodeShape {
+  static constexpr int kRowBytes = D * KvElem<KT>::kBytes;
+  static constexpr int kLanesPerKey = D / 8;          // 8 elements per lane
+  static constexpr int kKeysPerWarp = 32 / kLanesPerKey;
+  static constexpr int kTileKeys = kTileBytes / kRowBytes;
+  static constexpr int kRoundKeys = kConsumerWarps * kKeysPerWarp;
+  static constexpr int kRounds = kTileKeys / kRoundKeys;
+  static constexpr int kElemsPerTile = kTileKeys * D;
+  static_assert(kLanesPerKey >= 2 && kLanesPerKey <= 32, "head_dim 16..256");
+  static_assert(kRounds * kRoundKeys == kTileKeys, "tile holds whole rounds");
+  static constexpr size_t kSmemBytes = size_t(kStages) * 2 * kTileBytes + 2 * kStages * 8;
+};
+
+// The element index of lane-slot i (0..7) of sub-lane `sub` in a row: f32 rows are read as two
+// float4 at sub and sub + LPK (each group of 8 lanes reads 128 contiguous bytes), bf16 rows as
+// one 16-byte vector at sub.
+template <int D, typename KT>
+__device__ __forceinline__ int elem_of(int sub, int i) {
+  if constexpr (KvElem<KT>::kBytes == 4) {
+    constexpr int LPK = D / 8;
+    return i < 4 ? 4 * sub + i : 4 * (sub + LPK) + (i - 4);
+  } else {
+    return 8 * sub + i;
+  }
+}
+
+template <int D, typename KT>
+__device__ __forceinline__ void load8(const KT* row, int sub, float (&x)[8]) {
+  if constexpr (KvElem<KT>::kBytes == 4) {
+    constexpr int LPK = D / 8;
+    const float4 a = reinterpret_cast<const float4*>(row)[sub];
+    const float4 b = reinterpret_cast<const float4*>(row)[sub + LPK];
+    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+    x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+  } else {
+    const uint4 a = reinterpret_cast<const uint4*>(row)[sub];
+    x[0] = bf16_lo(a.x); x[1] = bf16_hi(a.x); x[2] = bf16_lo(a.y); x[3] = bf16_hi(a.y);
+    x[4] = bf16_lo(a.z); x[5] = bf16_hi(a.z); x[6] = bf16_lo(a.w); x[7] = bf16_hi(a.w);
+  }
+}
+
+// What every attend launch shares.
+struct AttendCommon {
+  int heads, kv_heads, group, hgroups;  // hgroups: CTAs per KV head (ceil(group / G))
+  int64_t kv_stride;                    // elements between consecutive KV heads' blocks
+  int64_t key_stride;                   // elements between consecutive key (value) rows
+  const float* q;                       // rotated queries: row r at q + r*q_stride
+  int64_t q_stride;
+  float q_scale;                        // log2(e)/sqrt(head_dim): scores in base-2 units
+  float* out;  // output row r at out + r*out_stride (heads x D), or nullptr for partial_out
+  int64_t out_stride;
+  float* partial_out;  // when out is nullptr: row r's merged (max, sum, o[D]) per head
+  float* part_o;   // chunk partials: slot (part_base + chunk) * heads + head, D floats each
+  float* part_ml;  // (max, sum) per slot
+  int* counters;   // per (row, kv group) arrival counters, zero between launches
+  unsigned* err;   // device error word
+};
+
+// One span over one cache: row r at position first + r, keys from the mask.
+struct SpanArgs {
+  AttendCommon c;
+  const void* k;  // keys of (layer, kv head 0)
+  const void* v;
+  int capacity;
+  int rows, first, end, kind, window, state, n_ends, chunks;
+  int rows_per_image;  // rows of one image (images attend within themselves: full-mask calls)
+  int keys_per_image;  // key rows between consecutive images
+  int ends[kMaxEnds];
+};
+
+// Independent rows (decode sequences), each with its own cache and key runs.
+struct BatchRow {
+  const void* k;
+  const void* v;
+  int capacity;
+  Runs runs;
+  int chunks;      // chunks of this row
+  int unit_begin;  // first CTA of this row
+  int part_base;   // first partial chunk slot of this row
+};
+struct BatchArgs {
+  AttendCommon c;
+  int n;
+  BatchRow rows[kMaxBatchRows];
+};
+
+template <int D, typename KT, int G, bool BATCH, typename Args>
+__global__ void __launch_bounds__(kDecodeThreads, 2) attend_kernel(const __grid_constant__ Args args) {
+  using S = DecodeShape<D, KT>;
+  constexpr int T = S::kTileKeys;
+  constexpr int LPK = S::kLanesPerKey;
+  constexpr int KPW = S::kKeysPerWarp;
+  const AttendCommon& c = args.c;
+
+  extern __shared__ __align__(128) unsigned char smem[];
+  KT* k_tiles = reinterpret_cast<KT*>(smem);
+  KT* v_tiles = reinterpret_cast<KT*>(smem + size_t(kStages) * kTileBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(kStages) * 2 * kTileBytes);
+  uint64_t* empty = full + kStages;
+  __shared__ int last_flag;
+  __shared__ int fail_flag;
+
+  // ---- which work unit this CTA is -----------------------------------------------------------
+  const int unit = blockIdx.x;
+  int row, kvg, chunk, chunks, capacity, part_base;
+  Runs runs;
+  const KT* kbase;
+  const KT* vbase;
+  if constexpr (BATCH) {
+    int lo = 0, hi = args.n - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (args.rows[mid].unit_begin <= unit) lo = mid; else hi = mid - 1;
+    }
+    row = lo;
+    const BatchRow& br = args.rows[row];
+    chunks = br.chunks;
+    const int local = unit - br.unit_begin;
+    kvg = local / chunks;
+    chunk = local % chunks;
+    runs = br.runs;
+    capacity = br.capacity;
+    part_base = br.part_base;
+    kbase = static_cast<const KT*>(br.k);
+    vbase = static_cast<const KT*>(br.v);
+  } else {
+    chunks = args.chunks;
+    const int per_row = c.kv_heads * c.hgroups * chunks;
+    row = unit / per_row;
+    const int local = unit % per_row;
+    kvg = local / chunks;
+    chunk = local % chunks;
+    runs = mask_runs(args.kind, args.window, args.state, args.n_ends, args.ends,
+                     args.first + row, args.end);
+    const int image_base = (row / args.rows_per_image) * args.keys_per_image;
+    runs.b0 += image_base;
+    runs.b1 += image_base;
+    capacity = args.capacity;
+    part_base = row * chunks;
+    kbase = static_cast<const KT*>(args.k);
+    vbase = static_cast<const KT*>(args.v);
+  }
+  const int kv = kvg / c.hgroups;
+  const int sg = kvg % c.hgroups;
+  const int h0 = kv * c.group + sg * G;
+  const int g = min(G, c.group - sg * G);
+  kbase += kv * c.kv_stride;
+  vbase += kv * c.kv_stride;
+  const int n = runs.n0 + runs.n1;
+  const int per = ((n + chunks - 1) / chunks + T - 1) / T * T;
+  const int j0 = min(n, chunk * per);
+  const int j1 = min(n, j0 + per);
+  const int tiles = (j1 - j0 + T - 1) / T;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    mbar_fence_init();
+    fail_flag = 0;
+  }
+  __syncthreads();
+
+  if (warp == kConsumerWarps) {
+    // ---- producer: one elected lane streams the chunk's K/V rows -----------------------------
+    if (lane == 0) {
+      const uint64_t policy = policy_evict_first();
+      int issued = 0;
+      for (int t = 0; t < tiles; ++t) {
+        const int s = t % kStages;
+        if (!mbar_wait(&empty[s], ((t / kStages) & 1) ^ 1, c.err)) break;
+        const int ja = j0 + t * T;
+        const int nk = min(T, j1 - ja);
+        mbar_arrive_expect_tx(&full[s], uint32_t(nk) * S::kRowBytes * 2);
+        KT* kd = k_tiles + size_t(s) * S::kElemsPerTile;
+        KT* vd = v_tiles + size_t(s) * S::kElemsPerTile;
+        int j = ja, at = 0;
+        while (j < ja + nk) {
+          int pos, left;
+          if (j < runs.n0) { pos = runs.b0 + j; left = runs.n0 - j; }
+          else { pos = runs.b1 + (j - runs.n0); left = n - j; }
+          const int slot = pos % capacity;
+          const int cnt = min(ja + nk - j, min(left, capacity - slot));
+          if (c.key_stride == D) {  // a cache: the run's rows are contiguous
+            const uint32_t bytes = uint32_t(cnt) * S::kRowBytes;
+            bulk_g2s_hint(kd + size_t(at) * D, kbase + int64_t(slot) * D, bytes, &full[s], policy);
+            bulk_g2s_hint(vd + size_t(at) * D, vbase + int64_t(slot) * D, bytes, &full[s], policy);
+          } else {  // strided operand rows: one copy per row
+            for (int i = 0; i < cnt; ++i) {
+              const int64_t src = int64_t(slot + i) * c.key_stride;
+              bulk_g2s_hint(kd + size_t(at + i) * D, kbase + src, S::kRowBytes, &full[s], policy);
+              bulk_g2s_hint(vd + size_t(at + i) * D, vbase + src, S::kRowBytes, &full[s], policy);
+            }
+          }
+          j += cnt;
+          at += cnt;
+        }
+        issued = t + 1;
+      }
+      // Wait for this CTA's copies still in flight before it may exit.
+      for (int t = max(0, issued - kStages); t < issued; ++t)
+        mbar_wait(&full[t % kStages], (t / kStages) & 1, c.err);
+    }
+    return;
+  }
+
+  // ---- consumers ------------------------------------------------------------------------------
+  const int grp = lane / LPK;
+  const int sub = lane % LPK;
+  const int ctid = threadIdx.x;  // 0 .. 127
+
+  float q[G][8];
+  const float* qrow = c.q + int64_t(row) * c.q_stride;
+#pragma unroll
+  for (int h = 0; h < G; ++h)
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      q[h][i] = h < g ? qrow[(h0 + h) * D + elem_of<D, KT>(sub, i)] * c.q_scale : 0.0f;
+
+  float m[G], l[G], o[G][8];
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    m[h] = -INFINITY;
+    l[h] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[h][i] = 0.0f;
+  }
+
+  bool ok = true;
+  for (int t = 0; t < tiles; ++t) {
+    const int s = t % kStages;
+    if (!mbar_wait(&full[s], (t / kStages) & 1, c.err)) { ok = false; break; }
+    const int nk = min(T, j1 - (j0 + t * T));
+    const KT* kt = k_tiles + size_t(s) * S::kElemsPerTile;
+    const KT* vt = v_tiles + size_t(s) * S::kElemsPerTile;
+#pragma unroll 1
+    for (int r = 0; r < S::kRounds; ++r) {
+      const int first_key = r * S::kRoundKeys + warp * KPW;
+      if (first_key >= nk) break;  // warp-uniform: no key of this warp left in the tile
+      const int kr = first_key + grp;
+      const bool valid = kr < nk;
+      const int rr = valid ? kr : first_key;
+      float kx[8], vx[8];
+      load8<D, KT>(kt + size_t(rr) * D, sub, kx);
+      load8<D, KT>(vt + size_t(rr) * D, sub, vx);
+      float sc[G];
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        float acc = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc = fmaf(q[h][i], kx[i], acc);
+#pragma unroll
+        for (int off = LPK / 2; off >= 1; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+        sc[h] = valid ? acc : -INFINITY;
+      }
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        float mx = sc[h];
+#pragma unroll
+        for (int off = LPK; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        if (mx > m[h]) {  // warp-uniform
+          const float alpha = exp2_approx(m[h] - mx);
+          l[h] *= alpha;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) o[h][i] *= alpha;
+          m[h] = mx;
+        }
+        const float p = valid ? exp2_approx(sc[h] - m[h]) : 0.0f;
+        l[h] += p;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[h][i] = fmaf(p, vx[i], o[h][i]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+
+  // ---- merge the warp's key groups (they share the warp-uniform max) ---------------------------
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+#pragma unroll
+    for (int off = LPK; off < 32; off <<= 1) {
+      l[h] += __shfl_xor_sync(0xffffffffu, l[h], off);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[h][i] += __shfl_xor_sync(0xffffffffu, o[h][i], off);
+    }
+  }
+  // All consumers are past their last tile: every copy has landed, the stages are free.
+  if (!ok) fail_flag = 1;
+  named_sync(1, kConsumerWarps * 32);
+  if (*static_cast<volatile int*>(&fail_flag) != 0) return;
+
+  float* red_m = reinterpret_cast<float*>(smem);           // [warps][G]
+  float* red_l = red_m + kConsumerWarps * G;               // [warps][G]
+  float* red_o = red_l + kConsumerWarps * G;               // [warps][G][D]
+  if (lane == 0) {
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      red_m[warp * G + h] = m[h];
+      red_l[warp * G + h] = l[h];
+    }
+  }
+  if (grp == 0) {
+#pragma unroll
+    for (int h = 0; h < G; ++h)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) red_o[(warp * G + h) * D + elem_of<D, KT>(sub, i)] = o[h][i];
+  }
+  named_sync(1, kConsumerWarps * 32);
+
+  const int count = g * D;
+  float* out_row = c.out != nullptr ? c.out + int64_t(row) * c.out_stride : nullptr;
+  float* part_row = c.partial_out != nullptr ? c.partial_out + int64_t(row) * c.heads * (D + 2) : nullptr;
+  // The row's merged state of head h0 + h: its output, or its (max, sum, o) when partial.
+  auto finish = [&](int h, int e, float mm, float ll, float oo) {
+    if (out_row != nullptr) {
+      out_row[(h0 + h) * D + e] = ll > 0.0f ? oo / ll : 0.0f;
+    } else {
+      float* pr = part_row + (h0 + h) * (D + 2);
+      if (e == 0) { pr[0] = mm; pr[1] = ll; }
+      pr[2 + e] = oo;
+    }
+  };
+  for (int idx = ctid; idx < count; idx += kConsumerWarps * 32) {
+    const int h = idx / D, e = idx % D;
+    float mm = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) mm = fmaxf(mm, red_m[w * G + h]);
+    float ll = 0.0f, oo = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) {
+      const float wm = red_m[w * G + h];
+      const float f = wm == -INFINITY ? 0.0f : exp2_approx(wm - mm);
+      ll = fmaf(red_l[w * G + h], f, ll);
+      oo = fmaf(red_o[(w * G + h) * D + e], f, oo);
+    }
+    if (chunks == 1) {
+      finish(h, e, mm, ll, oo);
+    } else {
+      const int64_t slot = int64_t(part_base + chunk) * c.heads + (h0 + h);
+      c.part_o[slot * D + e] = oo;
+      if (e == 0) {
+        c.part_ml[2 * slot] = mm;
+        c.part_ml[2 * slot + 1] = ll;
+      }
+    }
+  }
+  if (chunks == 1) return;
+
+  // ---- the last CTA of this (row, KV group) merges the chunks ---------------------------------
+  __threadfence();
+  named_sync(1, kConsumerWarps * 32);
+  int* counter = c.counters + int64_t(row) * c.kv_heads * c.hgroups + kvg;
+  if (ctid == 0) {
+    const int arrived = atomicAdd(counter, 1);
+    last_flag = arrived == chunks - 1;
+    if (last_flag) *counter = 0;  // ready for the next launch
+  }
+  named_sync(1, kConsumerWarps * 32);
+  if (!last_flag) return;
+  __threadfence();
+  for (int idx = ctid; idx < count; idx += kConsumerWarps * 32) {
+    const int h = idx / D, e = idx % D;
+    const int64_t base = int64_t(part_base) * c.heads + (h0 + h);
+    float mm = -INFINITY;
+    for (int ch = 0; ch < chunks; ++ch) mm = fmaxf(mm, __ldcg(&c.part_ml[2 * (base + int64_t(ch) * c.heads)]));
+    float ll = 0.0f, oo = 0.0f;
+    for (int ch = 0; ch < chunks; ++ch) {
+      const int64_t slot = base + int64_t(ch) * c.heads;
+      const float cm = __ldcg(&c.part_ml[2 * slot]);
+      const float f = cm == -INFINITY ? 0.0f : exp2_approx(cm - mm);
+      ll = fmaf(__ldcg(&c.part_ml[2 * slot + 1]), f, ll);
+      oo = fmaf(__ldcg(&c.part_o[slot * D + e]), f, oo);
+    }
+    finish(h, e, mm, ll, oo);
+  }
+}
+
+}  // namespace fa

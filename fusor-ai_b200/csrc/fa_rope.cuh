@@ -1,0 +1,135 @@
+// The attention input (Stack::attention_input + position, crates/blocks/src/layer.rs:175-234):
+// optional Qwen3 head RMSNorm (ops.rs:7-16), RoPE by halves or interleaved (ops.rs:77-95) on the
+// query and key heads, then KvCache::keep of the key and value heads (transformer.rs:164-180).
+//
+// One warp per (row, head unit). The rotation is the reference's arithmetic bit for bit: each
+// product rounded, then the difference or sum (no fused multiply-add), by the host's cos/sin
+// table, so the cache holds exactly the keys the CPU path would keep. The rotated queries go to
+// the workspace pre-scaled by log2(e)/sqrt(head_dim) for the base-2 softmax of the attention.
+#pragma once
+
+#include "fa_ptx.cuh"
+
+namespace fa {
+
+constexpr int kRopeWarps = 4;
+
+struct KeepRow {
+  void* k;       // keys of (layer, kv head 0) of this row's cache
+  void* v;
+  int capacity;
+  int position;
+};
+
+struct RopeArgs {
+  int heads, kv_heads, head_dim, rope, n_rows;
+  const float* qkv;  // row r at qkv + r*qkv_stride: heads, kv heads, kv heads of head_dim
+  int64_t qkv_stride;
+  const float* angles;  // row r at angles + r*head_dim: cosines then sines (or nullptr)
+  const float* q_norm;  // optional head norms (head_dim weights each)
+  const float* k_norm;
+  float eps;
+  float* q_out;  // rotated queries, row r at q_out + r*q_out_stride, head h at h*head_dim
+  int64_t q_out_stride;
+  float q_scale;         // scale applied to q_out (1 for the raw rotated queries)
+  int64_t kv_stride;     // elements between consecutive KV heads' blocks of a cache
+  int keep;              // 0: rotate queries only
+  int batch;             // 0: one cache (rows[0]), positions first + r; 1: rows[r] per row
+  int first;
+  KeepRow keep_rows[kMaxBatchRows];
+};
+
+template <typename KT>
+__device__ __forceinline__ KT to_kv(float x);
+template <>
+__device__ __forceinline__ float to_kv<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 to_kv<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
+}
+
+template <typename KT>
+__global__ void __launch_bounds__(kRopeWarps * 32) rope_keep_kernel(const __grid_constant__ RopeArgs a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x;
+  const int unit = blockIdx.y * kRopeWarps + warp;
+  const int units = a.heads + 2 * a.kv_heads;
+  if (unit >= units) return;
+  const bool is_query = unit < a.heads;
+  const bool is_key = !is_query && unit < a.heads + a.kv_heads;
+  if (!is_query && !a.keep) return;
+  const int d = a.head_dim, half = d / 2;
+  const float* head = a.qkv + int64_t(row) * a.qkv_stride + int64_t(unit) * d;
+
+  // Each lane holds the pairs p = lane, lane + 32, ... (up to 4 pairs: head_dim <= 256).
+  float x[4], y[4];
+  int lo[4], hi[4];
+  const int pairs = (half + 31) / 32;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int p = lane + 32 * j;
+    const bool live = j < pairs && p < half;
+    if (a.rope == 2) { lo[j] = 2 * p; hi[j] = 2 * p + 1; }
+    else { lo[j] = p; hi[j] = p + half; }
+    x[j] = live ? head[lo[j]] : 0.0f;
+    y[j] = live ? head[hi[j]] : 0.0f;
+    if (!live) lo[j] = -1;
+  }
+
+  if (is_query || is_key) {
+    const float* weight = is_query ? a.q_norm : a.k_norm;
+    if (weight != nullptr) {
+      float ss = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) ss += x[j] * x[j] + y[j] * y[j];
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+      const float mean = ss / float(d);
+      const float inverse = 1.0f / sqrtf(mean + a.eps);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (lo[j] < 0) continue;
+        x[j] = __fmul_rn(__fmul_rn(x[j], inverse), weight[lo[j]]);
+        y[j] = __fmul_rn(__fmul_rn(y[j], inverse), weight[hi[j]]);
+      }
+    }
+    if (a.rope != 0) {
+      const float* cs = a.angles + int64_t(row) * d;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (lo[j] < 0) continue;
+        const int p = lane + 32 * j;
+        const float c = cs[p], s = cs[half + p];
+        const float nx = __fsub_rn(__fmul_rn(x[j], c), __fmul_rn(y[j], s));
+        const float ny = __fadd_rn(__fmul_rn(y[j], c), __fmul_rn(x[j], s));
+        x[j] = nx;
+        y[j] = ny;
+      }
+    }
+  }
+
+  if (is_query) {
+    if (a.q_out == nullptr) return;
+    float* q = a.q_out + int64_t(row) * a.q_out_stride + int64_t(unit) * d;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (lo[j] < 0) continue;
+      q[lo[j]] = x[j] * a.q_scale;
+      q[hi[j]] = y[j] * a.q_scale;
+    }
+    return;
+  }
+  const KeepRow& kr = a.keep_rows[a.batch ? row : 0];
+  const int position = a.batch ? kr.position : a.first + row;
+  const int kv = (unit - a.heads) % a.kv_heads;
+  const int64_t at = int64_t(kv) * a.kv_stride + int64_t(position % kr.capacity) * d;
+  KT* target = static_cast<KT*>(is_key ? kr.k : kr.v) + at;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (lo[j] < 0) continue;
+    target[lo[j]] = to_kv<KT>(x[j]);
+    target[hi[j]] = to_kv<KT>(y[j]);
+  }
+}
+
+}  // namespace fa

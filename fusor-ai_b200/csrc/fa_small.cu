@@ -1,0 +1,85 @@
+// The small kernels around the attention: the RoPE + keep launch, query scaling for calls whose
+// queries arrive already rotated, and the log-sum-exp merge of KV-range shards' partials.
+#include <algorithm>
+
+#include "fa_launch.cuh"
+
+namespace fa {
+
+namespace {
+
+template <typename T>
+__device__ __forceinline__ float load_elem(const T* p);
+template <>
+__device__ __forceinline__ float load_elem<float>(const float* p) { return *p; }
+template <>
+__device__ __forceinline__ float load_elem<__nv_bfloat16>(const __nv_bfloat16* p) {
+  return __bfloat162float(*p);
+}
+
+// q_out[r][h][e] = scale * values[r * stride + offset + h * head_dim + e]
+template <typename T>
+__global__ void prepare_queries_kernel(const T* values, int64_t stride, int64_t offset, int rows,
+                                       int heads, int head_dim, float scale, float* q_out) {
+  const int64_t width = int64_t(heads) * head_dim;
+  const int64_t total = int64_t(rows) * width;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = i / width, c = i % width;
+    q_out[i] = load_elem<T>(values + r * stride + offset + c) * scale;
+  }
+}
+
+// out[h][e] = sum_s 2^(m_s - M) o_s[e] / sum_s 2^(m_s - M) l_s over the shards' partials.
+__global__ void merge_partials_kernel(const float* partials, int shards, int heads, int head_dim,
+                                      float* out) {
+  const int h = blockIdx.x;
+  const int64_t pitch = int64_t(heads) * (head_dim + 2);
+  float mm = -INFINITY;
+  for (int s = 0; s < shards; ++s) mm = fmaxf(mm, partials[s * pitch + h * (head_dim + 2)]);
+  for (int e = threadIdx.x; e < head_dim; e += blockDim.x) {
+    float ll = 0.0f, oo = 0.0f;
+    for (int s = 0; s < shards; ++s) {
+      const float* p = partials + s * pitch + h * (head_dim + 2);
+      const float f = p[0] == -INFINITY ? 0.0f : exp2f(p[0] - mm);
+      ll = fmaf(p[1], f, ll);
+      oo = fmaf(p[2 + e], f, oo);
+    }
+    out[int64_t(h) * head_dim + e] = ll > 0.0f ? oo / ll : 0.0f;
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_rope(int kt, const RopeArgs& args, cudaStream_t stream) {
+  const int units = args.heads + 2 * args.kv_heads;
+  const dim3 grid(args.n_rows, (units + kRopeWarps - 1) / kRopeWarps);
+  if (kt == kKtF32) rope_keep_kernel<float><<<grid, kRopeWarps * 32, 0, stream>>>(args);
+  else rope_keep_kernel<__nv_bfloat16><<<grid, kRopeWarps * 32, 0, stream>>>(args);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prepare_queries(int dtype, const void* values, int64_t stride, int64_t offset,
+                                   int rows, int heads, int head_dim, float scale, float* q_out,
+                                   cudaStream_t stream) {
+  const int64_t total = int64_t(rows) * heads * head_dim;
+  if (total == 0) return cudaSuccess;
+  const int blocks = int(std::min<int64_t>((total + 255) / 256, 148 * 16));
+  if (dtype == 0)
+    prepare_queries_kernel<float><<<blocks, 256, 0, stream>>>(
+        static_cast<const float*>(values), stride, offset, rows, heads, head_dim, scale, q_out);
+  else
+    prepare_queries_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(values), stride, offset, rows, heads, head_dim, scale,
+        q_out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_merge_partials(const float* partials, int shards, int heads, int head_dim,
+                                  float* out, cudaStream_t stream) {
+  merge_partials_kernel<<<heads, std::min(head_dim, 256), 0, stream>>>(partials, shards, heads,
+                                                                     head_dim, out);
+  return cudaGetLastError();
+}
+
+}  // namespace fa

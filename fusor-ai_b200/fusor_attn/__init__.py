@@ -1,0 +1,435 @@
+"""fusor_attn: the B200 attention hot path of fusor-ai behind its KvCache / Span / Mask API.
+
+A thin ctypes binding of ``libfa_attn.so`` (include/fa_attn.h) whose names follow the
+reference's ``blocks::transformer`` and ``blocks::attention`` (crates/blocks/src/transformer.rs,
+attention.rs, rotary.rs). Device tensors are torch tensors (PyTorch is the plumbing for memory
+and streams); every computation runs in this library's CUDA kernels. There is no CPU fallback:
+without the built library, or without a CUDA device, calls raise.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from dataclasses import dataclass, field
+from typing import Sequence
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libfa_attn.so")
+
+OK, ERR_ARG, ERR_SHAPE, ERR_CAPACITY, ERR_CUDA, ERR_TIMEOUT, ERR_UNSUPPORTED = range(7)
+F32, BF16 = 0, 1
+MASK_CAUSAL, MASK_WINDOW, MASK_FULL, MASK_GROUPS = range(4)
+ROPE_NONE, ROPE_HALF, ROPE_INTERLEAVED = range(3)
+(ROT_SEQUENCE, ROT_LINEAR, ROT_PARTIAL, ROT_MULTIMODAL, ROT_AXES, ROT_MULTIMODAL_INTERLEAVED,
+ ROT_GRID) = range(7)
+
+
+class FaError(RuntimeError):
+    """A non-zero status of the C ABI; `code` is the FA_ERR_* value."""
+
+    def __init__(self, code: int, message: str):
+        super().__init__(f"[{code}] {message}")
+        self.code = code
+
+
+class CapacityError(FaError):
+    """The span does not fit the cache: the reference panics with "the cache holds every key
+    the span sees" (transformer.rs:335-338)."""
+
+
+class ShapeError(FaError):
+    """heads % kv_heads != 0 and the like (transformer.rs:389-393)."""
+
+
+# ---- C structures (include/fa_attn.h) --------------------------------------------------------
+
+class _Mask(C.Structure):
+    _fields_ = [("kind", C.c_int32), ("window", C.c_int32), ("state", C.c_int32),
+                ("n_ends", C.c_int32), ("ends", C.POINTER(C.c_int32))]
+
+
+class _Span(C.Structure):
+    _fields_ = [("rows", C.c_int32), ("first", C.c_int32), ("mask", _Mask)]
+
+
+class _Position(C.Structure):
+    _fields_ = [("temporal", C.c_int32), ("height", C.c_int32), ("width", C.c_int32)]
+
+
+class _Rotation(C.Structure):
+    _fields_ = [("kind", C.c_int32), ("params", C.c_int32 * 3), ("base", C.c_float),
+                ("spatial_scale", C.c_float)]
+
+
+class _HeadNorm(C.Structure):
+    _fields_ = [("q_norm", C.c_void_p), ("k_norm", C.c_void_p), ("eps", C.c_float)]
+
+
+class _Operand(C.Structure):
+    _fields_ = [("values", C.c_void_p), ("stride", C.c_int64), ("offset", C.c_int64)]
+
+
+class _Call(C.Structure):
+    _fields_ = [("heads", C.c_int32), ("kv_heads", C.c_int32), ("head_dim", C.c_int32),
+                ("images", C.c_int32), ("queries", C.c_int32), ("keys", C.c_int32),
+                ("query", _Operand), ("key", _Operand), ("value", _Operand),
+                ("dtype", C.c_int32), ("out_dtype", C.c_int32)]
+
+
+_lib = None
+
+# name -> (restype, argtypes) for every entry point of include/fa_attn.h
+_P, _I32, _I64 = C.c_void_p, C.c_int32, C.c_int64
+SIGNATURES = {
+    "fa_last_error": (C.c_char_p, []),
+    "fa_capabilities": (C.c_int, [_P, _P, _I32, _P]),
+    "fa_kvcache_create": (C.c_int, [_I32, _I32, _I32, _I32, _I32, _I32, _I32, C.POINTER(_P)]),
+    "fa_kvcache_destroy": (C.c_int, [_P]),
+    "fa_kvcache_data": (C.c_int, [_P, C.POINTER(_P), C.POINTER(_P), _P, _P]),
+    "fa_kvcache_reserve": (C.c_int, [_P, _I32]),
+    "fa_kvcache_copy_rows": (C.c_int, [_P, _I32, _P, _P, _P]),
+    "fa_kvcache_put_rows": (C.c_int, [_P, _I32, _P, _P, _P]),
+    "fa_rotary_angles": (C.c_int, [_P, _I32, _P, _I32, _P]),
+    "fa_attention_input": (C.c_int, [_P, _I32, _P, _I32, _P, _P, _P, _I64, _P, _P]),
+    "fa_attend": (C.c_int, [_P, _I32, _P, _P, _I64, _P, _I64, _P]),
+    "fa_attention": (C.c_int, [_P, _I32, _P, _I32, _P, _P, _P, _I64, _P, _I64, _P]),
+    "fa_attention_host": (C.c_int, [_P, _I32, _P, _I32, _P, _P, _P, _I64, _P, _I64, _P]),
+    "fa_attention_batch": (C.c_int, [_P, _P, _I32, _I32, _I32, _P, _P, _P, _I64, _P, _I64, _P]),
+    "fa_attention_input_batch": (C.c_int, [_P, _P, _I32, _I32, _I32, _P, _P, _P, _I64, _P, _I64, _P]),
+    "fa_attend_batch": (C.c_int, [_P, _P, _I32, _I32, _P, _I64, _P, _I64, _P]),
+    "fa_attend_partial": (C.c_int, [_P, _I32, _P, _I32, _I32, _P, _P]),
+    "fa_merge_partials": (C.c_int, [_P, _I32, _I32, _I32, _P, _P]),
+    "fa_attend_full": (C.c_int, [_P, _P, _I64, _P]),
+    "fa_device_status": (C.c_int, [_P]),
+    "fa_rng_fill_normal": (C.c_int, [C.c_uint64, _P, _I64]),
+}
+
+
+def lib():
+    """The loaded library (built first if it is missing or stale in a source checkout)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            from . import _build
+            _build.build()
+        _lib = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(_lib, name)
+            fn.restype = res
+            fn.argtypes = args
+    return _lib
+
+
+def _check(rc: int):
+    if rc == OK:
+        return
+    msg = lib().fa_last_error().decode(errors="replace")
+    cls = {ERR_CAPACITY: CapacityError, ERR_SHAPE: ShapeError}.get(rc, FaError)
+    raise cls(rc, msg)
+
+
+def _stream(stream=None):
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+def _dptr(t):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+# ---- the reference's types -------------------------------------------------------------------
+
+@dataclass(frozen=True)
+class Mask:
+    """transformer::Mask (transformer.rs:97-111)."""
+    kind: int = MASK_CAUSAL
+    window: int = 0
+    state: int = 0
+    ends: tuple = ()
+
+    @staticmethod
+    def causal() -> "Mask":
+        return Mask(MASK_CAUSAL)
+
+    @staticmethod
+    def window_of(n: int) -> "Mask":
+        return Mask(MASK_WINDOW, window=n)
+
+    @staticmethod
+    def full() -> "Mask":
+        return Mask(MASK_FULL)
+
+    @staticmethod
+    def groups(state: int, ends: Sequence[int]) -> "Mask":
+        return Mask(MASK_GROUPS, state=state, ends=tuple(int(e) for e in ends))
+
+
+@dataclass(frozen=True)
+class Span:
+    """Span (transformer.rs:272-279): `rows` positions from `first` under `mask`."""
+    rows: int
+    first: int
+    mask: Mask = field(default_factory=Mask.causal)
+
+    def c(self) -> _Span:
+        ends = (C.c_int32 * max(len(self.mask.ends), 1))(*self.mask.ends)
+        s = _Span(self.rows, self.first,
+                  _Mask(self.mask.kind, self.mask.window, self.mask.state, len(self.mask.ends),
+                        C.cast(ends, C.POINTER(C.c_int32)) if self.mask.ends else None))
+        s._keep = ends  # keep the ends array alive with the struct
+        return s
+
+
+@dataclass(frozen=True)
+class Position:
+    """rotary::Position (rotary.rs:27-33)."""
+    temporal: int
+    height: int
+    width: int
+
+    @staticmethod
+    def uniform(index: int) -> "Position":
+        return Position(index, index, index)
+
+
+@dataclass(frozen=True)
+class Rotation:
+    """rotary::Rotation (rotary.rs:62-86) with the Rotary's base and spatial scale."""
+    kind: int = ROT_SEQUENCE
+    params: tuple = (0, 0, 0)
+    base: float = 10000.0
+    spatial_scale: float = 1.0
+
+    def c(self) -> _Rotation:
+        return _Rotation(self.kind, (C.c_int32 * 3)(*self.params), self.base, self.spatial_scale)
+
+
+def rotary_angles(rotation: Rotation, head_dim: int, positions) -> np.ndarray:
+    """Buffers.angles of rows at `positions` (ints or Position): per row the head_dim/2 cosines
+    then sines, computed on the host bit for bit as Rotary::angles (rotary.rs:170-178)."""
+    pos = [p if isinstance(p, Position) else Position.uniform(int(p)) for p in positions]
+    arr = (_Position * max(len(pos), 1))(*[_Position(p.temporal, p.height, p.width) for p in pos])
+    out = np.zeros((len(pos), head_dim), np.float32)
+    r = rotation.c()
+    _check(lib().fa_rotary_angles(C.byref(r), head_dim, arr, len(pos),
+                                  out.ctypes.data_as(C.c_void_p)))
+    return out
+
+
+@dataclass(frozen=True)
+class Shape:
+    """The attention part of transformer::Shape (transformer.rs:54-67)."""
+    layers: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+
+    @property
+    def qkv(self) -> int:
+        """Heads::qkv (layer.rs:45-48): columns of the fused QKV projection."""
+        return (self.heads + 2 * self.kv_heads) * self.head_dim
+
+    @property
+    def width(self) -> int:
+        """Heads::width (layer.rs:50-53)."""
+        return self.heads * self.head_dim
+
+
+class KvCache:
+    """transformer::KvCache (transformer.rs:131-270) in HBM: [layer][kv_head][slot][head_dim]."""
+
+    def __init__(self, shape: Shape, capacity: int, dtype: int = F32, device: int = 0):
+        self.shape, self.capacity, self.dtype, self.device = shape, capacity, dtype, device
+        h = C.c_void_p()
+        _check(lib().fa_kvcache_create(shape.layers, shape.heads, shape.kv_heads, shape.head_dim,
+                                       capacity, dtype, device, C.byref(h)))
+        self._h = h
+
+    def close(self):
+        if getattr(self, "_h", None) is not None and self._h.value:
+            lib().fa_kvcache_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def handle(self):
+        return self._h
+
+    def _torch_dtype(self):
+        import torch
+        return torch.float32 if self.dtype == F32 else torch.bfloat16
+
+    def reserve(self, rows: int):
+        _check(lib().fa_kvcache_reserve(self._h, rows))
+
+    def copy_rows(self, rows: int | None = None, stream=None):
+        """KvCache::copy_rows (transformer.rs:221-239) into new device tensors of
+        [layers][kv_heads][rows][head_dim]."""
+        import torch
+        rows = self.capacity if rows is None else rows
+        s = self.shape
+        dims = (s.layers, s.kv_heads, rows, s.head_dim)
+        dev = torch.device("cuda", self.device)
+        k = torch.empty(dims, dtype=self._torch_dtype(), device=dev)
+        v = torch.empty(dims, dtype=self._torch_dtype(), device=dev)
+        _check(lib().fa_kvcache_copy_rows(self._h, rows, _dptr(k), _dptr(v), _stream(stream)))
+        return k, v
+
+    def put_rows(self, keys, values, stream=None):
+        """KvCache::put_rows (transformer.rs:241-251): [layers][kv_heads][rows][head_dim]."""
+        rows = keys.shape[2]
+        keys = keys.contiguous()
+        values = values.contiguous()
+        _check(lib().fa_kvcache_put_rows(self._h, rows, _dptr(keys), _dptr(values),
+                                         _stream(stream)))
+
+    def attention_input(self, layer: int, span: Span, qkv, angles=None, rope: int = ROPE_HALF,
+                        norm=None, q_out=None, stream=None):
+        """RoPE (+ head norm) and keep of a span's rows (layer.rs:175-234)."""
+        sp = span.c()
+        nm = _norm(norm)
+        _check(lib().fa_attention_input(self._h, layer, C.byref(sp), rope if angles is not None else ROPE_NONE,
+                                        _dptr(angles), nm, _dptr(qkv), qkv.stride(0),
+                                        _dptr(q_out), _stream(stream)))
+
+    def attend(self, layer: int, span: Span, q, out, stream=None):
+        """KvCache::attend (transformer.rs:182-219) of rotated queries."""
+        sp = span.c()
+        _check(lib().fa_attend(self._h, layer, C.byref(sp), _dptr(q), q.stride(0), _dptr(out),
+                               out.stride(0), _stream(stream)))
+
+    def attention(self, layer: int, span: Span, qkv, out, angles=None, rope: int = ROPE_HALF,
+                  norm=None, stream=None):
+        """The attention phase of one layer (Cached::keep + Cached::attend) on device tensors."""
+        sp = span.c()
+        nm = _norm(norm)
+        _check(lib().fa_attention(self._h, layer, C.byref(sp),
+                                  rope if angles is not None else ROPE_NONE, _dptr(angles), nm,
+                                  _dptr(qkv), qkv.stride(0), _dptr(out), out.stride(0),
+                                  _stream(stream)))
+
+    def attention_host(self, layer: int, span: Span, qkv: np.ndarray, angles=None,
+                       rope: int = ROPE_HALF, norm=None, stream=None) -> np.ndarray:
+        """The same on host (numpy) rows, as the reference's host Buffers hold them."""
+        qkv = np.ascontiguousarray(qkv, np.float32)
+        out = np.zeros((span.rows, self.shape.width), np.float32)
+        ang = None if angles is None else np.ascontiguousarray(angles, np.float32)
+        sp = span.c()
+        nm = _norm(norm)
+        _check(lib().fa_attention_host(self._h, layer, C.byref(sp),
+                                       rope if ang is not None else ROPE_NONE,
+                                       None if ang is None else ang.ctypes.data_as(C.c_void_p), nm,
+                                       qkv.ctypes.data_as(C.c_void_p), qkv.shape[1],
+                                       out.ctypes.data_as(C.c_void_p), out.shape[1],
+                                       _stream(stream)))
+        return out
+
+    def attend_partial(self, layer: int, q, key_begin: int, key_end: int, partials, stream=None):
+        """A KV-range shard's (max, sum, o) per head over positions [key_begin, key_end)."""
+        _check(lib().fa_attend_partial(self._h, layer, _dptr(q), key_begin, key_end,
+                                       _dptr(partials), _stream(stream)))
+
+
+def _norm(norm):
+    if norm is None:
+        return None
+    q, k, eps = norm
+    return C.byref(_HeadNorm(_dptr(q), _dptr(k), eps))
+
+
+def attention_batch(caches: Sequence[KvCache], spans: Sequence[Span], layer: int, qkv, out,
+                    angles=None, rope: int = ROPE_HALF, norm=None, stream=None):
+    """One decode row of each of `len(caches)` sequences in one launch."""
+    n = len(caches)
+    handles = (C.c_void_p * n)(*[c.handle.value for c in caches])
+    cs = [s.c() for s in spans]
+    arr = (_Span * n)(*cs)
+    _check(lib().fa_attention_batch(handles, arr, n, layer,
+                                    rope if angles is not None else ROPE_NONE, _dptr(angles),
+                                    _norm(norm), _dptr(qkv), qkv.stride(0), _dptr(out),
+                                    out.stride(0), _stream(stream)))
+
+
+class Batch:
+    """A batch of one-row spans over caches of one shape, its C arrays built once."""
+
+    def __init__(self, caches: Sequence[KvCache], spans: Sequence[Span]):
+        n = len(caches)
+        self.n = n
+        self.caches = list(caches)
+        self.handles = (C.c_void_p * n)(*[c.handle.value for c in caches])
+        self.spans = (_Span * n)(*[s.c() for s in spans])
+
+    def attention_input(self, layer: int, qkv, q_out=None, angles=None, rope: int = ROPE_HALF,
+                        norm=None, stream=None):
+        _check(lib().fa_attention_input_batch(
+            self.handles, self.spans, self.n, layer, rope if angles is not None else ROPE_NONE,
+            _dptr(angles), _norm(norm), _dptr(qkv), qkv.stride(0), _dptr(q_out),
+            0 if q_out is None else q_out.stride(0), _stream(stream)))
+
+    def attend(self, layer: int, q, out, stream=None):
+        _check(lib().fa_attend_batch(self.handles, self.spans, self.n, layer, _dptr(q),
+                                     q.stride(0), _dptr(out), out.stride(0), _stream(stream)))
+
+    def attention(self, layer: int, qkv, out, angles=None, rope: int = ROPE_HALF, norm=None,
+                  stream=None):
+        _check(lib().fa_attention_batch(self.handles, self.spans, self.n, layer,
+                                        rope if angles is not None else ROPE_NONE, _dptr(angles),
+                                        _norm(norm), _dptr(qkv), qkv.stride(0), _dptr(out),
+                                        out.stride(0), _stream(stream)))
+
+
+def merge_partials(partials, out, stream=None):
+    """Log-sum-exp merge of shards' partials [shards][heads][head_dim + 2] into out."""
+    shards, heads, width = partials.shape
+    _check(lib().fa_merge_partials(_dptr(partials), shards, heads, width - 2, _dptr(out),
+                                   _stream(stream)))
+
+
+@dataclass
+class Operand:
+    """blocks::attention::Operand (attention.rs:24-31) over a device tensor."""
+    values: object
+    stride: int
+    offset: int = 0
+
+
+def attend_full(heads: int, kv_heads: int, head_dim: int, images: int, queries: int, keys: int,
+                query: Operand, key: Operand, value: Operand, out, stream=None):
+    """blocks::attention::attend / dit::Within: full-mask attention (attention.rs:79-95)."""
+    import torch
+    dt = {torch.float32: F32, torch.bfloat16: BF16}
+    call = _Call(heads, kv_heads, head_dim, images, queries, keys,
+                 _Operand(query.values.data_ptr(), query.stride, query.offset),
+                 _Operand(key.values.data_ptr(), key.stride, key.offset),
+                 _Operand(value.values.data_ptr(), value.stride, value.offset),
+                 dt[query.values.dtype], dt[out.dtype])
+    _check(lib().fa_attend_full(C.byref(call), _dptr(out), out.stride(0), _stream(stream)))
+
+
+def device_status(stream=None):
+    """Raises FaError(ERR_TIMEOUT) if a kernel gave up a device-side wait."""
+    _check(lib().fa_device_status(_stream(stream)))
+
+
+def rng_normal(seed: int, n: int) -> np.ndarray:
+    """kernels::rng::Rng::new(seed).fill_normal (rng.rs:5-52) of n values, on the host."""
+    out = np.empty(n, np.float32)
+    _check(lib().fa_rng_fill_normal(seed, out.ctypes.data_as(C.c_void_p), n))
+    return out
+
+
+def capabilities():
+    flags = C.c_int32()
+    dims = (C.c_int32 * 16)()
+    n = C.c_int32()
+    _check(lib().fa_capabilities(C.byref(flags), dims, 16, C.byref(n)))
+    return flags.value, list(dims[: n.value])

@@ -1,0 +1,257 @@
+/*
+ * fa_attn.h -- the C ABI of the B200 attention hot path of fusor-ai.
+ *
+ * It replaces the attention phase of blocks::transformer::Transformer::forward over a KvCache
+ * (RoPE + keep + grouped-query attention; decode and prefill under every Mask) and the
+ * full-mask attention of blocks::attention::attend / dit::Within. Every entry point cites the
+ * fusor-ai interface it replaces (paths relative to the fusor-ai project root).
+ *
+ * Conventions
+ *  - Plain C: pointers, sizes and status codes; no panics or aborts cross the boundary. Every
+ *    function returns FA_OK (0) or an FA_ERR_* code; fa_last_error() describes the last failure
+ *    of the calling thread.
+ *  - Device pointers unless a name or comment says "host". `stream` is a cudaStream_t (NULL is
+ *    the legacy default stream). Work is enqueued on `stream` and not waited for, except by the
+ *    *_host entry points, which return when their host outputs are written.
+ *  - Tensors are row-major with explicit element strides, as the reference's SharedBuf rows.
+ *  - A KvCache is used from one stream at a time, as the reference uses one from one team run.
+ */
+#ifndef FA_ATTN_H
+#define FA_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define FA_OK 0
+#define FA_ERR_ARG 1         /* a null pointer, a negative size, a bad enum value */
+#define FA_ERR_SHAPE 2       /* heads % kv_heads != 0 (transformer.rs:389-393), a layer or row
+                                count beyond what the cache or call holds (layer.rs:124-125) */
+#define FA_ERR_CAPACITY 3    /* the span does not fit the cache (transformer.rs:331-338) */
+#define FA_ERR_CUDA 4        /* a CUDA runtime error (allocation, launch) */
+#define FA_ERR_TIMEOUT 5     /* a device-side wait gave up (see fa_device_status) */
+#define FA_ERR_UNSUPPORTED 6 /* a head_dim or dtype this build has no kernel for */
+
+/* Element types of the cache and of full-mask operands. */
+#define FA_F32 0
+#define FA_BF16 1
+
+/* transformer::Mask (crates/blocks/src/transformer.rs:97-111). */
+#define FA_MASK_CAUSAL 0
+#define FA_MASK_WINDOW 1
+#define FA_MASK_FULL 2
+#define FA_MASK_GROUPS 3
+
+/* Rotary pairing of the layer spec (crates/blocks/src/layer/spec.rs Rope; ops.rs:77-95). */
+#define FA_ROPE_NONE 0
+#define FA_ROPE_HALF 1
+#define FA_ROPE_INTERLEAVED 2
+
+/* rotary::Rotation (crates/blocks/src/rotary.rs:62-86). */
+#define FA_ROT_SEQUENCE 0
+#define FA_ROT_LINEAR 1
+#define FA_ROT_PARTIAL 2
+#define FA_ROT_MULTIMODAL 3
+#define FA_ROT_AXES 4
+#define FA_ROT_MULTIMODAL_INTERLEAVED 5
+#define FA_ROT_GRID 6
+
+/* Mask (transformer.rs:99-111). `ends` is a HOST array of n_ends group ends (Groups only). */
+typedef struct {
+  int32_t kind;
+  int32_t window;
+  int32_t state;
+  int32_t n_ends;
+  const int32_t* ends;
+} fa_mask;
+
+/* Span (transformer.rs:272-279): `rows` consecutive positions from `first` under `mask`. */
+typedef struct {
+  int32_t rows;
+  int32_t first;
+  fa_mask mask;
+} fa_span;
+
+/* rotary::Position (rotary.rs:27-33). */
+typedef struct {
+  int32_t temporal;
+  int32_t height;
+  int32_t width;
+} fa_position;
+
+/* A Rotary's configuration: Rotary::new(rotation, base, head_dim) (rotary.rs:117-156), with
+ * params = the factor (Linear), the turning count (Partial) or the three sections; and
+ * spatially_scaled(spatial_scale) (rotary.rs:161-168; 1 leaves it as it is). */
+typedef struct {
+  int32_t kind;
+  int32_t params[3];
+  float base;
+  float spatial_scale;
+} fa_rotation;
+
+/* Optional Qwen3 head norms (layer.rs:220-228): device weight vectors of head_dim, or NULL. */
+typedef struct {
+  const float* q_norm;
+  const float* k_norm;
+  float eps;
+} fa_head_norm;
+
+/* blocks::attention::Operand (crates/blocks/src/attention.rs:24-31): head h of row r is the
+ * head_dim values at values + r * stride + offset + h * head_dim (elements of the call dtype). */
+typedef struct {
+  const void* values;
+  int64_t stride;
+  int64_t offset;
+} fa_operand;
+
+/* blocks::attention::Call (attention.rs:33-47) without the int8 Exponentials choice: `images`
+ * images of `queries` query rows over `keys` key/value rows; query row of image i is
+ * i * queries + q, key row i * keys + k. `dtype` is the operands' element type (FA_F32 or
+ * FA_BF16); `out_dtype` the output's. */
+typedef struct {
+  int32_t heads;
+  int32_t kv_heads;
+  int32_t head_dim;
+  int32_t images;
+  int32_t queries;
+  int32_t keys;
+  fa_operand query;
+  fa_operand key;
+  fa_operand value;
+  int32_t dtype;
+  int32_t out_dtype;
+} fa_call;
+
+typedef struct fa_kvcache fa_kvcache;
+
+/* The message of the calling thread's last failure ("" if none). */
+const char* fa_last_error(void);
+
+/* The build's capabilities: a bitmask of 1 = f32 cache, 2 = bf16 cache, 4 = tcgen05 prefill /
+ * full-mask kernels; and the supported head_dim values through *head_dims (may be NULL). */
+int fa_capabilities(int32_t* flags, int32_t* head_dims, int32_t max_head_dims,
+                    int32_t* n_head_dims);
+
+/* KvCache::new(shape, capacity) / KvCache::of (transformer.rs:148-162): a zeroed cache of
+ * layers x kv_heads x capacity x head_dim keys and as many values, in HBM on `device`, in the
+ * reference's layout [layer][kv_head][slot = position % capacity][head_dim]. `heads` is the
+ * query head count (a multiple of kv_heads). dtype FA_F32 (the reference's) or FA_BF16. */
+int fa_kvcache_create(int32_t layers, int32_t heads, int32_t kv_heads, int32_t head_dim,
+                      int32_t capacity, int32_t dtype, int32_t device, fa_kvcache** out);
+int fa_kvcache_destroy(fa_kvcache* cache);
+
+/* The cache's device arrays and shape, for callers that fill or read it directly. */
+int fa_kvcache_data(const fa_kvcache* cache, void** keys, void** values, int32_t* shape5,
+                    int32_t* dtype);
+
+/* Reserves the per-call workspace for spans of up to `rows` rows (otherwise it grows on the
+ * first call that needs more, which synchronizes the stream; do this before graph capture). */
+int fa_kvcache_reserve(fa_kvcache* cache, int32_t rows);
+
+/* KvCache::copy_rows (transformer.rs:221-239): the first `rows` rows of every (layer, kv head)
+ * block, keys then values, into device buffers of layers*kv_heads*rows*head_dim elements each,
+ * in block order. */
+int fa_kvcache_copy_rows(const fa_kvcache* cache, int32_t rows, void* keys_out,
+                         void* values_out, void* stream);
+/* KvCache::put_rows (transformer.rs:241-251): puts back what fa_kvcache_copy_rows copied. */
+int fa_kvcache_put_rows(fa_kvcache* cache, int32_t rows, const void* keys, const void* values,
+                        void* stream);
+
+/* Rotary::angles for `rows` positions (rotary.rs:170-178 via Stack::turn, layer.rs:140-154),
+ * on the HOST, bit for bit the reference's f32 arithmetic: per row head_dim/2 cosines then
+ * head_dim/2 sines (the layout of Buffers.angles, layer/buffers.rs:17-18). */
+int fa_rotary_angles(const fa_rotation* rotation, int32_t head_dim, const fa_position* positions,
+                     int32_t rows, float* angles_out);
+
+/* The attention input of Stack::attention_input (layer.rs:175-234) after the QKV projection:
+ * for each of span->rows rows of `qkv` (f32, qkv_stride elements apart; query heads, key
+ * heads, value heads of head_dim each), head-norm (optional) and RoPE (`rope`, by `angles`:
+ * rows x head_dim as fa_rotary_angles writes them; NULL when rope is FA_ROPE_NONE) the query
+ * and key heads, and keep the key and value heads at position first + row (KvCache::keep,
+ * transformer.rs:164-180). The rotated queries are written to q_out (rows x heads x head_dim
+ * f32) when it is not NULL; qkv is not modified. */
+int fa_attention_input(fa_kvcache* cache, int32_t layer, const fa_span* span, int32_t rope,
+                       const float* angles, const fa_head_norm* norm, const float* qkv,
+                       int64_t qkv_stride, float* q_out, void* stream);
+
+/* KvCache::attend (transformer.rs:182-219): the span's rows' rotated queries (q: rows x
+ * q_stride f32, heads x head_dim each) attend over the cache under span->mask into out (rows x
+ * out_stride f32, heads x head_dim each), scores scaled by 1/sqrt(head_dim). */
+int fa_attend(fa_kvcache* cache, int32_t layer, const fa_span* span, const float* q,
+              int64_t q_stride, float* out, int64_t out_stride, void* stream);
+
+/* The whole attention phase of one layer of Transformer::forward (transformer.rs:294-341 and
+ * the Cached attention, 344-380): the capacity rule, then fa_attention_input, then fa_attend.
+ * Replaces Cached::keep + Cached::attend behind the layer's Attention plugin (layer.rs:73-88). */
+int fa_attention(fa_kvcache* cache, int32_t layer, const fa_span* span, int32_t rope,
+                 const float* angles, const fa_head_norm* norm, const float* qkv,
+                 int64_t qkv_stride, float* out, int64_t out_stride, void* stream);
+
+/* fa_attention with HOST qkv, angles and out (the reference's Buffers live in host memory,
+ * layer/buffers.rs:10-29): copies the rows in, runs, copies the output back and returns when
+ * `out` holds it. */
+int fa_attention_host(fa_kvcache* cache, int32_t layer, const fa_span* span, int32_t rope,
+                      const float* angles_host, const fa_head_norm* norm, const float* qkv_host,
+                      int64_t qkv_stride, float* out_host, int64_t out_stride, void* stream);
+
+/* One decode step (Span rows = 1) of `batch` independent sequences, each with its own cache
+ * (all of one shape and device), in one launch: sequence i's row is row i of qkv (qkv_stride
+ * apart) at spans[i].first under spans[i].mask, angles row i (device, batch x head_dim; NULL
+ * for FA_ROPE_NONE), output row i of out. The reference runs one Transformer::forward per
+ * sequence (models/ming/model/src/session.rs:268-282); batch <= 1024. */
+int fa_attention_batch(fa_kvcache* const* caches, const fa_span* spans, int32_t batch,
+                       int32_t layer, int32_t rope, const float* angles,
+                       const fa_head_norm* norm, const float* qkv, int64_t qkv_stride,
+                       float* out, int64_t out_stride, void* stream);
+
+/* fa_attention_batch's first half: RoPE + keep of each sequence's row into its own cache, the
+ * rotated queries into q_out (batch rows, q_out_stride apart; may be NULL). */
+int fa_attention_input_batch(fa_kvcache* const* caches, const fa_span* spans, int32_t batch,
+                             int32_t layer, int32_t rope, const float* angles,
+                             const fa_head_norm* norm, const float* qkv, int64_t qkv_stride,
+                             float* q_out, int64_t q_out_stride, void* stream);
+
+/* fa_attention_batch's second half: KvCache::attend of each sequence's rotated query row (q,
+ * q_stride apart) over its own cache, all sequences in one launch. */
+int fa_attend_batch(fa_kvcache* const* caches, const fa_span* spans, int32_t batch,
+                    int32_t layer, const float* q, int64_t q_stride, float* out,
+                    int64_t out_stride, void* stream);
+
+/* One KV-range shard of a decode (split-KV across GPUs; the reference has no counterpart, it is
+ * the sharded form of ops::attend over keys key_begin..key_end, ops.rs:310-342): the rotated
+ * query row q (heads x head_dim f32) over cache positions [key_begin, key_end) of `layer`,
+ * all visible, into partials: per head [max, sum, o[head_dim]] with max the largest score in
+ * base-2 units (score * log2(e) / sqrt(head_dim)), sum = sum of 2^(score - max) and o the
+ * unnormalised sum of 2^(score - max) * value; heads x (head_dim + 2) f32. An empty range
+ * gives max = -inf, sum = 0, o = 0. */
+int fa_attend_partial(fa_kvcache* cache, int32_t layer, const float* q, int32_t key_begin,
+                      int32_t key_end, float* partials, void* stream);
+
+/* The log-sum-exp merge of `shards` partials (shards x heads x (head_dim + 2) f32, as
+ * fa_attend_partial writes them) into out (heads x head_dim f32). */
+int fa_merge_partials(const float* partials, int32_t shards, int32_t heads, int32_t head_dim,
+                      float* out, void* stream);
+
+/* blocks::attention::attend (attention.rs:79-95) and dit::Within::attend (dit.rs:135-166): full
+ * (non-causal) softmax attention of every query over every key of its image, scores scaled by
+ * 1/sqrt(head_dim), into out (images*queries rows of out_stride elements, heads x head_dim
+ * each, in call->out_dtype). The reference's int8 SageAttention-style approximation is replaced
+ * by f32 (FA_F32 operands) or bf16-in / f32-accumulate (FA_BF16) arithmetic. */
+int fa_attend_full(const fa_call* call, void* out, int64_t out_stride, void* stream);
+
+/* Waits for `stream` and reports whether any kernel of this library gave up a device-side wait
+ * since the last call (FA_ERR_TIMEOUT, clearing the flag) or FA_OK. */
+int fa_device_status(void* stream);
+
+/* The reference's seeded generator (crates/kernels/src/rng.rs:5-52: xoshiro256** seeded by
+ * SplitMix64, normals by Box-Muller), on the HOST: n standard normals into out. */
+int fa_rng_fill_normal(uint64_t seed, float* out, int64_t n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FA_ATTN_H */

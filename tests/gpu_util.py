@@ -1,0 +1,89 @@
+"""Helpers of the GPU parity tests: seeded inputs from the reference's generator, the same
+inputs in a device KvCache and in an oracle cache, and the reference's comparison metrics
+(crates/harness/src/parity.rs:12-45)."""
+from __future__ import annotations
+
+import numpy as np
+
+import fusor_attn as fa
+import oracle
+
+# Parity bar on the attention output with f32 I/O.
+TOL_F32 = 2e-3
+
+
+def relative_l2(ours, reference) -> float:
+    """harness::parity::relative_l2 (parity.rs:12-21), in f64."""
+    ours = np.asarray(ours, np.float64)
+    reference = np.asarray(reference, np.float64)
+    return float(np.sqrt(((ours - reference) ** 2).sum() / max((reference ** 2).sum(), 1e-300)))
+
+
+def max_abs(ours, reference) -> float:
+    """harness::parity::max_abs (parity.rs:23-28)."""
+    return float(np.abs(np.asarray(ours, np.float64) - np.asarray(reference, np.float64)).max())
+
+
+def compare(name, ours, reference) -> str:
+    """harness::parity::compare's line (parity.rs:30-45)."""
+    return (f"{name}: {np.size(ours)} values, rel {relative_l2(ours, reference):.2e}, "
+            f"max abs {max_abs(ours, reference):.2e}")
+
+
+def round_bf16(a: np.ndarray) -> np.ndarray:
+    """ops::round_bf16 (ops.rs:292-298) of every value."""
+    bits = np.ascontiguousarray(a, np.float32).view(np.uint32).astype(np.uint64)
+    rounding = 0x7FFF + ((bits >> 16) & 1)
+    return ((bits + rounding) & 0xFFFF0000).astype(np.uint32).view(np.float32)
+
+
+def normal(seed: int, shape) -> np.ndarray:
+    return fa.rng_normal(seed, int(np.prod(shape))).reshape(shape)
+
+
+class Pair:
+    """A device KvCache and an oracle cache holding the same keys and values."""
+
+    def __init__(self, shape: fa.Shape, capacity: int, dtype=fa.F32, filled: int = 0, seed: int = 1):
+        import torch
+        self.shape, self.capacity, self.dtype = shape, capacity, dtype
+        self.gpu = fa.KvCache(shape, capacity, dtype)
+        self.cpu = oracle.Cache(shape.layers, shape.heads, shape.kv_heads, shape.head_dim, capacity)
+        if filled:
+            dims = (shape.layers, shape.kv_heads, filled, shape.head_dim)
+            k = normal(seed, dims)
+            v = normal(seed + 1, dims)
+            if dtype == fa.BF16:
+                k, v = round_bf16(k), round_bf16(v)
+            self.cpu.keys[:, :, :filled] = k
+            self.cpu.values[:, :, :filled] = v
+            tdt = torch.float32 if dtype == fa.F32 else torch.bfloat16
+            self.gpu.put_rows(torch.from_numpy(k).to("cuda", tdt), torch.from_numpy(v).to("cuda", tdt))
+
+    def keep_rounding(self, layer, first, rows):
+        """A bf16 cache keeps bf16 rows: round the oracle's kept rows the same way."""
+        if self.dtype != fa.BF16:
+            return
+        for r in range(rows):
+            slot = (first + r) % self.capacity
+            self.cpu.keys[layer, :, slot] = round_bf16(self.cpu.keys[layer, :, slot])
+            self.cpu.values[layer, :, slot] = round_bf16(self.cpu.values[layer, :, slot])
+
+    def oracle_attention(self, layer, span: fa.Span, qkv: np.ndarray, angles, rope, threads=8):
+        """The reference's attention phase on the oracle cache: RoPE + keep, then attend."""
+        q = np.ascontiguousarray(qkv, np.float32).copy()
+        self.cpu.attention_input(layer, span.rows, span.first, rope if angles is not None else 0,
+                                 angles, q, q.shape[1])
+        self.keep_rounding(layer, span.first, span.rows)
+        mask = to_oracle_mask(span.mask)
+        return self.cpu.attend(layer, span.rows, span.first, mask, q, q.shape[1], threads=threads)
+
+
+def to_oracle_mask(mask: fa.Mask) -> oracle.Mask:
+    if mask.kind == fa.MASK_CAUSAL:
+        return oracle.Mask.causal()
+    if mask.kind == fa.MASK_WINDOW:
+        return oracle.Mask.window_of(mask.window)
+    if mask.kind == fa.MASK_FULL:
+        return oracle.Mask.full()
+    return oracle.Mask.groups(mask.state, list(mask.ends))

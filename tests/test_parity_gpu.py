@@ -1,0 +1,343 @@
+"""Parity of the CUDA path (through the C ABI) with the oracle, on the reference's own test
+shapes and masks and on the north-star configurations (full size where the oracle finishes in
+seconds, a bounded sample otherwise, with size-independent properties at full size).
+
+Bar: max abs error <= 2e-3 on the attention output with f32 I/O; bf16-storage and bf16-compute
+paths are held to the same bar against an oracle given the same bf16-rounded keys and values,
+and their error against the unrounded f32 inputs is reported separately."""
+import os
+
+import numpy as np
+import pytest
+
+import fusor_attn as fa
+import oracle
+from gpu_util import TOL_F32, Pair, compare, max_abs, normal, relative_l2, round_bf16
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+@pytest.fixture(scope="module")
+def torch():
+    import torch as t
+    assert t.cuda.is_available()
+    fa.lib()
+    return t
+
+
+def dev(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to("cuda")
+
+
+# ---- the reference's block tests: crates/blocks/tests/stacks.rs STREAMS ------------------------
+
+STREAM_MASKS = {
+    "window": fa.Mask.window_of(4),
+    "causal": fa.Mask.causal(),
+    "full": fa.Mask.full(),
+    "groups": fa.Mask.groups(3, [5, 6, 8]),
+}
+
+
+@pytest.mark.parametrize("name", list(STREAM_MASKS))
+@pytest.mark.parametrize("host", [False, True])
+def test_decoder_streams_match_the_oracle_and_the_f64_reference(torch, name, host):
+    g = np.load(os.path.join(GOLDEN, "decoder_attention.npz"))
+    heads, kv_heads, d, rows = (int(x) for x in g["dims"])
+    capacity, call, rope, _ = (int(x) for x in g[f"{name}_meta"])
+    shape = fa.Shape(1, heads, kv_heads, d)
+    pair = Pair(shape, capacity)
+    qkv_all = g["qkv"].reshape(rows, shape.qkv)
+    outs, wants = [], []
+    for first in range(0, rows, call):
+        n = min(call, rows - first)
+        span = fa.Span(n, first, STREAM_MASKS[name])
+        qkv = qkv_all[first:first + n]
+        angles = None
+        if rope > 0:
+            angles = fa.rotary_angles(fa.Rotation(fa.ROT_SEQUENCE, base=10000.0), d,
+                                      range(first, first + n))
+        if host:
+            got = pair.gpu.attention_host(0, span, qkv, angles, rope if rope > 0 else fa.ROPE_NONE)
+        else:
+            out = torch.zeros((n, shape.width), device="cuda")
+            pair.gpu.attention(0, span, dev(torch, qkv), out,
+                               None if angles is None else dev(torch, angles),
+                               rope if rope > 0 else fa.ROPE_NONE)
+            got = out.cpu().numpy()
+        want = pair.oracle_attention(0, span, qkv, angles, max(rope, 0), threads=1)
+        assert max_abs(got, want) <= 1e-5, compare(name, got, want)
+        outs.append(got)
+        wants.append(want)
+    fa.device_status()
+    got = np.concatenate(outs)
+    # the reference's own bar for f32 against its f64 reference (stacks.rs:51-56)
+    assert relative_l2(got, g[f"{name}_want"]) < 1e-6
+
+
+def test_the_cache_holds_the_reference_keys_bit_for_bit(torch):
+    """RoPE + keep on the device keeps exactly the rotated keys the CPU path keeps."""
+    shape = fa.Shape(2, 14, 2, 64)
+    pair = Pair(shape, 64)
+    qkv = normal(11, (5, shape.qkv))
+    angles = fa.rotary_angles(fa.Rotation(base=1e6), 64, range(7, 12))
+    span = fa.Span(5, 7, fa.Mask.causal())
+    out = torch.zeros((5, shape.width), device="cuda")
+    pair.gpu.attention(1, span, dev(torch, qkv), out, dev(torch, angles), fa.ROPE_HALF)
+    pair.oracle_attention(1, span, qkv, angles, fa.ROPE_HALF)
+    k, v = pair.gpu.copy_rows()
+    assert (k.cpu().numpy().view(np.uint32) == pair.cpu.keys.view(np.uint32)).all()
+    assert (v.cpu().numpy().view(np.uint32) == pair.cpu.values.view(np.uint32)).all()
+
+
+def test_head_norms_and_interleaved_rope(torch):
+    shape = fa.Shape(1, 8, 2, 64)
+    pair = Pair(shape, 300, filled=200, seed=5)
+    qkv = normal(12, (3, shape.qkv))
+    qn = 1.0 + 0.2 * normal(13, (64,))
+    kn = 1.0 + 0.2 * normal(14, (64,))
+    angles = fa.rotary_angles(fa.Rotation(base=1e4), 64, range(200, 203))
+    span = fa.Span(3, 200, fa.Mask.causal())
+    out = torch.zeros((3, shape.width), device="cuda")
+    pair.gpu.attention(0, span, dev(torch, qkv), out, dev(torch, angles), fa.ROPE_INTERLEAVED,
+                       norm=(dev(torch, qn), dev(torch, kn), 1e-6))
+    q = qkv.copy()
+    pair.cpu.attention_input(0, 3, 200, fa.ROPE_INTERLEAVED, angles, q, q.shape[1], qn, kn, 1e-6)
+    want = pair.cpu.attend(0, 3, 200, oracle.Mask.causal(), q, q.shape[1])
+    got = out.cpu().numpy()
+    assert max_abs(got, want) <= 1e-4, compare("head norm", got, want)
+
+
+@pytest.mark.parametrize("dtype", [fa.F32, fa.BF16])
+@pytest.mark.parametrize("head_dim", [16, 32, 64, 128, 256])
+def test_every_head_dim_and_storage(torch, dtype, head_dim):
+    shape = fa.Shape(1, 8, 2, head_dim)
+    pair = Pair(shape, 700, dtype, filled=600, seed=3)
+    qkv = normal(21, (2, shape.qkv))
+    angles = fa.rotary_angles(fa.Rotation(base=1e6), head_dim, [600, 601])
+    span = fa.Span(2, 600, fa.Mask.causal())
+    out = torch.zeros((2, shape.width), device="cuda")
+    pair.gpu.attention(0, span, dev(torch, qkv), out, dev(torch, angles), fa.ROPE_HALF)
+    want = pair.oracle_attention(0, span, qkv, angles, fa.ROPE_HALF)
+    got = out.cpu().numpy()
+    assert max_abs(got, want) <= TOL_F32, compare(f"d{head_dim}", got, want)
+
+
+def test_window_ring_wraps_and_groups(torch):
+    """A sliding window over a ring smaller than the sequence, streamed for many calls."""
+    shape = fa.Shape(1, 6, 3, 64)
+    window, call = 50, 7
+    pair = Pair(shape, window + call)
+    for first in range(0, 300, call):
+        span = fa.Span(call, first, fa.Mask.window_of(window))
+        qkv = normal(1000 + first, (call, shape.qkv))
+        angles = fa.rotary_angles(fa.Rotation(base=1e4), 64, range(first, first + call))
+        out = torch.zeros((call, shape.width), device="cuda")
+        pair.gpu.attention(0, span, dev(torch, qkv), out, dev(torch, angles), fa.ROPE_HALF)
+        want = pair.oracle_attention(0, span, qkv, angles, fa.ROPE_HALF)
+        assert max_abs(out.cpu().numpy(), want) <= TOL_F32
+    # Groups over a longer call
+    pair = Pair(shape, 400, filled=100, seed=9)
+    span = fa.Span(120, 100, fa.Mask.groups(130, [150, 151, 190, 220]))
+    qkv = normal(77, (120, shape.qkv))
+    out = torch.zeros((120, shape.width), device="cuda")
+    pair.gpu.attention(0, span, dev(torch, qkv), out)
+    want = pair.oracle_attention(0, span, qkv, None, 0)
+    assert max_abs(out.cpu().numpy(), want) <= TOL_F32
+
+
+def test_capacity_and_span_errors(torch):
+    shape = fa.Shape(1, 4, 2, 16)
+    cache = fa.KvCache(shape, 8)
+    qkv = torch.zeros((4, shape.qkv), device="cuda")
+    out = torch.zeros((4, shape.width), device="cuda")
+    with pytest.raises(fa.CapacityError):
+        cache.attention(0, fa.Span(4, 5, fa.Mask.causal()), qkv, out)
+    with pytest.raises(fa.CapacityError):
+        cache.attention(0, fa.Span(4, 100, fa.Mask.window_of(5)), qkv, out)
+    with pytest.raises(fa.ShapeError):
+        cache.attention(1, fa.Span(1, 0), qkv, out)
+    with pytest.raises(fa.FaError):
+        cache.attention(0, fa.Span(3, 0, fa.Mask.groups(1, [2, 4])), qkv, out)  # last end != 3
+    cache.attention(0, fa.Span(0, 0), qkv, out)  # an empty span is a no-op
+    fa.device_status()
+
+
+def test_copy_rows_put_rows_round_trip(torch):
+    shape = fa.Shape(2, 4, 2, 32)
+    pair = Pair(shape, 40, filled=40, seed=4)
+    k, v = pair.gpu.copy_rows(17)
+    pair.gpu.put_rows(torch.zeros_like(k), torch.zeros_like(v))
+    k0, _ = pair.gpu.copy_rows(17)
+    assert float(k0.abs().max()) == 0.0
+    pair.gpu.put_rows(k, v)
+    k2, v2 = pair.gpu.copy_rows()
+    assert (k2.cpu().numpy() == pair.cpu.keys).all() and (v2.cpu().numpy() == pair.cpu.values).all()
+
+
+# ---- north-star configurations ---------------------------------------------------------------
+
+def test_config1_qwen2_decode_full_size(torch):
+    """C1: 14 q / 2 kv heads, head_dim 64, decode at position 1024 over 1024 cached positions."""
+    shape = fa.Shape(1, 14, 2, 64)
+    pair = Pair(shape, 1025, filled=1024, seed=101)
+    qkv = normal(102, (1, shape.qkv))
+    angles = fa.rotary_angles(fa.Rotation(base=1e6), 64, [1024])
+    span = fa.Span(1, 1024, fa.Mask.causal())
+    out = torch.zeros((1, shape.width), device="cuda")
+    pair.gpu.attention(0, span, dev(torch, qkv), out, dev(torch, angles), fa.ROPE_HALF)
+    want = pair.oracle_attention(0, span, qkv, angles, fa.ROPE_HALF)
+    got = out.cpu().numpy()
+    print(compare("C1", got, want))
+    assert max_abs(got, want) <= TOL_F32
+
+
+def test_config2_qwen2_prefill_full_size(torch):
+    """C2: 512 rows from position 0, causal, the cache written by the same pass."""
+    shape = fa.Shape(1, 14, 2, 64)
+    pair = Pair(shape, 512)
+    qkv = normal(201, (512, shape.qkv))
+    angles = fa.rotary_angles(fa.Rotation(base=1e6), 64, range(512))
+    span = fa.Span(512, 0, fa.Mask.causal())
+    out = torch.zeros((512, shape.width), device="cuda")
+    pair.gpu.attention(0, span, dev(torch, qkv), out, dev(torch, angles), fa.ROPE_HALF)
+    want = pair.oracle_attention(0, span, qkv, angles, fa.ROPE_HALF)
+    got = out.cpu().numpy()
+    print(compare("C2", got, want))
+    assert max_abs(got, want) <= TOL_F32
+
+
+def c3_lengths(seed=301, n=64):
+    rng = np.random.default_rng(seed)
+    return rng.integers(512, 8193, size=n)
+
+
+@pytest.mark.parametrize("dtype", [fa.F32, fa.BF16])
+def test_config3_batched_decode_sample(torch, dtype):
+    """C3 on 8 of its sequences (32 q / 8 kv heads, head_dim 128), one launch."""
+    shape = fa.Shape(1, 32, 8, 128)
+    lengths = c3_lengths()[:8]
+    pairs = [Pair(shape, int(n) + 1, dtype, filled=int(n), seed=310 + i) for i, n in enumerate(lengths)]
+    qkv = normal(302, (len(pairs), shape.qkv))
+    angles = fa.rotary_angles(fa.Rotation(base=1e6), 128, [int(n) for n in lengths])
+    spans = [fa.Span(1, int(n), fa.Mask.causal()) for n in lengths]
+    out = torch.zeros((len(pairs), shape.width), device="cuda")
+    fa.attention_batch([p.gpu for p in pairs], spans, 0, dev(torch, qkv), out, dev(torch, angles),
+                       fa.ROPE_HALF)
+    fa.device_status()
+    got = out.cpu().numpy()
+    for i, (p, span) in enumerate(zip(pairs, spans)):
+        want = p.oracle_attention(0, span, qkv[i:i + 1], angles[i:i + 1], fa.ROPE_HALF)
+        assert max_abs(got[i:i + 1], want) <= TOL_F32, compare(f"C3 seq {i}", got[i:i + 1], want)
+
+
+def test_config3_batch_equals_one_call_per_sequence(torch):
+    """Batching is invisible: each sequence alone gives the same output (full C3 shape, a
+    quarter of the sequences to keep host memory small)."""
+    shape = fa.Shape(1, 32, 8, 128)
+    lengths = c3_lengths()[:16]
+    caches = []
+    for i, n in enumerate(lengths):
+        c = fa.KvCache(shape, int(n) + 1, fa.BF16)
+        k = torch.randn((1, 8, int(n), 128), device="cuda", generator=torch.Generator("cuda").manual_seed(i))
+        c.put_rows(k.to(torch.bfloat16), (-k).to(torch.bfloat16))
+        caches.append(c)
+    qkv = torch.randn((len(caches), shape.qkv), device="cuda")
+    spans = [fa.Span(1, int(n), fa.Mask.causal()) for n in lengths]
+    out = torch.zeros((len(caches), shape.width), device="cuda")
+    fa.attention_batch(caches, spans, 0, qkv, out)
+    for i, c in enumerate(caches):
+        one = torch.zeros((1, shape.width), device="cuda")
+        # the batch already kept row n; attend again over the same keys
+        q = qkv[i:i + 1, : shape.width].contiguous()
+        c.attend(0, spans[i], q, one)
+        assert torch.allclose(one, out[i:i + 1], atol=1e-5, rtol=0)
+
+
+def test_config4_long_context_sharded_matches_unsharded(torch):
+    """C4 at full size (131072 cached + 1 new, 16 q / 8 kv heads, head_dim 128): the KV range
+    split into G shards whose partials merge by log-sum-exp equals the single-cache decode, for
+    every G of the multi-GPU run; and the oracle agrees on a 16384-position prefix."""
+    shape = fa.Shape(1, 16, 8, 128)
+    total = 131072
+    cache = fa.KvCache(shape, total + 1)
+    gen = torch.Generator("cuda").manual_seed(401)
+    k = torch.randn((1, 8, total, 128), device="cuda", generator=gen)
+    v = torch.randn((1, 8, total, 128), device="cuda", generator=gen)
+    cache.put_rows(k, v)
+    qkv = torch.randn((1, shape.qkv), device="cuda", generator=gen)
+    angles = dev(torch, fa.rotary_angles(fa.Rotation(base=1e6), 128, [total]))
+    q = torch.zeros((1, shape.width), device="cuda")
+    span = fa.Span(1, total, fa.Mask.causal())
+    cache.attention_input(0, span, qkv, angles, fa.ROPE_HALF, q_out=q)
+    whole = torch.zeros((1, shape.width), device="cuda")
+    cache.attend(0, span, q, whole)
+    for shards in (1, 2, 4, 8):
+        bounds = np.linspace(0, total + 1, shards + 1).astype(int)
+        parts = torch.zeros((shards, 16, 130), device="cuda")
+        for s in range(shards):
+            cache.attend_partial(0, q, int(bounds[s]), int(bounds[s + 1]), parts[s])
+        merged = torch.zeros((16, 128), device="cuda")
+        fa.merge_partials(parts, merged)
+        assert torch.allclose(merged.reshape(1, -1), whole, atol=2e-5, rtol=0), shards
+    fa.device_status()
+    # oracle on a prefix
+    n = 16384
+    small = Pair(shape, n + 1, filled=n, seed=402)
+    qkv_np = normal(403, (1, shape.qkv))
+    ang = fa.rotary_angles(fa.Rotation(base=1e6), 128, [n])
+    q2 = torch.zeros((1, shape.width), device="cuda")
+    sp = fa.Span(1, n, fa.Mask.causal())
+    small.gpu.attention_input(0, sp, dev(torch, qkv_np), dev(torch, ang), fa.ROPE_HALF, q_out=q2)
+    parts = torch.zeros((3, 16, 130), device="cuda")
+    for s, (a, b) in enumerate([(0, 5000), (5000, 12000), (12000, n + 1)]):
+        small.gpu.attend_partial(0, q2, a, b, parts[s])
+    merged = torch.zeros((16, 128), device="cuda")
+    fa.merge_partials(parts, merged)
+    want = small.oracle_attention(0, sp, qkv_np, ang, fa.ROPE_HALF)
+    got = merged.reshape(1, -1).cpu().numpy()
+    print(compare("C4 prefix", got, want))
+    assert max_abs(got, want) <= TOL_F32
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_config5_full_mask_sample(torch, dtype):
+    """C5's shape (12 heads x 128, MHA, full mask) on 2048 tokens, the output checked on the
+    first and last 128 queries against the oracle (same bf16-rounded inputs for bf16)."""
+    heads, d, n = 12, 128, 2048
+    hidden = heads * d
+    qkv = normal(501, (n, 3 * hidden))
+    if dtype == "bf16":
+        qkv = round_bf16(qkv)
+    t = dev(torch, qkv)
+    if dtype == "bf16":
+        t = t.to(torch.bfloat16)
+    out = torch.zeros((n, hidden), device="cuda")
+    stride = 3 * hidden
+    fa.attend_full(heads, heads, d, 1, n, n, fa.Operand(t, stride, 0), fa.Operand(t, stride, hidden),
+                   fa.Operand(t, stride, 2 * hidden), out)
+    fa.device_status()
+    got = out.cpu().numpy()
+    want = np.zeros_like(got)
+    for qr in ((0, 128), (n - 128, n)):
+        oracle.attend_call(heads, heads, d, 1, n, n, qkv, stride, 0, qkv, stride, hidden,
+                           qkv, stride, 2 * hidden, query_range=qr, threads=8, out=want)
+    rows = np.r_[0:128, n - 128:n]
+    print(compare(f"C5 sample {dtype}", got[rows], want[rows]))
+    assert max_abs(got[rows], want[rows]) <= TOL_F32
+
+
+def test_full_mask_images_and_gqa(torch):
+    """blocks::attention::Call with several images and grouped KV heads."""
+    heads, kv, d, images, queries, keys = 8, 2, 64, 3, 40, 56
+    q = normal(601, (images * queries, heads * d))
+    k = normal(602, (images * keys, kv * d))
+    v = normal(603, (images * keys, kv * d))
+    out = torch.zeros((images * queries, heads * d), device="cuda")
+    fa.attend_full(heads, kv, d, images, queries, keys, fa.Operand(dev(torch, q), heads * d),
+                   fa.Operand(dev(torch, k), kv * d), fa.Operand(dev(torch, v), kv * d), out)
+    want = oracle.attend_call(heads, kv, d, images, queries, keys, q, heads * d, 0, k, kv * d, 0,
+                              v, kv * d, 0)
+    assert max_abs(out.cpu().numpy(), want) <= TOL_F32
