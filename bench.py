@@ -148,13 +148,13 @@ class Workload:
 
 
 class C3Decode(Workload):
-    def __init__(self, torch, fa, rank, world, dtype):
+    def __init__(self, torch, fa, rank, world, dtype, sequences=C3_SEQS):
         self.torch, self.fa = torch, fa
         self.dtype = dtype
         self.name = "c3" if dtype == fa.F32 else "c3bf16"
-        lengths = c3_lengths()
+        lengths = c3_lengths()[:sequences]
         mine = shard_sequences(lengths, world)[rank]
-        self.tokens = C3_SEQS
+        self.tokens = len(lengths)
         self.lengths = [int(lengths[i]) for i in mine]
         shape = fa.Shape(1, C3_HEADS, C3_KV, C3_D)
         self.shape = shape
@@ -434,7 +434,8 @@ def run_ours(args):
 
     def build(name):
         if name in ("c3", "c3bf16"):
-            return C3Decode(torch, fa, rank, world, fa.F32 if name == "c3" else fa.BF16)
+            return C3Decode(torch, fa, rank, world, fa.F32 if name == "c3" else fa.BF16,
+                            args.sequences)
         if name == "c1":
             return SingleDecode(torch, fa, "c1", 14, 2, 64, 1024)
         if name == "c4":
@@ -467,7 +468,7 @@ def run_ours(args):
     }
     del w
     torch.cuda.empty_cache()
-    if world == 1 and args.config == "c3" and not args.no_extras:
+    if world == 1 and args.config == "c3" and not args.no_extras and args.sequences == C3_SEQS:
         extras = {}
         for name in ("c1", "c2", "c3bf16", "c4"):
             x = build(name)
@@ -480,7 +481,8 @@ def run_ours(args):
             del x
             torch.cuda.empty_cache()
         line["configs"] = extras
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config.startswith("c3"):
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config.startswith("c3") \
+            and args.sequences == C3_SEQS:
         threads = min(host_threads(), C3_HEADS)
         v, meta = cpu_baseline_c3(threads)
         line["cpu_baseline"] = {"value": round(v, 3), "unit": "tokens/s", "cores": threads,
@@ -577,6 +579,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="c3", choices=["c1", "c2", "c3", "c3bf16", "c4"])
+    ap.add_argument("--sequences", type=int, default=C3_SEQS,
+                    help="C3 sequences (a smaller batch for profiling captures)")
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

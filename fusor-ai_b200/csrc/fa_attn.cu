@@ -323,7 +323,6 @@ int rope_rows(fa_kvcache* c, int layer, const fa_span* span, int rope, const flo
   a.q_out = q_out;
   a.q_out_stride = q_out_stride;
   a.q_scale = q_scale;
-  a.kv_stride = int64_t(c->capacity) * c->head_dim;
   a.keep = keep ? 1 : 0;
   a.batch = 0;
   a.first = span->first;
@@ -684,8 +683,7 @@ int check_batch(fa_kvcache* const* caches, const fa_span* spans, int32_t batch, 
     const fa_kvcache* c = caches[i];
     if (int rc = check_cache(c)) return rc;
     if (c->heads != c0->heads || c->kv_heads != c0->kv_heads || c->head_dim != c0->head_dim ||
-        c->layers != c0->layers || c->dtype != c0->dtype || c->device != c0->device ||
-        c->capacity != c0->capacity)
+        c->layers != c0->layers || c->dtype != c0->dtype || c->device != c0->device)
       return fail(FA_ERR_SHAPE, "sequence %d's cache differs in shape from the first", i);
     if (spans[i].rows != 1) return fail(FA_ERR_ARG, "batched spans are one row (decode)");
     if (spans[i].mask.kind == FA_MASK_GROUPS)
@@ -735,7 +733,6 @@ int fa_attention_input_batch(fa_kvcache* const* caches, const fa_span* spans, in
     ra.q_out = q_out ? q_out + int64_t(first) * q_out_stride : nullptr;
     ra.q_out_stride = q_out_stride;
     ra.q_scale = 1.0f;
-    ra.kv_stride = int64_t(c0->capacity) * c0->head_dim;
     ra.keep = 1;
     ra.batch = 1;
     for (int i = 0; i < n; ++i) {

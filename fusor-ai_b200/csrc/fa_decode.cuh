@@ -212,8 +212,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) attend_kernel(const __grid_
   const int sg = kvg % c.hgroups;
   const int h0 = kv * c.group + sg * G;
   const int g = min(G, c.group - sg * G);
-  kbase += kv * c.kv_stride;
-  vbase += kv * c.kv_stride;
+  // A batch row's KV heads are its own cache's blocks of capacity x D.
+  const int64_t kv_stride = BATCH ? int64_t(capacity) * D : c.kv_stride;
+  kbase += kv * kv_stride;
+  vbase += kv * kv_stride;
   const int n = runs.n0 + runs.n1;
   const int per = ((n + chunks - 1) / chunks + T - 1) / T * T;
   const int j0 = min(n, chunk * per);

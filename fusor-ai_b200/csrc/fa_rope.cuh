@@ -32,7 +32,6 @@ struct RopeArgs {
   float* q_out;  // rotated queries, row r at q_out + r*q_out_stride, head h at h*head_dim
   int64_t q_out_stride;
   float q_scale;         // scale applied to q_out (1 for the raw rotated queries)
-  int64_t kv_stride;     // elements between consecutive KV heads' blocks of a cache
   int keep;              // 0: rotate queries only
   int batch;             // 0: one cache (rows[0]), positions first + r; 1: rows[r] per row
   int first;
@@ -122,7 +121,8 @@ __global__ void __launch_bounds__(kRopeWarps * 32) rope_keep_kernel(const __grid
   const KeepRow& kr = a.keep_rows[a.batch ? row : 0];
   const int position = a.batch ? kr.position : a.first + row;
   const int kv = (unit - a.heads) % a.kv_heads;
-  const int64_t at = int64_t(kv) * a.kv_stride + int64_t(position % kr.capacity) * d;
+  // KV head blocks of capacity x head_dim (KvCache::offset, transformer.rs:263-269)
+  const int64_t at = (int64_t(kv) * kr.capacity + position % kr.capacity) * d;
   KT* target = static_cast<KT*>(is_key ? kr.k : kr.v) + at;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
