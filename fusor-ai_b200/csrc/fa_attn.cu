@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "fa_attn.h"
+#include "fa_fmha_launch.h"
 #include "fa_launch.cuh"
 
 namespace {
@@ -304,9 +305,59 @@ int attend_rows(fa_kvcache* c, int layer, const fa_span* span, const std::vector
   return FA_OK;
 }
 
+// Rows from which a span goes to the tensor-core kernel (below it the split-KV kernel, which
+// needs no 128-row tiles, is as fast).
+constexpr int kFmhaMinRows = 64;
+
+// Whether a span over the cache runs on the tcgen05 kernel: head_dim 64 or 128, enough rows,
+// and no key position wraps the cache's ring (a causal or full span never does; a window span
+// does once first + rows passes the capacity).
+bool span_on_tensor_cores(const fa_kvcache* c, const fa_span* span) {
+  if (span->rows < kFmhaMinRows) return false;
+  if (!fa::fmha_supported(c->dtype == FA_BF16, c->head_dim)) return false;
+  return int64_t(span->first) + span->rows <= c->capacity;
+}
+
+// The tcgen05 attention of a span's rows over the cache; q holds the rotated queries in the
+// cache's element type (rows x q_stride elements, heads x head_dim each).
+int attend_rows_tc(fa_kvcache* c, int layer, const fa_span* span, const std::vector<int>& ends,
+                   const void* q, int64_t q_stride, float* out, int64_t out_stride,
+                   cudaStream_t stream) {
+  fa::FmhaArgs a{};
+  a.heads = c->heads;
+  a.kv_heads = c->kv_heads;
+  a.group = c->heads / c->kv_heads;
+  a.rows = span->rows;
+  a.images = 1;
+  a.q_tiles = (span->rows + 127) / 128;
+  a.first = span->first;
+  a.end = span->first + span->rows;
+  a.kind = span->mask.kind;
+  a.window = span->mask.window;
+  a.state = span->mask.state;
+  a.n_ends = int(ends.size());
+  for (size_t i = 0; i < ends.size(); ++i) a.ends[i] = ends[i];
+  a.q_row_base_per_image = 0;
+  a.kv_row_base_per_image = 0;
+  a.kv_layer_base = layer * c->kv_heads;
+  a.scale_log2 = query_scale(c->head_dim);
+  a.out = out;
+  a.out_stride = out_stride;
+  a.out_bf16 = 0;
+  a.err = c->dev->err;
+  fa::FmhaLaunch l{c->dtype == FA_BF16 ? 1 : 0, c->head_dim, q, uint64_t(span->rows),
+                   uint64_t(c->heads), uint64_t(q_stride), uint64_t(c->head_dim), c->keys,
+                   c->values, uint64_t(c->capacity), uint64_t(c->layers) * c->kv_heads,
+                   uint64_t(c->head_dim), uint64_t(c->capacity) * c->head_dim, a};
+  cudaError_t e = fa::launch_fmha(l, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "tensor-core attention launch");
+  return FA_OK;
+}
+
 int rope_rows(fa_kvcache* c, int layer, const fa_span* span, int rope, const float* angles,
               const fa_head_norm* norm, const float* qkv, int64_t qkv_stride, float* q_out,
-              int64_t q_out_stride, float q_scale, bool keep, cudaStream_t stream) {
+              int64_t q_out_stride, float q_scale, bool keep, cudaStream_t stream,
+              bool q_out_bf16 = false) {
   if (span->rows == 0) return FA_OK;
   fa::RopeArgs a{};
   a.heads = c->heads;
@@ -323,6 +374,7 @@ int rope_rows(fa_kvcache* c, int layer, const fa_span* span, int rope, const flo
   a.q_out = q_out;
   a.q_out_stride = q_out_stride;
   a.q_scale = q_scale;
+  a.q_out_bf16 = q_out_bf16 ? 1 : 0;
   a.keep = keep ? 1 : 0;
   a.batch = 0;
   a.first = span->first;
@@ -416,7 +468,7 @@ const char* fa_last_error(void) { return g_last_error.c_str(); }
 int fa_capabilities(int32_t* flags, int32_t* head_dims, int32_t max_head_dims,
                     int32_t* n_head_dims) {
   static const int32_t dims[] = {16, 32, 64, 128, 256};
-  if (flags) *flags = 1 | 2;
+  if (flags) *flags = 1 | 2 | (fa::fmha_supported(1, 128) ? 4 : 0);
   const int n = int(sizeof dims / sizeof dims[0]);
   if (head_dims)
     for (int i = 0; i < n && i < max_head_dims; ++i) head_dims[i] = dims[i];
@@ -596,6 +648,18 @@ int fa_attend(fa_kvcache* cache, int32_t layer, const fa_span* span, const float
   auto s = static_cast<cudaStream_t>(stream);
   if (span->rows == 0) return FA_OK;
   Work w;
+  if (span_on_tensor_cores(cache, span) &&
+      (cache->dtype == FA_BF16 ||
+       ((reinterpret_cast<uintptr_t>(q) % 16) == 0 && (q_stride * 4) % 16 == 0))) {
+    if (cache->dtype == FA_F32)
+      return attend_rows_tc(cache, layer, span, ends, q, q_stride, out, out_stride, s);
+    // bf16 queries for a bf16 cache
+    if (int rc = ensure_work(cache, size_t(span->rows) * width, 0, 0, s, &w)) return rc;
+    cudaError_t e = fa::launch_prepare_queries(FA_F32, q, q_stride, 0, span->rows, cache->heads,
+                                               cache->head_dim, 1.0f, w.q, s, true);
+    if (e != cudaSuccess) return cuda_fail(e, "query conversion");
+    return attend_rows_tc(cache, layer, span, ends, w.q, width, out, out_stride, s);
+  }
   const Plan p = plan_for_span(cache, span, ends);
   if (int rc = ensure_work(cache, 0, size_t(span->rows) * p.chunks * cache->heads, 0, s, &w))
     return rc;
@@ -618,6 +682,14 @@ int fa_attention(fa_kvcache* cache, int32_t layer, const fa_span* span, int32_t 
   DeviceGuard guard(cache->device);
   auto s = static_cast<cudaStream_t>(stream);
   Work w;
+  if (span_on_tensor_cores(cache, span)) {
+    // rotated queries in the cache's element type, for the TMA loads of the tensor-core kernel
+    if (int rc = ensure_work(cache, size_t(span->rows) * width, 0, 0, s, &w)) return rc;
+    if (int rc = rope_rows(cache, layer, span, rope, angles, norm, qkv, qkv_stride, w.q, width,
+                           1.0f, true, s, cache->dtype == FA_BF16))
+      return rc;
+    return attend_rows_tc(cache, layer, span, ends, w.q, width, out, out_stride, s);
+  }
   const Plan p = plan_for_span(cache, span, ends);
   if (int rc = ensure_work(cache, size_t(span->rows) * width,
                            size_t(span->rows) * p.chunks * cache->heads, 0, s, &w))
@@ -906,7 +978,8 @@ int fa_attend_full(const fa_call* call, void* out, int64_t out_stride, void* str
   if (k.heads % k.kv_heads != 0) return fail(FA_ERR_SHAPE, "%d heads over %d KV heads", k.heads, k.kv_heads);
   if (!supported_head_dim(k.head_dim)) return fail(FA_ERR_UNSUPPORTED, "head_dim %d", k.head_dim);
   if (k.dtype != FA_F32 && k.dtype != FA_BF16) return fail(FA_ERR_ARG, "dtype %d", k.dtype);
-  if (k.out_dtype != FA_F32) return fail(FA_ERR_UNSUPPORTED, "full-mask output dtype %d", k.out_dtype);
+  if (k.out_dtype != FA_F32 && k.out_dtype != FA_BF16)
+    return fail(FA_ERR_ARG, "output dtype %d", k.out_dtype);
   if (k.images == 0 || k.queries == 0) return FA_OK;
   if (k.keys == 0) return fail(FA_ERR_ARG, "a full-mask call without keys");
   if (k.query.values == nullptr || k.key.values == nullptr || k.value.values == nullptr)
@@ -924,6 +997,45 @@ int fa_attend_full(const fa_call* call, void* out, int64_t out_stride, void* str
   Device* dev = nullptr;
   if (int rc = device_state(device, &dev)) return rc;
   auto s = static_cast<cudaStream_t>(stream);
+  const size_t oesize = k.out_dtype == FA_F32 ? 4 : 2;
+  const bool tma_ok = k.query.stride % align == 0 && k.query.offset % align == 0 &&
+                      reinterpret_cast<uintptr_t>(k.query.values) % 16 == 0 &&
+                      (out_stride * int64_t(oesize)) % 16 == 0 &&
+                      reinterpret_cast<uintptr_t>(out) % 16 == 0;
+  if (tma_ok && fa::fmha_supported(k.dtype == FA_BF16, k.head_dim)) {
+    fa::FmhaArgs a{};
+    a.heads = k.heads;
+    a.kv_heads = k.kv_heads;
+    a.group = k.heads / k.kv_heads;
+    a.rows = k.queries;
+    a.images = k.images;
+    a.q_tiles = (k.queries + 127) / 128;
+    a.first = 0;
+    a.end = k.keys;
+    a.kind = FA_MASK_FULL;
+    a.q_row_base_per_image = k.queries;
+    a.kv_row_base_per_image = k.keys;
+    a.kv_layer_base = 0;
+    a.scale_log2 = query_scale(k.head_dim);
+    a.out = out;
+    a.out_stride = out_stride;
+    a.out_bf16 = k.out_dtype == FA_BF16 ? 1 : 0;
+    a.err = dev->err;
+    fa::FmhaLaunch l{k.dtype == FA_BF16 ? 1 : 0, k.head_dim,
+                     static_cast<const unsigned char*>(k.query.values) + k.query.offset * esize,
+                     uint64_t(k.images) * k.queries, uint64_t(k.heads), uint64_t(k.query.stride),
+                     uint64_t(k.head_dim),
+                     static_cast<const unsigned char*>(k.key.values) + k.key.offset * esize,
+                     static_cast<const unsigned char*>(k.value.values) + k.value.offset * esize,
+                     uint64_t(k.images) * k.keys, uint64_t(k.kv_heads), uint64_t(k.key.stride),
+                     uint64_t(k.head_dim), a};
+    cudaError_t e = fa::launch_fmha(l, s);
+    if (e != cudaSuccess) return cuda_fail(e, "tensor-core attention launch");
+    return FA_OK;
+  }
+  if (k.out_dtype != FA_F32)
+    return fail(FA_ERR_UNSUPPORTED, "bf16 output needs the tensor-core path (head_dim 64/128, "
+                                    "16-byte aligned rows)");
   // A call-local workspace, kept per device and grown on demand.
   static Buffer work[64];
   static Buffer counters[64];

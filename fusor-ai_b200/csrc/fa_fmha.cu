@@ -1,0 +1,94 @@
+// Host side of the tcgen05 attention kernel: TMA tensor maps (encoded through the driver entry
+// point, so the library needs no link-time libcuda) and the launches of its instantiations.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "fa_fmha.cuh"
+#include "fa_fmha_launch.h"
+
+namespace fa {
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// A 3-D map over [z][y][x] elements (x innermost, contiguous) with byte strides for y and z and
+// a box of (box_x, box_y, 1), 128-byte swizzled.
+bool make_map(CUtensorMap* map, bool bf16, const void* base, uint64_t x, uint64_t y, uint64_t z,
+              uint64_t y_stride_bytes, uint64_t z_stride_bytes, uint32_t box_x, uint32_t box_y) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[3] = {x, y, z};
+  const cuuint64_t strides[2] = {y_stride_bytes, z_stride_bytes};
+  const cuuint32_t box[3] = {box_x, box_y, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                        3, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <typename T, int D>
+cudaError_t launch_t(const FmhaLaunch& l, cudaStream_t stream) {
+  using S = FmhaShape<T, D>;
+  constexpr bool bf16 = sizeof(T) == 2;
+  const size_t e = sizeof(T);
+  CUtensorMap qm, km, vm;
+  if (!make_map(&qm, bf16, l.q, D, l.q_rows, l.q_heads, l.q_row_stride * e, l.q_head_stride * e,
+                S::kBlock, S::BM) ||
+      !make_map(&km, bf16, l.k, D, l.kv_rows, l.kv_z, l.kv_row_stride * e, l.kv_z_stride * e,
+                S::kBlock, S::BN) ||
+      !make_map(&vm, bf16, l.v, D, l.kv_rows, l.kv_z, l.kv_row_stride * e, l.kv_z_stride * e,
+                S::kBlock, S::BN))
+    return cudaErrorInvalidValue;
+  auto kernel = fmha_kernel<T, D>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           int(S::kSmemBytes));
+    if (err != cudaSuccess) return err;
+    configured = true;
+  }
+  const dim3 grid(l.args.images * l.args.q_tiles, l.args.heads);
+  kernel<<<grid, kFmhaThreads, S::kSmemBytes, stream>>>(qm, km, vm, l.args);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool fmha_supported(int dtype_bf16, int head_dim) {
+  (void)dtype_bf16;
+  return (head_dim == 64 || head_dim == 128) && encode_fn() != nullptr;
+}
+
+int fmha_block_n(int dtype_bf16, int head_dim) {
+  return (!dtype_bf16 && head_dim == 128) ? 64 : 128;
+}
+
+cudaError_t launch_fmha(const FmhaLaunch& l, cudaStream_t stream) {
+  if (l.bf16) {
+    if (l.head_dim == 64) return launch_t<__nv_bfloat16, 64>(l, stream);
+    if (l.head_dim == 128) return launch_t<__nv_bfloat16, 128>(l, stream);
+  } else {
+    if (l.head_dim == 64) return launch_t<float, 64>(l, stream);
+    if (l.head_dim == 128) return launch_t<float, 128>(l, stream);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace fa

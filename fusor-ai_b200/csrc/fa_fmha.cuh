@@ -1,0 +1,337 @@
+// The compute-bound half of the hot path: prefill (Span rows > 1) and full-mask attention as a
+// tcgen05 tensor-core flash-attention forward pass (KvCache::attend over many rows,
+// transformer.rs:182-219; blocks::attention::attend / dit::Within, attention.rs:79-95,
+// dit.rs:135-166), with the f32 ops::attend semantics (ops.rs:310-342).
+//
+// One CTA = 128 query rows of one query head. Warp roles:
+//   warp 0      TMA producer: Q once, then K and V tiles into a ring of shared-memory stages
+//               (128-byte swizzled, plain per-CTA loads: no cluster multicast);
+//   warp 1      TMEM owner and MMA issuer (one thread): S = Q K^T into one of two TMEM
+//               buffers, then O += P V with P read from TMEM (the TS form);
+//   warps 4-7   softmax: thread i owns query row i (TMEM lane i); it loads its S row, masks,
+//               updates the running max lazily (the output is rescaled only when the max grows
+//               by more than 2^8, FA4's trick), writes P back into the S buffer (bf16 pairs, or
+//               tf32) and finally normalises O and stores it.
+// The MMA order S_0, S_1, PV_0, S_2, PV_1, ... keeps the tensor core on S_{j+1} while the
+// softmax works on S_j.
+//
+// T = __nv_bfloat16 runs kind::f16 (bf16 operands, f32 accumulation); T = float runs kind::tf32
+// on f32 data (the f32-I/O path).
+#pragma once
+
+#include "fa_decode.cuh"
+#include "fa_fmha_launch.h"
+#include "fa_tc.cuh"
+
+namespace fa {
+
+template <typename T, int D>
+struct FmhaShape {
+  static constexpr bool kTf32 = sizeof(T) == 4;
+  static constexpr int BM = 128;                               // query rows per CTA
+  static constexpr int BN = (kTf32 && D == 128) ? 64 : 128;    // keys per KV tile
+  static constexpr int kElem = int(sizeof(T));
+  static constexpr int kBlock = 128 / kElem;                   // elements per swizzled 128 B row
+  static constexpr int kDBlocks = D / kBlock;
+  static constexpr int kKStep = 32 / kElem;                    // elements per MMA K step
+  static constexpr int kStages = 2;
+  static constexpr int kQBytes = BM * D * kElem;
+  static constexpr int kKVBytes = BN * D * kElem;
+  static constexpr int kSCols = BN;                            // TMEM columns of one S buffer
+  static constexpr int kOCol = 256;                            // TMEM column of O
+  static constexpr int kPCols = kTf32 ? BN : BN / 2;           // TMEM columns of P
+  static constexpr size_t kSmemBytes =
+      size_t(kQBytes) + size_t(kStages) * 2 * kKVBytes + 1024 /* alignment */ + 256 /* bars */;
+  static_assert(D % kBlock == 0, "head_dim a multiple of the swizzle block");
+  static_assert(BN % 32 == 0 && D % 32 == 0, "TMEM loads of 32 columns");
+};
+
+constexpr int kFmhaThreads = 256;
+
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kFmhaThreads, 1)
+    fmha_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
+                const __grid_constant__ CUtensorMap v_map, const __grid_constant__ FmhaArgs a) {
+  using S = FmhaShape<T, D>;
+  constexpr int BM = S::BM, BN = S::BN;
+  constexpr bool kTf32 = S::kTf32;
+  constexpr uint32_t kFmt = kTf32 ? 2u : 1u;
+  constexpr uint32_t kIdescQK = tc::instr_desc(kFmt, false, BN, BM);
+  constexpr uint32_t kIdescPV = tc::instr_desc(kFmt, true, D, BM);
+
+  extern __shared__ unsigned char smem_raw[];
+  // 1024-byte alignment for the 128-byte swizzle atoms.
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* sQ = smem;
+  unsigned char* sK = sQ + S::kQBytes;
+  unsigned char* sV = sK + S::kStages * S::kKVBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + S::kStages * S::kKVBytes);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = k_full + S::kStages;
+  uint64_t* v_full = k_empty + S::kStages;
+  uint64_t* v_empty = v_full + S::kStages;
+  uint64_t* s_full = v_empty + S::kStages;  // [2]
+  uint64_t* p_full = s_full + 2;            // [2]
+  uint64_t* o_done = p_full + 2;
+  uint64_t* mma_drained = o_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_drained + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int head = blockIdx.y;
+  const int kv = head / a.group;
+  // heavier (later, for causal masks) tiles first
+  const int tile_id = int(gridDim.x) - 1 - int(blockIdx.x);
+  const int image = tile_id / a.q_tiles;
+  const int r0 = (tile_id % a.q_tiles) * BM;
+  const int r_last = min(r0 + BM, a.rows) - 1;
+
+  // KV tiles the CTA's rows see: the union of their key runs.
+  int lo, hi;
+  {
+    const Runs first_runs = mask_runs(a.kind, a.window, a.state, a.n_ends, a.ends, a.first + r0, a.end);
+    const Runs last_runs = mask_runs(a.kind, a.window, a.state, a.n_ends, a.ends, a.first + r_last, a.end);
+    lo = first_runs.b0;
+    hi = max(last_runs.b0 + last_runs.n0, last_runs.b1 + last_runs.n1);
+    if (a.kind == 3) { lo = 0; hi = a.end; }  // Groups: every run lies in [0, end)
+  }
+  const int t0 = lo / BN;
+  const int n_tiles = (hi + BN - 1) / BN - t0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < S::kStages; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&p_full[b], 128);
+    }
+    mbar_init(o_done, 1);
+    mbar_init(mma_drained, 1);
+    mbar_fence_init();
+  }
+  if (warp == 1) tc::tmem_alloc(tmem_slot, 512);
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---- TMA producer --------------------------------------------------------------------
+    if (lane == 0) {
+      tc::tma_prefetch_map(&q_map);
+      tc::tma_prefetch_map(&k_map);
+      tc::tma_prefetch_map(&v_map);
+      mbar_arrive_expect_tx(q_full, S::kQBytes);
+      const int qy = image * a.q_row_base_per_image + r0;
+      for (int db = 0; db < S::kDBlocks; ++db)
+        tc::tma_load_3d(sQ + db * BM * 128, &q_map, db * S::kBlock, qy, head, q_full);
+      const int kz = a.kv_layer_base + kv;
+      const int ky0 = image * a.kv_row_base_per_image;
+      int issued = 0;
+      for (int j = 0; j < n_tiles; ++j) {
+        const int st = j % S::kStages;
+        const uint32_t ph = ((j / S::kStages) & 1) ^ 1;
+        const int ky = ky0 + (t0 + j) * BN;
+        if (!mbar_wait(&k_empty[st], ph, a.err)) break;
+        mbar_arrive_expect_tx(&k_full[st], S::kKVBytes);
+        for (int db = 0; db < S::kDBlocks; ++db)
+          tc::tma_load_3d(sK + st * S::kKVBytes + db * BN * 128, &k_map, db * S::kBlock, ky, kz,
+                          &k_full[st]);
+        if (!mbar_wait(&v_empty[st], ph, a.err)) break;
+        mbar_arrive_expect_tx(&v_full[st], S::kKVBytes);
+        for (int db = 0; db < S::kDBlocks; ++db)
+          tc::tma_load_3d(sV + st * S::kKVBytes + db * BN * 128, &v_map, db * S::kBlock, ky, kz,
+                          &v_full[st]);
+        issued = j + 1;
+      }
+      // The loads still in flight land before the CTA may exit (they have, unless a wait gave
+      // up: every full barrier of the last stages completes once its bytes arrive).
+      mbar_wait(q_full, 0, a.err);
+      for (int j = max(0, issued - S::kStages); j < issued; ++j) {
+        mbar_wait(&k_full[j % S::kStages], (j / S::kStages) & 1, a.err);
+        mbar_wait(&v_full[j % S::kStages], (j / S::kStages) & 1, a.err);
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer ----------------------------------------------------------------------
+    if (lane == 0) {
+      const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV);
+      bool ok = mbar_wait(q_full, 0, a.err);
+      auto issue_pv = [&](int j) {
+        const int st = j % S::kStages;
+        const int b = j & 1;
+        if (!mbar_wait(&p_full[b], (j >> 1) & 1, a.err)) return false;
+        if (!mbar_wait(&v_full[st], (j / S::kStages) & 1, a.err)) return false;
+        tc::fence_after_sync();
+        const uint32_t p_tmem = tmem + uint32_t(b * S::kSCols);
+#pragma unroll
+        for (int k = 0; k < BN / S::kKStep; ++k) {
+          const uint64_t vd = tc::smem_desc_sw128(
+              v_base + st * S::kKVBytes + k * S::kKStep * 128, BN * 128, 1024);
+          tc::mma_ts<kTf32>(tmem + S::kOCol, p_tmem + k * 8, vd, kIdescPV,
+                            (j > 0 || k > 0) ? 1u : 0u);
+        }
+        tc::commit(o_done);
+        tc::commit(&v_empty[st]);
+        return true;
+      };
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        const int st = j % S::kStages;
+        const int b = j & 1;
+        if (!mbar_wait(&k_full[st], (j / S::kStages) & 1, a.err)) { ok = false; break; }
+        tc::fence_after_sync();
+#pragma unroll
+        for (int k = 0; k < D / S::kKStep; ++k) {
+          const int db = k / (128 / 32), koff = (k % (128 / 32)) * 32;
+          const uint64_t qd = tc::smem_desc_sw128(q_base + db * BM * 128 + koff, 16, 1024);
+          const uint64_t kd =
+              tc::smem_desc_sw128(k_base + st * S::kKVBytes + db * BN * 128 + koff, 16, 1024);
+          tc::mma_ss<kTf32>(tmem + b * S::kSCols, qd, kd, kIdescQK, k > 0 ? 1u : 0u);
+        }
+        tc::commit(&s_full[b]);
+        tc::commit(&k_empty[st]);
+        if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+      }
+      if (ok && n_tiles > 0) issue_pv(n_tiles - 1);
+      // Every MMA this thread issued has completed before the CTA may free TMEM.
+      tc::commit(mma_drained);
+      mbar_wait(mma_drained, 0, a.err);
+    }
+  } else if (warp >= 4) {
+    // ---- softmax + epilogue ----------------------------------------------------------------
+    const int wq = warp - 4;
+    const int r = r0 + wq * 32 + lane;  // this thread's query row within the image
+    const bool row_valid = r < a.rows;
+    const Runs runs = mask_runs(a.kind, a.window, a.state, a.n_ends, a.ends, a.first + r, a.end);
+    const uint32_t lane_base = tmem + (uint32_t(wq * 32) << 16);
+    float m_used = -INFINITY, l_sum = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int b = j & 1;
+      const int kp = (t0 + j) * BN;  // first key position of the tile
+      // Every decision before a whole-warp tcgen05 instruction is made warp-uniform.
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[b], (j >> 1) & 1, a.err))) { ok = false; break; }
+      tc::fence_after_sync();
+      uint32_t sreg[BN];
+      if constexpr (BN == 128) tc::tmem_ld128_wait(lane_base + b * S::kSCols, sreg);
+      else tc::tmem_ld64_wait(lane_base + b * S::kSCols, sreg);
+      float* s = reinterpret_cast<float*>(sreg);
+      const bool all_in = row_valid &&
+                          ((kp >= runs.b0 && kp + BN <= runs.b0 + runs.n0) ||
+                           (kp >= runs.b1 && kp + BN <= runs.b1 + runs.n1));
+      if (!all_in) {
+#pragma unroll
+        for (int c = 0; c < BN; ++c) {
+          const int key = kp + c;
+          const bool vis = row_valid && ((key >= runs.b0 && key < runs.b0 + runs.n0) ||
+                                         (key >= runs.b1 && key < runs.b1 + runs.n1));
+          if (!vis) s[c] = -INFINITY;
+        }
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BN; ++c) mx = fmaxf(mx, s[c]);
+      const float m_tile = mx * a.scale_log2;  // -inf stays -inf
+      // Lazy rescale: move the reference max only when the tile's max exceeds it by 2^8 (the
+      // first finite max just sets it: nothing has accumulated for the row yet).
+      float alpha = 1.0f;
+      if (m_tile > m_used + 8.0f || (m_used == -INFINITY && m_tile > -INFINITY)) {
+        if (m_used > -INFINITY) alpha = exp2_approx(m_used - m_tile);
+        m_used = m_tile;
+      }
+      if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+        // O holds PV of tiles < j: wait for PV_{j-1}, then rescale the warp's rows.
+        l_sum *= alpha;
+        if (!__all_sync(0xffffffffu, mbar_wait(o_done, (j - 1) & 1, a.err))) { ok = false; break; }
+        tc::fence_after_sync();
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tc::tmem_ld32_wait(lane_base + S::kOCol + c * 32, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tc::tmem_st32(lane_base + S::kOCol + c * 32, o);
+          tc::tmem_wait_st();  // the registers are free again only after the store lands
+        }
+      }
+      const float ms = m_used == -INFINITY ? 0.0f : m_used;
+      float sum = 0.0f;
+      if constexpr (kTf32) {
+#pragma unroll
+        for (int c = 0; c < BN; ++c) {
+          const float p = exp2_approx(fmaf(s[c], a.scale_log2, -ms));
+          sum += p;
+          sreg[c] = tc::round_tf32(p);
+        }
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c)
+          tc::tmem_st32(lane_base + b * S::kSCols + c * 32,
+                        *reinterpret_cast<const uint32_t(*)[32]>(&sreg[c * 32]));
+      } else {
+        // pairs of probabilities packed in place: sreg[c / 2] is written only after s[c] and
+        // s[c + 1] are read
+#pragma unroll
+        for (int c = 0; c < BN; c += 2) {
+          const float p0 = exp2_approx(fmaf(s[c], a.scale_log2, -ms));
+          const float p1 = exp2_approx(fmaf(s[c + 1], a.scale_log2, -ms));
+          sum += p0 + p1;
+          sreg[c / 2] = tc::pack_bf16(p0, p1);
+        }
+#pragma unroll
+        for (int c = 0; c < BN / 64; ++c)
+          tc::tmem_st32(lane_base + b * S::kSCols + c * 32,
+                        *reinterpret_cast<const uint32_t(*)[32]>(&sreg[c * 32]));
+      }
+      l_sum += sum;
+      tc::tmem_wait_st();
+      tc::fence_before_sync();
+      mbar_arrive(&p_full[b]);
+    }
+    // ---- epilogue: O / l -------------------------------------------------------------------
+    if (__all_sync(0xffffffffu, ok && n_tiles > 0 && mbar_wait(o_done, (n_tiles - 1) & 1, a.err))) {
+      tc::fence_after_sync();
+      const float inv = l_sum > 0.0f ? 1.0f / l_sum : 0.0f;
+      const int64_t orow = int64_t(image) * a.rows + r;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tc::tmem_ld32_wait(lane_base + S::kOCol + c * 32, o);
+        if (!row_valid) continue;
+        if (a.out_bf16) {
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) +
+                                                orow * a.out_stride + head * D + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            dst[i] = make_uint4(
+                tc::pack_bf16(__uint_as_float(o[8 * i + 0]) * inv, __uint_as_float(o[8 * i + 1]) * inv),
+                tc::pack_bf16(__uint_as_float(o[8 * i + 2]) * inv, __uint_as_float(o[8 * i + 3]) * inv),
+                tc::pack_bf16(__uint_as_float(o[8 * i + 4]) * inv, __uint_as_float(o[8 * i + 5]) * inv),
+                tc::pack_bf16(__uint_as_float(o[8 * i + 6]) * inv, __uint_as_float(o[8 * i + 7]) * inv));
+        } else {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) +
+                                                  orow * a.out_stride + head * D + c * 32);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            dst[i] = make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
+                                 __uint_as_float(o[4 * i + 2]) * inv, __uint_as_float(o[4 * i + 3]) * inv);
+        }
+      }
+    }
+  }
+
+  // ---- teardown: every TMEM user is done before the owner frees it ---------------------------
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace fa

@@ -1,0 +1,51 @@
+// The tcgen05 attention launch as the C ABI sees it (no CUDA device code in this header).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "fa_ptx.cuh"
+
+namespace fa {
+
+// The tcgen05 kernel's arguments (kernel parameter; plain data).
+struct FmhaArgs {
+  int heads, kv_heads, group;
+  int rows;            // valid query rows per image
+  int images;
+  int q_tiles;         // query tiles per image
+  // key positions of a row: mask kind over positions first + r (cache path); for a full-mask
+  // call kind is Full with end = keys
+  int first, end, kind, window, state, n_ends;
+  int ends[kMaxEnds];
+  int q_row_base_per_image;   // Q rows of image i start at i * this (TMA y coordinate)
+  int kv_row_base_per_image;  // K/V rows of image i start at i * this
+  int kv_layer_base;          // TMA z of kv head 0 (layer * kv_heads for a cache)
+  float scale_log2;           // log2(e) / sqrt(head_dim)
+  void* out;                  // row (image * rows + r) at out + that * out_stride
+  int64_t out_stride;
+  int out_bf16;
+  unsigned* err;
+};
+
+
+// Q, K and V as 3-D tensors of [z][row][head_dim] elements for the TMA maps: Q rows are query
+// rows and z its query heads; K/V rows are key positions and z (layer x) KV heads.
+struct FmhaLaunch {
+  int bf16;      // operands bf16 (kind::f16) or f32 (kind::tf32)
+  int head_dim;  // 64 or 128
+  const void* q;
+  uint64_t q_rows, q_heads;
+  uint64_t q_row_stride, q_head_stride;  // elements
+  const void* k;
+  const void* v;
+  uint64_t kv_rows, kv_z;
+  uint64_t kv_row_stride, kv_z_stride;   // elements
+  const FmhaArgs& args;
+};
+
+bool fmha_supported(int dtype_bf16, int head_dim);
+int fmha_block_n(int dtype_bf16, int head_dim);
+cudaError_t launch_fmha(const FmhaLaunch& launch, cudaStream_t stream);
+
+}  // namespace fa

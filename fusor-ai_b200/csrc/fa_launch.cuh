@@ -39,6 +39,6 @@ cudaError_t launch_merge_partials(const float* partials, int shards, int heads, 
 // Queries of a full-mask call, f32 or bf16 operand rows, scaled into q_out (rows x heads x D).
 cudaError_t launch_prepare_queries(int dtype, const void* values, int64_t stride, int64_t offset,
                                    int rows, int heads, int head_dim, float scale, float* q_out,
-                                   cudaStream_t stream);
+                                   cudaStream_t stream, bool out_bf16 = false);
 
 }  // namespace fa

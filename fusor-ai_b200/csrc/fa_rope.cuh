@@ -32,6 +32,7 @@ struct RopeArgs {
   float* q_out;  // rotated queries, row r at q_out + r*q_out_stride, head h at h*head_dim
   int64_t q_out_stride;
   float q_scale;         // scale applied to q_out (1 for the raw rotated queries)
+  int q_out_bf16;        // q_out holds bf16 (the tensor-core path over a bf16 cache)
   int keep;              // 0: rotate queries only
   int batch;             // 0: one cache (rows[0]), positions first + r; 1: rows[r] per row
   int first;
@@ -109,7 +110,18 @@ __global__ void __launch_bounds__(kRopeWarps * 32) rope_keep_kernel(const __grid
 
   if (is_query) {
     if (a.q_out == nullptr) return;
-    float* q = a.q_out + int64_t(row) * a.q_out_stride + int64_t(unit) * d;
+    const int64_t at = int64_t(row) * a.q_out_stride + int64_t(unit) * d;
+    if (a.q_out_bf16) {
+      __nv_bfloat16* q = reinterpret_cast<__nv_bfloat16*>(a.q_out) + at;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (lo[j] < 0) continue;
+        q[lo[j]] = __float2bfloat16_rn(x[j] * a.q_scale);
+        q[hi[j]] = __float2bfloat16_rn(y[j] * a.q_scale);
+      }
+      return;
+    }
+    float* q = a.q_out + at;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       if (lo[j] < 0) continue;

@@ -17,16 +17,18 @@ __device__ __forceinline__ float load_elem<__nv_bfloat16>(const __nv_bfloat16* p
   return __bfloat162float(*p);
 }
 
-// q_out[r][h][e] = scale * values[r * stride + offset + h * head_dim + e]
-template <typename T>
+// q_out[r][h][e] = scale * values[r * stride + offset + h * head_dim + e], in f32 or bf16
+template <typename T, typename O>
 __global__ void prepare_queries_kernel(const T* values, int64_t stride, int64_t offset, int rows,
-                                       int heads, int head_dim, float scale, float* q_out) {
+                                       int heads, int head_dim, float scale, O* q_out) {
   const int64_t width = int64_t(heads) * head_dim;
   const int64_t total = int64_t(rows) * width;
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total;
        i += int64_t(gridDim.x) * blockDim.x) {
     const int64_t r = i / width, c = i % width;
-    q_out[i] = load_elem<T>(values + r * stride + offset + c) * scale;
+    const float v = load_elem<T>(values + r * stride + offset + c) * scale;
+    if constexpr (sizeof(O) == 2) q_out[i] = __float2bfloat16_rn(v);
+    else q_out[i] = v;
   }
 }
 
@@ -61,17 +63,24 @@ cudaError_t launch_rope(int kt, const RopeArgs& args, cudaStream_t stream) {
 
 cudaError_t launch_prepare_queries(int dtype, const void* values, int64_t stride, int64_t offset,
                                    int rows, int heads, int head_dim, float scale, float* q_out,
-                                   cudaStream_t stream) {
+                                   cudaStream_t stream, bool out_bf16) {
   const int64_t total = int64_t(rows) * heads * head_dim;
   if (total == 0) return cudaSuccess;
   const int blocks = int(std::min<int64_t>((total + 255) / 256, 148 * 16));
-  if (dtype == 0)
-    prepare_queries_kernel<float><<<blocks, 256, 0, stream>>>(
-        static_cast<const float*>(values), stride, offset, rows, heads, head_dim, scale, q_out);
-  else
-    prepare_queries_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>(
-        static_cast<const __nv_bfloat16*>(values), stride, offset, rows, heads, head_dim, scale,
-        q_out);
+  auto* qb = reinterpret_cast<__nv_bfloat16*>(q_out);
+  if (dtype == 0) {
+    auto* v = static_cast<const float*>(values);
+    if (out_bf16)
+      prepare_queries_kernel<<<blocks, 256, 0, stream>>>(v, stride, offset, rows, heads, head_dim, scale, qb);
+    else
+      prepare_queries_kernel<<<blocks, 256, 0, stream>>>(v, stride, offset, rows, heads, head_dim, scale, q_out);
+  } else {
+    auto* v = static_cast<const __nv_bfloat16*>(values);
+    if (out_bf16)
+      prepare_queries_kernel<<<blocks, 256, 0, stream>>>(v, stride, offset, rows, heads, head_dim, scale, qb);
+    else
+      prepare_queries_kernel<<<blocks, 256, 0, stream>>>(v, stride, offset, rows, heads, head_dim, scale, q_out);
+  }
   return cudaGetLastError();
 }
 

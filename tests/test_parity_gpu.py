@@ -12,7 +12,7 @@ import pytest
 
 import fusor_attn as fa
 import oracle
-from gpu_util import TOL_F32, Pair, compare, max_abs, normal, relative_l2, round_bf16
+from gpu_util import TOL_BF16, TOL_F32, Pair, compare, max_abs, normal, relative_l2, round_bf16
 
 pytestmark = pytest.mark.gpu
 
@@ -326,7 +326,7 @@ def test_config5_full_mask_sample(torch, dtype):
                            qkv, stride, 2 * hidden, query_range=qr, threads=8, out=want)
     rows = np.r_[0:128, n - 128:n]
     print(compare(f"C5 sample {dtype}", got[rows], want[rows]))
-    assert max_abs(got[rows], want[rows]) <= TOL_F32
+    assert max_abs(got[rows], want[rows]) <= (TOL_F32 if dtype == "f32" else TOL_BF16)
 
 
 def test_full_mask_images_and_gqa(torch):
@@ -341,3 +341,43 @@ def test_full_mask_images_and_gqa(torch):
     want = oracle.attend_call(heads, kv, d, images, queries, keys, q, heads * d, 0, k, kv * d, 0,
                               v, kv * d, 0)
     assert max_abs(out.cpu().numpy(), want) <= TOL_F32
+
+
+@pytest.mark.parametrize("dtype", [fa.F32, fa.BF16])
+@pytest.mark.parametrize("head_dim", [64, 128])
+@pytest.mark.parametrize("mask_name", ["causal", "window", "full", "groups"])
+def test_prefill_on_tensor_cores_every_mask(torch, dtype, head_dim, mask_name):
+    """Spans of >= 64 rows run on the tcgen05 kernel: every mask, a cache already holding keys
+    (first > 0), GQA 12/4, a row count that is not a multiple of the 128-row tile."""
+    shape = fa.Shape(1, 12, 4, head_dim)
+    first, rows = 150, 200
+    mask = {"causal": fa.Mask.causal(), "window": fa.Mask.window_of(97), "full": fa.Mask.full(),
+            "groups": fa.Mask.groups(180, [200, 260, 300, 350])}[mask_name]
+    pair = Pair(shape, 400, dtype, filled=first, seed=7)
+    qkv = normal(71, (rows, shape.qkv))
+    angles = fa.rotary_angles(fa.Rotation(base=1e6), head_dim, range(first, first + rows))
+    span = fa.Span(rows, first, mask)
+    out = torch.zeros((rows, shape.width), device="cuda")
+    pair.gpu.attention(0, span, dev(torch, qkv), out, dev(torch, angles), fa.ROPE_HALF)
+    fa.device_status()
+    want = pair.oracle_attention(0, span, qkv, angles, fa.ROPE_HALF)
+    got = out.cpu().numpy()
+    print(compare(f"tc d{head_dim} {mask_name} {'f32' if dtype == fa.F32 else 'bf16'}", got, want))
+    assert max_abs(got, want) <= (TOL_F32 if dtype == fa.F32 else TOL_BF16)
+
+
+def test_tensor_core_and_split_kv_paths_agree(torch):
+    """The same rows through fa_attend on the tensor cores (64 rows) and through the split-KV
+    kernel (one row at a time) give the same attention within the f32 bar."""
+    shape = fa.Shape(1, 14, 2, 64)
+    pair = Pair(shape, 4096, filled=4000, seed=8)
+    q = torch.randn((64, shape.width), device="cuda")
+    span = fa.Span(64, 3900, fa.Mask.causal())
+    tc = torch.zeros((64, shape.width), device="cuda")
+    pair.gpu.attend(0, span, q, tc)
+    rows = torch.zeros_like(tc)
+    for r in range(64):
+        pair.gpu.attend(0, fa.Span(1, 3900 + r, fa.Mask.causal()), q[r:r + 1], rows[r:r + 1])
+    err = float((tc - rows).abs().max())
+    print(f"tensor cores vs split-KV: max abs {err:.2e}")
+    assert err <= TOL_F32
