@@ -40,8 +40,10 @@ struct FmhaShape {
   static constexpr int kSCols = BN;                            // TMEM columns of one S buffer
   static constexpr int kOCol = 256;                            // TMEM column of O
   static constexpr int kPCols = kTf32 ? BN : BN / 2;           // TMEM columns of P
-  static constexpr size_t kSmemBytes =
+  static constexpr size_t kSmemUsed =
       size_t(kQBytes) + size_t(kStages) * 2 * kKVBytes + 1024 /* alignment */ + 256 /* bars */;
+  // At least 120 KB so that one CTA holds an SM: each CTA allocates all 512 TMEM columns.
+  static constexpr size_t kSmemBytes = kSmemUsed > 122880 ? kSmemUsed : 122880;
   static_assert(D % kBlock == 0, "head_dim a multiple of the swizzle block");
   static_assert(BN % 32 == 0 && D % 32 == 0, "TMEM loads of 32 columns");
 };
