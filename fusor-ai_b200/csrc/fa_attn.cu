@@ -635,6 +635,37 @@ int fa_attention_input(fa_kvcache* cache, int32_t layer, const fa_span* span, in
                    static_cast<cudaStream_t>(stream));
 }
 
+int fa_rotate_queries(int32_t heads, int32_t head_dim, int32_t rows, int32_t rope,
+                      const float* angles, const fa_head_norm* norm, const float* qkv,
+                      int64_t qkv_stride, float* q_out, int64_t q_out_stride, void* stream) {
+  if (heads < 1 || rows < 0) return fail(FA_ERR_ARG, "heads %d rows %d", heads, rows);
+  if (!supported_head_dim(head_dim)) return fail(FA_ERR_UNSUPPORTED, "head_dim %d", head_dim);
+  if (int rc = check_rope(rope, angles)) return rc;
+  if (rows == 0) return FA_OK;
+  if (qkv == nullptr || q_out == nullptr) return fail(FA_ERR_ARG, "null qkv or q_out");
+  if (qkv_stride < int64_t(heads) * head_dim || q_out_stride < int64_t(heads) * head_dim)
+    return fail(FA_ERR_SHAPE, "row strides below heads x head_dim");
+  fa::RopeArgs a{};
+  a.heads = heads;
+  a.kv_heads = 1;  // units past the query heads are not visited: keep is off
+  a.head_dim = head_dim;
+  a.rope = rope;
+  a.n_rows = rows;
+  a.qkv = qkv;
+  a.qkv_stride = qkv_stride;
+  a.angles = angles;
+  a.q_norm = norm ? norm->q_norm : nullptr;
+  a.k_norm = nullptr;
+  a.eps = norm ? norm->eps : 0.0f;
+  a.q_out = q_out;
+  a.q_out_stride = q_out_stride;
+  a.q_scale = 1.0f;
+  a.keep = 0;
+  cudaError_t e = fa::launch_rope(fa::kKtF32, a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "rope launch");
+  return FA_OK;
+}
+
 int fa_attend(fa_kvcache* cache, int32_t layer, const fa_span* span, const float* q,
               int64_t q_stride, float* out, int64_t out_stride, void* stream) {
   if (int rc = check_cache(cache)) return rc;
@@ -1152,3 +1183,4 @@ int fa_rng_fill_normal(uint64_t seed, float* out, int64_t n) {
 }
 
 }  // extern "C"
+

@@ -29,7 +29,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // A 3-D map over [z][y][x] elements (x innermost, contiguous) with byte strides for y and z and
 // a box of (box_x, box_y, 1), 128-byte swizzled.
 bool make_map(CUtensorMap* map, bool bf16, const void* base, uint64_t x, uint64_t y, uint64_t z,
-              uint64_t y_stride_bytes, uint64_t z_stride_bytes, uint32_t box_x, uint32_t box_y) {
+              uint64_t y_stride_bytes, uint64_t z_stride_bytes, uint32_t box_x, uint32_t box_y,
+              CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   auto fn = encode_fn();
   if (fn == nullptr) return false;
   const cuuint64_t dims[3] = {x, y, z};
@@ -38,7 +39,7 @@ bool make_map(CUtensorMap* map, bool bf16, const void* base, uint64_t x, uint64_
   const cuuint32_t estr[3] = {1, 1, 1};
   const CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
                         3, const_cast<void*>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -54,7 +55,8 @@ cudaError_t launch_t(const FmhaLaunch& l, cudaStream_t stream) {
       !make_map(&km, bf16, l.k, D, l.kv_rows, l.kv_z, l.kv_row_stride * e, l.kv_z_stride * e,
                 S::kBlock, S::BN) ||
       !make_map(&vm, bf16, l.v, D, l.kv_rows, l.kv_z, l.kv_row_stride * e, l.kv_z_stride * e,
-                S::kBlock, S::BN))
+                S::kBlock, S::BN,
+                bf16 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
     return cudaErrorInvalidValue;
   auto kernel = fmha_kernel<T, D>;
   static bool configured = false;

@@ -5,7 +5,8 @@
 //
 // One CTA = 128 query rows of one query head. Warp roles:
 //   warp 0      TMA producer: Q once, then K and V tiles into a ring of shared-memory stages
-//               (128-byte swizzled, plain per-CTA loads: no cluster multicast);
+//               (128-byte swizzled; tf32 V with 32-byte swizzle atoms, the MN-major tf32
+//               layout; plain per-CTA loads: no cluster multicast);
 //   warp 1      TMEM owner and MMA issuer (one thread): S = Q K^T into one of two TMEM
 //               buffers, then O += P V with P read from TMEM (the TS form);
 //   warps 4-7   softmax: thread i owns query row i (TMEM lane i); it loads its S row, masks,
@@ -174,8 +175,14 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
         const uint32_t p_tmem = tmem + uint32_t(b * S::kSCols);
 #pragma unroll
         for (int k = 0; k < BN / S::kKStep; ++k) {
-          const uint64_t vd = tc::smem_desc_sw128(
-              v_base + st * S::kKVBytes + k * S::kKStep * 128, BN * 128, 1024);
+          // V is the MN-major B operand: rows of 128 bytes of one head_dim block, blocks BN*128
+          // bytes apart; bf16 in 8-row 128-byte-swizzle atoms, tf32 in the only MN-major tf32
+          // layout, 4-row atoms of 32-byte chunks.
+          const uint64_t vd = kTf32
+              ? tc::smem_desc(v_base + st * S::kKVBytes + k * S::kKStep * 128, BN * 128, 512,
+                              tc::kSwizzle128BAtom32B)
+              : tc::smem_desc(v_base + st * S::kKVBytes + k * S::kKStep * 128, BN * 128, 1024,
+                              tc::kSwizzle128B);
           tc::mma_ts<kTf32>(tmem + S::kOCol, p_tmem + k * 8, vd, kIdescPV,
                             (j > 0 || k > 0) ? 1u : 0u);
         }

@@ -55,17 +55,26 @@ __device__ __forceinline__ void fence_after_sync() {
 
 // ---- descriptors ----------------------------------------------------------------------------
 
+// Layout types of the descriptor (bits 61-63).
+constexpr uint32_t kSwizzle128B = 2;        // 16-byte chunks XOR-ed within 128-byte rows
+constexpr uint32_t kSwizzle128BAtom32B = 1; // 32-byte chunks within 128-byte rows (MN-major tf32)
+
 // Shared-memory matrix descriptor: start address, leading and stride byte offsets (all >> 4),
-// version 1 (bit 46) and the 128-byte swizzle layout (value 2 in bits 61-63).
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo_bytes,
-                                                    uint32_t sbo_bytes) {
+// version 1 (bit 46) and the layout type (bits 61-63).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                              uint32_t layout) {
   uint64_t d = 0;
   d |= uint64_t((addr >> 4) & 0x3FFFu);
   d |= uint64_t((lbo_bytes >> 4) & 0x3FFFu) << 16;
   d |= uint64_t((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= uint64_t(1) << 46;
-  d |= uint64_t(2) << 61;
+  d |= uint64_t(layout) << 61;
   return d;
+}
+
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo_bytes,
+                                                    uint32_t sbo_bytes) {
+  return smem_desc(addr, lbo_bytes, sbo_bytes, kSwizzle128B);
 }
 
 // Instruction descriptor of a dense MMA with f32 accumulation: a/b format (1 = bf16, 2 = tf32),

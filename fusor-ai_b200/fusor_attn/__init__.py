@@ -94,6 +94,7 @@ SIGNATURES = {
     "fa_rotary_angles": (C.c_int, [_P, _I32, _P, _I32, _P]),
     "fa_attention_input": (C.c_int, [_P, _I32, _P, _I32, _P, _P, _P, _I64, _P, _P]),
     "fa_attend": (C.c_int, [_P, _I32, _P, _P, _I64, _P, _I64, _P]),
+    "fa_rotate_queries": (C.c_int, [_I32, _I32, _I32, _I32, _P, _P, _P, _I64, _P, _I64, _P]),
     "fa_attention": (C.c_int, [_P, _I32, _P, _I32, _P, _P, _P, _I64, _P, _I64, _P]),
     "fa_attention_host": (C.c_int, [_P, _I32, _P, _I32, _P, _P, _P, _I64, _P, _I64, _P]),
     "fa_attention_batch": (C.c_int, [_P, _P, _I32, _I32, _I32, _P, _P, _P, _I64, _P, _I64, _P]),
@@ -385,6 +386,15 @@ class Batch:
                                         rope if angles is not None else ROPE_NONE, _dptr(angles),
                                         _norm(norm), _dptr(qkv), qkv.stride(0), _dptr(out),
                                         out.stride(0), _stream(stream)))
+
+
+def rotate_queries(heads: int, head_dim: int, qkv, q_out, angles=None, rope: int = ROPE_HALF,
+                   norm=None, stream=None):
+    """RoPE (+ query head norm) of the query heads of qkv's rows into q_out, no cache."""
+    _check(lib().fa_rotate_queries(heads, head_dim, qkv.shape[0],
+                                   rope if angles is not None else ROPE_NONE, _dptr(angles),
+                                   _norm(norm), _dptr(qkv), qkv.stride(0), _dptr(q_out),
+                                   q_out.stride(0), _stream(stream)))
 
 
 def merge_partials(partials, out, stream=None):

@@ -1,0 +1,97 @@
+"""Multi-GPU partitioning of the attention path: one process per GPU, torch.distributed for the
+plumbing, a collective only where the path has a real exchange step.
+
+- Independent sequences (batched decode): whole sequences per rank, balanced by keys, no
+  collective (`shard_sequences`).
+- One long context (split-KV decode): each rank holds a contiguous range of key positions in
+  its own KvCache (`kv_shards`); every rank attends its range and produces per-head
+  (max, sum, partial output) triples, which one all-gather over NCCL brings to every rank for
+  the log-sum-exp merge (`ShardedDecode`).
+- Full-mask attention: (head, 128-query tile) units split evenly over ranks, every rank reading
+  the K/V of its heads locally (`head_tile_units`), no collective.
+
+The reference has no multi-device path (one process, one thread team); these are the B200 forms
+of its one-call semantics, checked against the single-GPU result by the tests.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+
+def shard_sequences(lengths, world: int):
+    """Sequence indices of each rank: longest first onto the least-loaded rank (keys + 1)."""
+    order = sorted(range(len(lengths)), key=lambda i: -int(lengths[i]))
+    loads = [0] * world
+    parts = [[] for _ in range(world)]
+    for i in order:
+        r = min(range(world), key=lambda k: loads[k])
+        parts[r].append(i)
+        loads[r] += int(lengths[i]) + 1
+    return [sorted(p) for p in parts]
+
+
+def kv_shards(keys: int, world: int):
+    """Contiguous key-position ranges [lo, hi) of each rank, as even as integers allow."""
+    return [(keys * r // world, keys * (r + 1) // world) for r in range(world)]
+
+
+def head_tile_units(heads: int, rows: int, world: int, tile: int = 128):
+    """Each rank's (head, first row, end row) pieces: the heads x ceil(rows / tile) units of a
+    full-mask call split into `world` contiguous, equal runs (head-major)."""
+    tiles = (rows + tile - 1) // tile
+    total = heads * tiles
+    out = []
+    for r in range(world):
+        a, b = total * r // world, total * (r + 1) // world
+        pieces = []
+        u = a
+        while u < b:
+            h = u // tiles
+            t_end = min(b, (h + 1) * tiles)
+            pieces.append((h, (u % tiles) * tile, min(rows, ((t_end - 1) % tiles + 1) * tile)))
+            u = t_end
+        out.append(pieces)
+    return out
+
+
+@dataclass
+class ShardedDecode:
+    """One decode row over a context split by key position across the ranks of `group`.
+
+    Rank r's `cache` holds positions kv_shards(total, world)[r] at slots 0.. (its capacity is
+    its range, plus one slot for the new row on the last rank). A step rotates the query on
+    every rank, keeps the new row on the rank that holds its position, attends the local range
+    into (max, sum, o) per head, all-gathers those over NCCL and merges them."""
+
+    cache: object          # fusor_attn.KvCache of this rank's range
+    heads: int
+    head_dim: int
+    lo: int
+    hi: int                # this rank's key positions, hi exclusive (the new row included)
+    position: int          # the new row's position
+    world: int
+    group: object = None   # torch.distributed process group (None: the default group)
+
+    def __post_init__(self):
+        import torch
+        self.q = torch.zeros((1, self.heads * self.head_dim), device="cuda")
+        self.partials = torch.zeros((self.heads, self.head_dim + 2), device="cuda")
+        self.gathered = torch.zeros((self.world, self.heads, self.head_dim + 2), device="cuda")
+        self.out = torch.zeros((self.heads, self.head_dim), device="cuda")
+        self.owner = self.lo <= self.position < self.hi
+
+    def step(self, qkv, angles, rope, dist=None):
+        import fusor_attn as fa
+        if self.owner:
+            # keep the new row at its slot in this shard; the rotated query comes back with it
+            span = fa.Span(1, self.position - self.lo, fa.Mask.causal())
+            self.cache.attention_input(0, span, qkv, angles, rope, q_out=self.q)
+        else:
+            fa.rotate_queries(self.heads, self.head_dim, qkv, self.q, angles, rope)
+        self.cache.attend_partial(0, self.q, 0, self.hi - self.lo, self.partials)
+        if dist is not None and self.world > 1:
+            dist.all_gather_into_tensor(self.gathered, self.partials, group=self.group)
+        else:
+            self.gathered[0].copy_(self.partials)
+        fa.merge_partials(self.gathered, self.out)
+        return self.out

@@ -178,6 +178,13 @@ int fa_attention_input(fa_kvcache* cache, int32_t layer, const fa_span* span, in
                        const float* angles, const fa_head_norm* norm, const float* qkv,
                        int64_t qkv_stride, float* q_out, void* stream);
 
+/* The query half of fa_attention_input without a cache: head-norm (optional) and RoPE of the
+ * `heads` query heads of each row of qkv into q_out (rows x q_out_stride f32). The ranks of a
+ * KV-range-sharded decode that do not hold the new position rotate the query with this. */
+int fa_rotate_queries(int32_t heads, int32_t head_dim, int32_t rows, int32_t rope,
+                      const float* angles, const fa_head_norm* norm, const float* qkv,
+                      int64_t qkv_stride, float* q_out, int64_t q_out_stride, void* stream);
+
 /* KvCache::attend (transformer.rs:182-219): the span's rows' rotated queries (q: rows x
  * q_stride f32, heads x head_dim each) attend over the cache under span->mask into out (rows x
  * out_stride f32, heads x head_dim each), scores scaled by 1/sqrt(head_dim). */
