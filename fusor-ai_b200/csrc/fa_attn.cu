@@ -1184,3 +1184,128 @@ int fa_rng_fill_normal(uint64_t seed, float* out, int64_t n) {
 
 }  // extern "C"
 
+// ---- fa_attend_static: KvCache::attend without allocating ----------------------------------
+//
+// Some callers cannot allocate device memory at call time: a host that pre-reserves all of the
+// GPU's memory for its own pool (another framework's caching allocator, or an embedding runtime
+// with a fixed memory budget) has none left for cudaMalloc, and a latency-bound decode loop
+// cannot afford cudaMalloc's implicit device synchronisation when a span first outgrows the
+// cache's workspace. fa_attend_static serves them: the split-KV partials and arrival counters
+// of the attention live in one file-scope device array, the caller passes only its queries and
+// output. That array is kStaticScratchBytes on every GPU that loads the library, held until the
+// process exits.
+namespace {
+
+constexpr size_t kStaticScratchBytes = size_t(4) << 20;   // 4 MiB per device
+constexpr size_t kStaticCounterBytes = size_t(64) << 10;  // its first 64 KiB: arrival counters
+
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+// The array's device address, per device; in host code g_static_scratch names a host-side
+// stand-in, not device memory, so it is looked up once per device with that device current.
+unsigned char* g_static_scratch_addr[64];
+std::mutex g_static_scratch_mutex;
+
+int static_scratch_address(int device, unsigned char** out) {
+  std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
+  if (g_static_scratch_addr[device] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static scratch)");
+    g_static_scratch_addr[device] = static_cast<unsigned char*>(p);
+  }
+  *out = g_static_scratch_addr[device];
+  return FA_OK;
+}
+
+}  // namespace
+
+extern "C" int fa_attend_static(fa_kvcache* cache, int32_t layer, const fa_span* span,
+                                const float* q, int64_t q_stride, float* out, int64_t out_stride,
+                                void* stream) {
+  if (int rc = check_cache(cache)) return rc;
+  if (int rc = check_layer(cache, layer)) return rc;
+  if (span == nullptr) return fail(FA_ERR_ARG, "null span");
+  if (span->rows < 0 || span->first < 0) return fail(FA_ERR_ARG, "negative span");
+  const fa_mask& m = span->mask;
+  if (m.kind < FA_MASK_CAUSAL || m.kind > FA_MASK_GROUPS) return fail(FA_ERR_ARG, "mask kind %d", m.kind);
+  if (m.kind == FA_MASK_WINDOW && m.window < 1) return fail(FA_ERR_ARG, "window %d", m.window);
+  const int64_t end = int64_t(span->first) + span->rows;
+  const int64_t reach = m.kind == FA_MASK_WINDOW ? int64_t(m.window) + span->rows : end;
+  if (reach > cache->capacity)
+    return fail(FA_ERR_CAPACITY, "the cache holds every key the span sees: %lld > capacity %d",
+                (long long)reach, cache->capacity);
+  // Groups ends into a fixed array: nothing on this path allocates, on the host either.
+  int ends[fa::kMaxEnds];
+  int n_ends = 0;
+  if (m.kind == FA_MASK_GROUPS) {
+    if (m.n_ends < 1 || m.ends == nullptr || m.n_ends > fa::kMaxEnds)
+      return fail(FA_ERR_ARG, "Groups needs 1..%d ends", fa::kMaxEnds);
+    if (m.state < 0 || m.state > end) return fail(FA_ERR_ARG, "Groups state %d", m.state);
+    for (int i = 0; i < m.n_ends; ++i) {
+      if (m.ends[i] <= (i == 0 ? m.state - 1 : m.ends[i - 1]) || m.ends[i] > end)
+        return fail(FA_ERR_ARG, "Groups ends must rise after the state and end by the call's end");
+      ends[n_ends++] = m.ends[i];
+    }
+    if (ends[n_ends - 1] != end) return fail(FA_ERR_ARG, "the last group ends with the call");
+  }
+  const int64_t width = int64_t(cache->heads) * cache->head_dim;
+  if (span->rows == 0) return FA_OK;
+  if (q == nullptr || out == nullptr) return fail(FA_ERR_ARG, "null q or out");
+  if (q_stride < width || out_stride < width)
+    return fail(FA_ERR_SHAPE, "row strides below heads x head_dim");
+  // The split of fa_attend's split-KV kernel, and the scratch it needs.
+  int max_keys = 0;
+  for (int r = 0; r < span->rows; ++r) {
+    const fa::Runs runs = fa::mask_runs(m.kind, m.window, m.state, n_ends, ends,
+                                        span->first + r, int(end));
+    max_keys = std::max(max_keys, runs.n0 + runs.n1);
+  }
+  const Plan p = plan_span(cache, span->rows, max_keys);
+  const size_t counter_bytes = size_t(span->rows) * p.kv_groups * sizeof(int);
+  const size_t slots = size_t(span->rows) * p.chunks * cache->heads;
+  const size_t o_bytes = align_up(slots * cache->head_dim * 4, 256);
+  const size_t ml_bytes = align_up(slots * 2 * 4, 256);
+  if (counter_bytes > kStaticCounterBytes ||
+      o_bytes + ml_bytes > kStaticScratchBytes - kStaticCounterBytes)
+    return fail(FA_ERR_ARG,
+                "this span needs %zu bytes of split-KV scratch (%d rows x %d chunks x %d heads); "
+                "fa_attend_static holds %zu: use fa_attend",
+                counter_bytes + o_bytes + ml_bytes, span->rows, p.chunks, cache->heads,
+                kStaticScratchBytes);
+  DeviceGuard guard(cache->device);
+  auto s = static_cast<cudaStream_t>(stream);
+  unsigned char* scratch = nullptr;
+  if (int rc = static_scratch_address(cache->device, &scratch)) return rc;
+  // The counters must start at zero; the array keeps whatever the last call left there.
+  FA_CUDA(cudaMemsetAsync(scratch, 0, counter_bytes, s), "clear static counters");
+  fa::SpanArgs args{};
+  fill_common(&args.c, cache, p);
+  args.c.q = q;
+  args.c.q_stride = q_stride;
+  args.c.out = out;
+  args.c.out_stride = out_stride;
+  args.c.partial_out = nullptr;
+  args.c.counters = reinterpret_cast<int*>(scratch);
+  args.c.part_o = reinterpret_cast<float*>(scratch + kStaticCounterBytes);
+  args.c.part_ml = reinterpret_cast<float*>(scratch + kStaticCounterBytes + o_bytes);
+  args.k = layer_ptr(cache, cache->keys, layer);
+  args.v = layer_ptr(cache, cache->values, layer);
+  args.capacity = cache->capacity;
+  args.rows = span->rows;
+  args.first = span->first;
+  args.end = int(end);
+  args.kind = m.kind;
+  args.window = m.window;
+  args.state = m.state;
+  args.n_ends = n_ends;
+  args.chunks = p.chunks;
+  args.rows_per_image = span->rows;
+  args.keys_per_image = 0;
+  for (int i = 0; i < n_ends; ++i) args.ends[i] = ends[i];
+  fa::AttendLaunch l{cache->dtype == FA_F32 ? fa::kKtF32 : fa::kKtBf16, p.g, false, &args, nullptr,
+                     span->rows * p.kv_groups * p.chunks};
+  const cudaError_t e = launch_attend_d(cache->head_dim, l, s);
+  if (e != cudaSuccess) return cuda_fail(e, "attend launch");
+  return FA_OK;
+}

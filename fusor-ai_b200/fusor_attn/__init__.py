@@ -101,6 +101,7 @@ SIGNATURES = {
     "fa_attention_input_batch": (C.c_int, [_P, _P, _I32, _I32, _I32, _P, _P, _P, _I64, _P, _I64, _P]),
     "fa_attend_batch": (C.c_int, [_P, _P, _I32, _I32, _P, _I64, _P, _I64, _P]),
     "fa_attend_partial": (C.c_int, [_P, _I32, _P, _I32, _I32, _P, _P]),
+    "fa_attend_static": (C.c_int, [_P, _I32, _P, _P, _I64, _P, _I64, _P]),
     "fa_merge_partials": (C.c_int, [_P, _I32, _I32, _I32, _P, _P]),
     "fa_attend_full": (C.c_int, [_P, _P, _I64, _P]),
     "fa_device_status": (C.c_int, [_P]),

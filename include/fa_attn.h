@@ -250,6 +250,19 @@ int fa_merge_partials(const float* partials, int32_t shards, int32_t heads, int3
  * by f32 (FA_F32 operands) or bf16-in / f32-accumulate (FA_BF16) arithmetic. */
 int fa_attend_full(const fa_call* call, void* out, int64_t out_stride, void* stream);
 
+/* fa_attend (KvCache::attend) for callers that cannot allocate device memory when they call:
+ * a host whose GPU memory is all pre-reserved by its own pool, or a latency-bound decode loop
+ * that cannot take cudaMalloc's implicit synchronisation. No counterpart in the reference (its
+ * attention scratch is a host Vec per thread). It runs the split-KV kernel with its partials
+ * and arrival counters in one 4 MiB device array built into the library (every GPU that loads
+ * the library holds it until exit) and calls no allocator: spans whose split needs more
+ * scratch than that are rejected with FA_ERR_ARG. The first call on a device looks up the
+ * array's device address (once per device); make that first call before any stream capture.
+ * Every call on a device shares that device's array: calls whose kernels overlap on the GPU
+ * (on different streams) race, and the caller must serialise them. */
+int fa_attend_static(fa_kvcache* cache, int32_t layer, const fa_span* span, const float* q,
+                     int64_t q_stride, float* out, int64_t out_stride, void* stream);
+
 /* Waits for `stream` and reports whether any kernel of this library gave up a device-side wait
  * since the last call (FA_ERR_TIMEOUT, clearing the flag) or FA_OK. */
 int fa_device_status(void* stream);
