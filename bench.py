@@ -39,18 +39,6 @@ def c3_lengths():
     return np.random.default_rng(301).integers(512, 8193, size=C3_SEQS)
 
 
-def shard_sequences(lengths, world):
-    """Greedy longest-first split of sequences over ranks by total keys."""
-    order = sorted(range(len(lengths)), key=lambda i: -int(lengths[i]))
-    loads = [0] * world
-    parts = [[] for _ in range(world)]
-    for i in order:
-        r = min(range(world), key=lambda k: loads[k])
-        parts[r].append(i)
-        loads[r] += int(lengths[i]) + 1
-    return [sorted(p) for p in parts]
-
-
 def measured_peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -152,6 +140,7 @@ class C3Decode(Workload):
         self.torch, self.fa = torch, fa
         self.dtype = dtype
         self.name = "c3" if dtype == fa.F32 else "c3bf16"
+        from fusor_attn.shard import shard_sequences
         lengths = c3_lengths()[:sequences]
         mine = shard_sequences(lengths, world)[rank]
         self.tokens = len(lengths)
@@ -289,6 +278,85 @@ class C2Prefill(Workload):
         self.d_angles.copy_(self.h_angles, non_blocking=True)
         self.cache.attention(0, self.span, self.d_qkv, self.out, self.d_angles, self.fa.ROPE_HALF)
         self.h_out.copy_(self.out, non_blocking=True)
+
+    def algorithmic(self):
+        return self.flops
+
+
+class C4Sharded(Workload):
+    """C4 over `world` GPUs: each rank holds a contiguous range of the 131073 key positions in
+    its own cache; a step rotates the query everywhere, keeps the new row on its owner, attends
+    the local range into per-head (max, sum, o), all-gathers those over NCCL and merges them."""
+
+    def __init__(self, torch, fa, rank, world, dist):
+        from fusor_attn.shard import ShardedDecode, kv_shards
+        self.torch, self.fa, self.dist, self.name = torch, fa, dist, "c4"
+        heads, kv, d, position = 16, 8, 128, 131072
+        lo, hi = kv_shards(position + 1, world)[rank]
+        shape = fa.Shape(1, heads, kv, d)
+        self.cache = fa.KvCache(shape, hi - lo)
+        gen = torch.Generator("cuda").manual_seed(40 + rank)
+        filled = min(hi, position) - lo  # the new row's slot is kept by the step
+        k = torch.randn((1, kv, filled, d), device="cuda", generator=gen)
+        v = torch.randn((1, kv, filled, d), device="cuda", generator=gen)
+        self.cache.put_rows(k, v)
+        del k, v
+        gen0 = torch.Generator("cuda").manual_seed(7)
+        self.qkv = torch.randn((1, shape.qkv), device="cuda", generator=gen0)
+        self.angles = torch.from_numpy(fa.rotary_angles(fa.Rotation(base=1e6), d, [position])).cuda()
+        self.decode = ShardedDecode(self.cache, heads, d, lo, hi, position, world)
+        self.tokens = 1
+        self.launches_per_step = 3
+        self.bytes = (hi - lo) * kv * d * 2 * 4
+        self.h2d = self.d2h = 0
+
+    def step(self, mid=None):
+        if mid is not None:
+            mid.record()
+        self.decode.step(self.qkv, self.angles, self.fa.ROPE_HALF, self.dist)
+
+    def algorithmic(self):
+        return float(self.bytes)
+
+
+class C5Full(Workload):
+    """C5: DiT full-mask self-attention, 32760 tokens, 12 heads x 128, bf16 in / f32 accumulate,
+    bf16 out; (head, 128-query tile) units split evenly over the ranks."""
+
+    def __init__(self, torch, fa, rank, world):
+        from fusor_attn.shard import head_tile_units
+        self.torch, self.fa, self.name = torch, fa, "c5"
+        self.heads, self.d, self.n = 12, 128, 32760
+        hidden = self.heads * self.d
+        gen = torch.Generator("cuda").manual_seed(5)
+        self.qkv = torch.randn((self.n, 3 * hidden), device="cuda", generator=gen).to(torch.bfloat16)
+        self.out = torch.empty((self.n, hidden), device="cuda", dtype=torch.bfloat16)
+        pieces = head_tile_units(self.heads, self.n, world)[rank]
+        # consecutive whole heads go in one call (one launch over all their query tiles)
+        self.calls = []
+        for h, a, b in pieces:
+            last = self.calls[-1] if self.calls else None
+            if last and a == 0 and b == self.n and last[2] == 0 and last[3] == self.n and last[0] + last[1] == h:
+                self.calls[-1] = (last[0], last[1] + 1, 0, self.n)
+            else:
+                self.calls.append((h, 1, a, b))
+        self.tokens = self.n
+        self.bound = "tensor"
+        self.launches_per_step = len(self.calls)
+        self.flops = sum(4.0 * self.d * (b - a) * self.n * count for _, count, a, b in self.calls)
+        self.h2d = self.d2h = 0
+        self.stride = 3 * hidden
+
+    def step(self, mid=None):
+        fa, d, stride = self.fa, self.d, self.stride
+        if mid is not None:
+            mid.record()
+        for h, count, a, b in self.calls:
+            fa.attend_full(count, count, d, 1, b - a, self.n,
+                           fa.Operand(self.qkv, stride, a * stride + h * d),
+                           fa.Operand(self.qkv, stride, self.heads * d + h * d),
+                           fa.Operand(self.qkv, stride, 2 * self.heads * d + h * d),
+                           self.out[a:b, h * d:(h + count) * d])
 
     def algorithmic(self):
         return self.flops
@@ -439,7 +507,11 @@ def run_ours(args):
         if name == "c1":
             return SingleDecode(torch, fa, "c1", 14, 2, 64, 1024)
         if name == "c4":
+            if world > 1:
+                return C4Sharded(torch, fa, rank, world, dist)
             return SingleDecode(torch, fa, "c4", 16, 8, 128, 131072)
+        if name == "c5":
+            return C5Full(torch, fa, rank, world)
         if name == "c2":
             return C2Prefill(torch, fa)
         raise SystemExit(f"unknown config {name}")
@@ -468,16 +540,22 @@ def run_ours(args):
     }
     del w
     torch.cuda.empty_cache()
-    if world == 1 and args.config == "c3" and not args.no_extras and args.sequences == C3_SEQS:
+    if args.config == "c3" and not args.no_extras and args.sequences == C3_SEQS:
         extras = {}
-        for name in ("c1", "c2", "c3bf16", "c4"):
+        names = ("c1", "c2", "c3bf16", "c4", "c5") if world == 1 else ("c4", "c5")
+        for name in names:
             x = build(name)
-            xs = min(steps, 200)
+            xs = min(steps, 50 if name == "c5" else 200)
             ms_x, kern_x = time_workload(torch, dist, x, xs, warmup)
-            extras[name] = {"tokens_per_s": round(x.tokens / (ms_x * 1e-3), 2),
-                            "ms_per_step": round(ms_x, 5), "steps": xs,
-                            "config": config_of(name, 1), "roofline": roofline(x, kern_x, peaks),
-                            "l2": "flushed between steps" if x.flush_l2 else "inputs larger than L2"}
+            # replicas (c1, c2) run the whole config on every rank; the sharded ones split it
+            tokens = x.tokens * (world if name in ("c1", "c2") else 1)
+            entry = {"tokens_per_s": round(tokens / (ms_x * 1e-3), 2),
+                     "ms_per_step": round(ms_x, 5), "steps": xs,
+                     "config": config_of(name, world), "roofline": roofline(x, kern_x, peaks),
+                     "l2": "flushed between steps" if x.flush_l2 else "inputs larger than L2"}
+            if name == "c5":
+                entry["tflops"] = round(6.594e12 / (ms_x * 1e-3) / 1e12, 2)
+            extras[name] = entry
             del x
             torch.cuda.empty_cache()
         line["configs"] = extras
@@ -508,10 +586,17 @@ def config_of(name, world):
                "head_dim": 64, "mask": "causal"},
         "c4": {"workload": "C4 long-context decode", "keys": 131073, "heads": 16, "kv_heads": 8,
                "head_dim": 128},
+        "c5": {"workload": "C5 DiT full-mask self-attention", "tokens": 32760, "heads": 12,
+               "head_dim": 128, "dtype": "bf16 in, f32 accumulate, bf16 out", "mask": "full"},
     }
     c = dict(cfgs[name])
-    c["parallelism"] = f"sequences over {world} GPU(s), no collective" if name.startswith("c3") else f"replicas x{world}"
-    c["l2"] = "inputs larger than L2" if name.startswith("c3") or name == "c4" else "L2 flushed between steps"
+    c["parallelism"] = {
+        "c3": f"sequences over {world} GPU(s), no collective",
+        "c3bf16": f"sequences over {world} GPU(s), no collective",
+        "c4": f"KV range over {world} GPU(s), NCCL all-gather of (max, sum, o)" if world > 1 else "1 GPU",
+        "c5": f"(head, 128-query tile) units over {world} GPU(s), no collective",
+    }.get(name, f"replicas x{world}")
+    c["l2"] = "inputs larger than L2" if name in ("c3", "c3bf16", "c4", "c5") else "L2 flushed between steps"
     return c
 
 
@@ -578,7 +663,7 @@ def main():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", default="c3", choices=["c1", "c2", "c3", "c3bf16", "c4"])
+    ap.add_argument("--config", default="c3", choices=["c1", "c2", "c3", "c3bf16", "c4", "c5"])
     ap.add_argument("--sequences", type=int, default=C3_SEQS,
                     help="C3 sequences (a smaller batch for profiling captures)")
     ap.add_argument("--no-extras", action="store_true")
