@@ -50,6 +50,21 @@ struct FmhaShape {
 };
 
 constexpr int kFmhaThreads = 256;
+constexpr int kConvThreads = 64;  // warps 2-3: the tf32 rounding pass
+
+// Rounds `bytes` of f32 shared memory to tf32 (nearest, ties away) in place, 16 bytes per
+// thread per step. The swizzled layout is untouched: the same function of every element.
+__device__ __forceinline__ void round_tile_tf32(unsigned char* tile, int bytes, int tid) {
+  float4* v = reinterpret_cast<float4*>(tile);
+  for (int i = tid; i < bytes / 16; i += kConvThreads) {
+    float4 x = v[i];
+    x.x = __uint_as_float(tc::round_tf32(x.x));
+    x.y = __uint_as_float(tc::round_tf32(x.y));
+    x.z = __uint_as_float(tc::round_tf32(x.z));
+    x.w = __uint_as_float(tc::round_tf32(x.w));
+    v[i] = x;
+  }
+}
 
 
 template <typename T, int D>
@@ -79,8 +94,13 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
   uint64_t* s_full = v_empty + S::kStages;  // [2]
   uint64_t* p_full = s_full + 2;            // [2]
   uint64_t* o_done = p_full + 2;
-  uint64_t* mma_drained = o_done + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_drained + 1);
+  uint64_t* o_final = o_done + 1;  // the last P.V product has completed
+  uint64_t* mma_drained = o_final + 1;
+  // tf32: Q, K and V tiles rounded to tf32 in place by warps 2-3 before the MMA reads them
+  uint64_t* q_conv = mma_drained + 1;
+  uint64_t* k_conv = q_conv + 1;
+  uint64_t* v_conv = k_conv + S::kStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(v_conv + S::kStages);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int head = blockIdx.y;
@@ -116,7 +136,13 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
       mbar_init(&p_full[b], 128);
     }
     mbar_init(o_done, 1);
+    mbar_init(o_final, 1);
     mbar_init(mma_drained, 1);
+    mbar_init(q_conv, kConvThreads);
+    for (int st = 0; st < S::kStages; ++st) {
+      mbar_init(&k_conv[st], kConvThreads);
+      mbar_init(&v_conv[st], kConvThreads);
+    }
     mbar_fence_init();
   }
   if (warp == 1) tc::tmem_alloc(tmem_slot, 512);
@@ -165,12 +191,12 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
     // ---- MMA issuer ----------------------------------------------------------------------
     if (lane == 0) {
       const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV);
-      bool ok = mbar_wait(q_full, 0, a.err);
+      bool ok = mbar_wait(kTf32 ? q_conv : q_full, 0, a.err);
       auto issue_pv = [&](int j) {
         const int st = j % S::kStages;
         const int b = j & 1;
         if (!mbar_wait(&p_full[b], (j >> 1) & 1, a.err)) return false;
-        if (!mbar_wait(&v_full[st], (j / S::kStages) & 1, a.err)) return false;
+        if (!mbar_wait(kTf32 ? &v_conv[st] : &v_full[st], (j / S::kStages) & 1, a.err)) return false;
         tc::fence_after_sync();
         const uint32_t p_tmem = tmem + uint32_t(b * S::kSCols);
 #pragma unroll
@@ -193,7 +219,7 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
       for (int j = 0; ok && j < n_tiles; ++j) {
         const int st = j % S::kStages;
         const int b = j & 1;
-        if (!mbar_wait(&k_full[st], (j / S::kStages) & 1, a.err)) { ok = false; break; }
+        if (!mbar_wait(kTf32 ? &k_conv[st] : &k_full[st], (j / S::kStages) & 1, a.err)) { ok = false; break; }
         tc::fence_after_sync();
 #pragma unroll
         for (int k = 0; k < D / S::kKStep; ++k) {
@@ -207,10 +233,32 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
         tc::commit(&k_empty[st]);
         if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
       }
-      if (ok && n_tiles > 0) issue_pv(n_tiles - 1);
+      if (ok && n_tiles > 0 && issue_pv(n_tiles - 1)) tc::commit(o_final);
       // Every MMA this thread issued has completed before the CTA may free TMEM.
       tc::commit(mma_drained);
       mbar_wait(mma_drained, 0, a.err);
+    }
+  } else if (warp < 4) {
+    // ---- tf32: round Q, then every K and V tile, to nearest before the MMA reads them -------
+    if constexpr (kTf32) {
+      const int tid = threadIdx.x - 64;
+      auto convert = [&](uint64_t* full, uint64_t* conv, uint32_t parity, unsigned char* tile,
+                         int bytes) {
+        if (!mbar_wait(full, parity, a.err)) return false;
+        round_tile_tf32(tile, bytes, tid);
+        // generic-proxy writes become visible to the tensor core's async proxy
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive(conv);
+        return true;
+      };
+      if (convert(q_full, q_conv, 0, sQ, S::kQBytes)) {
+        for (int j = 0; j < n_tiles; ++j) {
+          const int st = j % S::kStages;
+          const uint32_t ph = (j / S::kStages) & 1;
+          if (!convert(&k_full[st], &k_conv[st], ph, sK + st * S::kKVBytes, S::kKVBytes)) break;
+          if (!convert(&v_full[st], &v_conv[st], ph, sV + st * S::kKVBytes, S::kKVBytes)) break;
+        }
+      }
     }
   } else if (warp >= 4) {
     // ---- softmax + epilogue ----------------------------------------------------------------
@@ -257,6 +305,9 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
       if (__any_sync(0xffffffffu, alpha != 1.0f)) {
         // O holds PV of tiles < j: wait for PV_{j-1}, then rescale the warp's rows.
         l_sum *= alpha;
+        // A parity wait names only the current or the previous phase of a barrier. Here it is
+        // unambiguous: S_j has completed (its commit tracks every earlier MMA, PV_{j-2} among
+        // them), so o_done is in the phase of PV_{j-1} or just past it.
         if (!__all_sync(0xffffffffu, mbar_wait(o_done, (j - 1) & 1, a.err))) { ok = false; break; }
         tc::fence_after_sync();
 #pragma unroll 1
@@ -303,7 +354,9 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
       mbar_arrive(&p_full[b]);
     }
     // ---- epilogue: O / l -------------------------------------------------------------------
-    if (__all_sync(0xffffffffu, ok && n_tiles > 0 && mbar_wait(o_done, (n_tiles - 1) & 1, a.err))) {
+    // The last P.V has its own single-phase barrier: after the loop o_done may still be two
+    // phases short of done, where a parity wait would match an older completed phase.
+    if (__all_sync(0xffffffffu, ok && n_tiles > 0 && mbar_wait(o_final, 0, a.err))) {
       tc::fence_after_sync();
       const float inv = l_sum > 0.0f ? 1.0f / l_sum : 0.0f;
       const int64_t orow = int64_t(image) * a.rows + r;
