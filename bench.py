@@ -125,7 +125,8 @@ class Workload:
     kernel alone; `e2e_step()` a pass through the public API from pinned host memory."""
 
     name = ""
-    tokens = 0             # tokens of the whole job per step
+    tokens = 0             # tokens of one step on this rank's share (the whole job if sharded)
+    sharded = False        # the job is split over the ranks (else every rank runs a replica)
     bound = "hbm"
     launches_per_step = 0
     flush_l2 = False
@@ -140,6 +141,7 @@ class C3Decode(Workload):
         self.torch, self.fa = torch, fa
         self.dtype = dtype
         self.name = "c3" if dtype == fa.F32 else "c3bf16"
+        self.sharded = True
         from fusor_attn.shard import shard_sequences
         lengths = c3_lengths()[:sequences]
         mine = shard_sequences(lengths, world)[rank]
@@ -291,6 +293,7 @@ class C4Sharded(Workload):
     def __init__(self, torch, fa, rank, world, dist):
         from fusor_attn.shard import ShardedDecode, kv_shards
         self.torch, self.fa, self.dist, self.name = torch, fa, dist, "c4"
+        self.sharded = True
         heads, kv, d, position = 16, 8, 128, 131072
         lo, hi = kv_shards(position + 1, world)[rank]
         shape = fa.Shape(1, heads, kv, d)
@@ -308,12 +311,22 @@ class C4Sharded(Workload):
         self.tokens = 1
         self.launches_per_step = 3
         self.bytes = (hi - lo) * kv * d * 2 * 4
-        self.h2d = self.d2h = 0
+        self.h_qkv = self.qkv.cpu().pin_memory()
+        self.h_angles = self.angles.cpu().pin_memory()
+        self.h_out = torch.zeros((heads, d), device="cpu").pin_memory()
+        self.h2d = (self.h_qkv.numel() + self.h_angles.numel()) * 4
+        self.d2h = self.h_out.numel() * 4
 
     def step(self, mid=None):
         if mid is not None:
             mid.record()
         self.decode.step(self.qkv, self.angles, self.fa.ROPE_HALF, self.dist)
+
+    def e2e_step(self):
+        self.qkv.copy_(self.h_qkv, non_blocking=True)
+        self.angles.copy_(self.h_angles, non_blocking=True)
+        out = self.decode.step(self.qkv, self.angles, self.fa.ROPE_HALF, self.dist)
+        self.h_out.copy_(out, non_blocking=True)
 
     def algorithmic(self):
         return float(self.bytes)
@@ -326,6 +339,7 @@ class C5Full(Workload):
     def __init__(self, torch, fa, rank, world):
         from fusor_attn.shard import head_tile_units
         self.torch, self.fa, self.name = torch, fa, "c5"
+        self.sharded = True
         self.heads, self.d, self.n = 12, 128, 32760
         hidden = self.heads * self.d
         gen = torch.Generator("cuda").manual_seed(5)
@@ -344,8 +358,12 @@ class C5Full(Workload):
         self.bound = "tensor"
         self.launches_per_step = len(self.calls)
         self.flops = sum(4.0 * self.d * (b - a) * self.n * count for _, count, a, b in self.calls)
-        self.h2d = self.d2h = 0
         self.stride = 3 * hidden
+        # e2e: the whole qkv from pinned host memory, this rank's output rows back
+        self.h_qkv = self.qkv.cpu().pin_memory()
+        self.h_out = torch.empty_like(self.out, device="cpu").pin_memory()
+        self.h2d = self.h_qkv.numel() * 2
+        self.d2h = sum((b - a) * count * self.d * 2 for _, count, a, b in self.calls)
 
     def step(self, mid=None):
         fa, d, stride = self.fa, self.d, self.stride
@@ -357,6 +375,13 @@ class C5Full(Workload):
                            fa.Operand(self.qkv, stride, self.heads * d + h * d),
                            fa.Operand(self.qkv, stride, 2 * self.heads * d + h * d),
                            self.out[a:b, h * d:(h + count) * d])
+
+    def e2e_step(self):
+        self.qkv.copy_(self.h_qkv, non_blocking=True)
+        self.step()
+        for h, count, a, b in self.calls:
+            self.h_out[a:b, h * self.d:(h + count) * self.d].copy_(
+                self.out[a:b, h * self.d:(h + count) * self.d], non_blocking=True)
 
     def algorithmic(self):
         return self.flops
@@ -521,17 +546,18 @@ def run_ours(args):
     ms, kern_ms = time_workload(torch, dist, w, steps, warmup, sampler)
     fa.device_status()
     e2e_ms = time_e2e(torch, dist, w, min(steps, 200), warmup)
-    value = w.tokens / (ms * 1e-3) if args.config.startswith("c3") else w.tokens * world / (ms * 1e-3)
+    job_tokens = w.tokens if w.sharded else w.tokens * world
+    value = job_tokens / (ms * 1e-3)
     line = {
         "metric": f"{args.config} attention tokens/s (decode attn HBM GB/s & prefill TFLOP/s as roofline)",
         "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": steps,
         "warmup": warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
-        "scaling": "strong" if args.config.startswith("c3") else "weak", "vs_baseline": None,
-        "dtype": "f32" if args.config != "c3bf16" else "bf16-kv/f32",
+        "scaling": "strong" if w.sharded else "weak", "vs_baseline": None,
+        "dtype": {"c3bf16": "bf16-kv/f32", "c5": "bf16/f32-acc"}.get(args.config, "f32"),
         "data": "synthetic N(0,1) (seeded), random keys/values of the config's shape",
         "config": config_of(args.config, world),
         "roofline": roofline(w, kern_ms, peaks),
-        "e2e": {"value": round((w.tokens if args.config.startswith("c3") else w.tokens * world) / (e2e_ms * 1e-3), 2),
+        "e2e": {"value": round(job_tokens / (e2e_ms * 1e-3), 2),
                 "unit": "tokens/s", "ms_per_step": round(e2e_ms, 4),
                 "h2d_bytes_per_step": w.h2d, "d2h_bytes_per_step": w.d2h,
                 "path": "pinned host rows -> fa_attention_batch / fa_attention -> pinned host output"},
@@ -548,7 +574,7 @@ def run_ours(args):
             xs = min(steps, 50 if name == "c5" else 200)
             ms_x, kern_x = time_workload(torch, dist, x, xs, warmup)
             # replicas (c1, c2) run the whole config on every rank; the sharded ones split it
-            tokens = x.tokens * (world if name in ("c1", "c2") else 1)
+            tokens = x.tokens if x.sharded else x.tokens * world
             entry = {"tokens_per_s": round(tokens / (ms_x * 1e-3), 2),
                      "ms_per_step": round(ms_x, 5), "steps": xs,
                      "config": config_of(name, world), "roofline": roofline(x, kern_x, peaks),
