@@ -49,14 +49,13 @@ def measured_peaks():
 
 
 def profile_traffic(kernel_key: str):
-    """DRAM bytes per launch of `kernel_key` from the committed ncu summary, or None."""
-    path = os.path.join(ROOT, "profiles", "ncu_summary.md")
-    try:
+    """DRAM bytes per launch of `kernel_key` from the committed ncu summaries (profiles/*.md,
+    a line `traffic_bytes_per_launch[<config>] = <bytes>`), or None."""
+    import glob
+    for path in sorted(glob.glob(os.path.join(ROOT, "profiles", "*.md"))):
         for line in open(path):
             if line.startswith(f"traffic_bytes_per_launch[{kernel_key}]"):
                 return float(line.split("=")[1].split()[0])
-    except OSError:
-        pass
     return None
 
 
@@ -247,6 +246,7 @@ class C2Prefill(Workload):
 
     def __init__(self, torch, fa):
         self.torch, self.fa, self.name = torch, fa, "c2"
+        self.kernel = "fmha_kernel"
         shape = fa.Shape(1, 14, 2, 64)
         self.shape = shape
         self.cache = fa.KvCache(shape, 512)
@@ -340,6 +340,7 @@ class C5Full(Workload):
         from fusor_attn.shard import head_tile_units
         self.torch, self.fa, self.name = torch, fa, "c5"
         self.sharded = True
+        self.kernel = "fmha_kernel"
         self.heads, self.d, self.n = 12, 128, 32760
         hidden = self.heads * self.d
         gen = torch.Generator("cuda").manual_seed(5)
@@ -455,7 +456,7 @@ def roofline(w: Workload, kern_ms: float, peaks):
         peak, unit = tflops, "TFLOP/s"
     return {"bound": w.bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
             "frac": round(achieved / peak, 4), "peak_source": kind,
-            "traffic": profile_traffic(w.name), "kernel": "attend_kernel",
+            "traffic": profile_traffic(w.name), "kernel": getattr(w, "kernel", "attend_kernel"),
             "algorithmic_per_launch": w.algorithmic()}
 
 
