@@ -6,7 +6,7 @@
 // One CTA = 128 query rows of one query head. Warp roles:
 //   warp 0      TMA producer: Q once, then K and V tiles into a ring of shared-memory stages
 //               (128-byte swizzled; tf32 V with 32-byte swizzle atoms, the MN-major tf32
-//               layout; plain per-CTA loads: no cluster multicast);
+//               layout; plain per-CTA loads only);
 //   warp 1      TMEM owner and MMA issuer (one thread): S = Q K^T into one of two TMEM
 //               buffers, then O += P V with P read from TMEM (the TS form);
 //   warps 4-7   softmax: thread i owns query row i (TMEM lane i); it loads its S row, masks,

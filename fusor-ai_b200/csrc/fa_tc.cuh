@@ -1,4 +1,4 @@
-// sm_100a tensor-core building blocks: TMA tensor loads (no multicast), the tcgen05 family
+// sm_100a tensor-core building blocks: TMA tensor loads (plain per-CTA loads), the tcgen05 family
 // (TMEM allocation, MMA from shared-memory descriptors or from TMEM, commit to an mbarrier,
 // TMEM loads and stores) and the descriptor encodings they take.
 //
