@@ -133,6 +133,38 @@ int check_cache(const fa_kvcache* cache) {
   return FA_OK;
 }
 
+// Whether the kernels on `device` may address `ptr`: memory of that device, managed memory, or
+// pinned host memory mapped into the device's address space. Another device's memory and
+// pageable host memory are rejected here: a kernel given them faults.
+int check_ptr(const void* ptr, int device, const char* what) {
+  if (ptr == nullptr) return FA_OK;
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, ptr) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(FA_ERR_ARG, "%s is not memory CUDA knows", what);
+  }
+  if (attr.type == cudaMemoryTypeDevice) {
+    if (attr.device != device)
+      return fail(FA_ERR_ARG, "%s is on device %d, the call runs on device %d", what, attr.device,
+                  device);
+    return FA_OK;
+  }
+  if (attr.type == cudaMemoryTypeManaged) return FA_OK;
+  if (attr.type == cudaMemoryTypeHost && attr.devicePointer != nullptr) return FA_OK;
+  return fail(FA_ERR_ARG, "%s is pageable host memory; device memory is needed here", what);
+}
+
+#define FA_PTR(ptr, device) \
+  do {                      \
+    if (int rc_ = check_ptr((ptr), (device), #ptr)) return rc_; \
+  } while (0)
+
+int current_device() {
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess) d = 0;
+  return d;
+}
+
 int ensure_counters(fa_kvcache* c, size_t n, cudaStream_t stream) {
   const size_t want = n * sizeof(int);
   const int epoch = c->dev->epoch.load();
@@ -563,6 +595,8 @@ int fa_kvcache_copy_rows(const fa_kvcache* cache, int32_t rows, void* keys_out,
   if (rows < 0 || rows > cache->capacity)
     return fail(FA_ERR_CAPACITY, "%d rows don't fit a cache of %d", rows, cache->capacity);
   if (keys_out == nullptr || values_out == nullptr) return fail(FA_ERR_ARG, "null output");
+  FA_PTR(keys_out, cache->device);
+  FA_PTR(values_out, cache->device);
   DeviceGuard guard(cache->device);
   const size_t width = size_t(rows) * cache->head_dim * cache->elem();
   const size_t pitch = size_t(cache->capacity) * cache->head_dim * cache->elem();
@@ -582,6 +616,8 @@ int fa_kvcache_put_rows(fa_kvcache* cache, int32_t rows, const void* keys, const
   if (rows < 0 || rows > cache->capacity)
     return fail(FA_ERR_CAPACITY, "%d rows don't fit a cache of %d", rows, cache->capacity);
   if (keys == nullptr || values == nullptr) return fail(FA_ERR_ARG, "null input");
+  FA_PTR(keys, cache->device);
+  FA_PTR(values, cache->device);
   DeviceGuard guard(cache->device);
   const size_t width = size_t(rows) * cache->head_dim * cache->elem();
   const size_t pitch = size_t(cache->capacity) * cache->head_dim * cache->elem();
@@ -626,6 +662,9 @@ int fa_attention_input(fa_kvcache* cache, int32_t layer, const fa_span* span, in
   if (int rc = check_span(cache, span, &ends)) return rc;
   if (int rc = check_rope(rope, angles)) return rc;
   if (qkv == nullptr && span->rows > 0) return fail(FA_ERR_ARG, "null qkv");
+  FA_PTR(qkv, cache->device);
+  FA_PTR(angles, cache->device);
+  FA_PTR(q_out, cache->device);
   if (qkv_stride < int64_t(cache->heads + 2 * cache->kv_heads) * cache->head_dim)
     return fail(FA_ERR_SHAPE, "qkv rows of %lld values hold fewer than the heads",
                 (long long)qkv_stride);
@@ -643,6 +682,9 @@ int fa_rotate_queries(int32_t heads, int32_t head_dim, int32_t rows, int32_t rop
   if (int rc = check_rope(rope, angles)) return rc;
   if (rows == 0) return FA_OK;
   if (qkv == nullptr || q_out == nullptr) return fail(FA_ERR_ARG, "null qkv or q_out");
+  FA_PTR(qkv, current_device());
+  FA_PTR(angles, current_device());
+  FA_PTR(q_out, current_device());
   if (qkv_stride < int64_t(heads) * head_dim || q_out_stride < int64_t(heads) * head_dim)
     return fail(FA_ERR_SHAPE, "row strides below heads x head_dim");
   fa::RopeArgs a{};
@@ -674,6 +716,8 @@ int fa_attend(fa_kvcache* cache, int32_t layer, const fa_span* span, const float
   if (int rc = check_span(cache, span, &ends)) return rc;
   const int64_t width = int64_t(cache->heads) * cache->head_dim;
   if (span->rows > 0 && (q == nullptr || out == nullptr)) return fail(FA_ERR_ARG, "null q or out");
+  FA_PTR(q, cache->device);
+  FA_PTR(out, cache->device);
   if (q_stride < width || out_stride < width) return fail(FA_ERR_SHAPE, "row strides below heads x head_dim");
   DeviceGuard guard(cache->device);
   auto s = static_cast<cudaStream_t>(stream);
@@ -707,6 +751,9 @@ int fa_attention(fa_kvcache* cache, int32_t layer, const fa_span* span, int32_t 
   if (int rc = check_rope(rope, angles)) return rc;
   const int64_t width = int64_t(cache->heads) * cache->head_dim;
   if (span->rows > 0 && (qkv == nullptr || out == nullptr)) return fail(FA_ERR_ARG, "null qkv or out");
+  FA_PTR(qkv, cache->device);
+  FA_PTR(angles, cache->device);
+  FA_PTR(out, cache->device);
   if (qkv_stride < int64_t(cache->heads + 2 * cache->kv_heads) * cache->head_dim || out_stride < width)
     return fail(FA_ERR_SHAPE, "row strides below the heads' widths");
   if (span->rows == 0) return FA_OK;
@@ -813,6 +860,9 @@ int fa_attention_input_batch(fa_kvcache* const* caches, const fa_span* spans, in
   fa_kvcache* c0 = caches[0];
   const int64_t width = int64_t(c0->heads) * c0->head_dim;
   if (qkv == nullptr) return fail(FA_ERR_ARG, "null qkv");
+  FA_PTR(qkv, c0->device);
+  FA_PTR(angles, c0->device);
+  FA_PTR(q_out, c0->device);
   if (qkv_stride < int64_t(c0->heads + 2 * c0->kv_heads) * c0->head_dim ||
       (q_out != nullptr && q_out_stride < width))
     return fail(FA_ERR_SHAPE, "row strides below the heads' widths");
@@ -861,6 +911,8 @@ int fa_attend_batch(fa_kvcache* const* caches, const fa_span* spans, int32_t bat
   fa_kvcache* c0 = caches[0];
   const int64_t width = int64_t(c0->heads) * c0->head_dim;
   if (q == nullptr || out == nullptr) return fail(FA_ERR_ARG, "null q or out");
+  FA_PTR(q, c0->device);
+  FA_PTR(out, c0->device);
   if (q_stride < width || out_stride < width) return fail(FA_ERR_SHAPE, "row strides below heads x head_dim");
   DeviceGuard guard(c0->device);
   auto s = static_cast<cudaStream_t>(stream);
@@ -941,6 +993,8 @@ int fa_attend_partial(fa_kvcache* cache, int32_t layer, const float* q, int32_t 
   if (int rc = check_cache(cache)) return rc;
   if (int rc = check_layer(cache, layer)) return rc;
   if (q == nullptr || partials == nullptr) return fail(FA_ERR_ARG, "null q or partials");
+  FA_PTR(q, cache->device);
+  FA_PTR(partials, cache->device);
   if (key_begin < 0 || key_end < key_begin) return fail(FA_ERR_ARG, "key range");
   if (key_end - key_begin > cache->capacity)
     return fail(FA_ERR_CAPACITY, "%d keys in a cache of %d", key_end - key_begin, cache->capacity);
@@ -993,6 +1047,8 @@ int fa_attend_partial(fa_kvcache* cache, int32_t layer, const float* q, int32_t 
 int fa_merge_partials(const float* partials, int32_t shards, int32_t heads, int32_t head_dim,
                       float* out, void* stream) {
   if (partials == nullptr || out == nullptr) return fail(FA_ERR_ARG, "null argument");
+  FA_PTR(partials, current_device());
+  FA_PTR(out, current_device());
   if (shards < 1 || heads < 1 || head_dim < 1 || head_dim > 1024)
     return fail(FA_ERR_ARG, "shards %d heads %d head_dim %d", shards, heads, head_dim);
   cudaError_t e = fa::launch_merge_partials(partials, shards, heads, head_dim, out,
@@ -1015,6 +1071,10 @@ int fa_attend_full(const fa_call* call, void* out, int64_t out_stride, void* str
   if (k.keys == 0) return fail(FA_ERR_ARG, "a full-mask call without keys");
   if (k.query.values == nullptr || k.key.values == nullptr || k.value.values == nullptr)
     return fail(FA_ERR_ARG, "null operand");
+  FA_PTR(k.query.values, current_device());
+  FA_PTR(k.key.values, current_device());
+  FA_PTR(k.value.values, current_device());
+  FA_PTR(out, current_device());
   const int64_t width = int64_t(k.heads) * k.head_dim;
   if (out_stride < width) return fail(FA_ERR_SHAPE, "output rows narrower than heads x head_dim");
   const size_t esize = k.dtype == FA_F32 ? 4 : 2;
@@ -1252,6 +1312,8 @@ extern "C" int fa_attend_static(fa_kvcache* cache, int32_t layer, const fa_span*
   const int64_t width = int64_t(cache->heads) * cache->head_dim;
   if (span->rows == 0) return FA_OK;
   if (q == nullptr || out == nullptr) return fail(FA_ERR_ARG, "null q or out");
+  FA_PTR(q, cache->device);
+  FA_PTR(out, cache->device);
   if (q_stride < width || out_stride < width)
     return fail(FA_ERR_SHAPE, "row strides below heads x head_dim");
   // The split of fa_attend's split-KV kernel, and the scratch it needs.

@@ -243,7 +243,10 @@ class Shape:
 class KvCache:
     """transformer::KvCache (transformer.rs:131-270) in HBM: [layer][kv_head][slot][head_dim]."""
 
-    def __init__(self, shape: Shape, capacity: int, dtype: int = F32, device: int = 0):
+    def __init__(self, shape: Shape, capacity: int, dtype: int = F32, device: int | None = None):
+        if device is None:  # the caller's current CUDA device, as torch tensors default to
+            import torch
+            device = torch.cuda.current_device() if torch.cuda.is_available() else 0
         self.shape, self.capacity, self.dtype, self.device = shape, capacity, dtype, device
         h = C.c_void_p()
         _check(lib().fa_kvcache_create(shape.layers, shape.heads, shape.kv_heads, shape.head_dim,

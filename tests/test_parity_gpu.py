@@ -162,6 +162,13 @@ def test_capacity_and_span_errors(torch):
     with pytest.raises(fa.FaError):
         cache.attention(0, fa.Span(3, 0, fa.Mask.groups(1, [2, 4])), qkv, out)  # last end != 3
     cache.attention(0, fa.Span(0, 0), qkv, out)  # an empty span is a no-op
+    # memory the kernels cannot address is refused before any launch, not faulted on
+    import ctypes as C
+    host = np.zeros((4, shape.width), np.float32)
+    sp = fa.Span(1, 3).c()
+    rc = fa.lib().fa_attend(cache.handle, 0, C.byref(sp), C.c_void_p(host.ctypes.data), shape.width,
+                            C.c_void_p(out.data_ptr()), shape.width, fa._stream())
+    assert rc == fa.ERR_ARG and b"pageable host memory" in fa.lib().fa_last_error()
     fa.device_status()
 
 
