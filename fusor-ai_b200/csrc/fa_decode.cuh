@@ -107,6 +107,25 @@ __device__ __forceinline__ void load8(const KT* row, int sub, float (&x)[8]) {
   }
 }
 
+// o = a * b + o on two f32 lanes at once (sm_100a fma.rn.f32x2; each lane rounds as fmaf).
+__device__ __forceinline__ void fma2(float& o0, float& o1, float a0, float a1, float b0, float b1) {
+  unsigned long long ra, rb, ro;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(ra) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(rb) : "f"(b0), "f"(b1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(ro) : "f"(o0), "f"(o1));
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(ro) : "l"(ra), "l"(rb));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(o0), "=f"(o1) : "l"(ro));
+}
+
+template <int N>
+struct Log2 {
+  static constexpr int value = N <= 1 ? 0 : 1 + Log2<N / 2>::value;
+};
+template <>
+struct Log2<1> {
+  static constexpr int value = 0;
+};
+
 // What every attend launch shares.
 struct AttendCommon {
   int heads, kv_heads, group, hgroups;  // hgroups: CTAs per KV head (ceil(group / G))
@@ -281,6 +300,15 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) attend_kernel(const __grid_
   const int grp = lane / LPK;
   const int sub = lane % LPK;
   const int ctid = threadIdx.x;  // 0 .. 127
+  // With 1 < G <= LPK the G head scores of a key are reduce-scattered over the key's LPK lanes
+  // (log2(G) halving exchanges, then plain folding): lane `sub` ends up owning head
+  // sub / (LPK / G), so the softmax of each head runs once per lane instead of once per head
+  // on every lane, and the probabilities go back to all lanes by G shuffles.
+  constexpr bool kScatter = G > 1 && G <= LPK;
+  constexpr int kHeadLanes = kScatter ? LPK / G : LPK;
+  constexpr int kLogG = Log2<G>::value;
+  const int own = kScatter ? sub / kHeadLanes : 0;
+  const int group_base = lane & ~(LPK - 1);
 
   float q[G][8];
   const float* qrow = c.q + int64_t(row) * c.q_stride;
@@ -290,6 +318,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) attend_kernel(const __grid_
     for (int i = 0; i < 8; ++i)
       q[h][i] = h < g ? qrow[(h0 + h) * D + elem_of<D, KT>(sub, i)] * c.q_scale : 0.0f;
 
+  // m[h], l[h]: every head (per-head path) or m[0], l[0]: the lane's own head (scatter path)
   float m[G], l[G], o[G][8];
 #pragma unroll
   for (int h = 0; h < G; ++h) {
@@ -316,32 +345,80 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) attend_kernel(const __grid_
       float kx[8], vx[8];
       load8<D, KT>(kt + size_t(rr) * D, sub, kx);
       load8<D, KT>(vt + size_t(rr) * D, sub, vx);
-      float sc[G];
+      float part[G];
 #pragma unroll
       for (int h = 0; h < G; ++h) {
-        float acc = 0.0f;
+        float a0 = 0.0f, a1 = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc = fmaf(q[h][i], kx[i], acc);
-#pragma unroll
-        for (int off = LPK / 2; off >= 1; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-        sc[h] = valid ? acc : -INFINITY;
+        for (int i = 0; i < 8; i += 2) fma2(a0, a1, q[h][i], q[h][i + 1], kx[i], kx[i + 1]);
+        part[h] = a0 + a1;
       }
+      if constexpr (kScatter) {
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        float mx = sc[h];
+        for (int k = 0; k < kLogG; ++k) {
+          const int off = LPK >> (k + 1);
+          const int half = G >> (k + 1);
+          const bool upper = (lane & off) != 0;
+#pragma unroll
+          for (int i = 0; i < half; ++i) {
+            const float send = upper ? part[i] : part[i + half];
+            const float keep = upper ? part[i + half] : part[i];
+            part[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+          }
+        }
+#pragma unroll
+        for (int off = LPK >> (kLogG + 1); off >= 1; off >>= 1)
+          part[0] += __shfl_xor_sync(0xffffffffu, part[0], off);
+        const float sc = valid ? part[0] : -INFINITY;
+        float mx = sc;
 #pragma unroll
         for (int off = LPK; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-        if (mx > m[h]) {  // warp-uniform
-          const float alpha = exp2_approx(m[h] - mx);
-          l[h] *= alpha;
+        const bool grew = mx > m[0];
+        if (__any_sync(0xffffffffu, grew)) {
+          const float alpha = grew ? exp2_approx(m[0] - mx) : 1.0f;
+          if (grew) m[0] = mx;
+          l[0] *= alpha;
 #pragma unroll
-          for (int i = 0; i < 8; ++i) o[h][i] *= alpha;
-          m[h] = mx;
+          for (int h = 0; h < G; ++h) {
+            const float ah = __shfl_sync(0xffffffffu, alpha, group_base + h * kHeadLanes);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[h][i] *= ah;
+          }
         }
-        const float p = valid ? exp2_approx(sc[h] - m[h]) : 0.0f;
-        l[h] += p;
+        const float p = valid ? exp2_approx(sc - m[0]) : 0.0f;
+        l[0] += p;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) o[h][i] = fmaf(p, vx[i], o[h][i]);
+        for (int h = 0; h < G; ++h) {
+          const float ph = __shfl_sync(0xffffffffu, p, group_base + h * kHeadLanes);
+#pragma unroll
+          for (int i = 0; i < 8; i += 2) fma2(o[h][i], o[h][i + 1], ph, ph, vx[i], vx[i + 1]);
+        }
+      } else {
+        float sc[G];
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+          float acc = part[h];
+#pragma unroll
+          for (int off = LPK / 2; off >= 1; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+          sc[h] = valid ? acc : -INFINITY;
+        }
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+          float mx = sc[h];
+#pragma unroll
+          for (int off = LPK; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+          if (mx > m[h]) {  // warp-uniform
+            const float alpha = exp2_approx(m[h] - mx);
+            l[h] *= alpha;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[h][i] *= alpha;
+            m[h] = mx;
+          }
+          const float p = valid ? exp2_approx(sc[h] - m[h]) : 0.0f;
+          l[h] += p;
+#pragma unroll
+          for (int i = 0; i < 8; i += 2) fma2(o[h][i], o[h][i + 1], p, p, vx[i], vx[i + 1]);
+        }
       }
     }
     __syncwarp();
@@ -349,14 +426,15 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) attend_kernel(const __grid_
   }
 
   // ---- merge the warp's key groups (they share the warp-uniform max) ---------------------------
+  constexpr int kOwnHeads = kScatter ? 1 : G;
 #pragma unroll
-  for (int h = 0; h < G; ++h) {
+  for (int off = LPK; off < 32; off <<= 1) {
 #pragma unroll
-    for (int off = LPK; off < 32; off <<= 1) {
-      l[h] += __shfl_xor_sync(0xffffffffu, l[h], off);
+    for (int h = 0; h < kOwnHeads; ++h) l[h] += __shfl_xor_sync(0xffffffffu, l[h], off);
+#pragma unroll
+    for (int h = 0; h < G; ++h)
 #pragma unroll
       for (int i = 0; i < 8; ++i) o[h][i] += __shfl_xor_sync(0xffffffffu, o[h][i], off);
-    }
   }
   // All consumers are past their last tile: every copy has landed, the stages are free.
   if (!ok) fail_flag = 1;
@@ -366,7 +444,12 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) attend_kernel(const __grid_
   float* red_m = reinterpret_cast<float*>(smem);           // [warps][G]
   float* red_l = red_m + kConsumerWarps * G;               // [warps][G]
   float* red_o = red_l + kConsumerWarps * G;               // [warps][G][D]
-  if (lane == 0) {
+  if constexpr (kScatter) {
+    if (grp == 0 && sub % kHeadLanes == 0) {  // the lane of group 0 that owns head `own`
+      red_m[warp * G + own] = m[0];
+      red_l[warp * G + own] = l[0];
+    }
+  } else if (lane == 0) {
 #pragma unroll
     for (int h = 0; h < G; ++h) {
       red_m[warp * G + h] = m[h];
