@@ -219,8 +219,8 @@ int pow2_heads(int group) {
   return g == 3 ? 4 : g;
 }
 
-// Work units wanted per launch: four waves of two CTAs per SM.
-int target_units(const Device* dev) { return std::max(dev->sms, 1) * 2 * 4; }
+// Work units wanted per launch: four waves of the split-KV kernel's resident CTAs.
+int target_units(const Device* dev) { return std::max(dev->sms, 1) * FA_DECODE_MIN_CTAS * 4; }
 
 struct Plan {
   int g = 1, hgroups = 1, kv_groups = 1, chunks = 1;

@@ -21,10 +21,23 @@
 
 namespace fa {
 
-constexpr int kConsumerWarps = 4;
+// Shape of the split-KV CTA (compile-time tunables; the defaults are the measured best).
+#ifndef FA_DECODE_WARPS
+#define FA_DECODE_WARPS 4
+#endif
+#ifndef FA_DECODE_STAGES
+#define FA_DECODE_STAGES 2
+#endif
+#ifndef FA_DECODE_TILE_BYTES
+#define FA_DECODE_TILE_BYTES 16384
+#endif
+#ifndef FA_DECODE_MIN_CTAS
+#define FA_DECODE_MIN_CTAS 3
+#endif
+constexpr int kConsumerWarps = FA_DECODE_WARPS;
 constexpr int kDecodeThreads = (kConsumerWarps + 1) * 32;
-constexpr int kStages = 3;
-constexpr int kTileBytes = 16384;  // bytes of one K (or V) tile of a stage
+constexpr int kStages = FA_DECODE_STAGES;
+constexpr int kTileBytes = FA_DECODE_TILE_BYTES;  // bytes of one K (or V) tile of a stage
 
 // Mask::keys (transformer.rs:116-128): the key positions of a row as two runs.
 struct Runs {
@@ -77,6 +90,9 @@ struct DecodeShape {
   static_assert(kLanesPerKey >= 2 && kLanesPerKey <= 32, "head_dim 16..256");
   static_assert(kRounds * kRoundKeys == kTileKeys, "tile holds whole rounds");
   static constexpr size_t kSmemBytes = size_t(kStages) * 2 * kTileBytes + 2 * kStages * 8;
+  // the warps' (max, sum, o) merge reuses the stages' memory
+  static_assert(size_t(kConsumerWarps) * 8 * (D + 2) * 4 <= size_t(kStages) * 2 * kTileBytes,
+                "the merge scratch fits the stages");
 };
 
 // The element index of lane-slot i (0..7) of sub-lane `sub` in a row: f32 rows are read as two
@@ -172,7 +188,7 @@ struct BatchArgs {
 };
 
 template <int D, typename KT, int G, bool BATCH, typename Args>
-__global__ void __launch_bounds__(kDecodeThreads, 2) attend_kernel(const __grid_constant__ Args args) {
+__global__ void __launch_bounds__(kDecodeThreads, FA_DECODE_MIN_CTAS) attend_kernel(const __grid_constant__ Args args) {
   using S = DecodeShape<D, KT>;
   constexpr int T = S::kTileKeys;
   constexpr int LPK = S::kLanesPerKey;

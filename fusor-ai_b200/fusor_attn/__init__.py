@@ -16,7 +16,8 @@ from typing import Sequence
 import numpy as np
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libfa_attn.so")
+# FA_ATTN_LIB points at another build of the library (a tuning variant); default in-tree.
+LIB_PATH = os.environ.get("FA_ATTN_LIB") or os.path.join(_HERE, "libfa_attn.so")
 
 OK, ERR_ARG, ERR_SHAPE, ERR_CAPACITY, ERR_CUDA, ERR_TIMEOUT, ERR_UNSUPPORTED = range(7)
 F32, BF16 = 0, 1
