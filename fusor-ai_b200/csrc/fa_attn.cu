@@ -18,6 +18,7 @@
 #include "fa_attn.h"
 #include "fa_fmha_launch.h"
 #include "fa_launch.cuh"
+#include "fa_relpos.h"
 
 namespace {
 
@@ -1187,6 +1188,49 @@ int fa_attend_full(const fa_call* call, void* out, int64_t out_stride, void* str
                      rows * p.kv_groups * p.chunks};
   e = launch_attend_d(k.head_dim, l, s);
   if (e != cudaSuccess) return cuda_fail(e, "attend launch");
+  return FA_OK;
+}
+
+int fa_attend_relpos(const fa_relpos_call* call, float* out, int64_t out_stride, void* stream) {
+  if (call == nullptr || out == nullptr) return fail(FA_ERR_ARG, "null argument");
+  const fa_relpos_call& c = *call;
+  if (c.heads < 1 || c.frames < 0) return fail(FA_ERR_ARG, "heads %d frames %d", c.heads, c.frames);
+  if (c.head_dim != 32 && c.head_dim != 64 && c.head_dim != 128 && c.head_dim != 256)
+    return fail(FA_ERR_UNSUPPORTED, "relative-position attention with head_dim %d", c.head_dim);
+  if (c.frames == 0) return FA_OK;
+  if (c.query.values == nullptr || c.key.values == nullptr || c.value.values == nullptr ||
+      c.positions == nullptr || c.bias_u == nullptr || c.bias_v == nullptr)
+    return fail(FA_ERR_ARG, "null operand");
+  const int64_t width = int64_t(c.heads) * c.head_dim;
+  if (c.key.stride != c.value.stride) return fail(FA_ERR_ARG, "keys and values need one stride");
+  if (c.query.stride < width || c.key.stride < width || c.positions_stride < width ||
+      out_stride < width)
+    return fail(FA_ERR_SHAPE, "rows narrower than heads x head_dim");
+  const int device = current_device();
+  FA_PTR(c.query.values, device);
+  FA_PTR(c.key.values, device);
+  FA_PTR(c.value.values, device);
+  FA_PTR(c.positions, device);
+  FA_PTR(c.bias_u, device);
+  FA_PTR(c.bias_v, device);
+  FA_PTR(out, device);
+  fa::RelposArgs a{};
+  a.heads = c.heads;
+  a.frames = c.frames;
+  a.q = static_cast<const float*>(c.query.values) + c.query.offset;
+  a.q_stride = c.query.stride;
+  a.k = static_cast<const float*>(c.key.values) + c.key.offset;
+  a.v = static_cast<const float*>(c.value.values) + c.value.offset;
+  a.kv_stride = c.key.stride;
+  a.positions = c.positions;
+  a.positions_stride = c.positions_stride;
+  a.bias_u = c.bias_u;
+  a.bias_v = c.bias_v;
+  a.scale_log2 = query_scale(c.head_dim);
+  a.out = out;
+  a.out_stride = out_stride;
+  const cudaError_t e = fa::launch_relpos(a, c.head_dim, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "relative-position attention launch");
   return FA_OK;
 }
 

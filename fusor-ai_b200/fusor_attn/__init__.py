@@ -79,6 +79,13 @@ class _Call(C.Structure):
                 ("dtype", C.c_int32), ("out_dtype", C.c_int32)]
 
 
+class _RelposCall(C.Structure):
+    _fields_ = [("heads", C.c_int32), ("head_dim", C.c_int32), ("frames", C.c_int32),
+                ("query", _Operand), ("key", _Operand), ("value", _Operand),
+                ("positions", C.c_void_p), ("positions_stride", C.c_int64),
+                ("bias_u", C.c_void_p), ("bias_v", C.c_void_p)]
+
+
 _lib = None
 
 # name -> (restype, argtypes) for every entry point of include/fa_attn.h
@@ -105,6 +112,7 @@ SIGNATURES = {
     "fa_attend_static": (C.c_int, [_P, _I32, _P, _P, _I64, _P, _I64, _P]),
     "fa_merge_partials": (C.c_int, [_P, _I32, _I32, _I32, _P, _P]),
     "fa_attend_full": (C.c_int, [_P, _P, _I64, _P]),
+    "fa_attend_relpos": (C.c_int, [_P, _P, _I64, _P]),
     "fa_device_status": (C.c_int, [_P]),
     "fa_rng_fill_normal": (C.c_int, [C.c_uint64, _P, _I64]),
 }
@@ -428,6 +436,19 @@ def attend_full(heads: int, kv_heads: int, head_dim: int, images: int, queries: 
                  _Operand(value.values.data_ptr(), value.stride, value.offset),
                  dt[query.values.dtype], dt[out.dtype])
     _check(lib().fa_attend_full(C.byref(call), _dptr(out), out.stride(0), _stream(stream)))
+
+
+def attend_relpos(heads: int, head_dim: int, frames: int, query: Operand, key: Operand,
+                  value: Operand, positions, bias_u, bias_v, out, stream=None):
+    """conformer::attention::attend (conformer/attention.rs:25-159): full-mask attention with
+    Transformer-XL relative-position scores over `positions` ((2 frames - 1) rows)."""
+    call = _RelposCall(heads, head_dim, frames,
+                       _Operand(query.values.data_ptr(), query.stride, query.offset),
+                       _Operand(key.values.data_ptr(), key.stride, key.offset),
+                       _Operand(value.values.data_ptr(), value.stride, value.offset),
+                       positions.data_ptr(), positions.stride(0), bias_u.data_ptr(),
+                       bias_v.data_ptr())
+    _check(lib().fa_attend_relpos(C.byref(call), _dptr(out), out.stride(0), _stream(stream)))
 
 
 def device_status(stream=None):

@@ -263,6 +263,28 @@ int fa_attend_full(const fa_call* call, void* out, int64_t out_stride, void* str
 int fa_attend_static(fa_kvcache* cache, int32_t layer, const fa_span* span, const float* q,
                      int64_t q_stride, float* out, int64_t out_stride, void* stream);
 
+/* The conformer's relative-position self-attention (crates/blocks/src/conformer/attention.rs:
+ * 25-159, Transformer-XL scores): for head h, query frame i and key frame j,
+ * score = ((q_i + u) . k_j + (q_i + v) . r_{frames-1-i+j}) / sqrt(head_dim), softmax over every
+ * key, times v_j. q, k, v: f32 operands (head h of row i at values + i*stride + offset +
+ * h*head_dim); positions: the projected relative-position table, 2*frames - 1 rows
+ * positions_stride apart (row frames - 1 - i + j pairs query i with key j; head h at
+ * h*head_dim); bias_u, bias_v: heads*head_dim each; head_dim 32, 64, 128 or 256. */
+typedef struct {
+  int32_t heads;
+  int32_t head_dim;
+  int32_t frames;
+  fa_operand query;
+  fa_operand key;
+  fa_operand value;
+  const float* positions;
+  int64_t positions_stride;
+  const float* bias_u;
+  const float* bias_v;
+} fa_relpos_call;
+
+int fa_attend_relpos(const fa_relpos_call* call, float* out, int64_t out_stride, void* stream);
+
 /* Waits for `stream` and reports whether any kernel of this library gave up a device-side wait
  * since the last call (FA_ERR_TIMEOUT, clearing the flag) or FA_OK. */
 int fa_device_status(void* stream);

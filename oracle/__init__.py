@@ -70,6 +70,7 @@ def lib():
             "oracle_decode_batch_team": (None, [p, i64, i64, p, p, i64, p, i64, i]),
             "oracle_attend_call": (None, [i64] * 6 + [p, i64, i64] * 3 + [p, i64, i64, i64, i64, i]),
             "oracle_team_release": (None, []),
+            "oracle_relpos_attend": (None, [i64, i64, i64, p, p, p, i64, p, i64, p, p, p]),
             "oracle_reference_attend_f64": (None, [p, i64, i64, i64, i64, p, p]),
         }
         for name, (res, args) in sig.items():
@@ -237,6 +238,19 @@ def reference_attend_f64(qkv_heads: np.ndarray, rows, heads, kv_heads, head_dim,
     m = mask.c()
     lib().oracle_reference_attend_f64(_ptr(h), rows, heads, kv_heads, head_dim, C.byref(m),
                                       _ptr(out))
+    return out
+
+
+def relpos_attend(heads, head_dim, frames, qkv, positions, bias_u, bias_v):
+    """conformer::attention::attend (conformer/attention.rs:25-159) on rows of qkv (frames x
+    3*heads*head_dim: queries, keys, values) and positions ((2 frames - 1) x heads*head_dim)."""
+    qkv = _f32(qkv)
+    hidden = heads * head_dim
+    out = np.zeros((frames, hidden), np.float32)
+    base = qkv.ctypes.data
+    lib().oracle_relpos_attend(heads, head_dim, frames, C.c_void_p(base), C.c_void_p(base + 4 * hidden),
+                               C.c_void_p(base + 8 * hidden), qkv.shape[1], _ptr(_f32(positions)),
+                               hidden, _ptr(_f32(bias_u)), _ptr(_f32(bias_v)), _ptr(out))
     return out
 
 

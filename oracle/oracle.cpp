@@ -484,6 +484,41 @@ void oracle_attend_call(int64_t heads, int64_t kv_heads, int64_t head_dim, int64
   team(std::max(threads, 1)).run(task);
 }
 
+void oracle_relpos_attend(int64_t heads, int64_t head_dim, int64_t frames, const float* q,
+                          const float* k, const float* v, int64_t qkv_stride,
+                          const float* positions, int64_t positions_stride, const float* bias_u,
+                          const float* bias_v, float* out) {
+  const int64_t d = head_dim;
+  std::vector<float> content(d), position(d), scores(frames);
+  const float scale = 1.0f / std::sqrt((float)d);
+  for (int64_t h = 0; h < heads; ++h) {
+    for (int64_t i = 0; i < frames; ++i) {
+      // biased_queries (attention.rs:77-99): f32 sums
+      const float* query = q + i * qkv_stride + h * d;
+      for (int64_t e = 0; e < d; ++e) {
+        content[e] = query[e] + bias_u[h * d + e];
+        position[e] = query[e] + bias_v[h * d + e];
+      }
+      // scores (attention.rs:101-135): the content dot, plus the position dot, then the scale
+      for (int64_t j = 0; j < frames; ++j) {
+        const float c = oracle_dot(k + j * qkv_stride + h * d, content.data(), (int)d);
+        const float* r = positions + (frames - 1 - i + j) * positions_stride + h * d;
+        float s = c;
+        s += oracle_dot(r, position.data(), (int)d);
+        scores[j] = s * scale;
+      }
+      // mix (attention.rs:137-159): softmax, then the values key by key
+      oracle_softmax(scores.data(), (int)frames);
+      float* o = out + i * heads * d + h * d;
+      for (int64_t e = 0; e < d; ++e) o[e] = 0.0f;
+      for (int64_t j = 0; j < frames; ++j) {
+        const float* value = v + j * qkv_stride + h * d;
+        for (int64_t e = 0; e < d; ++e) o[e] += scores[j] * value[e];
+      }
+    }
+  }
+}
+
 void oracle_team_release(void) {
   delete current_team;
   current_team = nullptr;

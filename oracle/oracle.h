@@ -130,6 +130,17 @@ void oracle_attend_call(int64_t heads, int64_t kv_heads, int64_t head_dim, int64
                         int64_t head_begin, int64_t head_end, int64_t query_begin,
                         int64_t query_end, int threads);
 
+/* Transformer-XL relative-position full-mask attention of one conformer layer
+ * (crates/blocks/src/conformer/attention.rs:25-159): for head h, query frame i and key frame j,
+ * score = ((q_i + u) . k_j + (q_i + v) . r_{frames-1-i+j}) / sqrt(head_dim), softmax over j, times
+ * v_j. Rows of q/k/v at q + i*q_stride + h*head_dim (and likewise), relative-position rows at
+ * positions + rel*positions_stride + h*head_dim, bias_u/bias_v of heads*head_dim, output rows of
+ * heads*head_dim. */
+void oracle_relpos_attend(int64_t heads, int64_t head_dim, int64_t frames, const float* q,
+                          const float* k, const float* v, int64_t qkv_stride,
+                          const float* positions, int64_t positions_stride, const float* bias_u,
+                          const float* bias_v, float* out);
+
 /* Joins the team's worker threads (they are started on the first threaded call). */
 void oracle_team_release(void);
 

@@ -392,3 +392,25 @@ def test_tensor_core_and_split_kv_paths_agree(torch):
     err = float((tc - rows).abs().max())
     print(f"tensor cores vs split-KV: max abs {err:.2e}")
     assert err <= TOL_F32
+
+
+@pytest.mark.parametrize("head_dim,frames", [(32, 7), (64, 150), (128, 257), (256, 33)])
+def test_conformer_relative_position_attention(torch, head_dim, frames):
+    """conformer::attention::attend: Transformer-XL scores over the projected relative-position
+    table, on the conformer's packed qkv rows (queries, keys, values of `hidden` each)."""
+    heads = 4
+    hidden = heads * head_dim
+    qkv = normal(801, (frames, 3 * hidden))
+    positions = normal(802, (2 * frames - 1, hidden))
+    bias_u = 0.1 * normal(803, (hidden,))
+    bias_v = 0.1 * normal(804, (hidden,))
+    t = dev(torch, qkv)
+    out = torch.zeros((frames, hidden), device="cuda")
+    fa.attend_relpos(heads, head_dim, frames, fa.Operand(t, 3 * hidden, 0),
+                     fa.Operand(t, 3 * hidden, hidden), fa.Operand(t, 3 * hidden, 2 * hidden),
+                     dev(torch, positions), dev(torch, bias_u), dev(torch, bias_v), out)
+    fa.device_status()
+    want = oracle.relpos_attend(heads, head_dim, frames, qkv, positions, bias_u, bias_v)
+    got = out.cpu().numpy()
+    print(compare(f"relpos d{head_dim} frames {frames}", got, want))
+    assert max_abs(got, want) <= TOL_F32
