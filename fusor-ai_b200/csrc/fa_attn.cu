@@ -390,12 +390,14 @@ int attend_rows_tc(fa_kvcache* c, int layer, const fa_span* span, const std::vec
 int rope_rows(fa_kvcache* c, int layer, const fa_span* span, int rope, const float* angles,
               const fa_head_norm* norm, const float* qkv, int64_t qkv_stride, float* q_out,
               int64_t q_out_stride, float q_scale, bool keep, cudaStream_t stream,
-              bool q_out_bf16 = false) {
+              bool q_out_bf16 = false, int gate_heads = 0, int rotary_dim = 0) {
   if (span->rows == 0) return FA_OK;
   fa::RopeArgs a{};
   a.heads = c->heads;
   a.kv_heads = c->kv_heads;
   a.head_dim = c->head_dim;
+  a.gate_heads = gate_heads;
+  a.rotary_dim = rotary_dim;
   a.rope = rope;
   a.n_rows = span->rows;
   a.qkv = qkv;
@@ -1231,6 +1233,117 @@ int fa_attend_relpos(const fa_relpos_call* call, float* out, int64_t out_stride,
   a.out_stride = out_stride;
   const cudaError_t e = fa::launch_relpos(a, c.head_dim, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "relative-position attention launch");
+  return FA_OK;
+}
+
+int fa_normalize_and_rotate(const fa_prologue* prologue, const float* qkv, int64_t qkv_stride,
+                            void* out, int64_t out_stride, int32_t out_dtype, void* stream) {
+  if (prologue == nullptr) return fail(FA_ERR_ARG, "null prologue");
+  const fa_prologue& p = *prologue;
+  if (p.tokens < 0 || p.heads < 1 || p.head_dim < 2 || p.head_dim > 256 || p.head_dim % 2 != 0)
+    return fail(FA_ERR_ARG, "tokens %d heads %d head_dim %d", p.tokens, p.heads, p.head_dim);
+  if (p.norm < FA_NORM_NONE || p.norm > FA_NORM_HEAD) return fail(FA_ERR_ARG, "norm %d", p.norm);
+  if (int rc = check_rope(p.rope, p.angles)) return rc;
+  if (out_dtype != FA_F32 && out_dtype != FA_BF16) return fail(FA_ERR_ARG, "out dtype %d", out_dtype);
+  if (p.tokens == 0) return FA_OK;
+  if (qkv == nullptr || out == nullptr) return fail(FA_ERR_ARG, "null qkv or out");
+  if (p.norm != FA_NORM_NONE && (p.q_norm == nullptr || p.k_norm == nullptr))
+    return fail(FA_ERR_ARG, "norm without weights");
+  const int64_t width = int64_t(p.heads) * p.head_dim;
+  if (qkv_stride < 3 * width || out_stride < 3 * width)
+    return fail(FA_ERR_SHAPE, "rows narrower than queries, keys and values");
+  const bool in_place = out == static_cast<const void*>(qkv);
+  if (in_place && (out_dtype != FA_F32 || out_stride != qkv_stride))
+    return fail(FA_ERR_ARG, "in place needs FA_F32 and one stride");
+  const int device = current_device();
+  FA_PTR(qkv, device);
+  FA_PTR(out, device);
+  FA_PTR(p.q_norm, device);
+  FA_PTR(p.k_norm, device);
+  FA_PTR(p.angles, device);
+  fa::PrologueArgs a{};
+  a.tokens = p.tokens;
+  a.heads = p.heads;
+  a.head_dim = p.head_dim;
+  a.norm = p.norm;
+  a.rope = p.rope;
+  a.rotated_rows = p.rope == FA_ROPE_NONE ? 0 : std::max(0, std::min(p.rotated_rows, p.tokens));
+  a.parts = in_place ? 2 : 3;
+  a.vec_in = reinterpret_cast<uintptr_t>(qkv) % 16 == 0 && qkv_stride % 4 == 0 && width % 4 == 0;
+  const int out_elem = out_dtype == FA_F32 ? 4 : 2;
+  a.vec_out = reinterpret_cast<uintptr_t>(out) % 16 == 0 && (out_stride * out_elem) % 16 == 0 &&
+              width % 4 == 0;
+  a.out_bf16 = out_dtype == FA_BF16 ? 1 : 0;
+  a.qkv = qkv;
+  a.qkv_stride = qkv_stride;
+  a.q_norm = p.q_norm;
+  a.k_norm = p.k_norm;
+  a.eps = p.eps;
+  a.angles = p.angles;
+  a.out = out;
+  a.out_stride = out_stride;
+  const cudaError_t e = fa::launch_prologue(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "prologue launch");
+  return FA_OK;
+}
+
+int fa_gated_attention(fa_kvcache* cache, int32_t layer, const fa_span* span, int32_t gate,
+                       int32_t rotary_dim, const float* angles, const fa_head_norm* norm,
+                       const float* qkv, int64_t qkv_stride, float* out, int64_t out_stride,
+                       void* stream) {
+  if (int rc = check_cache(cache)) return rc;
+  if (int rc = check_layer(cache, layer)) return rc;
+  std::vector<int> ends;
+  if (int rc = check_span(cache, span, &ends)) return rc;
+  if (gate < FA_GATE_NONE || gate > FA_GATE_HEADWISE) return fail(FA_ERR_ARG, "gate %d", gate);
+  const int d = cache->head_dim;
+  if (rotary_dim < 2 || rotary_dim > d || rotary_dim % 2 != 0)
+    return fail(FA_ERR_ARG, "rotary_dim %d of head_dim %d", rotary_dim, d);
+  if (int rc = check_rope(FA_ROPE_HALF, angles)) return rc;
+  const int gate_heads = gate == FA_GATE_ELEMENTWISE ? cache->heads : 0;
+  const int64_t head_columns = int64_t(cache->heads + gate_heads + 2 * cache->kv_heads) * d;
+  const int64_t columns = head_columns + (gate == FA_GATE_HEADWISE ? cache->heads : 0);
+  const int64_t width = int64_t(cache->heads) * d;
+  if (span->rows > 0 && (qkv == nullptr || out == nullptr)) return fail(FA_ERR_ARG, "null qkv or out");
+  FA_PTR(qkv, cache->device);
+  FA_PTR(angles, cache->device);
+  FA_PTR(out, cache->device);
+  if (qkv_stride < columns || out_stride < width)
+    return fail(FA_ERR_SHAPE, "row strides below the heads' widths");
+  if (span->rows == 0) return FA_OK;
+  DeviceGuard guard(cache->device);
+  auto s = static_cast<cudaStream_t>(stream);
+  Work w;
+  int rc = FA_OK;
+  if (span_on_tensor_cores(cache, span)) {
+    if ((rc = ensure_work(cache, size_t(span->rows) * width, 0, 0, s, &w))) return rc;
+    if ((rc = rope_rows(cache, layer, span, FA_ROPE_HALF, angles, norm, qkv, qkv_stride, w.q,
+                        width, 1.0f, true, s, cache->dtype == FA_BF16, gate_heads, rotary_dim)))
+      return rc;
+    rc = attend_rows_tc(cache, layer, span, ends, w.q, width, out, out_stride, s);
+  } else {
+    const Plan pl = plan_for_span(cache, span, ends);
+    if ((rc = ensure_work(cache, size_t(span->rows) * width,
+                          size_t(span->rows) * pl.chunks * cache->heads, 0, s, &w)))
+      return rc;
+    if ((rc = rope_rows(cache, layer, span, FA_ROPE_HALF, angles, norm, qkv, qkv_stride, w.q,
+                        width, 1.0f, true, s, false, gate_heads, rotary_dim)))
+      return rc;
+    rc = attend_rows(cache, layer, span, ends, pl, w, w.q, width, out, out_stride, nullptr, s);
+  }
+  if (rc != FA_OK || gate == FA_GATE_NONE) return rc;
+  fa::GateArgs g{};
+  g.rows = span->rows;
+  g.heads = cache->heads;
+  g.head_dim = d;
+  g.per_head = gate == FA_GATE_HEADWISE ? 1 : 0;
+  g.qkv = qkv;
+  g.qkv_stride = qkv_stride;
+  g.gate_offset = gate == FA_GATE_HEADWISE ? head_columns : width;
+  g.out = out;
+  g.out_stride = out_stride;
+  const cudaError_t e = fa::launch_gate(g, s);
+  if (e != cudaSuccess) return cuda_fail(e, "gate launch");
   return FA_OK;
 }
 

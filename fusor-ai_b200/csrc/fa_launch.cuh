@@ -41,4 +41,40 @@ cudaError_t launch_prepare_queries(int dtype, const void* values, int64_t stride
                                    int rows, int heads, int head_dim, float scale, float* q_out,
                                    cudaStream_t stream, bool out_bf16 = false);
 
+// The query/key prologue of the DiT blocks (fa_prologue.cu).
+constexpr int kNormNone = 0;
+constexpr int kNormRow = 1;   // RMSNorm over the whole query (key) row
+constexpr int kNormHead = 2;  // RMSNorm of each head
+struct PrologueArgs {
+  int tokens, heads, head_dim;
+  int norm;          // kNorm*
+  int rope;          // 0 none, 1 by halves, 2 interleaved
+  int rotated_rows;  // tokens [0, rotated_rows) are rotated
+  int parts;         // 2: queries and keys (in place); 3: and the values copied
+  int vec_in;        // qkv rows start 16-byte aligned, widths multiples of 4
+  int vec_out;       // out rows likewise (8-byte pairs for bf16)
+  int out_bf16;
+  const float* qkv;  // row t at qkv + t*qkv_stride: queries, keys, values of heads*head_dim
+  int64_t qkv_stride;
+  const float* q_norm;  // heads*head_dim (kNormRow) or head_dim (kNormHead) weights
+  const float* k_norm;
+  float eps;
+  const float* angles;  // row t at angles + t*head_dim: cosines then sines
+  void* out;            // row t at out + t*out_stride elements, laid out as qkv
+  int64_t out_stride;
+};
+cudaError_t launch_prologue(const PrologueArgs& args, cudaStream_t stream);
+
+// The sigmoid gate of the hybrid blocks' attention output (fa_prologue.cu).
+struct GateArgs {
+  int rows, heads, head_dim;
+  int per_head;         // one gate per query head (else one per element)
+  const float* qkv;     // gates at qkv + r*qkv_stride + gate_offset
+  int64_t qkv_stride;
+  int64_t gate_offset;
+  float* out;
+  int64_t out_stride;
+};
+cudaError_t launch_gate(const GateArgs& args, cudaStream_t stream);
+
 }  // namespace fa

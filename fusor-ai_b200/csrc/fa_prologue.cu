@@ -1,0 +1,216 @@
+// The steps either side of the full-mask and gated attentions that are not attention:
+//
+// * The query/key prologue of the video and image DiT blocks: Wan's normalize_and_rotate
+//   (crates/blocks/src/wan_dit/block.rs:109-140) and Pyramid's (pyramid_jit/block.rs:100-131)
+//   RMS-normalize every token's query row and key row over their whole width (row_work.rs:57-75,
+//   ops.rs:7-16), MMDiT's head_norms (mmdit/pass.rs:64-68,162-192) each head on its own; then
+//   each query and key head is turned by the token's rotary angles (rope_interleaved,
+//   ops.rs:87-95). One warp per (token, query | key | value row); the whole-row sum of squares
+//   is a first pass over the row, the second pass reads it again (from L1/L2) head by head and
+//   writes the normalized, rotated heads in f32 or bf16, the operand rows the tensor-core
+//   attention reads. A memory-bound kernel: per token it reads 3 rows and writes 3 rows.
+//
+// * The sigmoid gate of the hybrid blocks' attention output (hybrid/attention.rs:262-295):
+//   attended *= 1 / (1 + exp(-gate)), a gate per element (a gate head per query head) or one per
+//   query head.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "fa_launch.cuh"
+
+namespace fa {
+
+namespace {
+
+constexpr int kPrologueWarps = 8;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+// Row part `part` (0 queries, 1 keys) of one token: optional RMSNorm, then RoPE, into out.
+template <typename O>
+__device__ __forceinline__ void normalize_rotate_row(const PrologueArgs& a, int token, int part,
+                                                     int lane, O* out_row) {
+  const int d = a.head_dim, half = d / 2;
+  const int64_t width = int64_t(a.heads) * d;
+  const float* row = a.qkv + int64_t(token) * a.qkv_stride + part * width;
+  const float* weight = part == 0 ? a.q_norm : a.k_norm;
+  float inverse = 1.0f;
+  if (a.norm == kNormRow) {
+    // ops::rms_norm's mean of squares over the whole row (a tree sum rather than the CPU's
+    // sequential one: the same value within a few ulps)
+    float ss = 0.0f;
+    if (a.vec_in) {
+      const float4* r4 = reinterpret_cast<const float4*>(row);
+      for (int64_t c = lane; c < width / 4; c += 32) {
+        const float4 v = r4[c];
+        ss = fmaf(v.x, v.x, ss);
+        ss = fmaf(v.y, v.y, ss);
+        ss = fmaf(v.z, v.z, ss);
+        ss = fmaf(v.w, v.w, ss);
+      }
+    } else {
+      for (int64_t c = lane; c < width; c += 32) ss = fmaf(row[c], row[c], ss);
+    }
+    ss = warp_sum(ss);
+    inverse = 1.0f / sqrtf(ss / float(width) + a.eps);
+  }
+  const bool rotate = a.rope != 0 && token < a.rotated_rows;
+  const float* cs = a.angles + int64_t(token) * d;
+  const bool pairs_adjacent = a.rope != 1;  // interleaved pairs (2p, 2p + 1); or no rotation
+  for (int h = 0; h < a.heads; ++h) {
+    const float* hp = row + int64_t(h) * d;
+    float x[4], y[4];
+    int lo[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int p = lane + 32 * j;
+      lo[j] = -1;
+      x[j] = y[j] = 0.0f;
+      if (p >= half) continue;
+      if (pairs_adjacent) {
+        lo[j] = 2 * p;
+        if (a.vec_in) {
+          const float2 t = *reinterpret_cast<const float2*>(hp + 2 * p);
+          x[j] = t.x;
+          y[j] = t.y;
+        } else {
+          x[j] = hp[2 * p];
+          y[j] = hp[2 * p + 1];
+        }
+      } else {
+        lo[j] = p;
+        x[j] = hp[p];
+        y[j] = hp[p + half];
+      }
+    }
+    if (a.norm != kNormNone) {
+      float head_inverse = inverse;
+      if (a.norm == kNormHead) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) ss = fmaf(y[j], y[j], fmaf(x[j], x[j], ss));
+        ss = warp_sum(ss);
+        head_inverse = 1.0f / sqrtf(ss / float(d) + a.eps);
+      }
+      // whole-row weights are heads x head_dim wide; a head norm's head_dim wide
+      const float* w = a.norm == kNormRow ? weight + int64_t(h) * d : weight;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (lo[j] < 0) continue;
+        const int hi = pairs_adjacent ? lo[j] + 1 : lo[j] + half;
+        x[j] = __fmul_rn(__fmul_rn(x[j], head_inverse), w[lo[j]]);
+        y[j] = __fmul_rn(__fmul_rn(y[j], head_inverse), w[hi]);
+      }
+    }
+    if (rotate) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (lo[j] < 0) continue;
+        const int p = lane + 32 * j;
+        const float c = cs[p], s = cs[half + p];
+        const float nx = __fsub_rn(__fmul_rn(x[j], c), __fmul_rn(y[j], s));
+        const float ny = __fadd_rn(__fmul_rn(y[j], c), __fmul_rn(x[j], s));
+        x[j] = nx;
+        y[j] = ny;
+      }
+    }
+    O* op = out_row + part * width + int64_t(h) * d;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (lo[j] < 0) continue;
+      if constexpr (sizeof(O) == 2) {
+        if (pairs_adjacent && a.vec_out) {
+          *reinterpret_cast<__nv_bfloat162*>(op + lo[j]) = __floats2bfloat162_rn(x[j], y[j]);
+        } else {
+          op[lo[j]] = __float2bfloat16_rn(x[j]);
+          op[pairs_adjacent ? lo[j] + 1 : lo[j] + half] = __float2bfloat16_rn(y[j]);
+        }
+      } else {
+        if (pairs_adjacent && a.vec_out) {
+          *reinterpret_cast<float2*>(op + lo[j]) = make_float2(x[j], y[j]);
+        } else {
+          op[lo[j]] = x[j];
+          op[pairs_adjacent ? lo[j] + 1 : lo[j] + half] = y[j];
+        }
+      }
+    }
+  }
+}
+
+template <typename O>
+__device__ __forceinline__ void copy_values_row(const PrologueArgs& a, int token, int lane,
+                                                O* out_row) {
+  const int64_t width = int64_t(a.heads) * a.head_dim;
+  const float* row = a.qkv + int64_t(token) * a.qkv_stride + 2 * width;
+  O* op = out_row + 2 * width;
+  if (a.vec_in && a.vec_out) {
+    const float4* r4 = reinterpret_cast<const float4*>(row);
+    for (int64_t c = lane; c < width / 4; c += 32) {
+      const float4 v = r4[c];
+      if constexpr (sizeof(O) == 2) {
+        __nv_bfloat162 two[2] = {__floats2bfloat162_rn(v.x, v.y), __floats2bfloat162_rn(v.z, v.w)};
+        *reinterpret_cast<uint2*>(op + 4 * c) = *reinterpret_cast<const uint2*>(two);
+      } else {
+        *reinterpret_cast<float4*>(op + 4 * c) = v;
+      }
+    }
+    return;
+  }
+  for (int64_t c = lane; c < width; c += 32) {
+    if constexpr (sizeof(O) == 2) op[c] = __float2bfloat16_rn(row[c]);
+    else op[c] = row[c];
+  }
+}
+
+template <typename O>
+__global__ void __launch_bounds__(kPrologueWarps * 32) prologue_kernel(const PrologueArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t item = int64_t(blockIdx.x) * kPrologueWarps + (threadIdx.x >> 5);
+  if (item >= int64_t(a.tokens) * a.parts) return;
+  const int token = int(item / a.parts), part = int(item % a.parts);
+  O* out_row = static_cast<O*>(a.out) + int64_t(token) * a.out_stride;
+  if (part == 2) copy_values_row<O>(a, token, lane, out_row);
+  else normalize_rotate_row<O>(a, token, part, lane, out_row);
+}
+
+// out[r][h*d + e] *= sigmoid(gate), gate = qkv[r][gate_offset + h*d + e] (per element) or
+// qkv[r][gate_offset + h] (per head)
+__global__ void gate_kernel(const GateArgs a) {
+  const int64_t width = int64_t(a.heads) * a.head_dim;
+  const int64_t total = int64_t(a.rows) * width;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = i / width, c = i % width;
+    const float* g = a.qkv + r * a.qkv_stride + a.gate_offset;
+    const float gate = a.per_head ? g[c / a.head_dim] : g[c];
+    float* o = a.out + r * a.out_stride + c;
+    *o = *o * (1.0f / (1.0f + expf(-gate)));
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_prologue(const PrologueArgs& a, cudaStream_t stream) {
+  const int64_t items = int64_t(a.tokens) * a.parts;
+  if (items == 0) return cudaSuccess;
+  const dim3 grid(unsigned((items + kPrologueWarps - 1) / kPrologueWarps));
+  if (a.out_bf16) prologue_kernel<__nv_bfloat16><<<grid, kPrologueWarps * 32, 0, stream>>>(a);
+  else prologue_kernel<float><<<grid, kPrologueWarps * 32, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gate(const GateArgs& a, cudaStream_t stream) {
+  const int64_t total = int64_t(a.rows) * a.heads * a.head_dim;
+  if (total == 0) return cudaSuccess;
+  const int blocks = int(std::min<int64_t>((total + 255) / 256, 148 * 8));
+  gate_kernel<<<blocks, 256, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace fa

@@ -2,6 +2,12 @@
 // optional Qwen3 head RMSNorm (ops.rs:7-16), RoPE by halves or interleaved (ops.rs:77-95) on the
 // query and key heads, then KvCache::keep of the key and value heads (transformer.rs:164-180).
 //
+// The gated attention of the hybrid blocks (crates/blocks/src/hybrid/attention.rs:155-259) uses
+// the same kernel: its rows hold a gate head per query head between the query and key heads
+// (`gate_heads`, skipped here and read by the gate epilogue), and it rotates by halves only the
+// first `rotary_dim` elements of a head (rope_half over head[..rotary_dim], after the head norm
+// of the whole head).
+//
 // One warp per (row, head unit). The rotation is the reference's arithmetic bit for bit: each
 // product rounded, then the difference or sum (no fused multiply-add), by the host's cos/sin
 // table, so the cache holds exactly the keys the CPU path would keep. The rotated queries go to
@@ -23,9 +29,11 @@ struct KeepRow {
 
 struct RopeArgs {
   int heads, kv_heads, head_dim, rope, n_rows;
-  const float* qkv;  // row r at qkv + r*qkv_stride: heads, kv heads, kv heads of head_dim
+  int gate_heads;  // heads between the query and the key heads that are not rotated or kept
+  int rotary_dim;  // elements of a query or key head rotated, from its first (0: head_dim)
+  const float* qkv;  // row r at qkv + r*qkv_stride: heads, gate heads, kv heads, kv heads
   int64_t qkv_stride;
-  const float* angles;  // row r at angles + r*head_dim: cosines then sines (or nullptr)
+  const float* angles;  // row r at angles + r*rotary_dim: cosines then sines (or nullptr)
   const float* q_norm;  // optional head norms (head_dim weights each)
   const float* k_norm;
   float eps;
@@ -53,15 +61,20 @@ __global__ void __launch_bounds__(kRopeWarps * 32) rope_keep_kernel(const __grid
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x;
   const int unit = blockIdx.y * kRopeWarps + warp;
-  const int units = a.heads + 2 * a.kv_heads;
+  const int units = a.heads + a.gate_heads + 2 * a.kv_heads;
   if (unit >= units) return;
   const bool is_query = unit < a.heads;
-  const bool is_key = !is_query && unit < a.heads + a.kv_heads;
+  if (!is_query && unit < a.heads + a.gate_heads) return;
+  const int kunit = unit - a.gate_heads;  // the cache's numbering: query heads, then kv heads
+  const bool is_key = !is_query && kunit < a.heads + a.kv_heads;
   if (!is_query && !a.keep) return;
   const int d = a.head_dim, half = d / 2;
+  const int rd = a.rotary_dim > 0 ? a.rotary_dim : d, rhalf = rd / 2;
   const float* head = a.qkv + int64_t(row) * a.qkv_stride + int64_t(unit) * d;
 
-  // Each lane holds the pairs p = lane, lane + 32, ... (up to 4 pairs: head_dim <= 256).
+  // Each lane holds the pairs p = lane, lane + 32, ... (up to 4 pairs: head_dim <= 256). Pair p
+  // < rotary_dim/2 is the rotated pair (p, p + rotary_dim/2) by halves or (2p, 2p + 1)
+  // interleaved; past the rotated elements the pairs are (2p, 2p + 1), left as they are.
   float x[4], y[4];
   int lo[4], hi[4];
   const int pairs = (half + 31) / 32;
@@ -69,8 +82,9 @@ __global__ void __launch_bounds__(kRopeWarps * 32) rope_keep_kernel(const __grid
   for (int j = 0; j < 4; ++j) {
     const int p = lane + 32 * j;
     const bool live = j < pairs && p < half;
-    if (a.rope == 2) { lo[j] = 2 * p; hi[j] = 2 * p + 1; }
-    else { lo[j] = p; hi[j] = p + half; }
+    if (a.rope == 1 && p < rhalf) { lo[j] = p; hi[j] = p + rhalf; }
+    else if (p < rhalf) { lo[j] = 2 * p; hi[j] = 2 * p + 1; }
+    else { lo[j] = rd + 2 * (p - rhalf); hi[j] = lo[j] + 1; }
     x[j] = live ? head[lo[j]] : 0.0f;
     y[j] = live ? head[hi[j]] : 0.0f;
     if (!live) lo[j] = -1;
@@ -94,12 +108,12 @@ __global__ void __launch_bounds__(kRopeWarps * 32) rope_keep_kernel(const __grid
       }
     }
     if (a.rope != 0) {
-      const float* cs = a.angles + int64_t(row) * d;
+      const float* cs = a.angles + int64_t(row) * rd;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        if (lo[j] < 0) continue;
         const int p = lane + 32 * j;
-        const float c = cs[p], s = cs[half + p];
+        if (lo[j] < 0 || p >= rhalf) continue;
+        const float c = cs[p], s = cs[rhalf + p];
         const float nx = __fsub_rn(__fmul_rn(x[j], c), __fmul_rn(y[j], s));
         const float ny = __fadd_rn(__fmul_rn(y[j], c), __fmul_rn(x[j], s));
         x[j] = nx;
@@ -132,7 +146,7 @@ __global__ void __launch_bounds__(kRopeWarps * 32) rope_keep_kernel(const __grid
   }
   const KeepRow& kr = a.keep_rows[a.batch ? row : 0];
   const int position = a.batch ? kr.position : a.first + row;
-  const int kv = (unit - a.heads) % a.kv_heads;
+  const int kv = (kunit - a.heads) % a.kv_heads;
   // KV head blocks of capacity x head_dim (KvCache::offset, transformer.rs:263-269)
   const int64_t at = (int64_t(kv) * kr.capacity + position % kr.capacity) * d;
   KT* target = static_cast<KT*>(is_key ? kr.k : kr.v) + at;

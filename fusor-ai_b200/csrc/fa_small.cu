@@ -54,7 +54,7 @@ __global__ void merge_partials_kernel(const float* partials, int shards, int hea
 }  // namespace
 
 cudaError_t launch_rope(int kt, const RopeArgs& args, cudaStream_t stream) {
-  const int units = args.heads + 2 * args.kv_heads;
+  const int units = args.heads + args.gate_heads + 2 * args.kv_heads;
   const dim3 grid(args.n_rows, (units + kRopeWarps - 1) / kRopeWarps);
   if (kt == kKtF32) rope_keep_kernel<float><<<grid, kRopeWarps * 32, 0, stream>>>(args);
   else rope_keep_kernel<__nv_bfloat16><<<grid, kRopeWarps * 32, 0, stream>>>(args);

@@ -23,6 +23,8 @@ OK, ERR_ARG, ERR_SHAPE, ERR_CAPACITY, ERR_CUDA, ERR_TIMEOUT, ERR_UNSUPPORTED = r
 F32, BF16 = 0, 1
 MASK_CAUSAL, MASK_WINDOW, MASK_FULL, MASK_GROUPS = range(4)
 ROPE_NONE, ROPE_HALF, ROPE_INTERLEAVED = range(3)
+NORM_NONE, NORM_ROW, NORM_HEAD = range(3)
+GATE_NONE, GATE_ELEMENTWISE, GATE_HEADWISE = range(3)
 (ROT_SEQUENCE, ROT_LINEAR, ROT_PARTIAL, ROT_MULTIMODAL, ROT_AXES, ROT_MULTIMODAL_INTERLEAVED,
  ROT_GRID) = range(7)
 
@@ -86,6 +88,13 @@ class _RelposCall(C.Structure):
                 ("bias_u", C.c_void_p), ("bias_v", C.c_void_p)]
 
 
+class _Prologue(C.Structure):
+    _fields_ = [("tokens", C.c_int32), ("heads", C.c_int32), ("head_dim", C.c_int32),
+                ("norm", C.c_int32), ("q_norm", C.c_void_p), ("k_norm", C.c_void_p),
+                ("eps", C.c_float), ("rope", C.c_int32), ("angles", C.c_void_p),
+                ("rotated_rows", C.c_int32)]
+
+
 _lib = None
 
 # name -> (restype, argtypes) for every entry point of include/fa_attn.h
@@ -113,6 +122,8 @@ SIGNATURES = {
     "fa_merge_partials": (C.c_int, [_P, _I32, _I32, _I32, _P, _P]),
     "fa_attend_full": (C.c_int, [_P, _P, _I64, _P]),
     "fa_attend_relpos": (C.c_int, [_P, _P, _I64, _P]),
+    "fa_normalize_and_rotate": (C.c_int, [_P, _P, _I64, _P, _I64, _I32, _P]),
+    "fa_gated_attention": (C.c_int, [_P, _I32, _P, _I32, _I32, _P, _P, _P, _I64, _P, _I64, _P]),
     "fa_device_status": (C.c_int, [_P]),
     "fa_rng_fill_normal": (C.c_int, [C.c_uint64, _P, _I64]),
 }
@@ -330,6 +341,17 @@ class KvCache:
                                   _dptr(qkv), qkv.stride(0), _dptr(out), out.stride(0),
                                   _stream(stream)))
 
+    def gated_attention(self, layer: int, span: Span, qkv, out, gate: int, rotary_dim: int,
+                        angles, norm=None, stream=None):
+        """The hybrid blocks' gated attention phase (hybrid/attention.rs:153-295): the heads of
+        qkv's rows (query heads, gate heads for GATE_ELEMENTWISE, key heads, value heads, gates
+        of whole heads for GATE_HEADWISE) normed and rotated by halves in their first
+        rotary_dim elements, kept, attended, and the output times the sigmoid of its gates."""
+        sp = span.c()
+        _check(lib().fa_gated_attention(self._h, layer, C.byref(sp), gate, rotary_dim,
+                                        _dptr(angles), _norm(norm), _dptr(qkv), qkv.stride(0),
+                                        _dptr(out), out.stride(0), _stream(stream)))
+
     def attention_host(self, layer: int, span: Span, qkv: np.ndarray, angles=None,
                        rope: int = ROPE_HALF, norm=None, stream=None) -> np.ndarray:
         """The same on host (numpy) rows, as the reference's host Buffers hold them."""
@@ -449,6 +471,23 @@ def attend_relpos(heads: int, head_dim: int, frames: int, query: Operand, key: O
                        positions.data_ptr(), positions.stride(0), bias_u.data_ptr(),
                        bias_v.data_ptr())
     _check(lib().fa_attend_relpos(C.byref(call), _dptr(out), out.stride(0), _stream(stream)))
+
+
+def normalize_and_rotate(heads: int, head_dim: int, qkv, out, norm: int = NORM_ROW,
+                         q_norm=None, k_norm=None, eps: float = 1e-6, angles=None,
+                         rope: int = ROPE_INTERLEAVED, rotated_rows=None, stream=None):
+    """The DiT blocks' query/key prologue (wan_dit/block.rs:109-140, pyramid_jit/block.rs:
+    100-131 with NORM_ROW; mmdit/pass.rs:162-192 with NORM_HEAD): each token's query and key
+    rows of qkv (tokens x stride f32) RMS-normalized and rotated by `angles` (tokens x head_dim),
+    into out (f32 or bf16, queries/keys/values as in qkv; out may be qkv itself, f32)."""
+    import torch
+    tokens = qkv.shape[0]
+    p = _Prologue(tokens, heads, head_dim, norm, _dptr(q_norm), _dptr(k_norm), eps,
+                  rope if angles is not None else ROPE_NONE, _dptr(angles),
+                  tokens if rotated_rows is None else rotated_rows)
+    dt = F32 if out.dtype == torch.float32 else BF16
+    _check(lib().fa_normalize_and_rotate(C.byref(p), _dptr(qkv), qkv.stride(0), _dptr(out),
+                                         out.stride(0), dt, _stream(stream)))
 
 
 def device_status(stream=None):

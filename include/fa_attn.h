@@ -285,6 +285,53 @@ typedef struct {
 
 int fa_attend_relpos(const fa_relpos_call* call, float* out, int64_t out_stride, void* stream);
 
+/* Row norms of the query/key prologue. */
+#define FA_NORM_NONE 0
+#define FA_NORM_ROW 1  /* RMSNorm of the whole query (key) row: heads*head_dim weights */
+#define FA_NORM_HEAD 2 /* RMSNorm of each head on its own: head_dim weights */
+
+/* The query/key prologue of the DiT blocks' self-attention: Wan's normalize_and_rotate
+ * (crates/blocks/src/wan_dit/block.rs:109-140) and Pyramid's (pyramid_jit/block.rs:100-131)
+ * with FA_NORM_ROW, MMDiT's head_norms (mmdit/pass.rs:162-192) with FA_NORM_HEAD. */
+typedef struct {
+  int32_t tokens;
+  int32_t heads;        /* query = key = value heads (the full-mask blocks are multi-head) */
+  int32_t head_dim;
+  int32_t norm;         /* FA_NORM_* */
+  const float* q_norm;  /* device weights, as `norm` says (unused for FA_NORM_NONE) */
+  const float* k_norm;
+  float eps;
+  int32_t rope;         /* FA_ROPE_NONE, FA_ROPE_HALF or FA_ROPE_INTERLEAVED (the DiTs') */
+  const float* angles;  /* device, tokens x head_dim as fa_rotary_angles writes them */
+  int32_t rotated_rows; /* tokens [0, rotated_rows) are rotated, the rest only normalized */
+} fa_prologue;
+
+/* Each token's query row and key row of qkv (f32 device rows qkv_stride apart: queries, keys,
+ * values of heads*head_dim each) RMS-normalized and rotated, into out (tokens rows out_stride
+ * elements apart, laid out as qkv, in out_dtype), the values copied beside them: the operand
+ * rows of fa_attend_full. With out == qkv, FA_F32 and out_stride == qkv_stride it works in
+ * place and leaves the values where they are, as the reference does. */
+int fa_normalize_and_rotate(const fa_prologue* prologue, const float* qkv, int64_t qkv_stride,
+                            void* out, int64_t out_stride, int32_t out_dtype, void* stream);
+
+/* The gate of the hybrid blocks' attention output (hybrid/attention.rs:24-33). */
+#define FA_GATE_NONE 0
+#define FA_GATE_ELEMENTWISE 1 /* a gate head after each query head's block: per element */
+#define FA_GATE_HEADWISE 2    /* one gate per query head, after the value heads */
+
+/* The hybrid blocks' gated attention phase (hybrid/attention.rs:153-295, Weights::mix then the
+ * gate): each row of qkv (f32, qkv_stride apart) holds the query heads, with FA_GATE_ELEMENTWISE
+ * a gate head per query head, the key heads and the value heads (head_dim each), then with
+ * FA_GATE_HEADWISE one gate per query head. Query and key heads are head-normed (optional) and
+ * rotated by halves in their first rotary_dim elements by `angles` (rows x rotary_dim, as
+ * fa_rotary_angles writes them for a rotary of rotary_dim), keys and values kept at first + row,
+ * the queries attend over the cache under span->mask, and out (rows x out_stride f32, heads x
+ * head_dim) is multiplied by the sigmoid of its gates. */
+int fa_gated_attention(fa_kvcache* cache, int32_t layer, const fa_span* span, int32_t gate,
+                       int32_t rotary_dim, const float* angles, const fa_head_norm* norm,
+                       const float* qkv, int64_t qkv_stride, float* out, int64_t out_stride,
+                       void* stream);
+
 /* Waits for `stream` and reports whether any kernel of this library gave up a device-side wait
  * since the last call (FA_ERR_TIMEOUT, clearing the flag) or FA_OK. */
 int fa_device_status(void* stream);

@@ -72,6 +72,9 @@ def lib():
             "oracle_team_release": (None, []),
             "oracle_relpos_attend": (None, [i64, i64, i64, p, p, p, i64, p, i64, p, p, p]),
             "oracle_reference_attend_f64": (None, [p, i64, i64, i64, i64, p, p]),
+            "oracle_qk_prologue": (None, [i64, i64, i64, i, i, i64, p, p, p, f, p, i64]),
+            "oracle_gated_input": (None, [p, i64, i64, i64, i, i64, p, p, p, f, p, i64]),
+            "oracle_gate": (None, [i64, i64, i64, i64, i, p, i64, p]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(_lib, name)
@@ -203,6 +206,16 @@ class Cache:
                                      _ptr(None if k_norm is None else _f32(k_norm)),
                                      eps, _ptr(qkv), stride)
 
+    def gated_input(self, layer, rows, first, gate, rotary_dim, angles, qkv, stride,
+                    q_norm=None, k_norm=None, eps=1e-6):
+        """The hybrid blocks' projected heads (hybrid/attention.rs:180-235), in place on qkv."""
+        c = self.c()
+        lib().oracle_gated_input(C.byref(c), layer, rows, first, gate, rotary_dim,
+                                 _ptr(_f32(angles)),
+                                 _ptr(None if q_norm is None else _f32(q_norm)),
+                                 _ptr(None if k_norm is None else _f32(k_norm)),
+                                 eps, _ptr(qkv), stride)
+
     def attend(self, layer, rows, first, mask: Mask, qkv, stride, threads: int = 1) -> np.ndarray:
         out = np.zeros((rows, self.heads * self.head_dim), np.float32)
         c, m = self.c(), mask.c()
@@ -251,6 +264,27 @@ def relpos_attend(heads, head_dim, frames, qkv, positions, bias_u, bias_v):
     lib().oracle_relpos_attend(heads, head_dim, frames, C.c_void_p(base), C.c_void_p(base + 4 * hidden),
                                C.c_void_p(base + 8 * hidden), qkv.shape[1], _ptr(_f32(positions)),
                                hidden, _ptr(_f32(bias_u)), _ptr(_f32(bias_v)), _ptr(out))
+    return out
+
+
+def qk_prologue(tokens, heads, head_dim, norm, rope, rotated, angles, q_norm, k_norm, eps,
+                qkv) -> np.ndarray:
+    """The DiT blocks' query/key prologue (wan_dit/block.rs:109-140, mmdit/pass.rs:162-192) on a
+    copy of qkv (tokens x stride f32); returns the copy."""
+    out = _f32(qkv).copy()
+    lib().oracle_qk_prologue(tokens, heads, head_dim, norm, rope, rotated,
+                             _ptr(None if angles is None else _f32(angles)),
+                             _ptr(None if q_norm is None else _f32(q_norm)),
+                             _ptr(None if k_norm is None else _f32(k_norm)), eps, _ptr(out),
+                             out.shape[1])
+    return out
+
+
+def gate(rows, heads, kv_heads, head_dim, gate_kind, qkv, attention) -> np.ndarray:
+    """Weights::gate (hybrid/attention.rs:262-295) on a copy of attention."""
+    out = _f32(attention).copy()
+    q = _f32(qkv)
+    lib().oracle_gate(rows, heads, kv_heads, head_dim, gate_kind, _ptr(q), q.shape[1], _ptr(out))
     return out
 
 

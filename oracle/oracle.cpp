@@ -484,6 +484,92 @@ void oracle_attend_call(int64_t heads, int64_t kv_heads, int64_t head_dim, int64
   team(std::max(threads, 1)).run(task);
 }
 
+void oracle_qk_prologue(int64_t tokens, int64_t heads, int64_t head_dim, int norm, int rope,
+                        int64_t rotated, const float* angles, const float* q_norm,
+                        const float* k_norm, float eps, float* qkv, int64_t stride) {
+  const int64_t d = head_dim, width = heads * d;
+  std::vector<float> scratch(width);
+  for (int64_t t = 0; t < tokens; ++t) {
+    for (int part = 0; part < 2; ++part) {
+      float* run = qkv + t * stride + part * width;
+      const float* weight = part == 0 ? q_norm : k_norm;
+      if (norm == 1) {
+        // rms_rows: rms_norm of the run into scratch, copied back
+        oracle_rms_norm(run, weight, eps, (int)width, scratch.data());
+        std::memcpy(run, scratch.data(), sizeof(float) * width);
+      } else if (norm == 2) {
+        // normalize_heads: rms_norm's rows of weight.len() = head_dim
+        for (int64_t h = 0; h < heads; ++h)
+          oracle_rms_norm(run + h * d, weight, eps, (int)d, scratch.data() + h * d);
+        std::memcpy(run, scratch.data(), sizeof(float) * width);
+      }
+    }
+  }
+  if (rope == 0) return;
+  for (int64_t t = 0; t < tokens && t < rotated; ++t) {
+    const float* cos = angles + t * d;
+    const float* sin = cos + d / 2;
+    // the queries and keys of the token, head_dim chunks of its first 2 * width values
+    for (int64_t h = 0; h < 2 * heads; ++h) {
+      float* head = qkv + t * stride + h * d;
+      if (rope == 1) oracle_rope_half(head, (int)d, cos, sin);
+      else oracle_rope_interleaved(head, (int)d, cos, sin);
+    }
+  }
+}
+
+static float oracle_sigmoid(float x) { return 1.0f / (1.0f + oracle_exp(-x)); }
+
+void oracle_gated_input(oracle_cache* cache, int64_t layer, int64_t rows, int64_t first, int gate,
+                        int64_t rotary_dim, const float* angles, const float* q_norm,
+                        const float* k_norm, float norm_eps, float* qkv, int64_t stride) {
+  const int64_t d = cache->head_dim, heads = cache->heads, kv = cache->kv_heads;
+  const int64_t gate_heads = gate == 1 ? heads : 0;
+  const int64_t units = heads + gate_heads + 2 * kv;
+  std::vector<float> copy(d);
+  for (int64_t row = 0; row < rows; ++row) {
+    const int64_t position = first + row;
+    const float* cos = angles + row * rotary_dim;
+    const float* sin = cos + rotary_dim / 2;
+    for (int64_t unit = 0; unit < units; ++unit) {
+      float* head = qkv + row * stride + unit * d;
+      if (unit >= heads && unit < heads + gate_heads) {  // Role::Gate
+        for (int64_t e = 0; e < d; ++e) head[e] = oracle_sigmoid(head[e]);
+        continue;
+      }
+      const int64_t cache_unit = unit - gate_heads;  // Role::Key / Role::Value numbering
+      if (cache_unit < heads + kv) {                 // Role::Query or Role::Key: position()
+        const float* weight = cache_unit < heads ? q_norm : k_norm;
+        if (weight != nullptr) {
+          std::memcpy(copy.data(), head, sizeof(float) * d);
+          oracle_rms_norm(copy.data(), weight, norm_eps, (int)d, head);
+        }
+        oracle_rope_half(head, (int)rotary_dim, cos, sin);
+      }
+      if (cache_unit >= heads) oracle_cache_keep(cache, layer, cache_unit, position, head);
+    }
+    if (gate == 2) {  // project_head_gates
+      float* gates = qkv + row * stride + units * d;
+      for (int64_t h = 0; h < heads; ++h) gates[h] = oracle_sigmoid(gates[h]);
+    }
+  }
+}
+
+void oracle_gate(int64_t rows, int64_t heads, int64_t kv_heads, int64_t head_dim, int gate,
+                 const float* qkv, int64_t stride, float* attention) {
+  if (gate == 0) return;
+  const int64_t d = head_dim, width = heads * d;
+  const int64_t head_columns = (heads + (gate == 1 ? heads : 0) + 2 * kv_heads) * d;
+  for (int64_t h = 0; h < heads; ++h) {
+    for (int64_t row = 0; row < rows; ++row) {
+      const float* r = qkv + row * stride;
+      float* attended = attention + row * width + h * d;
+      for (int64_t e = 0; e < d; ++e)
+        attended[e] *= gate == 1 ? r[(heads + h) * d + e] : r[head_columns + h];
+    }
+  }
+}
+
 void oracle_relpos_attend(int64_t heads, int64_t head_dim, int64_t frames, const float* q,
                           const float* k, const float* v, int64_t qkv_stride,
                           const float* positions, int64_t positions_stride, const float* bias_u,

@@ -141,6 +141,31 @@ void oracle_relpos_attend(int64_t heads, int64_t head_dim, int64_t frames, const
                           const float* positions, int64_t positions_stride, const float* bias_u,
                           const float* bias_v, float* out);
 
+/* The query/key prologue of the DiT blocks, in place in qkv (tokens rows of `stride`: queries,
+ * keys, values of heads*head_dim): norm 1 is rms_rows over the whole query row and the whole key
+ * row (wan_dit/block.rs:109-126, row_work.rs:57-75; weights heads*head_dim wide), norm 2 each
+ * head on its own (mmdit/pass.rs:64-68,162-176; weights head_dim wide); then tokens below
+ * `rotated` have every query and key head turned by their angles row (tokens x head_dim), rope 1
+ * by halves, 2 interleaved (block.rs:127-139). */
+void oracle_qk_prologue(int64_t tokens, int64_t heads, int64_t head_dim, int norm, int rope,
+                        int64_t rotated, const float* angles, const float* q_norm,
+                        const float* k_norm, float eps, float* qkv, int64_t stride);
+
+/* The hybrid blocks' projected heads (hybrid/attention.rs:180-235): for each row and head unit
+ * of a row (query heads, gate heads when gate == 1, key heads, value heads; head_dim each),
+ * queries and keys head-normed (optional) and rotated by halves in their first rotary_dim
+ * elements by angles (rows x rotary_dim), gates through their sigmoid, keys and values kept at
+ * first + row; with gate == 2 the per-head gates after the value heads through their sigmoid
+ * too. In place in qkv. */
+void oracle_gated_input(oracle_cache* cache, int64_t layer, int64_t rows, int64_t first, int gate,
+                        int64_t rotary_dim, const float* angles, const float* q_norm,
+                        const float* k_norm, float norm_eps, float* qkv, int64_t stride);
+
+/* Weights::gate (hybrid/attention.rs:262-295): each query head of attention (rows x
+ * heads*head_dim) times its gates from qkv as oracle_gated_input left them. */
+void oracle_gate(int64_t rows, int64_t heads, int64_t kv_heads, int64_t head_dim, int gate,
+                 const float* qkv, int64_t stride, float* attention);
+
 /* Joins the team's worker threads (they are started on the first threaded call). */
 void oracle_team_release(void);
 

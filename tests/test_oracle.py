@@ -167,3 +167,129 @@ def test_attend_call_full_mask_matches_the_cache_path():
     cache.values[0] = v.reshape(n, heads, d).transpose(1, 0, 2)
     want = cache.attend(0, n, 0, oracle.Mask.full(), q, heads * d)
     assert (got == want).all()
+
+
+# ---- the hybrid blocks' gated attention and the DiT query/key prologue ------------------------
+
+def _rms_f64(x, w, eps):
+    """support::rms_norm (crates/blocks/tests/support/mod.rs:301-311) over rows of len(w)."""
+    x = x.reshape(-1, len(w))
+    inverse = 1.0 / np.sqrt((x * x).sum(axis=1, keepdims=True) / len(w) + eps)
+    return (x * inverse * w).reshape(-1)
+
+
+def _rotate_f64(head, angles, half_pairs):
+    """support::rotate (support/mod.rs:389-400) by halves or interleaved."""
+    half = len(head) // 2
+    out = head.copy()
+    for i, a in enumerate(angles):
+        f, s = (i, i + half) if half_pairs else (2 * i, 2 * i + 1)
+        x, y = head[f], head[s]
+        out[f] = x * np.cos(a) - y * np.sin(a)
+        out[s] = y * np.cos(a) + x * np.sin(a)
+    return out
+
+
+def _attend_f64(q, k, v, visible):
+    s = (q @ k.T) / np.sqrt(q.shape[-1])
+    s = np.where(visible, s, -np.inf)
+    p = np.exp(s - s.max(axis=1, keepdims=True))
+    return (p / p.sum(axis=1, keepdims=True)) @ v
+
+
+@pytest.mark.parametrize("gate", [0, 1, 2])
+@pytest.mark.parametrize("mask_name,call", [("causal", 3), ("full", 8)])
+def test_gated_attention_like_the_f64_reference(gate, mask_name, call):
+    """The hybrid stack's attention (stacks.rs:669-757 HYBRID: DECODER dims, half of each head
+    rotated; read in calls of 3 causal rows or one full call) against an f64 restatement of
+    support::gated_attention (support/mod.rs:720-757), every gate kind, within the stack test's
+    f32 tolerance (stacks.rs:51-56)."""
+    heads, kv, d, rows, rotary_dim, eps, base = 4, 2, 16, 8, 8, 1e-5, 10000.0
+    gate_heads = heads if gate == 1 else 0
+    head_columns = (heads + gate_heads + 2 * kv) * d
+    width = head_columns + (heads if gate == 2 else 0)
+    lcg = oracle.Lcg(11)
+    qkv = lcg.floats(rows * width, 0.0, 1.0).reshape(rows, width)
+    qn = 1.0 + 0.1 * lcg.floats(d, 0.0, 1.0)
+    kn = 1.0 + 0.1 * lcg.floats(d, 0.0, 1.0)
+    positions = list(range(rows))
+    inv = base ** (-np.arange(0, rotary_dim, 2) / rotary_dim)
+    # f64: heads normed and rotated, gates through their sigmoid, attention, times the gates
+    q64 = np.zeros((rows, heads, d)); k64 = np.zeros((rows, kv, d)); v64 = np.zeros((rows, kv, d))
+    g64 = np.zeros((rows, heads, d))
+    for r in range(rows):
+        row = qkv[r].astype(np.float64)
+        ang = positions[r] * inv
+        for h in range(heads):
+            x = _rms_f64(row[h * d:(h + 1) * d], qn, eps)
+            x[:rotary_dim] = _rotate_f64(x[:rotary_dim], ang, True)
+            q64[r, h] = x
+            if gate == 1:
+                g64[r, h] = 1.0 / (1.0 + np.exp(-row[(heads + h) * d:(heads + h + 1) * d]))
+            elif gate == 2:
+                g64[r, h] = 1.0 / (1.0 + np.exp(-row[head_columns + h]))
+            else:
+                g64[r, h] = 1.0
+        for j in range(kv):
+            at = (heads + gate_heads + j) * d
+            x = _rms_f64(row[at:at + d], kn, eps)
+            x[:rotary_dim] = _rotate_f64(x[:rotary_dim], ang, True)
+            k64[r, j] = x
+            v64[r, j] = row[(heads + gate_heads + kv + j) * d:(heads + gate_heads + kv + j + 1) * d]
+    visible = np.tril(np.ones((rows, rows), bool)) if mask_name == "causal" else np.ones((rows, rows), bool)
+    want = np.zeros((rows, heads, d))
+    for h in range(heads):
+        j = h // (heads // kv)
+        want[:, h] = _attend_f64(q64[:, h], k64[:, j], v64[:, j], visible) * g64[:, h]
+    # the oracle, in calls
+    cache = oracle.Cache(1, heads, kv, d, rows)
+    mask = oracle.Mask.causal() if mask_name == "causal" else oracle.Mask.full()
+    got = []
+    for first in range(0, rows, call):
+        n = min(call, rows - first)
+        part = qkv[first:first + n].copy()
+        angles = oracle.angles_table(oracle.ROT_SEQUENCE, base, rotary_dim,
+                                     list(range(first, first + n)))
+        cache.gated_input(0, n, first, gate, rotary_dim, angles, part, width, qn, kn, eps)
+        attended = cache.attend(0, n, first, mask, part, width)
+        got.append(oracle.gate(n, heads, kv, d, gate, part, attended))
+    got = np.concatenate(got).reshape(rows, heads, d)
+    rel = np.linalg.norm(got - want) / np.linalg.norm(want)
+    assert rel < 1e-6, rel
+
+
+@pytest.mark.parametrize("norm,rope", [(1, 2), (2, 2), (2, 1), (0, 2)])
+def test_qk_prologue_like_the_f64_reference(norm, rope):
+    """Wan's normalize_and_rotate (wan_dit/block.rs:109-140: whole-row RMSNorm, interleaved 3-D
+    RoPE by the token's frame, row and column, video.rs:48-55) and MMDiT's head norms
+    (mmdit/pass.rs:162-192) against f64, within 1e-6 relative."""
+    frames, grid_rows, cols, heads, d, eps, base = 2, 3, 4, 2, 16, 1e-6, 10000.0
+    tokens, width = frames * grid_rows * cols, heads * d
+    sections = (2, 3, 3)  # Rotation::Axes over d/2 = 8 pairs
+    lcg = oracle.Lcg(12)
+    qkv = lcg.floats(tokens * 3 * width, 0.0, 1.0).reshape(tokens, 3 * width)
+    wq = 1.0 + 0.1 * lcg.floats(width if norm == 1 else d, 0.0, 1.0)
+    wk = 1.0 + 0.1 * lcg.floats(width if norm == 1 else d, 0.0, 1.0)
+    pos = [(t // (grid_rows * cols), t // cols % grid_rows, t % cols) for t in range(tokens)]
+    angles = np.stack([np.concatenate(oracle.rotary_angles(oracle.ROT_AXES, base, d, p, sections))
+                       for p in pos])
+    got = oracle.qk_prologue(tokens, heads, d, norm, rope, tokens, angles, wq, wk, eps, qkv)
+    # f64: the frequencies of each axis section over 2 * section dims (rotary.rs:117-156)
+    inv = np.concatenate([base ** (-np.arange(0, 2 * s, 2) / (2 * s)) for s in sections])
+    axis = np.repeat([0, 1, 2], sections)
+    for t in range(tokens):
+        ang = np.array([pos[t][axis[i]] for i in range(d // 2)]) * inv
+        for part in range(2):
+            x = qkv[t, part * width:(part + 1) * width].astype(np.float64)
+            w = (wq if part == 0 else wk).astype(np.float64)
+            if norm == 1:
+                x = _rms_f64(x, w, eps)
+            elif norm == 2:
+                x = _rms_f64(x, w, eps)  # rows of len(w) = head_dim: each head on its own
+            if rope:
+                x = np.concatenate([_rotate_f64(x[h * d:(h + 1) * d], ang, rope == 1)
+                                    for h in range(heads)])
+            want = x
+            g = got[t, part * width:(part + 1) * width]
+            assert np.linalg.norm(g - want) / np.linalg.norm(want) < 1e-6
+        assert (got[t, 2 * width:] == qkv[t, 2 * width:]).all()
