@@ -10,7 +10,7 @@
 //    is split into pieces.
 //  - Four consumer warps score each key against the G query heads that share it (GQA reuse the
 //    CPU path lacks: it re-reads the KV head once per query head), LPK lanes per key with 8
-//    elements each, warp-shuffle reductions and an online softmax in base 2 (the queries are
+//    (16 for a bf16 cache) elements each, warp-shuffle reductions and an online softmax in base 2 (the queries are
 //    scaled by log2(e)/sqrt(head_dim) as they are loaded).
 //  - The warps' (max, sum, output) states merge in shared memory; a single-chunk row writes its
 //    output, otherwise the chunk's partial goes to the workspace and the last CTA of the row
@@ -78,15 +78,36 @@ struct KvElem<__nv_bfloat16> {
   static constexpr int kBytes = 2;
 };
 
-template <int D, typename KT>
+// Elements of a key (value) row each lane holds: 8, or 16 for a bf16 cache with at most 4 query
+// heads per CTA (twice the work per shuffle of the score reductions: a bf16 row carries half
+// the bytes of an f32 row for the same arithmetic, so its CTA must issue fewer instructions per
+// byte to keep up with HBM; more heads would spill the registers).
+#ifndef FA_DECODE_BF16_EPL
+#define FA_DECODE_BF16_EPL 16
+#endif
+#ifndef FA_DECODE_BF16_MIN_CTAS
+#define FA_DECODE_BF16_MIN_CTAS 2
+#endif
+template <int D, typename KT, int G>
+struct LaneElems {
+  static constexpr int value =
+      (KvElem<KT>::kBytes == 2 && G <= 4 && D / FA_DECODE_BF16_EPL >= 2) ? FA_DECODE_BF16_EPL : 8;
+};
+
+template <int D, typename KT, int G>
 struct DecodeShape {
   static constexpr int kRowBytes = D * KvElem<KT>::kBytes;
-  static constexpr int kLanesPerKey = D / 8;          // 8 elements per lane
+  static constexpr int kLaneElems = LaneElems<D, KT, G>::value;
+  static constexpr int kLanesPerKey = D / kLaneElems;
   static constexpr int kKeysPerWarp = 32 / kLanesPerKey;
   static constexpr int kTileKeys = kTileBytes / kRowBytes;
   static constexpr int kRoundKeys = kConsumerWarps * kKeysPerWarp;
   static constexpr int kRounds = kTileKeys / kRoundKeys;
   static constexpr int kElemsPerTile = kTileKeys * D;
+  // resident CTAs per SM the registers are sized for: 16 elements per lane, or 8 query heads,
+  // need more than a third of the register file per CTA
+  static constexpr int kMinCtas =
+      (kLaneElems == 16 || G >= 8) ? FA_DECODE_BF16_MIN_CTAS : FA_DECODE_MIN_CTAS;
   static_assert(kLanesPerKey >= 2 && kLanesPerKey <= 32, "head_dim 16..256");
   static_assert(kRounds * kRoundKeys == kTileKeys, "tile holds whole rounds");
   static constexpr size_t kSmemBytes = size_t(kStages) * 2 * kTileBytes + 2 * kStages * 8;
@@ -95,43 +116,57 @@ struct DecodeShape {
                 "the merge scratch fits the stages");
 };
 
-// The element index of lane-slot i (0..7) of sub-lane `sub` in a row: f32 rows are read as two
-// float4 at sub and sub + LPK (each group of 8 lanes reads 128 contiguous bytes), bf16 rows as
-// one 16-byte vector at sub.
-template <int D, typename KT>
+// The element index of lane-slot i (0..E-1) of sub-lane `sub` in a row, LPK = D / E lanes per
+// row: f32 rows are read as two float4 at sub and sub + LPK, bf16 rows as one 16-byte vector at
+// sub (E = 8) or two at sub and sub + LPK (E = 16); either way each group of 8 lanes reads 128
+// contiguous bytes of shared memory (no bank conflicts).
+template <int D, typename KT, int E>
 __device__ __forceinline__ int elem_of(int sub, int i) {
+  constexpr int LPK = D / E;
   if constexpr (KvElem<KT>::kBytes == 4) {
-    constexpr int LPK = D / 8;
     return i < 4 ? 4 * sub + i : 4 * (sub + LPK) + (i - 4);
-  } else {
+  } else if constexpr (E == 8) {
     return 8 * sub + i;
+  } else {
+    return i < 8 ? 8 * sub + i : 8 * (sub + LPK) + (i - 8);
   }
 }
 
-template <int D, typename KT>
-__device__ __forceinline__ void load8(const KT* row, int sub, float (&x)[8]) {
+// bf16 pairs of a 32-bit word as an f32 pair (the low element first).
+__device__ __forceinline__ float2 bf16x2_to_float2(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+
+__device__ __forceinline__ void unpack_bf16x8(const uint4 a, float2* x) {
+  x[0] = bf16x2_to_float2(a.x);
+  x[1] = bf16x2_to_float2(a.y);
+  x[2] = bf16x2_to_float2(a.z);
+  x[3] = bf16x2_to_float2(a.w);
+}
+
+// A lane's E elements of a row as E/2 f32 pairs, pair i = elements (elem_of(2i), elem_of(2i+1)).
+template <int D, typename KT, int E>
+__device__ __forceinline__ void load_lane(const KT* row, int sub, float2 (&x)[E / 2]) {
+  constexpr int LPK = D / E;
   if constexpr (KvElem<KT>::kBytes == 4) {
-    constexpr int LPK = D / 8;
+    static_assert(E == 8, "f32 rows: 8 elements per lane");
     const float4 a = reinterpret_cast<const float4*>(row)[sub];
     const float4 b = reinterpret_cast<const float4*>(row)[sub + LPK];
-    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
-    x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+    x[0] = make_float2(a.x, a.y);
+    x[1] = make_float2(a.z, a.w);
+    x[2] = make_float2(b.x, b.y);
+    x[3] = make_float2(b.z, b.w);
+  } else if constexpr (E == 8) {
+    unpack_bf16x8(reinterpret_cast<const uint4*>(row)[sub], x);
   } else {
-    const uint4 a = reinterpret_cast<const uint4*>(row)[sub];
-    x[0] = bf16_lo(a.x); x[1] = bf16_hi(a.x); x[2] = bf16_lo(a.y); x[3] = bf16_hi(a.y);
-    x[4] = bf16_lo(a.z); x[5] = bf16_hi(a.z); x[6] = bf16_lo(a.w); x[7] = bf16_hi(a.w);
+    unpack_bf16x8(reinterpret_cast<const uint4*>(row)[sub], x);
+    unpack_bf16x8(reinterpret_cast<const uint4*>(row)[sub + LPK], x + 4);
   }
 }
 
-// o = a * b + o on two f32 lanes at once (sm_100a fma.rn.f32x2; each lane rounds as fmaf).
-__device__ __forceinline__ void fma2(float& o0, float& o1, float a0, float a1, float b0, float b1) {
-  unsigned long long ra, rb, ro;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(ra) : "f"(a0), "f"(a1));
-  asm("mov.b64 %0, {%1, %2};" : "=l"(rb) : "f"(b0), "f"(b1));
-  asm("mov.b64 %0, {%1, %2};" : "=l"(ro) : "f"(o0), "f"(o1));
-  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(ro) : "l"(ra), "l"(rb));
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(o0), "=f"(o1) : "l"(ro));
-}
+// Two f32 lanes at once (sm_100a's paired FFMA/FMUL; each lane rounds as fmaf / __fmul_rn).
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
 
 template <int N>
 struct Log2 {
@@ -188,8 +223,9 @@ struct BatchArgs {
 };
 
 template <int D, typename KT, int G, bool BATCH, typename Args>
-__global__ void __launch_bounds__(kDecodeThreads, FA_DECODE_MIN_CTAS) attend_kernel(const __grid_constant__ Args args) {
-  using S = DecodeShape<D, KT>;
+__global__ void __launch_bounds__(kDecodeThreads, (DecodeShape<D, KT, G>::kMinCtas)) attend_kernel(const __grid_constant__ Args args) {
+  using S = DecodeShape<D, KT, G>;
+  constexpr int E = S::kLaneElems;
   constexpr int T = S::kTileKeys;
   constexpr int LPK = S::kLanesPerKey;
   constexpr int KPW = S::kKeysPerWarp;
@@ -326,22 +362,27 @@ __global__ void __launch_bounds__(kDecodeThreads, FA_DECODE_MIN_CTAS) attend_ker
   const int own = kScatter ? sub / kHeadLanes : 0;
   const int group_base = lane & ~(LPK - 1);
 
-  float q[G][8];
+  constexpr int P = E / 2;  // f32 pairs per lane
+  float2 q[G][P];
   const float* qrow = c.q + int64_t(row) * c.q_stride;
 #pragma unroll
   for (int h = 0; h < G; ++h)
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
-      q[h][i] = h < g ? qrow[(h0 + h) * D + elem_of<D, KT>(sub, i)] * c.q_scale : 0.0f;
+    for (int i = 0; i < P; ++i) {
+      const int at = (h0 + h) * D + elem_of<D, KT, E>(sub, 2 * i);
+      q[h][i] = h < g ? make_float2(qrow[at] * c.q_scale, qrow[at + 1] * c.q_scale)
+                      : make_float2(0.0f, 0.0f);
+    }
 
   // m[h], l[h]: every head (per-head path) or m[0], l[0]: the lane's own head (scatter path)
-  float m[G], l[G], o[G][8];
+  float m[G], l[G];
+  float2 o[G][P];
 #pragma unroll
   for (int h = 0; h < G; ++h) {
     m[h] = -INFINITY;
     l[h] = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) o[h][i] = 0.0f;
+    for (int i = 0; i < P; ++i) o[h][i] = make_float2(0.0f, 0.0f);
   }
 
   bool ok = true;
@@ -358,17 +399,17 @@ __global__ void __launch_bounds__(kDecodeThreads, FA_DECODE_MIN_CTAS) attend_ker
       const int kr = first_key + grp;
       const bool valid = kr < nk;
       const int rr = valid ? kr : first_key;
-      float kx[8], vx[8];
-      load8<D, KT>(kt + size_t(rr) * D, sub, kx);
-      load8<D, KT>(vt + size_t(rr) * D, sub, vx);
+      float2 kx[P], vx[P];
+      load_lane<D, KT, E>(kt + size_t(rr) * D, sub, kx);
       float part[G];
 #pragma unroll
       for (int h = 0; h < G; ++h) {
-        float a0 = 0.0f, a1 = 0.0f;
+        float2 a = make_float2(0.0f, 0.0f);
 #pragma unroll
-        for (int i = 0; i < 8; i += 2) fma2(a0, a1, q[h][i], q[h][i + 1], kx[i], kx[i + 1]);
-        part[h] = a0 + a1;
+        for (int i = 0; i < P; ++i) a = fma2(q[h][i], kx[i], a);
+        part[h] = a.x + a.y;
       }
+      load_lane<D, KT, E>(vt + size_t(rr) * D, sub, vx);
       if constexpr (kScatter) {
 #pragma unroll
         for (int k = 0; k < kLogG; ++k) {
@@ -398,7 +439,7 @@ __global__ void __launch_bounds__(kDecodeThreads, FA_DECODE_MIN_CTAS) attend_ker
           for (int h = 0; h < G; ++h) {
             const float ah = __shfl_sync(0xffffffffu, alpha, group_base + h * kHeadLanes);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) o[h][i] *= ah;
+            for (int i = 0; i < P; ++i) o[h][i] = mul2(o[h][i], make_float2(ah, ah));
           }
         }
         const float p = valid ? exp2_approx(sc - m[0]) : 0.0f;
@@ -407,7 +448,7 @@ __global__ void __launch_bounds__(kDecodeThreads, FA_DECODE_MIN_CTAS) attend_ker
         for (int h = 0; h < G; ++h) {
           const float ph = __shfl_sync(0xffffffffu, p, group_base + h * kHeadLanes);
 #pragma unroll
-          for (int i = 0; i < 8; i += 2) fma2(o[h][i], o[h][i + 1], ph, ph, vx[i], vx[i + 1]);
+          for (int i = 0; i < P; ++i) o[h][i] = fma2(make_float2(ph, ph), vx[i], o[h][i]);
         }
       } else {
         float sc[G];
@@ -427,13 +468,13 @@ __global__ void __launch_bounds__(kDecodeThreads, FA_DECODE_MIN_CTAS) attend_ker
             const float alpha = exp2_approx(m[h] - mx);
             l[h] *= alpha;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) o[h][i] *= alpha;
+            for (int i = 0; i < P; ++i) o[h][i] = mul2(o[h][i], make_float2(alpha, alpha));
             m[h] = mx;
           }
           const float p = valid ? exp2_approx(sc[h] - m[h]) : 0.0f;
           l[h] += p;
 #pragma unroll
-          for (int i = 0; i < 8; i += 2) fma2(o[h][i], o[h][i + 1], p, p, vx[i], vx[i + 1]);
+          for (int i = 0; i < P; ++i) o[h][i] = fma2(make_float2(p, p), vx[i], o[h][i]);
         }
       }
     }
@@ -450,7 +491,10 @@ __global__ void __launch_bounds__(kDecodeThreads, FA_DECODE_MIN_CTAS) attend_ker
 #pragma unroll
     for (int h = 0; h < G; ++h)
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[h][i] += __shfl_xor_sync(0xffffffffu, o[h][i], off);
+      for (int i = 0; i < P; ++i) {
+        o[h][i].x += __shfl_xor_sync(0xffffffffu, o[h][i].x, off);
+        o[h][i].y += __shfl_xor_sync(0xffffffffu, o[h][i].y, off);
+      }
   }
   // All consumers are past their last tile: every copy has landed, the stages are free.
   if (!ok) fail_flag = 1;
@@ -476,7 +520,11 @@ __global__ void __launch_bounds__(kDecodeThreads, FA_DECODE_MIN_CTAS) attend_ker
 #pragma unroll
     for (int h = 0; h < G; ++h)
 #pragma unroll
-      for (int i = 0; i < 8; ++i) red_o[(warp * G + h) * D + elem_of<D, KT>(sub, i)] = o[h][i];
+      for (int i = 0; i < P; ++i) {
+        float* at = red_o + (warp * G + h) * D + elem_of<D, KT, E>(sub, 2 * i);
+        at[0] = o[h][i].x;
+        at[1] = o[h][i].y;
+      }
   }
   named_sync(1, kConsumerWarps * 32);
 
@@ -531,20 +579,62 @@ __global__ void __launch_bounds__(kDecodeThreads, FA_DECODE_MIN_CTAS) attend_ker
   named_sync(1, kConsumerWarps * 32);
   if (!last_flag) return;
   __threadfence();
-  for (int idx = ctid; idx < count; idx += kConsumerWarps * 32) {
-    const int h = idx / D, e = idx % D;
-    const int64_t base = int64_t(part_base) * c.heads + (h0 + h);
+  // Each head's largest chunk max M and sum L = sum 2^(m - M) l, one warp per head over the
+  // chunks; then the outputs sum 2^(m - M) o over the chunks with the weights staged in shared
+  // memory (the stages are free), each thread's elements' loads of several chunks in flight.
+  __shared__ float merge_m[G], merge_l[G];
+  const int64_t base = int64_t(part_base) * c.heads + h0;  // slot of (chunk 0, head h0)
+  for (int h = warp; h < g; h += kConsumerWarps) {
     float mm = -INFINITY;
-    for (int ch = 0; ch < chunks; ++ch) mm = fmaxf(mm, __ldcg(&c.part_ml[2 * (base + int64_t(ch) * c.heads)]));
-    float ll = 0.0f, oo = 0.0f;
-    for (int ch = 0; ch < chunks; ++ch) {
-      const int64_t slot = base + int64_t(ch) * c.heads;
+    for (int ch = lane; ch < chunks; ch += 32)
+      mm = fmaxf(mm, __ldcg(&c.part_ml[2 * (base + int64_t(ch) * c.heads + h)]));
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, off));
+    float ll = 0.0f;
+    for (int ch = lane; ch < chunks; ch += 32) {
+      const int64_t slot = base + int64_t(ch) * c.heads + h;
       const float cm = __ldcg(&c.part_ml[2 * slot]);
       const float f = cm == -INFINITY ? 0.0f : exp2_approx(cm - mm);
       ll = fmaf(__ldcg(&c.part_ml[2 * slot + 1]), f, ll);
-      oo = fmaf(__ldcg(&c.part_o[slot * D + e]), f, oo);
     }
-    finish(h, e, mm, ll, oo);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) ll += __shfl_xor_sync(0xffffffffu, ll, off);
+    if (lane == 0) {
+      merge_m[h] = mm;
+      merge_l[h] = ll;
+    }
+  }
+  named_sync(1, kConsumerWarps * 32);
+  constexpr int kThreads = kConsumerWarps * 32;
+  constexpr int kPer = (G * D + kThreads - 1) / kThreads;  // output elements per thread
+  constexpr int kCap = int(size_t(kStages) * 2 * kTileBytes / (4 * G));  // chunks per block
+  float* wts = reinterpret_cast<float*>(smem);  // [chunk of the block][G]
+  float acc[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) acc[j] = 0.0f;
+  for (int cb = 0; cb < chunks; cb += kCap) {
+    const int nb = min(kCap, chunks - cb);
+    for (int i = ctid; i < nb * g; i += kThreads) {
+      const int k = i / g, h = i % g;
+      const float cm = __ldcg(&c.part_ml[2 * (base + int64_t(cb + k) * c.heads + h)]);
+      wts[k * G + h] = cm == -INFINITY ? 0.0f : exp2_approx(cm - merge_m[h]);
+    }
+    named_sync(1, kThreads);
+#pragma unroll 4
+    for (int k = 0; k < nb; ++k) {
+      const float* po = c.part_o + (base + int64_t(cb + k) * c.heads) * D;
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const int idx = ctid + j * kThreads;
+        if (idx < count) acc[j] = fmaf(__ldcg(&po[idx]), wts[k * G + idx / D], acc[j]);
+      }
+    }
+    named_sync(1, kThreads);
+  }
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int idx = ctid + j * kThreads;
+    if (idx < count) finish(idx / D, idx % D, merge_m[idx / D], merge_l[idx / D], acc[j]);
   }
 }
 

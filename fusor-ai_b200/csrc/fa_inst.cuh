@@ -10,7 +10,7 @@ namespace {
 template <int D, typename KT, int G, bool BATCH, typename Args>
 cudaError_t launch_one(const Args& args, int grid, cudaStream_t stream) {
   auto kernel = attend_kernel<D, KT, G, BATCH, Args>;
-  constexpr size_t smem = DecodeShape<D, KT>::kSmemBytes;
+  constexpr size_t smem = DecodeShape<D, KT, G>::kSmemBytes;
   static bool configured = false;  // per instantiation, per process
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
