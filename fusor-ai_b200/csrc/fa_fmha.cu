@@ -6,6 +6,7 @@
 #include <mutex>
 
 #include "fa_fmha.cuh"
+#include "fa_fmha2.cuh"
 #include "fa_fmha_launch.h"
 
 namespace fa {
@@ -71,6 +72,31 @@ cudaError_t launch_t(const FmhaLaunch& l, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+// bf16: two query tiles per CTA (fa_fmha2.cuh).
+template <int D>
+cudaError_t launch_bf16_pairs(const FmhaLaunch& l, cudaStream_t stream) {
+  using S = Fmha2Shape<D>;
+  CUtensorMap qm, km, vm;
+  if (!make_map(&qm, true, l.q, D, l.q_rows, l.q_heads, l.q_row_stride * 2, l.q_head_stride * 2,
+                S::kBlock, S::BM) ||
+      !make_map(&km, true, l.k, D, l.kv_rows, l.kv_z, l.kv_row_stride * 2, l.kv_z_stride * 2,
+                S::kBlock, S::BN) ||
+      !make_map(&vm, true, l.v, D, l.kv_rows, l.kv_z, l.kv_row_stride * 2, l.kv_z_stride * 2,
+                S::kBlock, S::BN))
+    return cudaErrorInvalidValue;
+  auto kernel = fmha2_kernel<D>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           int(S::kSmemBytes));
+    if (err != cudaSuccess) return err;
+    configured = true;
+  }
+  const dim3 grid(l.args.images * ((l.args.q_tiles + 1) / 2), l.args.heads);
+  kernel<<<grid, kFmha2Threads, S::kSmemBytes, stream>>>(qm, km, vm, l.args);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 bool fmha_supported(int dtype_bf16, int head_dim) {
@@ -84,8 +110,13 @@ int fmha_block_n(int dtype_bf16, int head_dim) {
 
 cudaError_t launch_fmha(const FmhaLaunch& l, cudaStream_t stream) {
   if (l.bf16) {
+#ifdef FA_FMHA_ONE_TILE
     if (l.head_dim == 64) return launch_t<__nv_bfloat16, 64>(l, stream);
     if (l.head_dim == 128) return launch_t<__nv_bfloat16, 128>(l, stream);
+#else
+    if (l.head_dim == 64) return launch_bf16_pairs<64>(l, stream);
+    if (l.head_dim == 128) return launch_bf16_pairs<128>(l, stream);
+#endif
   } else {
     if (l.head_dim == 64) return launch_t<float, 64>(l, stream);
     if (l.head_dim == 128) return launch_t<float, 128>(l, stream);

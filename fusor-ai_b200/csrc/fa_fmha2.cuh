@@ -1,0 +1,364 @@
+// The bf16 tensor-core attention with two query tiles per CTA in ping-pong (prefill over a bf16
+// cache and bf16 full-mask calls; the same semantics as fmha_kernel, fa_fmha.cuh).
+//
+// One CTA = 2 x 128 query rows of one query head. Warp roles:
+//   warp 0      TMA producer: both Q tiles once, then K and V tiles into a 2-stage ring;
+//   warp 1      TMEM owner and MMA issuer (one thread);
+//   warps 2-5   softmax of query tile 0 (thread = one row, TMEM lane (warp % 4) * 32 + lane);
+//   warps 6-9   softmax of query tile 1.
+// TMEM: S0 | O0 | S1 | O1, 128 columns each (P_i overwrites S_i as bf16 pairs). The MMA order per
+// KV tile j is PV0_j, S0_{j+1}, PV1_j, S1_{j+1}: while one softmax group works on its S, the
+// tensor core runs the other group's two products, so the exponentials of one tile overlap the
+// matrix products of the other (one S buffer per tile suffices: the tensor core executes one
+// thread's MMAs in issue order, so PV_i reads P_i before S_i is written again).
+// A query tile takes part in the KV tiles its rows see (the union of their key runs); the other
+// tile's barriers count only its own participating tiles.
+#pragma once
+
+#include "fa_fmha.cuh"
+
+namespace fa {
+
+template <int D>
+struct Fmha2Shape {
+  static constexpr int BM = 128;   // rows of one query tile
+  static constexpr int BN = 128;   // keys per KV tile
+  static constexpr int kBlock = 64;  // bf16 elements per swizzled 128-byte row
+  static constexpr int kDBlocks = D / kBlock;
+  static constexpr int kKStep = 16;  // bf16 elements per MMA K step
+  static constexpr int kStages = 2;
+  static constexpr int kQBytes = BM * D * 2;
+  static constexpr int kKVBytes = BN * D * 2;
+  static constexpr int kTileCols = 256;  // TMEM columns of one query tile: S (128) then O
+  static constexpr size_t kSmemUsed =
+      size_t(2 * kQBytes) + size_t(kStages) * 2 * kKVBytes + 1024 /* alignment */ + 256;
+  // At least 120 KB so that one CTA holds an SM: each CTA allocates all 512 TMEM columns.
+  static constexpr size_t kSmemBytes = kSmemUsed > 122880 ? kSmemUsed : 122880;
+  static_assert(D == 64 || D == 128, "head_dim 64 or 128");
+};
+
+constexpr int kFmha2Threads = 320;
+
+template <int D>
+__global__ void __launch_bounds__(kFmha2Threads, 1)
+    fmha2_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
+                 const __grid_constant__ CUtensorMap v_map, const __grid_constant__ FmhaArgs a) {
+  using S = Fmha2Shape<D>;
+  constexpr int BM = S::BM, BN = S::BN;
+  constexpr uint32_t kIdescQK = tc::instr_desc(1u, false, BN, BM);
+  constexpr uint32_t kIdescPV = tc::instr_desc(1u, true, D, BM);
+
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* sQ = smem;  // tile i at sQ + i * kQBytes
+  unsigned char* sK = sQ + 2 * S::kQBytes;
+  unsigned char* sV = sK + S::kStages * S::kKVBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + S::kStages * S::kKVBytes);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = k_full + S::kStages;
+  uint64_t* v_full = k_empty + S::kStages;
+  uint64_t* v_empty = v_full + S::kStages;
+  uint64_t* s_full = v_empty + S::kStages;  // [query tile]
+  uint64_t* p_full = s_full + 2;            // [query tile]
+  uint64_t* o_done = p_full + 2;            // [query tile]
+  uint64_t* o_final = o_done + 2;           // [query tile]: its last P.V has completed
+  uint64_t* mma_drained = o_final + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_drained + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int head = blockIdx.y;
+  const int kv = head / a.group;
+  const int pairs = (a.q_tiles + 1) / 2;
+  // heavier (later, for causal masks) tiles first
+  const int pair_id = int(gridDim.x) - 1 - int(blockIdx.x);
+  const int image = pair_id / pairs;
+  const int r0 = (pair_id % pairs) * 2 * BM;  // first row of query tile 0
+
+  // KV tiles each query tile's rows see (the union of their key runs), and their union.
+  int tb[2], te[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int first_row = r0 + i * BM;
+    const int last_row = min(first_row + BM, a.rows) - 1;
+    if (first_row >= a.rows) { tb[i] = te[i] = 0; continue; }
+    const Runs fr = mask_runs(a.kind, a.window, a.state, a.n_ends, a.ends, a.first + first_row, a.end);
+    const Runs lr = mask_runs(a.kind, a.window, a.state, a.n_ends, a.ends, a.first + last_row, a.end);
+    int lo = fr.b0, hi = max(lr.b0 + lr.n0, lr.b1 + lr.n1);
+    if (a.kind == 3) { lo = 0; hi = a.end; }  // Groups: every run lies in [0, end)
+    tb[i] = lo / BN;
+    te[i] = hi > lo ? (hi + BN - 1) / BN : tb[i];
+  }
+  const bool any0 = te[0] > tb[0], any1 = te[1] > tb[1];
+  const int t0 = any0 && any1 ? min(tb[0], tb[1]) : (any0 ? tb[0] : tb[1]);
+  const int t_end = any0 && any1 ? max(te[0], te[1]) : (any0 ? te[0] : te[1]);
+  const int n_tiles = (any0 || any1) ? t_end - t0 : 0;
+  auto part = [&](int i, int L) {  // query tile i takes part in union tile L
+    const int t = t0 + L;
+    return t >= tb[i] && t < te[i];
+  };
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < S::kStages; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_done[i], 1);
+      mbar_init(&o_final[i], 1);
+    }
+    mbar_init(mma_drained, 1);
+    mbar_fence_init();
+  }
+  if (warp == 1) tc::tmem_alloc(tmem_slot, 512);
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---- TMA producer --------------------------------------------------------------------
+    if (lane == 0) {
+      tc::tma_prefetch_map(&q_map);
+      tc::tma_prefetch_map(&k_map);
+      tc::tma_prefetch_map(&v_map);
+      mbar_arrive_expect_tx(q_full, 2 * S::kQBytes);
+      const int qy = image * a.q_row_base_per_image + r0;
+      for (int i = 0; i < 2; ++i)
+        for (int db = 0; db < S::kDBlocks; ++db)
+          tc::tma_load_3d(sQ + i * S::kQBytes + db * BM * 128, &q_map, db * S::kBlock, qy + i * BM,
+                          head, q_full);
+      const int kz = a.kv_layer_base + kv;
+      const int ky0 = image * a.kv_row_base_per_image;
+      int issued = 0;
+      for (int L = 0; L < n_tiles; ++L) {
+        const int st = L % S::kStages;
+        const uint32_t ph = ((L / S::kStages) & 1) ^ 1;
+        const int ky = ky0 + (t0 + L) * BN;
+        if (!mbar_wait(&k_empty[st], ph, a.err)) break;
+        mbar_arrive_expect_tx(&k_full[st], S::kKVBytes);
+        for (int db = 0; db < S::kDBlocks; ++db)
+          tc::tma_load_3d(sK + st * S::kKVBytes + db * BN * 128, &k_map, db * S::kBlock, ky, kz,
+                          &k_full[st]);
+        if (!mbar_wait(&v_empty[st], ph, a.err)) break;
+        mbar_arrive_expect_tx(&v_full[st], S::kKVBytes);
+        for (int db = 0; db < S::kDBlocks; ++db)
+          tc::tma_load_3d(sV + st * S::kKVBytes + db * BN * 128, &v_map, db * S::kBlock, ky, kz,
+                          &v_full[st]);
+        issued = L + 1;
+      }
+      // The loads still in flight land before the CTA may exit.
+      mbar_wait(q_full, 0, a.err);
+      for (int L = max(0, issued - S::kStages); L < issued; ++L) {
+        mbar_wait(&k_full[L % S::kStages], (L / S::kStages) & 1, a.err);
+        mbar_wait(&v_full[L % S::kStages], (L / S::kStages) & 1, a.err);
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer ----------------------------------------------------------------------
+    if (lane == 0) {
+      const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV);
+      bool ok = mbar_wait(q_full, 0, a.err);
+      int pv_count[2] = {0, 0};
+      auto issue_s = [&](int i, int L) {
+        const int st = L % S::kStages;
+#pragma unroll
+        for (int k = 0; k < D / S::kKStep; ++k) {
+          const int db = k / 4, koff = (k % 4) * 32;
+          const uint64_t qd =
+              tc::smem_desc_sw128(q_base + i * S::kQBytes + db * BM * 128 + koff, 16, 1024);
+          const uint64_t kd =
+              tc::smem_desc_sw128(k_base + st * S::kKVBytes + db * BN * 128 + koff, 16, 1024);
+          tc::mma_ss<false>(tmem + i * S::kTileCols, qd, kd, kIdescQK, k > 0 ? 1u : 0u);
+        }
+        tc::commit(&s_full[i]);
+      };
+      auto issue_pv = [&](int i, int L) {
+        const int st = L % S::kStages;
+        const int c = pv_count[i];
+        if (!mbar_wait(&p_full[i], c & 1, a.err)) return false;
+        if (!mbar_wait(&v_full[st], (L / S::kStages) & 1, a.err)) return false;
+        tc::fence_after_sync();
+        const uint32_t p_tmem = tmem + i * S::kTileCols;
+#pragma unroll
+        for (int k = 0; k < BN / S::kKStep; ++k) {
+          const uint64_t vd = tc::smem_desc(v_base + st * S::kKVBytes + k * S::kKStep * 128,
+                                            BN * 128, 1024, tc::kSwizzle128B);
+          tc::mma_ts<false>(tmem + i * S::kTileCols + 128, p_tmem + k * 8, vd, kIdescPV,
+                            (c > 0 || k > 0) ? 1u : 0u);
+        }
+        tc::commit(&o_done[i]);
+        pv_count[i] = c + 1;
+        return true;
+      };
+      if (ok && n_tiles > 0) {
+        ok = mbar_wait(&k_full[0], 0, a.err);
+        if (ok) {
+          tc::fence_after_sync();
+          if (part(0, 0)) issue_s(0, 0);
+          if (part(1, 0)) issue_s(1, 0);
+          tc::commit(&k_empty[0]);
+        }
+      }
+      for (int L = 0; ok && L < n_tiles; ++L) {
+        const bool next = L + 1 < n_tiles;
+        if (next) {
+          const int sn = (L + 1) % S::kStages;
+          if (!mbar_wait(&k_full[sn], ((L + 1) / S::kStages) & 1, a.err)) { ok = false; break; }
+          tc::fence_after_sync();
+        }
+        if (part(0, L) && !issue_pv(0, L)) { ok = false; break; }
+        if (next && part(0, L + 1)) issue_s(0, L + 1);
+        if (part(1, L) && !issue_pv(1, L)) { ok = false; break; }
+        if (next && part(1, L + 1)) issue_s(1, L + 1);
+        if (next) tc::commit(&k_empty[(L + 1) % S::kStages]);
+        tc::commit(&v_empty[L % S::kStages]);
+      }
+      if (ok) {
+        if (pv_count[0] > 0) tc::commit(&o_final[0]);
+        if (pv_count[1] > 0) tc::commit(&o_final[1]);
+      }
+      // Every MMA this thread issued has completed before the CTA may free TMEM.
+      tc::commit(mma_drained);
+      mbar_wait(mma_drained, 0, a.err);
+    }
+  } else {
+    // ---- softmax + epilogue of query tile i ----------------------------------------------
+    const int i = warp < 6 ? 0 : 1;
+    const int wq = warp & 3;  // the TMEM lane quarter this warp may access
+    const int r = r0 + i * BM + wq * 32 + lane;  // this thread's query row within the image
+    const bool row_valid = r < a.rows;
+    const Runs runs = mask_runs(a.kind, a.window, a.state, a.n_ends, a.ends, a.first + r, a.end);
+    const uint32_t lane_base = tmem + i * S::kTileCols + (uint32_t(wq * 32) << 16);
+    const uint32_t o_base = lane_base + 128;
+    float m_used = -INFINITY, l_sum = 0.0f;
+    bool ok = true;
+    int c = 0;  // this tile's participating KV tiles so far
+    for (int L = 0; L < n_tiles; ++L) {
+      if (!part(i, L)) continue;
+      const int kp = (t0 + L) * BN;  // first key position of the tile
+      // Every decision before a whole-warp tcgen05 instruction is made warp-uniform.
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[i], c & 1, a.err))) { ok = false; break; }
+      tc::fence_after_sync();
+      uint32_t sreg[BN];
+      tc::tmem_ld128_wait(lane_base, sreg);
+      float* s = reinterpret_cast<float*>(sreg);
+      const bool all_in = row_valid &&
+                          ((kp >= runs.b0 && kp + BN <= runs.b0 + runs.n0) ||
+                           (kp >= runs.b1 && kp + BN <= runs.b1 + runs.n1));
+      if (!all_in) {
+#pragma unroll
+        for (int cc = 0; cc < BN; ++cc) {
+          const int key = kp + cc;
+          const bool vis = row_valid && ((key >= runs.b0 && key < runs.b0 + runs.n0) ||
+                                         (key >= runs.b1 && key < runs.b1 + runs.n1));
+          if (!vis) s[cc] = -INFINITY;
+        }
+      }
+      // the tile's max in four independent chains
+      float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
+#pragma unroll
+      for (int cc = 4; cc < BN; cc += 4) {
+        mx0 = fmaxf(mx0, s[cc]);
+        mx1 = fmaxf(mx1, s[cc + 1]);
+        mx2 = fmaxf(mx2, s[cc + 2]);
+        mx3 = fmaxf(mx3, s[cc + 3]);
+      }
+      const float m_tile = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * a.scale_log2;
+      // Lazy rescale: move the reference max only when the tile's max exceeds it by 2^8 (the
+      // first finite max just sets it: nothing has accumulated for the row yet).
+      float alpha = 1.0f;
+      if (m_tile > m_used + 8.0f || (m_used == -INFINITY && m_tile > -INFINITY)) {
+        if (m_used > -INFINITY) alpha = exp2_approx(m_used - m_tile);
+        m_used = m_tile;
+      }
+      const float ms = m_used == -INFINITY ? 0.0f : m_used;
+      const float2 scale2 = make_float2(a.scale_log2, a.scale_log2);
+      const float2 neg2 = make_float2(-ms, -ms);
+      float2 sum2a = make_float2(0.0f, 0.0f), sum2b = make_float2(0.0f, 0.0f);
+      // pairs of probabilities packed in place: sreg[cc / 2] is written only after s[cc] and
+      // s[cc + 1] are read
+#pragma unroll
+      for (int cc = 0; cc < BN; cc += 4) {
+        const float2 x0 = __ffma2_rn(make_float2(s[cc], s[cc + 1]), scale2, neg2);
+        const float2 x1 = __ffma2_rn(make_float2(s[cc + 2], s[cc + 3]), scale2, neg2);
+        const float2 p0 = make_float2(exp2_approx(x0.x), exp2_approx(x0.y));
+        const float2 p1 = make_float2(exp2_approx(x1.x), exp2_approx(x1.y));
+        sum2a = __fadd2_rn(sum2a, p0);
+        sum2b = __fadd2_rn(sum2b, p1);
+        sreg[cc / 2] = tc::pack_bf16(p0.x, p0.y);
+        sreg[cc / 2 + 1] = tc::pack_bf16(p1.x, p1.y);
+      }
+#pragma unroll
+      for (int cc = 0; cc < BN / 64; ++cc)
+        tc::tmem_st32(lane_base + cc * 32, *reinterpret_cast<const uint32_t(*)[32]>(&sreg[cc * 32]));
+      l_sum = l_sum * alpha + ((sum2a.x + sum2a.y) + (sum2b.x + sum2b.y));
+      if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+        // O_i holds the products of this tile's earlier KV tiles. S_i of this KV tile has
+        // completed, and with it (issue order) the P.V of the previous one: o_done[i] is in
+        // that phase, and the next cannot start before this group's P is written. (Done after
+        // P is written, so that the S row's registers are free for O's.)
+        if (!__all_sync(0xffffffffu, mbar_wait(&o_done[i], (c - 1) & 1, a.err))) { ok = false; break; }
+        tc::fence_after_sync();
+#pragma unroll 1
+        for (int cc = 0; cc < D / 32; ++cc) {
+          uint32_t o[32];
+          tc::tmem_ld32_wait(o_base + cc * 32, o);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tc::tmem_st32(o_base + cc * 32, o);
+          tc::tmem_wait_st();  // the registers are free again only after the store lands
+        }
+      }
+      tc::tmem_wait_st();
+      tc::fence_before_sync();
+      mbar_arrive(&p_full[i]);
+      ++c;
+    }
+    // ---- epilogue: O / l -------------------------------------------------------------------
+    if (__all_sync(0xffffffffu, ok && c > 0 && mbar_wait(&o_final[i], 0, a.err))) {
+      tc::fence_after_sync();
+      const float inv = l_sum > 0.0f ? 1.0f / l_sum : 0.0f;
+      const int64_t orow = int64_t(image) * a.rows + r;
+#pragma unroll 1
+      for (int cc = 0; cc < D / 32; ++cc) {
+        uint32_t o[32];
+        tc::tmem_ld32_wait(o_base + cc * 32, o);
+        if (!row_valid) continue;
+        if (a.out_bf16) {
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) +
+                                                orow * a.out_stride + head * D + cc * 32);
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            dst[e] = make_uint4(
+                tc::pack_bf16(__uint_as_float(o[8 * e + 0]) * inv, __uint_as_float(o[8 * e + 1]) * inv),
+                tc::pack_bf16(__uint_as_float(o[8 * e + 2]) * inv, __uint_as_float(o[8 * e + 3]) * inv),
+                tc::pack_bf16(__uint_as_float(o[8 * e + 4]) * inv, __uint_as_float(o[8 * e + 5]) * inv),
+                tc::pack_bf16(__uint_as_float(o[8 * e + 6]) * inv, __uint_as_float(o[8 * e + 7]) * inv));
+        } else {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) +
+                                                  orow * a.out_stride + head * D + cc * 32);
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            dst[e] = make_float4(__uint_as_float(o[4 * e]) * inv, __uint_as_float(o[4 * e + 1]) * inv,
+                                 __uint_as_float(o[4 * e + 2]) * inv, __uint_as_float(o[4 * e + 3]) * inv);
+        }
+      }
+    }
+  }
+
+  // ---- teardown: every TMEM user is done before the owner frees it ---------------------------
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace fa
