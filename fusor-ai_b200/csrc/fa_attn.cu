@@ -227,14 +227,20 @@ struct Plan {
   int g = 1, hgroups = 1, kv_groups = 1, chunks = 1;
 };
 
-Plan plan_span(const fa_kvcache* c, int rows, int max_keys) {
+Plan plan_span(const fa_kvcache* c, int rows, int max_keys, bool split_small = true) {
   Plan p;
   const int group = c->heads / c->kv_heads;
   p.g = pow2_heads(group);
-  p.hgroups = (group + p.g - 1) / p.g;
-  p.kv_groups = c->kv_heads * p.hgroups;
   const int tile = fa::tile_keys(c->head_dim, c->dtype == FA_F32 ? fa::kKtF32 : fa::kKtBf16);
   const int max_chunks = std::max(1, (max_keys + tile - 1) / tile);
+  // A launch too small for a CTA on every SM (a short decode, C1's 1025 keys) splits each KV
+  // head's query heads over more CTAs: each re-reads the KV head, from L2 at these sizes.
+  auto units = [&](int g) {
+    return int64_t(rows) * c->kv_heads * ((group + g - 1) / g) * max_chunks;
+  };
+  while (split_small && p.g > 2 && units(p.g / 2) <= c->dev->sms) p.g /= 2;
+  p.hgroups = (group + p.g - 1) / p.g;
+  p.kv_groups = c->kv_heads * p.hgroups;
   const int want = (target_units(c->dev) + rows * p.kv_groups - 1) / std::max(rows * p.kv_groups, 1);
   p.chunks = std::min(max_chunks, std::max(1, want));
   return p;
@@ -340,7 +346,10 @@ int attend_rows(fa_kvcache* c, int layer, const fa_span* span, const std::vector
 
 // Rows from which a span goes to the tensor-core kernel (below it the split-KV kernel, which
 // needs no 128-row tiles, is as fast).
-constexpr int kFmhaMinRows = 64;
+#ifndef FA_TC_MIN_ROWS
+#define FA_TC_MIN_ROWS 64
+#endif
+constexpr int kFmhaMinRows = FA_TC_MIN_ROWS;
 
 // Whether a span over the cache runs on the tcgen05 kernel: head_dim 64 or 128, enough rows,
 // and no key position wraps the cache's ring (a causal or full span never does; a window span
@@ -587,7 +596,9 @@ int fa_kvcache_reserve(fa_kvcache* cache, int32_t rows) {
                            size_t(rows) * p.chunks * cache->heads, 0, nullptr, &w))
     return rc;
   if (int rc = cache->staging.ensure(staging, nullptr)) return rc;
-  if (int rc = ensure_counters(cache, size_t(rows) * p.kv_groups, nullptr)) return rc;
+  // a short span may split a KV head's query heads over several CTAs: a counter per query head
+  // covers every split
+  if (int rc = ensure_counters(cache, size_t(rows) * cache->heads, nullptr)) return rc;
   FA_CUDA(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
   return FA_OK;
 }
@@ -919,7 +930,7 @@ int fa_attend_batch(fa_kvcache* const* caches, const fa_span* spans, int32_t bat
   if (q_stride < width || out_stride < width) return fail(FA_ERR_SHAPE, "row strides below heads x head_dim");
   DeviceGuard guard(c0->device);
   auto s = static_cast<cudaStream_t>(stream);
-  const Plan base = plan_span(c0, 1, 1);
+  const Plan base = plan_span(c0, 1, 1, false);
   const int tile = fa::tile_keys(c0->head_dim, c0->dtype == FA_F32 ? fa::kKtF32 : fa::kKtBf16);
   const int64_t want = target_units(c0->dev);
   int64_t chunk_keys = (total_keys * base.kv_groups + want - 1) / want;

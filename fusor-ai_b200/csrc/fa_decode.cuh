@@ -308,6 +308,7 @@ __global__ void __launch_bounds__(kDecodeThreads, (DecodeShape<D, KT, G>::kMinCt
   if (warp == kConsumerWarps) {
     // ---- producer: one elected lane streams the chunk's K/V rows -----------------------------
     if (lane == 0) {
+      pdl_wait();  // the keys and values kept by the kernel before this one
       const uint64_t policy = policy_evict_first();
       int issued = 0;
       for (int t = 0; t < tiles; ++t) {
@@ -364,6 +365,7 @@ __global__ void __launch_bounds__(kDecodeThreads, (DecodeShape<D, KT, G>::kMinCt
 
   constexpr int P = E / 2;  // f32 pairs per lane
   float2 q[G][P];
+  pdl_wait();  // the rotated queries written by the kernel before this one
   const float* qrow = c.q + int64_t(row) * c.q_stride;
 #pragma unroll
   for (int h = 0; h < G; ++h)

@@ -7,6 +7,7 @@
 
 #include "fa_fmha.cuh"
 #include "fa_fmha2.cuh"
+#include "fa_launch.cuh"
 #include "fa_fmha_launch.h"
 
 namespace fa {
@@ -68,8 +69,7 @@ cudaError_t launch_t(const FmhaLaunch& l, cudaStream_t stream) {
     configured = true;
   }
   const dim3 grid(l.args.images * l.args.q_tiles, l.args.heads);
-  kernel<<<grid, kFmhaThreads, S::kSmemBytes, stream>>>(qm, km, vm, l.args);
-  return cudaGetLastError();
+  return launch_pdl(kernel, grid, dim3(kFmhaThreads), S::kSmemBytes, stream, qm, km, vm, l.args);
 }
 
 // bf16: two query tiles per CTA (fa_fmha2.cuh).
@@ -93,8 +93,7 @@ cudaError_t launch_bf16_pairs(const FmhaLaunch& l, cudaStream_t stream) {
     configured = true;
   }
   const dim3 grid(l.args.images * ((l.args.q_tiles + 1) / 2), l.args.heads);
-  kernel<<<grid, kFmha2Threads, S::kSmemBytes, stream>>>(qm, km, vm, l.args);
-  return cudaGetLastError();
+  return launch_pdl(kernel, grid, dim3(kFmha2Threads), S::kSmemBytes, stream, qm, km, vm, l.args);
 }
 
 }  // namespace

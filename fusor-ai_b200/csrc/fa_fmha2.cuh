@@ -127,6 +127,7 @@ __global__ void __launch_bounds__(kFmha2Threads, 1)
       tc::tma_prefetch_map(&q_map);
       tc::tma_prefetch_map(&k_map);
       tc::tma_prefetch_map(&v_map);
+      pdl_wait();  // the queries (and a cache's kept rows) written by the kernel before this one
       mbar_arrive_expect_tx(q_full, 2 * S::kQBytes);
       const int qy = image * a.q_row_base_per_image + r0;
       for (int i = 0; i < 2; ++i)

@@ -18,8 +18,7 @@ cudaError_t launch_one(const Args& args, int grid, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  kernel<<<grid, kDecodeThreads, smem, stream>>>(args);
-  return cudaGetLastError();
+  return launch_pdl(kernel, dim3(grid), dim3(kDecodeThreads), smem, stream, args);
 }
 
 template <int D, typename KT, int G>

@@ -4,10 +4,31 @@
 
 #include <cuda_runtime.h>
 
+#include <utility>
+
 #include "fa_decode.cuh"
 #include "fa_rope.cuh"
 
 namespace fa {
+
+// Launches `kernel` with programmatic stream serialization: its CTAs may be scheduled while the
+// previous kernel of the stream (the RoPE + keep kernel, which triggers early) finishes; the
+// kernel waits (pdl_wait) before it reads what that kernel wrote.
+template <typename... Params, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 constexpr int kKtF32 = 0;
 constexpr int kKtBf16 = 1;

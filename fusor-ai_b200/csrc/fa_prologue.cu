@@ -170,6 +170,7 @@ __device__ __forceinline__ void copy_values_row(const PrologueArgs& a, int token
 
 template <typename O>
 __global__ void __launch_bounds__(kPrologueWarps * 32) prologue_kernel(const PrologueArgs a) {
+  pdl_trigger();  // the attention kernel after it may be scheduled now (it waits for this one)
   const int lane = threadIdx.x & 31;
   const int64_t item = int64_t(blockIdx.x) * kPrologueWarps + (threadIdx.x >> 5);
   if (item >= int64_t(a.tokens) * a.parts) return;

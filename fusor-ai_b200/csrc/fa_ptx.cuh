@@ -95,6 +95,16 @@ __device__ __forceinline__ void bulk_g2s_hint(void* smem_dst, const void* gmem_s
 }
 
 // An L2 policy that evicts streamed data first (each K/V byte is read once per launch).
+// Programmatic dependent launch: a kernel launched with programmatic stream serialization may
+// start while the kernel before it in the stream still runs; pdl_wait() blocks the calling
+// thread until that kernel has completed and its memory is visible (at once when there is no
+// such kernel). pdl_trigger() lets the next kernel of the stream start early (a no-op when it
+// was launched without the attribute).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t policy;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));

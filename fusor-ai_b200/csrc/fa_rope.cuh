@@ -58,6 +58,7 @@ __device__ __forceinline__ __nv_bfloat16 to_kv<__nv_bfloat16>(float x) {
 
 template <typename KT>
 __global__ void __launch_bounds__(kRopeWarps * 32) rope_keep_kernel(const __grid_constant__ RopeArgs a) {
+  pdl_trigger();  // the attention kernel after it may be scheduled now (it waits for this one)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x;
   const int unit = blockIdx.y * kRopeWarps + warp;
