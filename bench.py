@@ -372,7 +372,7 @@ class C5Full(Workload):
         from fusor_attn.shard import head_tile_units
         self.torch, self.fa, self.name = torch, fa, "c5"
         self.sharded = True
-        self.kernel = "fmha_kernel"
+        self.kernel = "fmha2_kernel"  # bf16: two query tiles per CTA
         self.heads, self.d, self.n = 12, 128, 32760
         hidden = self.heads * self.d
         gen = torch.Generator("cuda").manual_seed(5)
