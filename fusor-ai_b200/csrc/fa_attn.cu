@@ -12,12 +12,14 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <queue>
 #include <string>
 #include <vector>
 
 #include "fa_attn.h"
 #include "fa_fmha_launch.h"
 #include "fa_launch.cuh"
+#include "fa_decode_tc.h"
 #include "fa_relpos.h"
 
 namespace {
@@ -122,6 +124,7 @@ struct fa_kvcache {
   Buffer work;       // queries and partials
   Buffer staging;    // fa_attention_host's device copies of the host rows
   Buffer counters;   // arrival counters (kept zero between launches)
+  Buffer tc_maps;    // bf16, head_dim 128: TMA maps over the keys and values (tensor-core decode)
   int counters_epoch = 0;
   size_t elem() const { return dtype == FA_F32 ? 4 : 2; }
   int64_t layer_elems() const { return int64_t(kv_heads) * capacity * head_dim; }
@@ -552,6 +555,26 @@ int fa_kvcache_create(int32_t layers, int32_t heads, int32_t kv_heads, int32_t h
     fa_kvcache_destroy(c);
     return cuda_fail(e, "cache allocation");
   }
+  if (dtype == FA_BF16 && head_dim == 128) {
+    // TMA maps of the keys and values for the tensor-core decode, made once: [layers x kv heads]
+    // [capacity][128] (a cache that cannot have them decodes on the CUDA cores)
+    alignas(64) unsigned char maps[256];
+    const uint64_t z_stride = uint64_t(capacity) * 128 * 2;
+    if (fa::encode_cache_map_bf16(maps, c->keys, uint64_t(capacity), uint64_t(layers) * kv_heads,
+                                  z_stride) &&
+        fa::encode_cache_map_bf16(maps + 128, c->values, uint64_t(capacity),
+                                  uint64_t(layers) * kv_heads, z_stride)) {
+      e = cudaMalloc(&c->tc_maps.ptr, sizeof(maps));
+      if (e == cudaSuccess) {
+        c->tc_maps.bytes = sizeof(maps);
+        e = cudaMemcpy(c->tc_maps.ptr, maps, sizeof(maps), cudaMemcpyHostToDevice);
+      }
+      if (e != cudaSuccess) {
+        fa_kvcache_destroy(c);
+        return cuda_fail(e, "cache tensor maps");
+      }
+    }
+  }
   *out = c;
   return FA_OK;
 }
@@ -564,6 +587,7 @@ int fa_kvcache_destroy(fa_kvcache* cache) {
   cache->work.release();
   cache->staging.release();
   cache->counters.release();
+  cache->tc_maps.release();
   delete cache;
   return FA_OK;
 }
@@ -915,6 +939,135 @@ int fa_attention_input_batch(fa_kvcache* const* caches, const fa_span* spans, in
   return FA_OK;
 }
 
+}  // extern "C"
+
+namespace {
+
+// Whether a batch of one-row decodes runs on the tensor cores: bf16 caches of head_dim 128 with
+// their TMA maps, at most 16 query heads per KV head, and every row's keys one run of cache slots
+// without a ring wrap (a window that wraps, or Groups' two runs, decode on the CUDA cores).
+#ifndef FA_DECODE_TC
+#define FA_DECODE_TC 1
+#endif
+bool decode_on_tensor_cores(fa_kvcache* const* caches, const std::vector<fa::Runs>& runs,
+                            int batch) {
+  if (!FA_DECODE_TC) return false;
+  const fa_kvcache* c0 = caches[0];
+  if (c0->dtype != FA_BF16 || c0->head_dim != 128 || c0->heads / c0->kv_heads > fa::kDtcN)
+    return false;
+  for (int i = 0; i < batch; ++i) {
+    const fa_kvcache* c = caches[i];
+    if (c->tc_maps.ptr == nullptr || runs[i].n1 != 0 || runs[i].n0 < 1 ||
+        runs[i].b0 + runs[i].n0 > c->capacity)
+      return false;
+  }
+  return true;
+}
+
+// The tensor-core decode of a batch: chunks of a common length (a multiple of 128 keys) so that
+// the persistent CTAs (one per SM) each take about four (row, KV head, chunk) units.
+int attend_batch_tc(fa_kvcache* const* caches, const std::vector<fa::Runs>& runs, int batch,
+                    int layer, const float* q, int64_t q_stride, float* out, int64_t out_stride,
+                    cudaStream_t s) {
+  fa_kvcache* c0 = caches[0];
+  int64_t total_keys = 0;
+  for (int i = 0; i < batch; ++i) total_keys += runs[i].n0;
+  const int sms = std::max(1, std::min(c0->dev->sms, fa::kDtcMaxCtas));
+  // about six units per CTA (the schedule below balances them), at most kDtcMaxUnits a launch
+  int64_t want = int64_t(sms) * 6;
+  int64_t chunk_keys = 0;
+  for (;; want = want * 3 / 4) {
+    chunk_keys = (total_keys * c0->kv_heads + want - 1) / want;
+    chunk_keys = std::max<int64_t>(fa::kDtcKeys, (chunk_keys + fa::kDtcKeys - 1) / fa::kDtcKeys * fa::kDtcKeys);
+    int64_t units = 0;
+    for (int i = 0; i < std::min(batch, fa::kMaxBatchRows); ++i)
+      units += c0->kv_heads * ((runs[i].n0 + chunk_keys - 1) / chunk_keys);
+    if (units <= fa::kDtcMaxUnits || want <= 1) break;
+  }
+  std::vector<int> chunks(batch), part_base(batch);
+  int64_t slots = 0;
+  for (int i = 0; i < batch; ++i) {
+    chunks[i] = int((runs[i].n0 + chunk_keys - 1) / chunk_keys);
+    part_base[i] = int(slots);
+    slots += chunks[i];
+  }
+  Work w;
+  if (int rc = ensure_work(c0, 0, size_t(slots) * c0->heads, 0, s, &w)) return rc;
+  if (int rc = ensure_counters(c0, size_t(batch) * c0->kv_heads, s)) return rc;
+  for (int first = 0; first < batch; first += fa::kMaxBatchRows) {
+    const int n = std::min(batch - first, fa::kMaxBatchRows);
+    fa::DtcArgs a{};
+    a.heads = c0->heads;
+    a.kv_heads = c0->kv_heads;
+    a.group = c0->heads / c0->kv_heads;
+    a.n_rows = n;
+    a.chunk_keys = int(chunk_keys);
+    a.q = q + int64_t(first) * q_stride;
+    a.q_stride = q_stride;
+    a.scale_log2 = query_scale(c0->head_dim);
+    a.out = out + int64_t(first) * out_stride;
+    a.out_stride = out_stride;
+    a.part_o = w.part_o;
+    a.part_ml = w.part_ml;
+    a.counters = static_cast<int*>(c0->counters.ptr) + int64_t(first) * c0->kv_heads;
+    a.err = c0->dev->err;
+    int units = 0;
+    for (int i = 0; i < n; ++i) {
+      const fa_kvcache* c = caches[first + i];
+      fa::DtcRow& r = a.rows[i];
+      r.kmap = c->tc_maps.ptr;
+      r.vmap = static_cast<const unsigned char*>(c->tc_maps.ptr) + 128;
+      r.z0 = layer * c->kv_heads;
+      r.b0 = runs[first + i].b0;
+      r.n = runs[first + i].n0;
+      r.chunks = chunks[first + i];
+      r.unit_begin = units;
+      r.part_base = part_base[first + i];
+      units += c0->kv_heads * r.chunks;
+    }
+    a.n_units = units;
+    // Longest processing time first: the units by tiles, longest first (a counting sort), each
+    // to the least loaded CTA (a heap); each CTA's list keeps that order.
+    const int ctas = std::min(units, sms);
+    const int max_tiles = int((chunk_keys + fa::kDtcKeys - 1) / fa::kDtcKeys);
+    std::vector<int> unit_tiles(units), count(max_tiles + 2, 0);
+    for (int i = 0, u = 0; i < n; ++i) {
+      const int64_t nk = a.rows[i].n;
+      for (int k = 0; k < c0->kv_heads; ++k)
+        for (int ch = 0; ch < a.rows[i].chunks; ++ch, ++u) {
+          const int64_t keys = std::min<int64_t>(nk, int64_t(ch + 1) * chunk_keys) - int64_t(ch) * chunk_keys;
+          unit_tiles[u] = int((keys + fa::kDtcKeys - 1) / fa::kDtcKeys);
+          ++count[max_tiles - unit_tiles[u]];
+        }
+    }
+    for (int t = 1; t <= max_tiles + 1; ++t) count[t] += count[t - 1];
+    std::vector<int> sorted(units);
+    for (int u = units - 1; u >= 0; --u) sorted[--count[max_tiles - unit_tiles[u]]] = u;
+    using Load = std::pair<int64_t, int>;  // (tiles assigned, CTA)
+    std::priority_queue<Load, std::vector<Load>, std::greater<Load>> heap;
+    for (int c = 0; c < ctas; ++c) heap.push({0, c});
+    std::vector<int> owner(units), per_cta(ctas + 1, 0);
+    for (int u : sorted) {
+      Load l = heap.top();
+      heap.pop();
+      owner[u] = l.second;
+      ++per_cta[l.second + 1];
+      l.first += unit_tiles[u] + 1;  // a unit's own start and end cost about a tile
+      heap.push(l);
+    }
+    for (int c = 0; c < ctas; ++c) per_cta[c + 1] += per_cta[c];
+    for (int c = 0; c <= ctas; ++c) a.cta_first[c] = uint16_t(per_cta[c]);
+    for (int u : sorted) a.order[per_cta[owner[u]]++] = uint16_t(u);
+    cudaError_t e = fa::launch_decode_tc(a, ctas, s);
+    if (e != cudaSuccess) return cuda_fail(e, "tensor-core decode launch");
+  }
+  return FA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
 int fa_attend_batch(fa_kvcache* const* caches, const fa_span* spans, int32_t batch,
                     int32_t layer, const float* q, int64_t q_stride, float* out,
                     int64_t out_stride, void* stream) {
@@ -930,6 +1083,8 @@ int fa_attend_batch(fa_kvcache* const* caches, const fa_span* spans, int32_t bat
   if (q_stride < width || out_stride < width) return fail(FA_ERR_SHAPE, "row strides below heads x head_dim");
   DeviceGuard guard(c0->device);
   auto s = static_cast<cudaStream_t>(stream);
+  if (decode_on_tensor_cores(caches, runs, batch))
+    return attend_batch_tc(caches, runs, batch, layer, q, q_stride, out, out_stride, s);
   const Plan base = plan_span(c0, 1, 1, false);
   const int tile = fa::tile_keys(c0->head_dim, c0->dtype == FA_F32 ? fa::kKtF32 : fa::kKtBf16);
   const int64_t want = target_units(c0->dev);

@@ -222,6 +222,73 @@ struct BatchArgs {
   BatchRow rows[kMaxBatchRows];
 };
 
+// The log-sum-exp merge of one row's `chunks` partials (slot (part_base + chunk) * heads + head:
+// D floats of unnormalised output, and (max, sum) in base 2) for query heads h0 .. h0 + g - 1,
+// by the kThreads threads (tid 0 .. kThreads - 1) of named barrier `bar`, in the last CTA of
+// the row to arrive. Each head's largest chunk max M and sum L = sum 2^(m - M) l take one warp
+// per head over the chunks; the outputs sum 2^(m - M) o over the chunks with the weights staged
+// in shared memory (`wts`, room for cap_chunks x G floats), each thread's output elements'
+// loads of several chunks in flight. finish(h, e, M, L, o) stores element e of head h0 + h.
+template <int G, int D, int kThreads, typename Finish>
+__device__ __forceinline__ void merge_chunk_partials(const float* part_o, const float* part_ml,
+                                                     int heads, int h0, int g, int part_base,
+                                                     int chunks, float* wts, int cap_chunks,
+                                                     int bar, int tid, Finish finish) {
+  __shared__ float merge_m[G], merge_l[G];
+  const int warp = tid >> 5, lane = tid & 31;
+  const int64_t base = int64_t(part_base) * heads + h0;  // slot of (chunk 0, head h0)
+  for (int h = warp; h < g; h += kThreads / 32) {
+    float mm = -INFINITY;
+    for (int ch = lane; ch < chunks; ch += 32)
+      mm = fmaxf(mm, __ldcg(&part_ml[2 * (base + int64_t(ch) * heads + h)]));
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, off));
+    float ll = 0.0f;
+    for (int ch = lane; ch < chunks; ch += 32) {
+      const int64_t slot = base + int64_t(ch) * heads + h;
+      const float cm = __ldcg(&part_ml[2 * slot]);
+      const float f = cm == -INFINITY ? 0.0f : exp2_approx(cm - mm);
+      ll = fmaf(__ldcg(&part_ml[2 * slot + 1]), f, ll);
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) ll += __shfl_xor_sync(0xffffffffu, ll, off);
+    if (lane == 0) {
+      merge_m[h] = mm;
+      merge_l[h] = ll;
+    }
+  }
+  named_sync(bar, kThreads);
+  constexpr int kPer = (G * D + kThreads - 1) / kThreads;  // output elements per thread
+  const int count = g * D;
+  float acc[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) acc[j] = 0.0f;
+  for (int cb = 0; cb < chunks; cb += cap_chunks) {
+    const int nb = min(cap_chunks, chunks - cb);
+    for (int i = tid; i < nb * g; i += kThreads) {
+      const int k = i / g, h = i % g;
+      const float cm = __ldcg(&part_ml[2 * (base + int64_t(cb + k) * heads + h)]);
+      wts[k * G + h] = cm == -INFINITY ? 0.0f : exp2_approx(cm - merge_m[h]);
+    }
+    named_sync(bar, kThreads);
+#pragma unroll 4
+    for (int k = 0; k < nb; ++k) {
+      const float* po = part_o + (base + int64_t(cb + k) * heads) * D;
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const int idx = tid + j * kThreads;
+        if (idx < count) acc[j] = fmaf(__ldcg(&po[idx]), wts[k * G + idx / D], acc[j]);
+      }
+    }
+    named_sync(bar, kThreads);
+  }
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int idx = tid + j * kThreads;
+    if (idx < count) finish(idx / D, idx % D, merge_m[idx / D], merge_l[idx / D], acc[j]);
+  }
+}
+
 template <int D, typename KT, int G, bool BATCH, typename Args>
 __global__ void __launch_bounds__(kDecodeThreads, (DecodeShape<D, KT, G>::kMinCtas)) attend_kernel(const __grid_constant__ Args args) {
   using S = DecodeShape<D, KT, G>;
@@ -581,63 +648,9 @@ __global__ void __launch_bounds__(kDecodeThreads, (DecodeShape<D, KT, G>::kMinCt
   named_sync(1, kConsumerWarps * 32);
   if (!last_flag) return;
   __threadfence();
-  // Each head's largest chunk max M and sum L = sum 2^(m - M) l, one warp per head over the
-  // chunks; then the outputs sum 2^(m - M) o over the chunks with the weights staged in shared
-  // memory (the stages are free), each thread's elements' loads of several chunks in flight.
-  __shared__ float merge_m[G], merge_l[G];
-  const int64_t base = int64_t(part_base) * c.heads + h0;  // slot of (chunk 0, head h0)
-  for (int h = warp; h < g; h += kConsumerWarps) {
-    float mm = -INFINITY;
-    for (int ch = lane; ch < chunks; ch += 32)
-      mm = fmaxf(mm, __ldcg(&c.part_ml[2 * (base + int64_t(ch) * c.heads + h)]));
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, off));
-    float ll = 0.0f;
-    for (int ch = lane; ch < chunks; ch += 32) {
-      const int64_t slot = base + int64_t(ch) * c.heads + h;
-      const float cm = __ldcg(&c.part_ml[2 * slot]);
-      const float f = cm == -INFINITY ? 0.0f : exp2_approx(cm - mm);
-      ll = fmaf(__ldcg(&c.part_ml[2 * slot + 1]), f, ll);
-    }
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) ll += __shfl_xor_sync(0xffffffffu, ll, off);
-    if (lane == 0) {
-      merge_m[h] = mm;
-      merge_l[h] = ll;
-    }
-  }
-  named_sync(1, kConsumerWarps * 32);
-  constexpr int kThreads = kConsumerWarps * 32;
-  constexpr int kPer = (G * D + kThreads - 1) / kThreads;  // output elements per thread
-  constexpr int kCap = int(size_t(kStages) * 2 * kTileBytes / (4 * G));  // chunks per block
-  float* wts = reinterpret_cast<float*>(smem);  // [chunk of the block][G]
-  float acc[kPer];
-#pragma unroll
-  for (int j = 0; j < kPer; ++j) acc[j] = 0.0f;
-  for (int cb = 0; cb < chunks; cb += kCap) {
-    const int nb = min(kCap, chunks - cb);
-    for (int i = ctid; i < nb * g; i += kThreads) {
-      const int k = i / g, h = i % g;
-      const float cm = __ldcg(&c.part_ml[2 * (base + int64_t(cb + k) * c.heads + h)]);
-      wts[k * G + h] = cm == -INFINITY ? 0.0f : exp2_approx(cm - merge_m[h]);
-    }
-    named_sync(1, kThreads);
-#pragma unroll 4
-    for (int k = 0; k < nb; ++k) {
-      const float* po = c.part_o + (base + int64_t(cb + k) * c.heads) * D;
-#pragma unroll
-      for (int j = 0; j < kPer; ++j) {
-        const int idx = ctid + j * kThreads;
-        if (idx < count) acc[j] = fmaf(__ldcg(&po[idx]), wts[k * G + idx / D], acc[j]);
-      }
-    }
-    named_sync(1, kThreads);
-  }
-#pragma unroll
-  for (int j = 0; j < kPer; ++j) {
-    const int idx = ctid + j * kThreads;
-    if (idx < count) finish(idx / D, idx % D, merge_m[idx / D], merge_l[idx / D], acc[j]);
-  }
+  merge_chunk_partials<G, D, kConsumerWarps * 32>(
+      c.part_o, c.part_ml, c.heads, h0, g, part_base, chunks, reinterpret_cast<float*>(smem),
+      int(size_t(kStages) * 2 * kTileBytes / (4 * G)), 1, ctid, finish);
 }
 
 }  // namespace fa

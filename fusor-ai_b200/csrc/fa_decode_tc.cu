@@ -1,0 +1,36 @@
+// Host side of the tensor-core decode (fa_decode_tc.cuh): its launch.
+#include <cuda_runtime.h>
+
+#include "fa_decode_tc.cuh"
+#include "fa_launch.cuh"
+
+namespace fa {
+
+namespace {
+
+template <int kG>
+cudaError_t launch_g(const DtcArgs& args, int grid, cudaStream_t stream) {
+  static bool configured = false;  // per instantiation, per process
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(decode_tc_kernel<kG>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         int(kDtcSmemBytes));
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  return launch_pdl(decode_tc_kernel<kG>, dim3(grid), dim3(kDtcThreads), kDtcSmemBytes, stream,
+                    args);
+}
+
+}  // namespace
+
+cudaError_t launch_decode_tc(const DtcArgs& args, int grid, cudaStream_t stream) {
+  if (args.group <= 1) return launch_g<1>(args, grid, stream);
+  if (args.group <= 2) return launch_g<2>(args, grid, stream);
+  if (args.group <= 4) return launch_g<4>(args, grid, stream);
+  if (args.group <= 8) return launch_g<8>(args, grid, stream);
+  if (args.group <= 16) return launch_g<16>(args, grid, stream);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace fa

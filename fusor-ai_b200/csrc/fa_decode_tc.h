@@ -1,0 +1,60 @@
+// The tensor-core decode's launch arguments (the kernel: fa_decode_tc.cuh).
+#pragma once
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "fa_ptx.cuh"
+
+namespace fa {
+
+constexpr int kDtcD = 128;      // head_dim (the M of O^T)
+constexpr int kDtcKeys = 128;   // keys per tile (the M of S^T)
+constexpr int kDtcN = 16;       // query heads per KV head, padded (the N of both products)
+constexpr int kDtcStages = 3;
+constexpr int kDtcThreads = 224;
+constexpr int kDtcTileBytes = kDtcKeys * kDtcD * 2;   // one K (or V) tile, bf16
+constexpr int kDtcOpBytes = kDtcN * kDtcD * 2;        // Q^T or one P^T buffer: 16 rows x 256 B
+constexpr int kDtcMergeBytes = 4096;
+// K and V stages, two Q^T buffers, three P^T buffers, the merge's weights
+constexpr size_t kDtcSmemBytes = size_t(2 * kDtcStages) * kDtcTileBytes + 5 * kDtcOpBytes +
+                                 kDtcMergeBytes + 1024 /* alignment */ + 512 /* barriers */;
+
+// One decode row: its cache's key and value tensor maps (device CUtensorMap, 64-byte aligned:
+// [layers x kv_heads][capacity][128] bf16, 64 x 128 boxes, 128-byte swizzle) and its keys, the
+// cache slots b0 .. b0 + n - 1 (one run, no ring wrap).
+struct DtcRow {
+  const void* kmap;
+  const void* vmap;
+  int z0;          // layer * kv_heads
+  int b0, n;
+  int chunks;      // chunks of chunk_keys keys
+  int unit_begin;  // first unit of this row: units are (kv head, chunk), kv head major
+  int part_base;   // first partial chunk slot of this row
+};
+
+constexpr int kDtcMaxCtas = 160;     // persistent CTAs (one per SM)
+constexpr int kDtcMaxUnits = 4096;   // units of one launch
+
+struct DtcArgs {
+  int heads, kv_heads, group;  // group <= kDtcN
+  int n_rows, n_units;
+  int chunk_keys;              // a multiple of kDtcKeys
+  const float* q;              // rotated queries, row r at q + r * q_stride (heads x 128, f32)
+  int64_t q_stride;
+  float scale_log2;            // log2(e) / sqrt(head_dim)
+  float* out;
+  int64_t out_stride;
+  float* part_o;               // chunk partials: slot (part_base + chunk) * heads + head
+  float* part_ml;
+  int* counters;               // per (row, kv head), zero between launches
+  unsigned* err;
+  DtcRow rows[kMaxBatchRows];
+  // The schedule: CTA c takes units order[cta_first[c]] .. order[cta_first[c + 1] - 1], the
+  // units dealt longest first to the least loaded CTA (each CTA's list longest first).
+  uint16_t cta_first[kDtcMaxCtas + 1];
+  uint16_t order[kDtcMaxUnits];
+};
+static_assert(sizeof(DtcArgs) <= 32764, "kernel parameters");
+
+}  // namespace fa

@@ -98,6 +98,12 @@ cudaError_t launch_bf16_pairs(const FmhaLaunch& l, cudaStream_t stream) {
 
 }  // namespace
 
+bool encode_cache_map_bf16(void* map, const void* base, uint64_t rows, uint64_t z,
+                           uint64_t z_stride_bytes) {
+  return make_map(static_cast<CUtensorMap*>(map), true, base, 128, rows, z, 128 * 2,
+                  z_stride_bytes, 64, 128);
+}
+
 bool fmha_supported(int dtype_bf16, int head_dim) {
   (void)dtype_bf16;
   return (head_dim == 64 || head_dim == 128) && encode_fn() != nullptr;

@@ -45,6 +45,11 @@ struct FmhaLaunch {
 };
 
 bool fmha_supported(int dtype_bf16, int head_dim);
+// A TMA map (written to the 128 bytes at `map`, 64-byte aligned) over a bf16 cache's keys or
+// values: [z][rows][128] elements, z_stride_bytes apart, 64 x 128 boxes, 128-byte swizzle (the
+// tensor-core decode's K and V tiles).
+bool encode_cache_map_bf16(void* map, const void* base, uint64_t rows, uint64_t z,
+                           uint64_t z_stride_bytes);
 int fmha_block_n(int dtype_bf16, int head_dim);
 cudaError_t launch_fmha(const FmhaLaunch& launch, cudaStream_t stream);
 

@@ -98,4 +98,8 @@ struct GateArgs {
 };
 cudaError_t launch_gate(const GateArgs& args, cudaStream_t stream);
 
+// The tensor-core decode over bf16 caches (fa_decode_tc.cu): `grid` persistent CTAs.
+struct DtcArgs;
+cudaError_t launch_decode_tc(const DtcArgs& args, int grid, cudaStream_t stream);
+
 }  // namespace fa

@@ -237,12 +237,15 @@ def test_config3_batched_decode_sample(torch, dtype):
     got = out.cpu().numpy()
     for i, (p, span) in enumerate(zip(pairs, spans)):
         want = p.oracle_attention(0, span, qkv[i:i + 1], angles[i:i + 1], fa.ROPE_HALF)
-        assert max_abs(got[i:i + 1], want) <= TOL_F32, compare(f"C3 seq {i}", got[i:i + 1], want)
+        # a bf16 cache decodes on the tensor cores (bf16 queries and probabilities)
+        tol = TOL_F32 if dtype == fa.F32 else TOL_BF16
+        assert max_abs(got[i:i + 1], want) <= tol, compare(f"C3 seq {i}", got[i:i + 1], want)
 
 
 def test_config3_batch_equals_one_call_per_sequence(torch):
     """Batching is invisible: each sequence alone gives the same output (full C3 shape, a
-    quarter of the sequences to keep host memory small)."""
+    quarter of the sequences to keep host memory small). Over a bf16 cache the batch decodes on
+    the tensor cores and a single span on the CUDA cores: they agree within the bf16 bar."""
     shape = fa.Shape(1, 32, 8, 128)
     lengths = c3_lengths()[:16]
     caches = []
@@ -260,7 +263,7 @@ def test_config3_batch_equals_one_call_per_sequence(torch):
         # the batch already kept row n; attend again over the same keys
         q = qkv[i:i + 1, : shape.width].contiguous()
         c.attend(0, spans[i], q, one)
-        assert torch.allclose(one, out[i:i + 1], atol=1e-5, rtol=0)
+        assert torch.allclose(one, out[i:i + 1], atol=TOL_BF16, rtol=0)
 
 
 def test_config4_long_context_sharded_matches_unsharded(torch):
