@@ -973,8 +973,12 @@ int attend_batch_tc(fa_kvcache* const* caches, const std::vector<fa::Runs>& runs
   int64_t total_keys = 0;
   for (int i = 0; i < batch; ++i) total_keys += runs[i].n0;
   const int sms = std::max(1, std::min(c0->dev->sms, fa::kDtcMaxCtas));
-  // about six units per CTA (the schedule below balances them), at most kDtcMaxUnits a launch
-  int64_t want = int64_t(sms) * 6;
+  // about FA_DTC_UNITS units per CTA (measured best: 1, the fewest unit ends and chunk merges;
+  // the schedule below balances whole rows), at most kDtcMaxUnits
+#ifndef FA_DTC_UNITS
+#define FA_DTC_UNITS 1
+#endif
+  int64_t want = int64_t(sms) * FA_DTC_UNITS;
   int64_t chunk_keys = 0;
   for (;; want = want * 3 / 4) {
     chunk_keys = (total_keys * c0->kv_heads + want - 1) / want;
