@@ -308,6 +308,160 @@ Plan plan_for_span(const fa_kvcache* c, const fa_span* span, const std::vector<i
   return plan_span(c, std::max(span->rows, 1), max_keys);
 }
 
+// Whether a batch of one-row decodes runs on the tensor cores: bf16 caches of head_dim 128 with
+// their TMA maps, at most 16 query heads per KV head, and every row's keys one run of cache slots
+// without a ring wrap (a window that wraps, or Groups' two runs, decode on the CUDA cores).
+#ifndef FA_DECODE_TC
+#define FA_DECODE_TC 1
+#endif
+bool decode_on_tensor_cores(fa_kvcache* const* caches, const std::vector<fa::Runs>& runs,
+                            int batch) {
+  if (!FA_DECODE_TC) return false;
+  const fa_kvcache* c0 = caches[0];
+  if (c0->dtype != FA_BF16 || c0->head_dim != 128 || c0->heads / c0->kv_heads > fa::kDtcN)
+    return false;
+  for (int i = 0; i < batch; ++i) {
+    const fa_kvcache* c = caches[i];
+    if (c->tc_maps.ptr == nullptr || runs[i].n1 != 0 || runs[i].n0 < 1 ||
+        runs[i].b0 + runs[i].n0 > c->capacity)
+      return false;
+  }
+  return true;
+}
+
+// The chunking of a tensor-core decode: chunks of a common length (a multiple of 128 keys), about
+// FA_DTC_UNITS (row, KV head, chunk) units per CTA (measured best: 1, the fewest unit ends and
+// chunk merges; the schedule balances whole rows), at most kDtcMaxUnits a launch.
+#ifndef FA_DTC_UNITS
+#define FA_DTC_UNITS 1
+#endif
+struct DtcPlan {
+  int64_t chunk_keys = 0;
+  int64_t slots = 0;  // partial chunk slots of every row (heads each)
+  std::vector<int> chunks, part_base;
+};
+
+DtcPlan plan_decode_tc(const fa_kvcache* c0, const std::vector<fa::Runs>& runs, int batch) {
+  DtcPlan p;
+  int64_t total_keys = 0;
+  for (int i = 0; i < batch; ++i) total_keys += runs[i].n0;
+  const int sms = std::max(1, std::min(c0->dev->sms, fa::kDtcMaxCtas));
+  for (int64_t want = int64_t(sms) * FA_DTC_UNITS;; want = want * 3 / 4) {
+    p.chunk_keys = (total_keys * c0->kv_heads + want - 1) / want;
+    p.chunk_keys = std::max<int64_t>(fa::kDtcKeys, (p.chunk_keys + fa::kDtcKeys - 1) / fa::kDtcKeys * fa::kDtcKeys);
+    int64_t units = 0;
+    for (int i = 0; i < std::min(batch, fa::kMaxBatchRows); ++i)
+      units += c0->kv_heads * ((runs[i].n0 + p.chunk_keys - 1) / p.chunk_keys);
+    if (units <= fa::kDtcMaxUnits || want <= 1) break;
+  }
+  p.chunks.resize(batch);
+  p.part_base.resize(batch);
+  for (int i = 0; i < batch; ++i) {
+    p.chunks[i] = int((runs[i].n0 + p.chunk_keys - 1) / p.chunk_keys);
+    p.part_base[i] = int(p.slots);
+    p.slots += p.chunks[i];
+  }
+  return p;
+}
+
+// A span's rows as the tensor-core decode's batch rows (each row its keys from the mask), when
+// the span decodes there: rows of one run of cache slots each.
+bool span_decode_tc(fa_kvcache* c, const fa_span* span, const std::vector<int>& ends,
+                    std::vector<fa::Runs>* runs) {
+  runs->resize(span->rows);
+  for (int r = 0; r < span->rows; ++r)
+    (*runs)[r] = fa::mask_runs(span->mask.kind, span->mask.window, span->mask.state,
+                               int(ends.size()), ends.data(), span->first + r,
+                               span->first + span->rows);
+  std::vector<fa_kvcache*> caches(span->rows, c);
+  return span->rows > 0 && decode_on_tensor_cores(caches.data(), *runs, span->rows);
+}
+
+// The tensor-core decode of a batch (persistent CTAs, one per SM; `given`: the caller's workspace,
+// sized for plan_decode_tc's slots).
+int attend_batch_tc(fa_kvcache* const* caches, const std::vector<fa::Runs>& runs, int batch,
+                    int layer, const float* q, int64_t q_stride, float* out, int64_t out_stride,
+                    cudaStream_t s, const Work* given = nullptr) {
+  fa_kvcache* c0 = caches[0];
+  const int sms = std::max(1, std::min(c0->dev->sms, fa::kDtcMaxCtas));
+  const DtcPlan plan = plan_decode_tc(c0, runs, batch);
+  const int64_t chunk_keys = plan.chunk_keys;
+  const std::vector<int>& chunks = plan.chunks;
+  const std::vector<int>& part_base = plan.part_base;
+  Work w;
+  if (given != nullptr) w = *given;  // sized by the caller (tc_decode_slots)
+  else if (int rc = ensure_work(c0, 0, size_t(plan.slots) * c0->heads, 0, s, &w)) return rc;
+  if (int rc = ensure_counters(c0, size_t(batch) * c0->kv_heads, s)) return rc;
+  for (int first = 0; first < batch; first += fa::kMaxBatchRows) {
+    const int n = std::min(batch - first, fa::kMaxBatchRows);
+    fa::DtcArgs a{};
+    a.heads = c0->heads;
+    a.kv_heads = c0->kv_heads;
+    a.group = c0->heads / c0->kv_heads;
+    a.n_rows = n;
+    a.chunk_keys = int(chunk_keys);
+    a.q = q + int64_t(first) * q_stride;
+    a.q_stride = q_stride;
+    a.scale_log2 = query_scale(c0->head_dim);
+    a.out = out + int64_t(first) * out_stride;
+    a.out_stride = out_stride;
+    a.part_o = w.part_o;
+    a.part_ml = w.part_ml;
+    a.counters = static_cast<int*>(c0->counters.ptr) + int64_t(first) * c0->kv_heads;
+    a.err = c0->dev->err;
+    int units = 0;
+    for (int i = 0; i < n; ++i) {
+      const fa_kvcache* c = caches[first + i];
+      fa::DtcRow& r = a.rows[i];
+      r.kmap = c->tc_maps.ptr;
+      r.vmap = static_cast<const unsigned char*>(c->tc_maps.ptr) + 128;
+      r.z0 = layer * c->kv_heads;
+      r.b0 = runs[first + i].b0;
+      r.n = runs[first + i].n0;
+      r.chunks = chunks[first + i];
+      r.unit_begin = units;
+      r.part_base = part_base[first + i];
+      units += c0->kv_heads * r.chunks;
+    }
+    a.n_units = units;
+    // Longest processing time first: the units by tiles, longest first (a counting sort), each
+    // to the least loaded CTA (a heap); each CTA's list keeps that order.
+    const int ctas = std::min(units, sms);
+    const int max_tiles = int((chunk_keys + fa::kDtcKeys - 1) / fa::kDtcKeys);
+    std::vector<int> unit_tiles(units), count(max_tiles + 2, 0);
+    for (int i = 0, u = 0; i < n; ++i) {
+      const int64_t nk = a.rows[i].n;
+      for (int k = 0; k < c0->kv_heads; ++k)
+        for (int ch = 0; ch < a.rows[i].chunks; ++ch, ++u) {
+          const int64_t keys = std::min<int64_t>(nk, int64_t(ch + 1) * chunk_keys) - int64_t(ch) * chunk_keys;
+          unit_tiles[u] = int((keys + fa::kDtcKeys - 1) / fa::kDtcKeys);
+          ++count[max_tiles - unit_tiles[u]];
+        }
+    }
+    for (int t = 1; t <= max_tiles + 1; ++t) count[t] += count[t - 1];
+    std::vector<int> sorted(units);
+    for (int u = units - 1; u >= 0; --u) sorted[--count[max_tiles - unit_tiles[u]]] = u;
+    using Load = std::pair<int64_t, int>;  // (tiles assigned, CTA)
+    std::priority_queue<Load, std::vector<Load>, std::greater<Load>> heap;
+    for (int c = 0; c < ctas; ++c) heap.push({0, c});
+    std::vector<int> owner(units), per_cta(ctas + 1, 0);
+    for (int u : sorted) {
+      Load l = heap.top();
+      heap.pop();
+      owner[u] = l.second;
+      ++per_cta[l.second + 1];
+      l.first += unit_tiles[u] + 1;  // a unit's own start and end cost about a tile
+      heap.push(l);
+    }
+    for (int c = 0; c < ctas; ++c) per_cta[c + 1] += per_cta[c];
+    for (int c = 0; c <= ctas; ++c) a.cta_first[c] = uint16_t(per_cta[c]);
+    for (int u : sorted) a.order[per_cta[owner[u]]++] = uint16_t(u);
+    cudaError_t e = fa::launch_decode_tc(a, ctas, s);
+    if (e != cudaSuccess) return cuda_fail(e, "tensor-core decode launch");
+  }
+  return FA_OK;
+}
+
 // The attention of a span's rows over the cache, queries already rotated and scaled in q;
 // `w` holds the partials of `p`.
 int attend_rows(fa_kvcache* c, int layer, const fa_span* span, const std::vector<int>& ends,
@@ -773,6 +927,13 @@ int fa_attend(fa_kvcache* cache, int32_t layer, const fa_span* span, const float
     if (e != cudaSuccess) return cuda_fail(e, "query conversion");
     return attend_rows_tc(cache, layer, span, ends, w.q, width, out, out_stride, s);
   }
+  std::vector<fa::Runs> truns;
+  if (span_decode_tc(cache, span, ends, &truns)) {
+    const DtcPlan plan = plan_decode_tc(cache, truns, span->rows);
+    if (int rc = ensure_work(cache, 0, size_t(plan.slots) * cache->heads, 0, s, &w)) return rc;
+    std::vector<fa_kvcache*> same(span->rows, cache);
+    return attend_batch_tc(same.data(), truns, span->rows, layer, q, q_stride, out, out_stride, s, &w);
+  }
   const Plan p = plan_for_span(cache, span, ends);
   if (int rc = ensure_work(cache, 0, size_t(span->rows) * p.chunks * cache->heads, 0, s, &w))
     return rc;
@@ -805,6 +966,19 @@ int fa_attention(fa_kvcache* cache, int32_t layer, const fa_span* span, int32_t 
                            1.0f, true, s, cache->dtype == FA_BF16))
       return rc;
     return attend_rows_tc(cache, layer, span, ends, w.q, width, out, out_stride, s);
+  }
+  std::vector<fa::Runs> truns;
+  if (span_decode_tc(cache, span, ends, &truns)) {
+    const DtcPlan plan = plan_decode_tc(cache, truns, span->rows);
+    if (int rc = ensure_work(cache, size_t(span->rows) * width, size_t(plan.slots) * cache->heads,
+                             0, s, &w))
+      return rc;
+    if (int rc = rope_rows(cache, layer, span, rope, angles, norm, qkv, qkv_stride, w.q, width,
+                           1.0f, true, s))
+      return rc;
+    std::vector<fa_kvcache*> same(span->rows, cache);
+    return attend_batch_tc(same.data(), truns, span->rows, layer, w.q, width, out, out_stride, s,
+                           &w);
   }
   const Plan p = plan_for_span(cache, span, ends);
   if (int rc = ensure_work(cache, size_t(span->rows) * width,
@@ -938,139 +1112,6 @@ int fa_attention_input_batch(fa_kvcache* const* caches, const fa_span* spans, in
   }
   return FA_OK;
 }
-
-}  // extern "C"
-
-namespace {
-
-// Whether a batch of one-row decodes runs on the tensor cores: bf16 caches of head_dim 128 with
-// their TMA maps, at most 16 query heads per KV head, and every row's keys one run of cache slots
-// without a ring wrap (a window that wraps, or Groups' two runs, decode on the CUDA cores).
-#ifndef FA_DECODE_TC
-#define FA_DECODE_TC 1
-#endif
-bool decode_on_tensor_cores(fa_kvcache* const* caches, const std::vector<fa::Runs>& runs,
-                            int batch) {
-  if (!FA_DECODE_TC) return false;
-  const fa_kvcache* c0 = caches[0];
-  if (c0->dtype != FA_BF16 || c0->head_dim != 128 || c0->heads / c0->kv_heads > fa::kDtcN)
-    return false;
-  for (int i = 0; i < batch; ++i) {
-    const fa_kvcache* c = caches[i];
-    if (c->tc_maps.ptr == nullptr || runs[i].n1 != 0 || runs[i].n0 < 1 ||
-        runs[i].b0 + runs[i].n0 > c->capacity)
-      return false;
-  }
-  return true;
-}
-
-// The tensor-core decode of a batch: chunks of a common length (a multiple of 128 keys) so that
-// the persistent CTAs (one per SM) each take about four (row, KV head, chunk) units.
-int attend_batch_tc(fa_kvcache* const* caches, const std::vector<fa::Runs>& runs, int batch,
-                    int layer, const float* q, int64_t q_stride, float* out, int64_t out_stride,
-                    cudaStream_t s) {
-  fa_kvcache* c0 = caches[0];
-  int64_t total_keys = 0;
-  for (int i = 0; i < batch; ++i) total_keys += runs[i].n0;
-  const int sms = std::max(1, std::min(c0->dev->sms, fa::kDtcMaxCtas));
-  // about FA_DTC_UNITS units per CTA (measured best: 1, the fewest unit ends and chunk merges;
-  // the schedule below balances whole rows), at most kDtcMaxUnits
-#ifndef FA_DTC_UNITS
-#define FA_DTC_UNITS 1
-#endif
-  int64_t want = int64_t(sms) * FA_DTC_UNITS;
-  int64_t chunk_keys = 0;
-  for (;; want = want * 3 / 4) {
-    chunk_keys = (total_keys * c0->kv_heads + want - 1) / want;
-    chunk_keys = std::max<int64_t>(fa::kDtcKeys, (chunk_keys + fa::kDtcKeys - 1) / fa::kDtcKeys * fa::kDtcKeys);
-    int64_t units = 0;
-    for (int i = 0; i < std::min(batch, fa::kMaxBatchRows); ++i)
-      units += c0->kv_heads * ((runs[i].n0 + chunk_keys - 1) / chunk_keys);
-    if (units <= fa::kDtcMaxUnits || want <= 1) break;
-  }
-  std::vector<int> chunks(batch), part_base(batch);
-  int64_t slots = 0;
-  for (int i = 0; i < batch; ++i) {
-    chunks[i] = int((runs[i].n0 + chunk_keys - 1) / chunk_keys);
-    part_base[i] = int(slots);
-    slots += chunks[i];
-  }
-  Work w;
-  if (int rc = ensure_work(c0, 0, size_t(slots) * c0->heads, 0, s, &w)) return rc;
-  if (int rc = ensure_counters(c0, size_t(batch) * c0->kv_heads, s)) return rc;
-  for (int first = 0; first < batch; first += fa::kMaxBatchRows) {
-    const int n = std::min(batch - first, fa::kMaxBatchRows);
-    fa::DtcArgs a{};
-    a.heads = c0->heads;
-    a.kv_heads = c0->kv_heads;
-    a.group = c0->heads / c0->kv_heads;
-    a.n_rows = n;
-    a.chunk_keys = int(chunk_keys);
-    a.q = q + int64_t(first) * q_stride;
-    a.q_stride = q_stride;
-    a.scale_log2 = query_scale(c0->head_dim);
-    a.out = out + int64_t(first) * out_stride;
-    a.out_stride = out_stride;
-    a.part_o = w.part_o;
-    a.part_ml = w.part_ml;
-    a.counters = static_cast<int*>(c0->counters.ptr) + int64_t(first) * c0->kv_heads;
-    a.err = c0->dev->err;
-    int units = 0;
-    for (int i = 0; i < n; ++i) {
-      const fa_kvcache* c = caches[first + i];
-      fa::DtcRow& r = a.rows[i];
-      r.kmap = c->tc_maps.ptr;
-      r.vmap = static_cast<const unsigned char*>(c->tc_maps.ptr) + 128;
-      r.z0 = layer * c->kv_heads;
-      r.b0 = runs[first + i].b0;
-      r.n = runs[first + i].n0;
-      r.chunks = chunks[first + i];
-      r.unit_begin = units;
-      r.part_base = part_base[first + i];
-      units += c0->kv_heads * r.chunks;
-    }
-    a.n_units = units;
-    // Longest processing time first: the units by tiles, longest first (a counting sort), each
-    // to the least loaded CTA (a heap); each CTA's list keeps that order.
-    const int ctas = std::min(units, sms);
-    const int max_tiles = int((chunk_keys + fa::kDtcKeys - 1) / fa::kDtcKeys);
-    std::vector<int> unit_tiles(units), count(max_tiles + 2, 0);
-    for (int i = 0, u = 0; i < n; ++i) {
-      const int64_t nk = a.rows[i].n;
-      for (int k = 0; k < c0->kv_heads; ++k)
-        for (int ch = 0; ch < a.rows[i].chunks; ++ch, ++u) {
-          const int64_t keys = std::min<int64_t>(nk, int64_t(ch + 1) * chunk_keys) - int64_t(ch) * chunk_keys;
-          unit_tiles[u] = int((keys + fa::kDtcKeys - 1) / fa::kDtcKeys);
-          ++count[max_tiles - unit_tiles[u]];
-        }
-    }
-    for (int t = 1; t <= max_tiles + 1; ++t) count[t] += count[t - 1];
-    std::vector<int> sorted(units);
-    for (int u = units - 1; u >= 0; --u) sorted[--count[max_tiles - unit_tiles[u]]] = u;
-    using Load = std::pair<int64_t, int>;  // (tiles assigned, CTA)
-    std::priority_queue<Load, std::vector<Load>, std::greater<Load>> heap;
-    for (int c = 0; c < ctas; ++c) heap.push({0, c});
-    std::vector<int> owner(units), per_cta(ctas + 1, 0);
-    for (int u : sorted) {
-      Load l = heap.top();
-      heap.pop();
-      owner[u] = l.second;
-      ++per_cta[l.second + 1];
-      l.first += unit_tiles[u] + 1;  // a unit's own start and end cost about a tile
-      heap.push(l);
-    }
-    for (int c = 0; c < ctas; ++c) per_cta[c + 1] += per_cta[c];
-    for (int c = 0; c <= ctas; ++c) a.cta_first[c] = uint16_t(per_cta[c]);
-    for (int u : sorted) a.order[per_cta[owner[u]]++] = uint16_t(u);
-    cudaError_t e = fa::launch_decode_tc(a, ctas, s);
-    if (e != cudaSuccess) return cuda_fail(e, "tensor-core decode launch");
-  }
-  return FA_OK;
-}
-
-}  // namespace
-
-extern "C" {
 
 int fa_attend_batch(fa_kvcache* const* caches, const fa_span* spans, int32_t batch,
                     int32_t layer, const float* q, int64_t q_stride, float* out,
@@ -1491,6 +1532,16 @@ int fa_gated_attention(fa_kvcache* cache, int32_t layer, const fa_span* span, in
                         width, 1.0f, true, s, cache->dtype == FA_BF16, gate_heads, rotary_dim)))
       return rc;
     rc = attend_rows_tc(cache, layer, span, ends, w.q, width, out, out_stride, s);
+  } else if (std::vector<fa::Runs> truns; span_decode_tc(cache, span, ends, &truns)) {
+    const DtcPlan plan = plan_decode_tc(cache, truns, span->rows);
+    if ((rc = ensure_work(cache, size_t(span->rows) * width, size_t(plan.slots) * cache->heads, 0,
+                          s, &w)))
+      return rc;
+    if ((rc = rope_rows(cache, layer, span, FA_ROPE_HALF, angles, norm, qkv, qkv_stride, w.q,
+                        width, 1.0f, true, s, false, gate_heads, rotary_dim)))
+      return rc;
+    std::vector<fa_kvcache*> same(span->rows, cache);
+    rc = attend_batch_tc(same.data(), truns, span->rows, layer, w.q, width, out, out_stride, s, &w);
   } else {
     const Plan pl = plan_for_span(cache, span, ends);
     if ((rc = ensure_work(cache, size_t(span->rows) * width,

@@ -122,7 +122,9 @@ def test_every_head_dim_and_storage(torch, dtype, head_dim):
     pair.gpu.attention(0, span, dev(torch, qkv), out, dev(torch, angles), fa.ROPE_HALF)
     want = pair.oracle_attention(0, span, qkv, angles, fa.ROPE_HALF)
     got = out.cpu().numpy()
-    assert max_abs(got, want) <= TOL_F32, compare(f"d{head_dim}", got, want)
+    # a bf16 cache of head_dim 128 decodes on the tensor cores (bf16 queries and probabilities)
+    tol = TOL_BF16 if dtype == fa.BF16 and head_dim == 128 else TOL_F32
+    assert max_abs(got, want) <= tol, compare(f"d{head_dim}", got, want)
 
 
 def test_window_ring_wraps_and_groups(torch):
