@@ -172,6 +172,8 @@ class C3Decode(Workload):
         self.torch, self.fa = torch, fa
         self.dtype = dtype
         self.name = "c3" if dtype == fa.F32 else "c3bf16"
+        # f32 caches decode on the CUDA cores (split-KV), bf16 caches on the tensor cores
+        self.kernel = "attend_kernel" if dtype == fa.F32 else "decode_tc_kernel"
         self.sharded = True
         from fusor_attn.shard import shard_sequences
         lengths = c3_lengths()[:sequences]
