@@ -223,8 +223,13 @@ int pow2_heads(int group) {
   return g == 3 ? 4 : g;
 }
 
-// Work units wanted per launch: four waves of the split-KV kernel's resident CTAs.
-int target_units(const Device* dev) { return std::max(dev->sms, 1) * FA_DECODE_MIN_CTAS * 4; }
+// Work units wanted per launch: FA_DECODE_WAVES waves of the split-KV kernel's resident CTAs.
+#ifndef FA_DECODE_WAVES
+#define FA_DECODE_WAVES 4
+#endif
+int target_units(const Device* dev) {
+  return std::max(dev->sms, 1) * FA_DECODE_MIN_CTAS * FA_DECODE_WAVES;
+}
 
 struct Plan {
   int g = 1, hgroups = 1, kv_groups = 1, chunks = 1;
