@@ -75,6 +75,7 @@ def lib():
             "oracle_qk_prologue": (None, [i64, i64, i64, i, i, i64, p, p, p, f, p, i64]),
             "oracle_gated_input": (None, [p, i64, i64, i64, i, i64, p, p, p, f, p, i64]),
             "oracle_gate": (None, [i64, i64, i64, i64, i, p, i64, p]),
+            "oracle_attend_int8": (None, [i64] * 5 + [p, i64] * 3 + [i, p]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(_lib, name)
@@ -285,6 +286,16 @@ def gate(rows, heads, kv_heads, head_dim, gate_kind, qkv, attention) -> np.ndarr
     out = _f32(attention).copy()
     q = _f32(qkv)
     lib().oracle_gate(rows, heads, kv_heads, head_dim, gate_kind, _ptr(q), q.shape[1], _ptr(out))
+    return out
+
+
+def attend_int8(heads, kv_heads, head_dim, q, k, v, fast=False) -> np.ndarray:
+    """blocks::attention::attend's int8 approximation (attention.rs:79-214) of one image: q
+    (queries x heads*head_dim), k and v (keys x kv_heads*head_dim)."""
+    q, k, v = _f32(q), _f32(k), _f32(v)
+    out = np.zeros((q.shape[0], heads * head_dim), np.float32)
+    lib().oracle_attend_int8(heads, kv_heads, head_dim, q.shape[0], k.shape[0], _ptr(q), q.shape[1],
+                             _ptr(k), k.shape[1], _ptr(v), v.shape[1], int(fast), _ptr(out))
     return out
 
 

@@ -570,6 +570,91 @@ void oracle_gate(int64_t rows, int64_t heads, int64_t kv_heads, int64_t head_dim
   }
 }
 
+/* One block of 32 values as Q7b32 levels (quant.rs:142-149): returns the scale. */
+static float oracle_q7_block(const float* x, int8_t* levels) {
+  float absmax = 0.0f;
+  for (int i = 0; i < 32; ++i) absmax = maxf(absmax, std::fabs(x[i]));
+  const float scale = absmax == 0.0f ? 1.0f : absmax / 63.0f;
+  for (int i = 0; i < 32; ++i) {
+    float l = std::nearbyint(x[i] / scale);  // ties to even (the default rounding mode)
+    if (l > 63.0f) l = 63.0f;
+    if (l < -63.0f) l = -63.0f;
+    levels[i] = (int8_t)l;
+  }
+  return scale;
+}
+
+/* One block of 32 activations as int8 (d = absmax / 127, ties-even). */
+static float oracle_a8_block(const float* x, int8_t* levels) {
+  float absmax = 0.0f;
+  for (int i = 0; i < 32; ++i) absmax = maxf(absmax, std::fabs(x[i]));
+  const float scale = absmax == 0.0f ? 1.0f : absmax / 127.0f;
+  for (int i = 0; i < 32; ++i) {
+    float l = std::nearbyint(x[i] / scale);
+    if (l > 127.0f) l = 127.0f;
+    if (l < -127.0f) l = -127.0f;
+    levels[i] = (int8_t)l;
+  }
+  return scale;
+}
+
+void oracle_attend_int8(int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t queries,
+                        int64_t keys, const float* q, int64_t q_stride, const float* k,
+                        int64_t k_stride, const float* v, int64_t v_stride, int fast, float* out) {
+  const int64_t d = head_dim, dp = (d + 31) / 32 * 32, kp = (keys + 31) / 32 * 32;
+  const int64_t db = dp / 32, kb = kp / 32;
+  std::vector<float> mean(d), row(std::max(dp, kp)), scores(keys);
+  std::vector<int8_t> kq(keys * dp), vq(d * kp), aq(std::max(dp, kp));
+  std::vector<float> ks(keys * db), vs(d * kb), as_(std::max(db, kb));
+  const int64_t group = heads / kv_heads;
+  for (int64_t kvh = 0; kvh < kv_heads; ++kvh) {
+    // the keys less their mean, as Q7b32 rows of dp values
+    for (int64_t e = 0; e < d; ++e) mean[e] = 0.0f;
+    for (int64_t j = 0; j < keys; ++j)
+      for (int64_t e = 0; e < d; ++e) mean[e] += k[j * k_stride + kvh * d + e];
+    for (int64_t e = 0; e < d; ++e) mean[e] /= (float)keys;
+    for (int64_t j = 0; j < keys; ++j) {
+      for (int64_t e = 0; e < dp; ++e) row[e] = e < d ? k[j * k_stride + kvh * d + e] - mean[e] : 0.0f;
+      for (int64_t b = 0; b < db; ++b) ks[j * db + b] = oracle_q7_block(&row[b * 32], &kq[j * dp + b * 32]);
+    }
+    // the values transposed: a row per channel over kp keys
+    for (int64_t e = 0; e < d; ++e) {
+      for (int64_t j = 0; j < kp; ++j) row[j] = j < keys ? v[j * v_stride + kvh * d + e] : 0.0f;
+      for (int64_t b = 0; b < kb; ++b) vs[e * kb + b] = oracle_q7_block(&row[b * 32], &vq[e * kp + b * 32]);
+    }
+    for (int64_t hh = 0; hh < group; ++hh) {
+      const int64_t h = kvh * group + hh;
+      for (int64_t i = 0; i < queries; ++i) {
+        for (int64_t e = 0; e < dp; ++e) row[e] = e < d ? q[i * q_stride + h * d + e] : 0.0f;
+        for (int64_t b = 0; b < db; ++b) as_[b] = oracle_a8_block(&row[b * 32], &aq[b * 32]);
+        const float scale = 1.0f / std::sqrt((float)d);
+        for (int64_t j = 0; j < keys; ++j) {
+          float s = 0.0f;
+          for (int64_t b = 0; b < db; ++b) {
+            int32_t acc = 0;
+            for (int t = 0; t < 32; ++t) acc += int32_t(kq[j * dp + b * 32 + t]) * int32_t(aq[b * 32 + t]);
+            s += (float)acc * (ks[j * db + b] * as_[b]);
+          }
+          scores[j] = s * scale;
+        }
+        const float sum = oracle_exponentials_apply(fast, scores.data(), (int)keys);
+        // the exponentials as int8 activations of P.V^T
+        for (int64_t j = 0; j < kp; ++j) row[j] = j < keys ? scores[j] : 0.0f;
+        for (int64_t b = 0; b < kb; ++b) as_[b] = oracle_a8_block(&row[b * 32], &aq[b * 32]);
+        for (int64_t e = 0; e < d; ++e) {
+          float o = 0.0f;
+          for (int64_t b = 0; b < kb; ++b) {
+            int32_t acc = 0;
+            for (int t = 0; t < 32; ++t) acc += int32_t(vq[e * kp + b * 32 + t]) * int32_t(aq[b * 32 + t]);
+            o += (float)acc * (vs[e * kb + b] * as_[b]);
+          }
+          out[i * heads * d + h * d + e] = o / sum;
+        }
+      }
+    }
+  }
+}
+
 void oracle_relpos_attend(int64_t heads, int64_t head_dim, int64_t frames, const float* q,
                           const float* k, const float* v, int64_t qkv_stride,
                           const float* positions, int64_t positions_stride, const float* bias_u,

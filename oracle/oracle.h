@@ -166,6 +166,19 @@ void oracle_gated_input(oracle_cache* cache, int64_t layer, int64_t rows, int64_
 void oracle_gate(int64_t rows, int64_t heads, int64_t kv_heads, int64_t head_dim, int gate,
                  const float* qkv, int64_t stride, float* attention);
 
+/* blocks::attention::attend's int8 approximation (crates/blocks/src/attention.rs:79-214) of one
+ * image's full-mask attention, for the comparison with the f32 and bf16 paths: per (head),
+ * the keys less their mean over the keys (SageAttention's smoothing) and the transposed values
+ * quantized as Q7b32 rows (per block of 32: d = absmax / 63, ties-even levels clamped to +-63,
+ * quant.rs:131-149), the queries and the exponentials as int8 activations (per block of 32:
+ * d = absmax / 127, matmul.rs:229-260), integer dot products per block scaled by d_w * d_a,
+ * scores times 1/sqrt(head_dim), Exponentials::apply (exact or fast, ops.rs:163-191), and the
+ * outputs divided by the exponentials' sums. q, k, v rows `*_stride` apart (head h at
+ * h * head_dim), out rows of heads * head_dim. */
+void oracle_attend_int8(int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t queries,
+                        int64_t keys, const float* q, int64_t q_stride, const float* k,
+                        int64_t k_stride, const float* v, int64_t v_stride, int fast, float* out);
+
 /* Joins the team's worker threads (they are started on the first threaded call). */
 void oracle_team_release(void);
 

@@ -293,3 +293,22 @@ def test_qk_prologue_like_the_f64_reference(norm, rope):
             g = got[t, part * width:(part + 1) * width]
             assert np.linalg.norm(g - want) / np.linalg.norm(want) < 1e-6
         assert (got[t, 2 * width:] == qkv[t, 2 * width:]).all()
+
+
+def test_int8_approximation_of_blocks_attention():
+    """blocks::attention::attend's int8 path (attention.rs:79-214: Q7b32 keys less their mean and
+    values, int8 queries and exponentials) against the f32 attention on C5-like heads: within
+    the reference's own bar for quantized paths (stacks.rs:51-56, 3e-2 relative), and the fast
+    exponentials no worse than that either."""
+    rng = np.random.default_rng(3)
+    heads, d, n = 2, 128, 256
+    q = rng.standard_normal((n, heads * d)).astype(np.float32)
+    k = rng.standard_normal((n, heads * d)).astype(np.float32)
+    v = rng.standard_normal((n, heads * d)).astype(np.float32)
+    exact = oracle.attend_call(heads, heads, d, 1, n, n, q, heads * d, 0, k, heads * d, 0,
+                               v, heads * d, 0)
+    for fast in (False, True):
+        approx = oracle.attend_int8(heads, heads, d, q, k, v, fast=fast)
+        rel = np.linalg.norm(approx - exact) / np.linalg.norm(exact)
+        print(f"int8 {'fast' if fast else 'exact'} exponentials: relative L2 {rel:.2e}")
+        assert rel < 3e-2, rel

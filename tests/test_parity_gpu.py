@@ -341,6 +341,28 @@ def test_config5_full_mask_sample(torch, dtype):
     assert max_abs(got[rows], want[rows]) <= (TOL_F32 if dtype == "f32" else TOL_BF16)
 
 
+def test_bf16_tensor_cores_beat_the_reference_int8_approximation(torch):
+    """The full-mask attention the reference runs in int8 (attention.rs:79-214, restated in the
+    oracle) against this build's bf16 tensor-core path on the same f32 inputs (rounded to bf16
+    on the way in): both against the f32 attention, the bf16 path's error the smaller."""
+    heads, d, n = 2, 128, 512
+    q = normal(701, (n, heads * d))
+    k = normal(702, (n, heads * d))
+    v = normal(703, (n, heads * d))
+    exact = oracle.attend_call(heads, heads, d, 1, n, n, q, heads * d, 0, k, heads * d, 0,
+                               v, heads * d, 0)
+    int8 = oracle.attend_int8(heads, heads, d, q, k, v)
+    ops = [dev(torch, x).to(torch.bfloat16) for x in (q, k, v)]
+    out = torch.zeros((n, heads * d), device="cuda")
+    fa.attend_full(heads, heads, d, 1, n, n, fa.Operand(ops[0], heads * d),
+                   fa.Operand(ops[1], heads * d), fa.Operand(ops[2], heads * d), out)
+    fa.device_status()
+    got = out.cpu().numpy()
+    e_bf16, e_int8 = relative_l2(got, exact), relative_l2(int8, exact)
+    print(f"relative L2 against f32: bf16 tensor cores {e_bf16:.2e}, reference int8 {e_int8:.2e}")
+    assert e_bf16 < e_int8
+
+
 def test_full_mask_images_and_gqa(torch):
     """blocks::attention::Call with several images and grouped KV heads."""
     heads, kv, d, images, queries, keys = 8, 2, 64, 3, 40, 56
