@@ -261,16 +261,20 @@ __global__ void __launch_bounds__(kFmha2Threads, 1)
           if (!vis) s[cc] = -INFINITY;
         }
       }
-      // the tile's max in four independent chains
-      float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
+      // the tile's max in four independent chains of three-input maxima: 12 + 14 x 8 + 4 keys
+      static_assert(BN == 128, "the max chains cover 128 keys");
+      float mx0 = fmax3(s[0], s[1], s[2]), mx1 = fmax3(s[3], s[4], s[5]);
+      float mx2 = fmax3(s[6], s[7], s[8]), mx3 = fmax3(s[9], s[10], s[11]);
 #pragma unroll
-      for (int cc = 4; cc < BN; cc += 4) {
-        mx0 = fmaxf(mx0, s[cc]);
-        mx1 = fmaxf(mx1, s[cc + 1]);
-        mx2 = fmaxf(mx2, s[cc + 2]);
-        mx3 = fmaxf(mx3, s[cc + 3]);
+      for (int cc = 12; cc < 124; cc += 8) {
+        mx0 = fmax3(mx0, s[cc], s[cc + 1]);
+        mx1 = fmax3(mx1, s[cc + 2], s[cc + 3]);
+        mx2 = fmax3(mx2, s[cc + 4], s[cc + 5]);
+        mx3 = fmax3(mx3, s[cc + 6], s[cc + 7]);
       }
-      const float m_tile = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * a.scale_log2;
+      mx0 = fmax3(mx0, s[124], s[125]);
+      mx1 = fmax3(mx1, s[126], s[127]);
+      const float m_tile = fmax3(mx0, mx1, fmaxf(mx2, mx3)) * a.scale_log2;
       // Lazy rescale: move the reference max only when the tile's max exceeds it by 2^8 (the
       // first finite max just sets it: nothing has accumulated for the row yet).
       float alpha = 1.0f;

@@ -129,6 +129,13 @@ __device__ __forceinline__ bool named_sync_or(int id, int threads, bool pred) {
   return r != 0;
 }
 
+// max(a, b, c) in one instruction (sm_100a's three-input max).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 __device__ __forceinline__ float exp2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
