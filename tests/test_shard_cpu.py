@@ -76,7 +76,7 @@ def free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 4])
 def test_kv_range_split_over_gloo_ranks_matches_the_oracle(world):
     import torch.multiprocessing as mp
 
