@@ -53,10 +53,26 @@ constexpr int kFmhaThreads = 256;
 constexpr int kConvThreads = 64;  // warps 2-3: the tf32 rounding pass
 
 // Rounds `bytes` of f32 shared memory to tf32 (nearest, ties away) in place, 16 bytes per
-// thread per step. The swizzled layout is untouched: the same function of every element.
+// thread per step, four steps' loads in flight at a time (the pass is on the critical path of
+// every KV tile). The swizzled layout is untouched: the same function of every element.
 __device__ __forceinline__ void round_tile_tf32(unsigned char* tile, int bytes, int tid) {
   float4* v = reinterpret_cast<float4*>(tile);
-  for (int i = tid; i < bytes / 16; i += kConvThreads) {
+  const int n = bytes / 16;
+  int i = tid;
+  for (; i + 3 * kConvThreads < n; i += 4 * kConvThreads) {
+    float4 x[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) x[k] = v[i + k * kConvThreads];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      x[k].x = __uint_as_float(tc::round_tf32(x[k].x));
+      x[k].y = __uint_as_float(tc::round_tf32(x[k].y));
+      x[k].z = __uint_as_float(tc::round_tf32(x[k].z));
+      x[k].w = __uint_as_float(tc::round_tf32(x[k].w));
+      v[i + k * kConvThreads] = x[k];
+    }
+  }
+  for (; i < n; i += kConvThreads) {
     float4 x = v[i];
     x.x = __uint_as_float(tc::round_tf32(x.x));
     x.y = __uint_as_float(tc::round_tf32(x.y));
