@@ -233,8 +233,12 @@ int target_units(const Device* dev) {
 
 struct Plan {
   int g = 1, hgroups = 1, kv_groups = 1, chunks = 1;
+  int cluster = 0;  // > 1: a row's chunks form a thread-block cluster and merge in shared memory
 };
 
+#ifndef FA_DECODE_CLUSTER
+#define FA_DECODE_CLUSTER 1
+#endif
 Plan plan_span(const fa_kvcache* c, int rows, int max_keys, bool split_small = true) {
   Plan p;
   const int group = c->heads / c->kv_heads;
@@ -251,6 +255,16 @@ Plan plan_span(const fa_kvcache* c, int rows, int max_keys, bool split_small = t
   p.kv_groups = c->kv_heads * p.hgroups;
   const int want = (target_units(c->dev) + rows * p.kv_groups - 1) / std::max(rows * p.kv_groups, 1);
   p.chunks = std::min(max_chunks, std::max(1, want));
+  // A short row (at most four tiles per CTA of a cluster) in a launch that fits on the SMs has
+  // its chunks as one cluster, merged in shared memory (no partials through HBM, no arrival
+  // counter): the latency of a short decode (C1's 1025 keys).
+  const int clustered = std::min(p.chunks, fa::kMaxClusterChunks);
+  if (split_small && FA_DECODE_CLUSTER && p.chunks > 1 &&
+      max_chunks <= 4 * fa::kMaxClusterChunks &&
+      int64_t(rows) * p.kv_groups * clustered <= c->dev->sms) {
+    p.chunks = clustered;
+    p.cluster = clustered;
+  }
   return p;
 }
 
@@ -496,6 +510,7 @@ int attend_rows(fa_kvcache* c, int layer, const fa_span* span, const std::vector
   args.state = span->mask.state;
   args.n_ends = int(ends.size());
   args.chunks = p.chunks;
+  args.c.cluster = p.cluster;
   args.rows_per_image = rows;
   args.keys_per_image = 0;
   for (size_t i = 0; i < ends.size(); ++i) args.ends[i] = ends[i];
@@ -1254,6 +1269,7 @@ int fa_attend_partial(fa_kvcache* cache, int32_t layer, const float* q, int32_t 
   args.kind = FA_MASK_WINDOW;
   args.window = n;
   args.chunks = p.chunks;
+  args.c.cluster = p.cluster;
   args.rows_per_image = 1;
   args.keys_per_image = 0;
   fa::AttendLaunch l{cache->dtype == FA_F32 ? fa::kKtF32 : fa::kKtBf16, p.g, false, &args, nullptr,
@@ -1400,6 +1416,7 @@ int fa_attend_full(const fa_call* call, void* out, int64_t out_stride, void* str
   args.end = k.keys;
   args.kind = FA_MASK_FULL;
   args.chunks = p.chunks;
+  args.c.cluster = p.cluster;
   args.rows_per_image = k.queries;
   args.keys_per_image = k.keys;
   fa::AttendLaunch l{k.dtype == FA_F32 ? fa::kKtF32 : fa::kKtBf16, p.g, false, &args, nullptr,
@@ -1745,6 +1762,7 @@ extern "C" int fa_attend_static(fa_kvcache* cache, int32_t layer, const fa_span*
   args.state = m.state;
   args.n_ends = n_ends;
   args.chunks = p.chunks;
+  args.c.cluster = p.cluster;
   args.rows_per_image = span->rows;
   args.keys_per_image = 0;
   for (int i = 0; i < n_ends; ++i) args.ends[i] = ends[i];

@@ -38,6 +38,11 @@ constexpr int kConsumerWarps = FA_DECODE_WARPS;
 constexpr int kDecodeThreads = (kConsumerWarps + 1) * 32;
 constexpr int kStages = FA_DECODE_STAGES;
 constexpr int kTileBytes = FA_DECODE_TILE_BYTES;  // bytes of one K (or V) tile of a stage
+// Where a clustered chunk leaves its (max, sum, o) state: past the warps' merge scratch
+// (<= 4 warps x 8 heads x (256 + 2) floats) in the stages' memory.
+constexpr int kClusterPartialOffset = 40960;
+// Chunks of a row merged within one thread-block cluster (the portable cluster size).
+constexpr int kMaxClusterChunks = 8;
 
 // Mask::keys (transformer.rs:116-128): the key positions of a row as two runs.
 struct Runs {
@@ -111,9 +116,13 @@ struct DecodeShape {
   static_assert(kLanesPerKey >= 2 && kLanesPerKey <= 32, "head_dim 16..256");
   static_assert(kRounds * kRoundKeys == kTileKeys, "tile holds whole rounds");
   static constexpr size_t kSmemBytes = size_t(kStages) * 2 * kTileBytes + 2 * kStages * 8;
-  // the warps' (max, sum, o) merge reuses the stages' memory
-  static_assert(size_t(kConsumerWarps) * 8 * (D + 2) * 4 <= size_t(kStages) * 2 * kTileBytes,
-                "the merge scratch fits the stages");
+  // the warps' (max, sum, o) merge reuses the stages' memory, and so does a clustered chunk's
+  // state past it
+  static_assert(size_t(kConsumerWarps) * 8 * (D + 2) * 4 <= size_t(kClusterPartialOffset),
+                "the merge scratch fits below the cluster state");
+  static_assert(size_t(kClusterPartialOffset) + size_t(G) * (D + 2) * 4 <=
+                    size_t(kStages) * 2 * kTileBytes,
+                "the cluster state fits the stages");
 };
 
 // The element index of lane-slot i (0..E-1) of sub-lane `sub` in a row, LPK = D / E lanes per
@@ -192,6 +201,7 @@ struct AttendCommon {
   float* part_ml;  // (max, sum) per slot
   int* counters;   // per (row, kv group) arrival counters, zero between launches
   unsigned* err;   // device error word
+  int cluster;     // spans: a row's chunks are one thread-block cluster (merged in shared memory)
 };
 
 // One span over one cache: row r at position first + r, keys from the mask.
@@ -413,6 +423,11 @@ __global__ void __launch_bounds__(kDecodeThreads, (DecodeShape<D, KT, G>::kMinCt
       for (int t = max(0, issued - kStages); t < issued; ++t)
         mbar_wait(&full[t % kStages], (t / kStages) & 1, c.err);
     }
+    __syncwarp();
+    if (c.cluster) {  // the chunk merge's two cluster barriers
+      cluster_sync();
+      cluster_sync();
+    }
     return;
   }
 
@@ -568,7 +583,13 @@ __global__ void __launch_bounds__(kDecodeThreads, (DecodeShape<D, KT, G>::kMinCt
   // All consumers are past their last tile: every copy has landed, the stages are free.
   if (!ok) fail_flag = 1;
   named_sync(1, kConsumerWarps * 32);
-  if (*static_cast<volatile int*>(&fail_flag) != 0) return;
+  if (*static_cast<volatile int*>(&fail_flag) != 0) {
+    if (c.cluster) {  // every thread of the cluster reaches both of its barriers
+      cluster_sync();
+      cluster_sync();
+    }
+    return;
+  }
 
   float* red_m = reinterpret_cast<float*>(smem);           // [warps][G]
   float* red_l = red_m + kConsumerWarps * G;               // [warps][G]
@@ -625,6 +646,14 @@ __global__ void __launch_bounds__(kDecodeThreads, (DecodeShape<D, KT, G>::kMinCt
     }
     if (chunks == 1) {
       finish(h, e, mm, ll, oo);
+    } else if (c.cluster) {
+      // the chunk's state for the cluster merge, in this CTA's shared memory
+      float* cp = reinterpret_cast<float*>(smem + kClusterPartialOffset);
+      cp[2 * G + idx] = oo;
+      if (e == 0) {
+        cp[h] = mm;
+        cp[G + h] = ll;
+      }
     } else {
       const int64_t slot = int64_t(part_base + chunk) * c.heads + (h0 + h);
       c.part_o[slot * D + e] = oo;
@@ -635,6 +664,28 @@ __global__ void __launch_bounds__(kDecodeThreads, (DecodeShape<D, KT, G>::kMinCt
     }
   }
   if (chunks == 1) return;
+  if (c.cluster) {
+    // ---- the row's chunks are one cluster: CTA 0 merges their states from shared memory ----
+    cluster_sync();
+    if (cluster_rank() == 0) {
+      const float* cp = reinterpret_cast<const float*>(smem + kClusterPartialOffset);
+      for (int idx = ctid; idx < count; idx += kConsumerWarps * 32) {
+        const int h = idx / D, e = idx % D;
+        float mm = -INFINITY;
+        for (int r = 0; r < chunks; ++r) mm = fmaxf(mm, ld_cluster_f32(cp + h, r));
+        float ll = 0.0f, oo = 0.0f;
+        for (int r = 0; r < chunks; ++r) {
+          const float cm = ld_cluster_f32(cp + h, r);
+          const float f = cm == -INFINITY ? 0.0f : exp2_approx(cm - mm);
+          ll = fmaf(ld_cluster_f32(cp + G + h, r), f, ll);
+          oo = fmaf(ld_cluster_f32(cp + 2 * G + idx, r), f, oo);
+        }
+        finish(h, e, mm, ll, oo);
+      }
+    }
+    cluster_sync();  // no CTA leaves while CTA 0 reads its shared memory
+    return;
+  }
 
   // ---- the last CTA of this (row, KV group) merges the chunks ---------------------------------
   __threadfence();

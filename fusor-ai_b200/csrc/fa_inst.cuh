@@ -18,7 +18,8 @@ cudaError_t launch_one(const Args& args, int grid, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  return launch_pdl(kernel, dim3(grid), dim3(kDecodeThreads), smem, stream, args);
+  return launch_pdl_cluster(kernel, dim3(grid), dim3(kDecodeThreads), smem, stream,
+                            args.c.cluster > 1 ? args.c.cluster : 1, args);
 }
 
 template <int D, typename KT, int G>

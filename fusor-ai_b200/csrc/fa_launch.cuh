@@ -14,20 +14,34 @@ namespace fa {
 // Launches `kernel` with programmatic stream serialization: its CTAs may be scheduled while the
 // previous kernel of the stream (the RoPE + keep kernel, which triggers early) finishes; the
 // kernel waits (pdl_wait) before it reads what that kernel wrote.
+// With `cluster` > 1, consecutive groups of that many CTAs (along x) form a thread-block cluster.
 template <typename... Params, typename... Args>
-cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
-                       cudaStream_t stream, Args&&... args) {
+cudaError_t launch_pdl_cluster(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+                               cudaStream_t stream, int cluster, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (cluster > 1) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = unsigned(cluster);
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+  }
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+template <typename... Params, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args&&... args) {
+  return launch_pdl_cluster(kernel, grid, block, smem, stream, 1, std::forward<Args>(args)...);
 }
 
 constexpr int kKtF32 = 0;

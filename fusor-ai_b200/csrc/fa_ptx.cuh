@@ -129,6 +129,26 @@ __device__ __forceinline__ bool named_sync_or(int id, int threads, bool pred) {
   return r != 0;
 }
 
+// Every thread of every CTA of the cluster arrives (release) and waits (acquire); hardware
+// barrier, so every thread of the cluster must reach it.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// A float of CTA `rank`'s shared memory at the address of `local` in this CTA's.
+__device__ __forceinline__ float ld_cluster_f32(const float* local, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return v;
+}
+
 // max(a, b, c) in one instruction (sm_100a's three-input max).
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float r;
