@@ -1154,7 +1154,13 @@ int fa_attend_batch(fa_kvcache* const* caches, const fa_span* spans, int32_t bat
   const int tile = fa::tile_keys(c0->head_dim, c0->dtype == FA_F32 ? fa::kKtF32 : fa::kKtBf16);
   const int64_t want = target_units(c0->dev);
   int64_t chunk_keys = (total_keys * base.kv_groups + want - 1) / want;
-  chunk_keys = std::max<int64_t>(tile, (chunk_keys + tile - 1) / tile * tile);
+  // at least FA_DECODE_MIN_CHUNK_TILES tiles a chunk: a small batch (a GPU's share of C3 over 8
+  // GPUs) otherwise splits into chunks too short for their fixed costs
+#ifndef FA_DECODE_MIN_CHUNK_TILES
+#define FA_DECODE_MIN_CHUNK_TILES 8
+#endif
+  chunk_keys = std::max<int64_t>(int64_t(tile) * FA_DECODE_MIN_CHUNK_TILES,
+                                 (chunk_keys + tile - 1) / tile * tile);
   // Chunks and partial slots of every row, then one launch per kMaxBatchRows rows.
   std::vector<int> chunks(batch), part_base(batch);
   int64_t slots = 0;
