@@ -72,6 +72,28 @@ __host__ __device__ inline Runs mask_runs(int kind, int window, int state, int n
   return r;
 }
 
+// The bits of key word `w` (keys kp + 32w .. kp + 32w + 31) that lie in [b, b + n).
+__device__ __forceinline__ uint32_t run_word(int b, int n, int kp, int w) {
+  const int base = kp + 32 * w;
+  const int lo = min(max(b - base, 0), 32), hi = min(max(b + n - base, 0), 32);
+  const uint32_t below_hi = hi >= 32 ? 0xffffffffu : (1u << hi) - 1u;
+  const uint32_t below_lo = lo >= 32 ? 0xffffffffu : (1u << lo) - 1u;
+  return below_hi & ~below_lo;
+}
+
+// Sets to -inf the scores s[0..N) of the keys kp .. kp + N - 1 that neither run of `r` covers:
+// the runs become a bit mask once per 32 keys, so a key costs a bit test and a select.
+template <int N>
+__device__ __forceinline__ void mask_scores(const Runs& r, int kp, float* s) {
+#pragma unroll
+  for (int w = 0; w < N / 32; ++w) {
+    const uint32_t bits = run_word(r.b0, r.n0, kp, w) | run_word(r.b1, r.n1, kp, w);
+#pragma unroll
+    for (int c = 0; c < 32; ++c)
+      if (!((bits >> c) & 1u)) s[32 * w + c] = -INFINITY;
+  }
+}
+
 template <typename KT>
 struct KvElem;
 template <>

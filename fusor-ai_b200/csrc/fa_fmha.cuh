@@ -296,18 +296,13 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
       if constexpr (BN == 128) tc::tmem_ld128_wait(lane_base + b * S::kSCols, sreg);
       else tc::tmem_ld64_wait(lane_base + b * S::kSCols, sreg);
       float* s = reinterpret_cast<float*>(sreg);
-      const bool all_in = row_valid &&
-                          ((kp >= runs.b0 && kp + BN <= runs.b0 + runs.n0) ||
-                           (kp >= runs.b1 && kp + BN <= runs.b1 + runs.n1));
-      if (!all_in) {
-#pragma unroll
-        for (int c = 0; c < BN; ++c) {
-          const int key = kp + c;
-          const bool vis = row_valid && ((key >= runs.b0 && key < runs.b0 + runs.n0) ||
-                                         (key >= runs.b1 && key < runs.b1 + runs.n1));
-          if (!vis) s[c] = -INFINITY;
-        }
-      }
+      // A row past the end of the image's queries is never written back, and its P row reaches
+      // only its own O row (the tensor-core product is row by row), so it skips the masking:
+      // its Q row (the next image's query, or the TMA's zero fill) needs no -inf either.
+      const bool all_in = !row_valid ||
+                          (kp >= runs.b0 && kp + BN <= runs.b0 + runs.n0) ||
+                          (kp >= runs.b1 && kp + BN <= runs.b1 + runs.n1);
+      if (!all_in) mask_scores<BN>(runs, kp, s);
       float mx = -INFINITY;
 #pragma unroll
       for (int c = 0; c < BN; ++c) mx = fmaxf(mx, s[c]);

@@ -249,18 +249,13 @@ __global__ void __launch_bounds__(kFmha2Threads, 1)
       uint32_t sreg[BN];
       tc::tmem_ld128_wait(lane_base, sreg);
       float* s = reinterpret_cast<float*>(sreg);
-      const bool all_in = row_valid &&
-                          ((kp >= runs.b0 && kp + BN <= runs.b0 + runs.n0) ||
-                           (kp >= runs.b1 && kp + BN <= runs.b1 + runs.n1));
-      if (!all_in) {
-#pragma unroll
-        for (int cc = 0; cc < BN; ++cc) {
-          const int key = kp + cc;
-          const bool vis = row_valid && ((key >= runs.b0 && key < runs.b0 + runs.n0) ||
-                                         (key >= runs.b1 && key < runs.b1 + runs.n1));
-          if (!vis) s[cc] = -INFINITY;
-        }
-      }
+      // A row past the end of the image's queries is never written back, and its P row reaches
+      // only its own O row (the tensor-core product is row by row), so it skips the masking:
+      // its Q row (the next image's query, or the TMA's zero fill) needs no -inf either.
+      const bool all_in = !row_valid ||
+                          (kp >= runs.b0 && kp + BN <= runs.b0 + runs.n0) ||
+                          (kp >= runs.b1 && kp + BN <= runs.b1 + runs.n1);
+      if (!all_in) mask_scores<BN>(runs, kp, s);
       // the tile's max in four independent chains of three-input maxima: 12 + 14 x 8 + 4 keys
       static_assert(BN == 128, "the max chains cover 128 keys");
       float mx0 = fmax3(s[0], s[1], s[2]), mx1 = fmax3(s[3], s[4], s[5]);
