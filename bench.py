@@ -370,10 +370,11 @@ class C4Sharded(Workload):
 
 class C5Full(Workload):
     """C5: DiT full-mask self-attention, 32760 tokens, 12 heads x 128, bf16 in / f32 accumulate,
-    bf16 out; (head, 128-query tile) units split evenly over the ranks."""
+    bf16 out; the query rows split over the ranks in whole 256-row pairs, one call per rank
+    over all heads (the keys and values whole on every rank)."""
 
     def __init__(self, torch, fa, rank, world):
-        from fusor_attn.shard import head_tile_units
+        from fusor_attn.shard import query_row_shards
         self.torch, self.fa, self.name = torch, fa, "c5"
         self.sharded = True
         self.kernel = "fmha2_kernel"  # bf16: two query tiles per CTA
@@ -382,43 +383,33 @@ class C5Full(Workload):
         gen = torch.Generator("cuda").manual_seed(5)
         self.qkv = torch.randn((self.n, 3 * hidden), device="cuda", generator=gen).to(torch.bfloat16)
         self.out = torch.empty((self.n, hidden), device="cuda", dtype=torch.bfloat16)
-        pieces = head_tile_units(self.heads, self.n, world)[rank]
-        # consecutive whole heads go in one call (one launch over all their query tiles)
-        self.calls = []
-        for h, a, b in pieces:
-            last = self.calls[-1] if self.calls else None
-            if last and a == 0 and b == self.n and last[2] == 0 and last[3] == self.n and last[0] + last[1] == h:
-                self.calls[-1] = (last[0], last[1] + 1, 0, self.n)
-            else:
-                self.calls.append((h, 1, a, b))
+        self.lo, self.hi = query_row_shards(self.n, world)[rank]
         self.tokens = self.n
         self.bound = "tensor"
-        self.launches_per_step = len(self.calls)
-        self.flops = sum(4.0 * self.d * (b - a) * self.n * count for _, count, a, b in self.calls)
+        self.launches_per_step = 1 if self.hi > self.lo else 0
+        self.flops = 4.0 * self.d * (self.hi - self.lo) * self.n * self.heads
         self.stride = 3 * hidden
         # e2e: the whole qkv from pinned host memory, this rank's output rows back
         self.h_qkv = self.qkv.cpu().pin_memory()
         self.h_out = torch.empty_like(self.out, device="cpu").pin_memory()
         self.h2d = self.h_qkv.numel() * 2
-        self.d2h = sum((b - a) * count * self.d * 2 for _, count, a, b in self.calls)
+        self.d2h = (self.hi - self.lo) * hidden * 2
 
     def step(self, mid=None):
-        fa, d, stride = self.fa, self.d, self.stride
+        fa, d, stride, lo, hi = self.fa, self.d, self.stride, self.lo, self.hi
         if mid is not None:
             mid.record()
-        for h, count, a, b in self.calls:
-            fa.attend_full(count, count, d, 1, b - a, self.n,
-                           fa.Operand(self.qkv, stride, a * stride + h * d),
-                           fa.Operand(self.qkv, stride, self.heads * d + h * d),
-                           fa.Operand(self.qkv, stride, 2 * self.heads * d + h * d),
-                           self.out[a:b, h * d:(h + count) * d])
+        if hi > lo:
+            fa.attend_full(self.heads, self.heads, d, 1, hi - lo, self.n,
+                           fa.Operand(self.qkv, stride, lo * stride),
+                           fa.Operand(self.qkv, stride, self.heads * d),
+                           fa.Operand(self.qkv, stride, 2 * self.heads * d),
+                           self.out[lo:hi])
 
     def e2e_step(self):
         self.qkv.copy_(self.h_qkv, non_blocking=True)
         self.step()
-        for h, count, a, b in self.calls:
-            self.h_out[a:b, h * self.d:(h + count) * self.d].copy_(
-                self.out[a:b, h * self.d:(h + count) * self.d], non_blocking=True)
+        self.h_out[self.lo:self.hi].copy_(self.out[self.lo:self.hi], non_blocking=True)
 
     def algorithmic(self):
         return self.flops
@@ -674,7 +665,7 @@ def config_of(name, world):
         "c3": f"sequences over {world} GPU(s), no collective",
         "c3bf16": f"sequences over {world} GPU(s), no collective",
         "c4": f"KV range over {world} GPU(s), NCCL all-gather of (max, sum, o)" if world > 1 else "1 GPU",
-        "c5": f"(head, 128-query tile) units over {world} GPU(s), no collective",
+        "c5": f"query rows in whole 256-row pairs over {world} GPU(s), all heads, no collective",
     }.get(name, f"replicas x{world}")
     c["l2"] = "inputs larger than L2" if name in ("c3", "c3bf16", "c4", "c5") else "L2 flushed between steps"
     if name in ("c1", "c2", "c3", "c3bf16"):

@@ -11,6 +11,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <queue>
 #include <string>
@@ -113,6 +114,51 @@ struct Buffer {
 };
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// The schedule of a bf16 full-mask call's units (query head, pair of 128-row query tiles) over
+// `sms` SMs: the first `whole` units run as one CTA each and every later unit as `splits` pieces
+// over equal shares of its `kv_tiles` key tiles. Units whose count is not a multiple of the SM
+// count leave the last wave partly idle; cutting the units after the last full wave (or the last
+// two) into shorter pieces fills it. Cost model, in units of one whole unit's time: a wave of
+// whole units costs 1, a wave of pieces 1 / splits plus a fixed cost per CTA of about 16 key
+// tiles (start, pipeline fill, partials and merge: measured on B200 with 256-tile units, where
+// a whole unit is about 500 us and splitting one in two costs about 30 us more in all). A split
+// is taken when it saves at least 2%.
+void plan_full_split(int64_t units, int sms, int kv_tiles, int64_t* whole, int* splits) {
+  *whole = units;
+  *splits = 1;
+  if (units <= 0 || sms <= 0 || units % sms == 0) return;
+  const int64_t full = units / sms;
+  const double unsplit = double(full + 1);
+  const double fixed = 16.0 / std::max(kv_tiles, 1);
+  double best = unsplit;
+  for (int64_t lead_waves = std::max<int64_t>(full - 1, 0); lead_waves <= full; ++lead_waves) {
+    const int64_t tail = units - lead_waves * sms;
+    for (int s = 2; s <= fa::kFmhaMaxSplits && kv_tiles >= 4 * s; ++s) {
+      const double cost = double(lead_waves) + double((tail * s + sms - 1) / sms) * (1.0 / s + fixed);
+      if (cost < best) {
+        best = cost;
+        *whole = lead_waves * sms;
+        *splits = s;
+      }
+    }
+  }
+  if (*splits > 1 && best >= 0.98 * unsplit) {
+    *whole = units;
+    *splits = 1;
+  }
+}
+
+// Partials and arrival counters of split full-mask calls, one set per (device, stream): calls on
+// one stream run in order, so they can share it; calls on different streams get their own.
+struct SplitWork {
+  Buffer partials;
+  Buffer counters;  // zero between launches (the last piece of a unit resets its counter)
+  int counters_epoch = -1;
+};
+std::mutex g_split_mutex;
+std::map<std::pair<int, cudaStream_t>, SplitWork> g_split_work;
+constexpr size_t kMaxSplitBytes = size_t(512) << 20;
 
 }  // namespace
 
@@ -1353,6 +1399,31 @@ int fa_attend_full(const fa_call* call, void* out, int64_t out_stride, void* str
     a.out_stride = out_stride;
     a.out_bf16 = k.out_dtype == FA_BF16 ? 1 : 0;
     a.err = dev->err;
+    if (fa::fmha_splits_supported(k.dtype == FA_BF16)) {
+      const int64_t units = int64_t(k.images) * ((a.q_tiles + 1) / 2) * k.heads;
+      int64_t whole = units;
+      int splits = 1;
+      plan_full_split(units, dev->sms, (k.keys + 127) / 128, &whole, &splits);
+      const size_t tail = size_t(units - whole);
+      const size_t o_bytes = align_up(tail * splits * 256 * k.head_dim * 4, 256);
+      const size_t ml_bytes = align_up(tail * splits * 256 * 2 * 4, 256);
+      if (splits > 1 && o_bytes + ml_bytes <= kMaxSplitBytes) {
+        std::lock_guard<std::mutex> lock(g_split_mutex);
+        SplitWork& w = g_split_work[{device, s}];
+        if (int rc = w.partials.ensure(o_bytes + ml_bytes, s)) return rc;
+        const int epoch = dev->epoch.load();
+        if (tail * 8 * sizeof(int) > w.counters.bytes || w.counters_epoch != epoch) {
+          if (int rc = w.counters.ensure(tail * 8 * sizeof(int), s)) return rc;
+          FA_CUDA(cudaMemsetAsync(w.counters.ptr, 0, w.counters.bytes, s), "clear split counters");
+          w.counters_epoch = epoch;
+        }
+        a.whole_units = int(whole);
+        a.splits = splits;
+        a.part_o = static_cast<float*>(w.partials.ptr);
+        a.part_ml = reinterpret_cast<float*>(static_cast<unsigned char*>(w.partials.ptr) + o_bytes);
+        a.counters = static_cast<int*>(w.counters.ptr);
+      }
+    }
     fa::FmhaLaunch l{k.dtype == FA_BF16 ? 1 : 0, k.head_dim,
                      static_cast<const unsigned char*>(k.query.values) + k.query.offset * esize,
                      uint64_t(k.images) * k.queries, uint64_t(k.heads), uint64_t(k.query.stride),

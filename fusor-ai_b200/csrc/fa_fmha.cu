@@ -92,8 +92,17 @@ cudaError_t launch_bf16_pairs(const FmhaLaunch& l, cudaStream_t stream) {
     if (err != cudaSuccess) return err;
     configured = true;
   }
-  const dim3 grid(l.args.images * ((l.args.q_tiles + 1) / 2), l.args.heads);
-  return launch_pdl(kernel, grid, dim3(kFmha2Threads), S::kSmemBytes, stream, qm, km, vm, l.args);
+  const int64_t units = int64_t(l.args.images) * ((l.args.q_tiles + 1) / 2) * l.args.heads;
+  int64_t grid = units;
+  if (l.args.splits > 1) {
+    if (l.args.splits > kFmhaMaxSplits || l.args.whole_units < 0 || l.args.whole_units > units ||
+        l.args.part_o == nullptr || l.args.part_ml == nullptr || l.args.counters == nullptr)
+      return cudaErrorInvalidValue;
+    grid = l.args.whole_units + (units - l.args.whole_units) * l.args.splits;
+  }
+  if (grid > 0x7fffffff) return cudaErrorInvalidValue;
+  return launch_pdl(kernel, dim3(unsigned(grid)), dim3(kFmha2Threads), S::kSmemBytes, stream, qm,
+                    km, vm, l.args);
 }
 
 }  // namespace
@@ -107,6 +116,15 @@ bool encode_cache_map_bf16(void* map, const void* base, uint64_t rows, uint64_t 
 bool fmha_supported(int dtype_bf16, int head_dim) {
   (void)dtype_bf16;
   return (head_dim == 64 || head_dim == 128) && encode_fn() != nullptr;
+}
+
+bool fmha_splits_supported(int dtype_bf16) {
+#ifdef FA_FMHA_ONE_TILE
+  (void)dtype_bf16;
+  return false;
+#else
+  return dtype_bf16 != 0;
+#endif
 }
 
 int fmha_block_n(int dtype_bf16, int head_dim) {

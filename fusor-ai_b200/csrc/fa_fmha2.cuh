@@ -13,6 +13,12 @@
 // thread's MMAs in issue order, so PV_i reads P_i before S_i is written again).
 // A query tile takes part in the KV tiles its rows see (the union of their key runs); the other
 // tile's barriers count only its own participating tiles.
+// Schedule (FmhaArgs::whole_units / splits): a 1-D grid over the units (query head, pair of query
+// tiles), head-major. The leading units run whole; with splits > 1 each later unit runs as that
+// many consecutive CTAs, each over an equal share of the pair's KV tiles, so that the last waves
+// of a call whose units do not fill the SMs evenly are cut into shorter pieces. A piece writes
+// its rows' (max, sum, unnormalised O) partials; the last piece of the unit to finish (an
+// arrival counter) merges them in log-sum-exp fashion and writes the output.
 #pragma once
 
 #include "fa_fmha.cuh"
@@ -36,6 +42,96 @@ struct Fmha2Shape {
   static constexpr size_t kSmemBytes = kSmemUsed > 122880 ? kSmemUsed : 122880;
   static_assert(D == 64 || D == 128, "head_dim 64 or 128");
 };
+
+// The last piece of a split unit: row `orow`'s output (query head `head`) from the n_pieces
+// partials (max, sum, unnormalised O) at slots slot0 + j x 256, merged in log-sum-exp fashion.
+template <int D>
+__device__ __forceinline__ void merge_pieces(const FmhaArgs& a, int64_t slot0, int n_pieces,
+                                          int64_t orow, int head) {
+  constexpr int kSlots = 256;  // rows of a pair of query tiles
+  float m_max = -INFINITY;
+  for (int j = 0; j < n_pieces; ++j)
+    m_max = fmaxf(m_max, __ldcg(a.part_ml + 2 * (slot0 + int64_t(j) * kSlots)));
+  float w[kFmhaMaxSplits];
+  float l_total = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kFmhaMaxSplits; ++j) {
+    w[j] = 0.0f;
+    if (j >= n_pieces) continue;
+    const float* ml = a.part_ml + 2 * (slot0 + int64_t(j) * kSlots);
+    const float mj = __ldcg(ml);
+    if (mj == -INFINITY) continue;  // no visible key in that piece
+    w[j] = exp2_approx(mj - m_max);
+    l_total = fmaf(w[j], __ldcg(ml + 1), l_total);
+  }
+  const float inv = l_total > 0.0f ? 1.0f / l_total : 0.0f;
+#pragma unroll 1
+  for (int cc = 0; cc < D / 32; ++cc) {
+    float acc[32];
+#pragma unroll
+    for (int e = 0; e < 32; ++e) acc[e] = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kFmhaMaxSplits; ++j) {
+      if (j >= n_pieces || w[j] == 0.0f) continue;
+      const float4* src =
+          reinterpret_cast<const float4*>(a.part_o + (slot0 + int64_t(j) * kSlots) * D + cc * 32);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float4 v = __ldcg(src + e);
+        acc[4 * e] = fmaf(w[j], v.x, acc[4 * e]);
+        acc[4 * e + 1] = fmaf(w[j], v.y, acc[4 * e + 1]);
+        acc[4 * e + 2] = fmaf(w[j], v.z, acc[4 * e + 2]);
+        acc[4 * e + 3] = fmaf(w[j], v.w, acc[4 * e + 3]);
+      }
+    }
+    if (a.out_bf16) {
+      uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) +
+                                            orow * a.out_stride + head * D + cc * 32);
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        dst[e] = make_uint4(tc::pack_bf16(acc[8 * e + 0] * inv, acc[8 * e + 1] * inv),
+                            tc::pack_bf16(acc[8 * e + 2] * inv, acc[8 * e + 3] * inv),
+                            tc::pack_bf16(acc[8 * e + 4] * inv, acc[8 * e + 5] * inv),
+                            tc::pack_bf16(acc[8 * e + 6] * inv, acc[8 * e + 7] * inv));
+    } else {
+      float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + orow * a.out_stride +
+                                              head * D + cc * 32);
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        dst[e] = make_float4(acc[4 * e] * inv, acc[4 * e + 1] * inv, acc[4 * e + 2] * inv,
+                             acc[4 * e + 3] * inv);
+    }
+  }
+}
+
+// A CTA's unit of work: query head, image, first query row of the pair, and its piece.
+struct Fmha2Unit {
+  int head, image, r0;
+  int piece, n_pieces, tail_unit;  // n_pieces 1 for a whole unit
+};
+
+__device__ __forceinline__ Fmha2Unit fmha2_unit(const FmhaArgs& a, uint32_t cta) {
+  const int pairs = (a.q_tiles + 1) / 2;
+  const int per_head = a.images * pairs;
+  const int whole = a.splits > 1 ? a.whole_units : per_head * a.heads;
+  Fmha2Unit u;
+  int unit = int(cta);
+  u.piece = 0;
+  u.n_pieces = 1;
+  u.tail_unit = 0;
+  if (unit >= whole) {
+    const int p = unit - whole;
+    u.tail_unit = p / a.splits;
+    u.piece = p % a.splits;
+    u.n_pieces = a.splits;
+    unit = whole + u.tail_unit;
+  }
+  u.head = unit / per_head;
+  const int pair_id = per_head - 1 - unit % per_head;  // heavier (later, for causal masks) first
+  u.image = pair_id / pairs;
+  u.r0 = (pair_id % pairs) * 256;
+  return u;
+}
 
 constexpr int kFmha2Threads = 320;
 
@@ -68,13 +164,9 @@ __global__ void __launch_bounds__(kFmha2Threads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_drained + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int head = blockIdx.y;
+  const Fmha2Unit u = fmha2_unit(a, ctaid_x());
+  const int head = u.head, image = u.image, r0 = u.r0, piece = u.piece, n_pieces = u.n_pieces;
   const int kv = head / a.group;
-  const int pairs = (a.q_tiles + 1) / 2;
-  // heavier (later, for causal masks) tiles first
-  const int pair_id = int(gridDim.x) - 1 - int(blockIdx.x);
-  const int image = pair_id / pairs;
-  const int r0 = (pair_id % pairs) * 2 * BM;  // first row of query tile 0
 
   // KV tiles each query tile's rows see (the union of their key runs), and their union.
   int tb[2], te[2];
@@ -89,6 +181,20 @@ __global__ void __launch_bounds__(kFmha2Threads, 1)
     if (a.kind == 3) { lo = 0; hi = a.end; }  // Groups: every run lies in [0, end)
     tb[i] = lo / BN;
     te[i] = hi > lo ? (hi + BN - 1) / BN : tb[i];
+  }
+  if (n_pieces > 1) {
+    // this piece's share of the union of the two tiles' KV tiles
+    const bool u0 = te[0] > tb[0], u1 = te[1] > tb[1];
+    const int ub = u0 && u1 ? min(tb[0], tb[1]) : (u0 ? tb[0] : tb[1]);
+    const int ue = u0 && u1 ? max(te[0], te[1]) : (u0 ? te[0] : te[1]);
+    const int n = (u0 || u1) ? ue - ub : 0;
+    const int lo = ub + int(int64_t(n) * piece / n_pieces);
+    const int hi = ub + int(int64_t(n) * (piece + 1) / n_pieces);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      tb[i] = max(tb[i], lo);
+      te[i] = max(min(te[i], hi), tb[i]);
+    }
   }
   const bool any0 = te[0] > tb[0], any1 = te[1] > tb[1];
   const int t0 = any0 && any1 ? min(tb[0], tb[1]) : (any0 ? tb[0] : tb[1]);
@@ -320,33 +426,76 @@ __global__ void __launch_bounds__(kFmha2Threads, 1)
       mbar_arrive(&p_full[i]);
       ++c;
     }
-    // ---- epilogue: O / l -------------------------------------------------------------------
-    if (__all_sync(0xffffffffu, ok && c > 0 && mbar_wait(&o_final[i], 0, a.err))) {
+    const bool have = __all_sync(0xffffffffu, ok && c > 0 && mbar_wait(&o_final[i], 0, a.err));
+    // The unit is decoded again from the CTA index (a volatile read: nothing of it stays live
+    // through the softmax loop, whose registers are at the kernel's limit).
+    const Fmha2Unit e = fmha2_unit(a, ctaid_x());
+    const int64_t orow_base = int64_t(e.image) * a.rows + e.r0 + i * BM + wq * 32;  // + lane
+    const bool row_ok = e.r0 + i * BM + wq * 32 + lane < a.rows;
+    if (e.n_pieces > 1) {
+      // ---- a piece: its partials, then the last piece of the unit merges ------------------
+      const int row_in_pair = i * BM + wq * 32 + lane;
+      const int64_t slot0 = int64_t(e.tail_unit) * e.n_pieces * (2 * BM) + row_in_pair;
+      const int64_t slot = slot0 + int64_t(e.piece) * (2 * BM);
+      if (have) {
+        tc::fence_after_sync();
+#pragma unroll 1
+        for (int cc = 0; cc < D / 32; ++cc) {
+          uint32_t o[32];
+          tc::tmem_ld32_wait(o_base + cc * 32, o);
+          if (!row_ok) continue;
+          float4* dst = reinterpret_cast<float4*>(a.part_o + slot * D + cc * 32);
+#pragma unroll
+          for (int x = 0; x < 8; ++x)
+            dst[x] = make_float4(__uint_as_float(o[4 * x]), __uint_as_float(o[4 * x + 1]),
+                                 __uint_as_float(o[4 * x + 2]), __uint_as_float(o[4 * x + 3]));
+        }
+      }
+      if (row_ok) {
+        a.part_ml[2 * slot] = have ? m_used : -INFINITY;
+        a.part_ml[2 * slot + 1] = have ? l_sum : 0.0f;
+      }
+      // Each warp's 32 rows count their pieces on their own counter: the warp of the last piece
+      // to arrive merges those rows (no barrier across the CTA's warps).
+      __threadfence();  // the partials are visible device-wide before the arrival is counted
+      __syncwarp();
+      int last = 0;
+      if (lane == 0) {
+        int* counter = a.counters + int64_t(e.tail_unit) * 8 + (i * 4 + wq);
+        last = atomicAdd(counter, 1) == e.n_pieces - 1;
+        if (last) *counter = 0;  // every piece has arrived: ready for the next launch
+      }
+      if (__shfl_sync(0xffffffffu, last, 0) != 0 && row_ok) {
+        __threadfence();
+        merge_pieces<D>(a, slot0, e.n_pieces, orow_base + lane, e.head);
+      }
+    } else if (have) {
+      // ---- epilogue: O / l -----------------------------------------------------------------
       tc::fence_after_sync();
       const float inv = l_sum > 0.0f ? 1.0f / l_sum : 0.0f;
-      const int64_t orow = int64_t(image) * a.rows + r;
+      const int64_t orow = orow_base + lane;
 #pragma unroll 1
       for (int cc = 0; cc < D / 32; ++cc) {
         uint32_t o[32];
         tc::tmem_ld32_wait(o_base + cc * 32, o);
-        if (!row_valid) continue;
+        if (!row_ok) continue;
         if (a.out_bf16) {
           uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) +
-                                                orow * a.out_stride + head * D + cc * 32);
+                                                orow * a.out_stride + e.head * D + cc * 32);
 #pragma unroll
-          for (int e = 0; e < 4; ++e)
-            dst[e] = make_uint4(
-                tc::pack_bf16(__uint_as_float(o[8 * e + 0]) * inv, __uint_as_float(o[8 * e + 1]) * inv),
-                tc::pack_bf16(__uint_as_float(o[8 * e + 2]) * inv, __uint_as_float(o[8 * e + 3]) * inv),
-                tc::pack_bf16(__uint_as_float(o[8 * e + 4]) * inv, __uint_as_float(o[8 * e + 5]) * inv),
-                tc::pack_bf16(__uint_as_float(o[8 * e + 6]) * inv, __uint_as_float(o[8 * e + 7]) * inv));
+          for (int x = 0; x < 4; ++x)
+            dst[x] = make_uint4(
+                tc::pack_bf16(__uint_as_float(o[8 * x + 0]) * inv, __uint_as_float(o[8 * x + 1]) * inv),
+                tc::pack_bf16(__uint_as_float(o[8 * x + 2]) * inv, __uint_as_float(o[8 * x + 3]) * inv),
+                tc::pack_bf16(__uint_as_float(o[8 * x + 4]) * inv, __uint_as_float(o[8 * x + 5]) * inv),
+                tc::pack_bf16(__uint_as_float(o[8 * x + 6]) * inv, __uint_as_float(o[8 * x + 7]) * inv));
         } else {
           float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) +
-                                                  orow * a.out_stride + head * D + cc * 32);
+                                                  orow * a.out_stride + e.head * D + cc * 32);
 #pragma unroll
-          for (int e = 0; e < 8; ++e)
-            dst[e] = make_float4(__uint_as_float(o[4 * e]) * inv, __uint_as_float(o[4 * e + 1]) * inv,
-                                 __uint_as_float(o[4 * e + 2]) * inv, __uint_as_float(o[4 * e + 3]) * inv);
+          for (int x = 0; x < 8; ++x)
+            dst[x] = make_float4(__uint_as_float(o[4 * x]) * inv, __uint_as_float(o[4 * x + 1]) * inv,
+                                 __uint_as_float(o[4 * x + 2]) * inv, __uint_as_float(o[4 * x + 3]) * inv);
         }
       }
     }

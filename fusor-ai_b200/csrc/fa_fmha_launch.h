@@ -26,7 +26,21 @@ struct FmhaArgs {
   int64_t out_stride;
   int out_bf16;
   unsigned* err;
+  // The two-tile kernel's schedule: units (query head, pair of query tiles), head-major; units
+  // [0, whole_units) run whole, one CTA each, and with splits > 1 every later unit runs as
+  // `splits` consecutive CTAs over equal shares of its KV tiles. A piece writes its rows'
+  // (max, sum, unnormalised O) to part_ml / part_o (slot (tail unit x splits + piece) x 256 +
+  // row of the pair); each of its 8 softmax warps counts itself in counters[tail unit x 8 +
+  // warp], and the warp of the last piece to arrive merges its 32 rows, writes them out and sets
+  // the counter back to zero.
+  int whole_units;
+  int splits;
+  float* part_o;
+  float* part_ml;
+  int* counters;
 };
+
+constexpr int kFmhaMaxSplits = 8;
 
 
 // Q, K and V as 3-D tensors of [z][row][head_dim] elements for the TMA maps: Q rows are query
@@ -45,6 +59,8 @@ struct FmhaLaunch {
 };
 
 bool fmha_supported(int dtype_bf16, int head_dim);
+// Whether launch_fmha honours FmhaArgs::splits for these operands (the two-tile bf16 kernel).
+bool fmha_splits_supported(int dtype_bf16);
 // A TMA map (written to the 128 bytes at `map`, 64-byte aligned) over a bf16 cache's keys or
 // values: [z][rows][128] elements, z_stride_bytes apart, 64 x 128 boxes, 128-byte swizzle (the
 // tensor-core decode's K and V tiles).

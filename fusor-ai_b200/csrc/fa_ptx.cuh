@@ -149,6 +149,14 @@ __device__ __forceinline__ float ld_cluster_f32(const float* local, uint32_t ran
   return v;
 }
 
+// blockIdx.x read as a volatile special register: never merged with an earlier read, so a value
+// derived from it is recomputed where it is needed instead of being held in a register.
+__device__ __forceinline__ uint32_t ctaid_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%ctaid.x;" : "=r"(r));
+  return r;
+}
+
 // max(a, b, c) in one instruction (sm_100a's three-input max).
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float r;

@@ -7,8 +7,8 @@ plumbing, a collective only where the path has a real exchange step.
   its own KvCache (`kv_shards`); every rank attends its range and produces per-head
   (max, sum, partial output) triples, which one all-gather over NCCL brings to every rank for
   the log-sum-exp merge (`ShardedDecode`).
-- Full-mask attention: (head, 128-query tile) units split evenly over ranks, every rank reading
-  the K/V of its heads locally (`head_tile_units`), no collective.
+- Full-mask attention: contiguous runs of 256-query pairs (all heads) split evenly over ranks,
+  every rank reading the K/V locally and making one call (`query_row_shards`), no collective.
 
 The reference has no multi-device path (one process, one thread team); these are the B200 forms
 of its one-call semantics, checked against the single-GPU result by the tests.
@@ -35,23 +35,13 @@ def kv_shards(keys: int, world: int):
     return [(keys * r // world, keys * (r + 1) // world) for r in range(world)]
 
 
-def head_tile_units(heads: int, rows: int, world: int, tile: int = 128):
-    """Each rank's (head, first row, end row) pieces: the heads x ceil(rows / tile) units of a
-    full-mask call split into `world` contiguous, equal runs (head-major)."""
-    tiles = (rows + tile - 1) // tile
-    total = heads * tiles
-    out = []
-    for r in range(world):
-        a, b = total * r // world, total * (r + 1) // world
-        pieces = []
-        u = a
-        while u < b:
-            h = u // tiles
-            t_end = min(b, (h + 1) * tiles)
-            pieces.append((h, (u % tiles) * tile, min(rows, ((t_end - 1) % tiles + 1) * tile)))
-            u = t_end
-        out.append(pieces)
-    return out
+def query_row_shards(rows: int, world: int, pair: int = 256):
+    """Each rank's query rows [lo, hi) of a full-mask call: the ceil(rows / pair) pairs of query
+    tiles (the two-tile kernel's unit, one per query head) in `world` contiguous, equal runs, so
+    that every rank makes one call over all heads and ragged tiles occur only at the end."""
+    pairs = (rows + pair - 1) // pair
+    return [(min(rows, pairs * r // world * pair), min(rows, pairs * (r + 1) // world * pair))
+            for r in range(world)]
 
 
 @dataclass

@@ -8,7 +8,7 @@ import socket
 import numpy as np
 import pytest
 
-from fusor_attn.shard import head_tile_units, kv_shards, shard_sequences
+from fusor_attn.shard import kv_shards, query_row_shards, shard_sequences
 
 LOG2E = 1.4426950408889634
 
@@ -30,14 +30,16 @@ def test_kv_shards_tile_the_range():
         assert max(h - l for l, h in s) - min(h - l for l, h in s) <= 1
 
 
-def test_head_tile_units_cover_every_row_of_every_head_once():
-    for heads, rows in ((12, 32760), (12, 300), (5, 129)):
+def test_query_row_shards_tile_the_rows_in_whole_pairs():
+    for rows in (32760, 300, 129, 256, 5):
         for world in (1, 2, 3, 8):
-            seen = np.zeros((heads, rows), np.int32)
-            for pieces in head_tile_units(heads, rows, world):
-                for h, a, b in pieces:
-                    seen[h, a:b] += 1
-            assert (seen == 1).all(), (heads, rows, world)
+            s = query_row_shards(rows, world)
+            assert s[0][0] == 0 and s[-1][1] == rows
+            assert all(a[1] == b[0] for a, b in zip(s, s[1:]))
+            # every boundary but the end falls on a 256-row pair
+            assert all(a % 256 == 0 for a, _ in s if a < rows)
+            pairs = [(-(-(hi - lo) // 256)) for lo, hi in s]
+            assert max(pairs) - min(pairs) <= 1, (rows, world, s)
 
 
 def partial_np(q, keys, values):
