@@ -247,7 +247,11 @@ int fa_merge_partials(const float* partials, int32_t shards, int32_t heads, int3
  * (non-causal) softmax attention of every query over every key of its image, scores scaled by
  * 1/sqrt(head_dim), into out (images*queries rows of out_stride elements, heads x head_dim
  * each, in call->out_dtype). The reference's int8 SageAttention-style approximation is replaced
- * by f32 (FA_F32 operands) or bf16-in / f32-accumulate (FA_BF16) arithmetic. */
+ * by f32 (FA_F32 operands) or bf16-in / f32-accumulate (FA_BF16) arithmetic.
+ * A bf16 call whose (query head, 256-query) units leave the GPU's last wave partly idle runs
+ * those units in pieces over key ranges, merged on the device; their partials live in a
+ * workspace kept per (device, stream) and grown on demand (the first such call on a stream may
+ * allocate device memory: make it before a stream capture). */
 int fa_attend_full(const fa_call* call, void* out, int64_t out_stride, void* stream);
 
 /* fa_attend (KvCache::attend) for callers that cannot allocate device memory when they call:
