@@ -277,6 +277,51 @@ class SingleDecode(Workload):
         return float(self.bytes)
 
 
+class ProjectedInput(Workload):
+    """Stack::attention_input of one decode row with its qkv projection on the device
+    (fa_attention_input_projected: projection, RoPE and keep in one kernel), Llama-8B-shaped:
+    32/8 heads x 128, hidden 4096, f32 weights (6144 x 4096, 100.7 MB) and bias, position 4096.
+    Bound by the weight bytes; L2 (126 MB) flushed between steps."""
+
+    def __init__(self, torch, fa):
+        self.torch, self.fa, self.name = torch, fa, "proj"
+        self.kernel = "project_keep_kernel"
+        heads, kv, d, self.hidden, position = 32, 8, 128, 4096, 4096
+        shape = fa.Shape(1, heads, kv, d)
+        self.cache = fa.KvCache(shape, position + 1)
+        gen = torch.Generator("cuda").manual_seed(9)
+        self.weight = torch.randn((shape.qkv, self.hidden), device="cuda", generator=gen) / 64.0
+        self.bias = torch.randn((shape.qkv,), device="cuda", generator=gen)
+        self.x = torch.randn((1, self.hidden), device="cuda", generator=gen)
+        self.span = fa.Span(1, position, fa.Mask.causal())
+        self.angles = torch.from_numpy(fa.rotary_angles(fa.Rotation(base=1e6), d, [position])).cuda()
+        self.q = torch.zeros((1, shape.width), device="cuda")
+        self.tokens = 1
+        self.launches_per_step = 1
+        self.flush_l2 = True
+        self.graphs = True
+        self.h_x = self.x.cpu().pin_memory()
+        self.h_q = torch.zeros_like(self.q, device="cpu").pin_memory()
+        self.h2d = self.h_x.numel() * 4
+        self.d2h = self.h_q.numel() * 4
+        self.bytes = (self.weight.numel() + self.bias.numel() + self.x.numel()
+                      + 2 * kv * d + shape.width) * 4
+
+    def phases(self):
+        return (lambda: None,
+                lambda: self.cache.attention_input_projected(
+                    0, self.span, self.x, self.weight, self.bias, angles=self.angles,
+                    rope=self.fa.ROPE_HALF, q_out=self.q))
+
+    def e2e_step(self):
+        self.x.copy_(self.h_x, non_blocking=True)
+        self.phases()[1]()
+        self.h_q.copy_(self.q, non_blocking=True)
+
+    def algorithmic(self):
+        return float(self.bytes)
+
+
 class C2Prefill(Workload):
     """C2: 512 rows from position 0, causal, 14/2 heads, d64; the cache written by the pass."""
 
@@ -582,6 +627,8 @@ def run_ours(args):
             return C5Full(torch, fa, rank, world)
         if name == "c2":
             return C2Prefill(torch, fa)
+        if name == "proj":
+            return ProjectedInput(torch, fa)
         raise SystemExit(f"unknown config {name}")
 
     w = build(args.config)
@@ -611,7 +658,7 @@ def run_ours(args):
     torch.cuda.empty_cache()
     if args.config == "c3" and not args.no_extras and args.sequences == C3_SEQS:
         extras = {}
-        names = ("c1", "c2", "c3bf16", "c4", "c5") if world == 1 else ("c4", "c5")
+        names = ("c1", "c2", "c3bf16", "c4", "c5", "proj") if world == 1 else ("c4", "c5")
         for name in names:
             x = build(name)
             xs = min(steps, 50 if name == "c5" else 200)
@@ -659,6 +706,9 @@ def config_of(name, world):
                "head_dim": 128},
         "c5": {"workload": "C5 DiT full-mask self-attention", "tokens": 32760, "heads": 12,
                "head_dim": 128, "dtype": "bf16 in, f32 accumulate, bf16 out", "mask": "full"},
+        "proj": {"workload": "attention input with its qkv projection (fused), one decode row",
+                 "heads": 32, "kv_heads": 8, "head_dim": 128, "hidden": 4096,
+                 "weights": "f32 6144 x 4096 + bias", "position": 4096},
     }
     c = dict(cfgs[name])
     c["parallelism"] = {
@@ -668,7 +718,7 @@ def config_of(name, world):
         "c5": f"query rows in whole 256-row pairs over {world} GPU(s), all heads, no collective",
     }.get(name, f"replicas x{world}")
     c["l2"] = "inputs larger than L2" if name in ("c3", "c3bf16", "c4", "c5") else "L2 flushed between steps"
-    if name in ("c1", "c2", "c3", "c3bf16"):
+    if name in ("c1", "c2", "c3", "c3bf16", "proj"):
         c["launch"] = "the step's calls replayed as captured CUDA graphs"
     return c
 
@@ -736,7 +786,7 @@ def main():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", default="c3", choices=["c1", "c2", "c3", "c3bf16", "c4", "c5"])
+    ap.add_argument("--config", default="c3", choices=["c1", "c2", "c3", "c3bf16", "c4", "c5", "proj"])
     ap.add_argument("--sequences", type=int, default=C3_SEQS,
                     help="C3 sequences (a smaller batch for profiling captures)")
     ap.add_argument("--no-extras", action="store_true")

@@ -112,6 +112,26 @@ struct GateArgs {
 };
 cudaError_t launch_gate(const GateArgs& args, cudaStream_t stream);
 
+// The QKV projection fused with head norm, RoPE and keep (fa_project.cu). The RopeArgs give the
+// epilogue (its qkv is not read; gate_heads must be 0); grid (head units, row blocks, splits).
+struct ProjectArgs {
+  const float* x;        // row r at x + r*x_stride: hidden values
+  int64_t x_stride;
+  const float* weight;   // output column c at weight + c*w_stride: hidden values
+  int64_t w_stride;
+  const float* bias;     // (heads + 2 kv_heads) x head_dim values, or nullptr
+  int hidden, rows;
+  int row_block;         // rows per CTA, a multiple of the rows per pass
+  int splits, chunk;     // splits of the hidden dimension, chunk values each (a multiple of 128)
+  float* partials;       // [unit][row block][split][row_block][head_dim] when splits > 1
+  int* counters;         // [unit][row block], zero between launches
+  float* qkv_out;        // optional: the projected rows, before head norm and RoPE
+  int64_t qkv_out_stride;
+};
+// nr: rows per pass (1, 4 or 8); smem: (row_block x chunk + row_block x head_dim) floats.
+cudaError_t launch_project(int kt, int nr, const ProjectArgs& p, const RopeArgs& r, size_t smem,
+                           cudaStream_t stream);
+
 // The tensor-core decode over bf16 caches (fa_decode_tc.cu): `grid` persistent CTAs.
 struct DtcArgs;
 cudaError_t launch_decode_tc(const DtcArgs& args, int grid, cudaStream_t stream);

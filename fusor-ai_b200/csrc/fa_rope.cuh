@@ -56,14 +56,12 @@ __device__ __forceinline__ __nv_bfloat16 to_kv<__nv_bfloat16>(float x) {
   return __float2bfloat16_rn(x);
 }
 
+// Head `unit` (the qkv row's numbering: query heads, gate heads, key heads, value heads) of row
+// `row`, whose head_dim values are at `head`: head norm and RoPE of a query or key head, then the
+// rotated query into q_out or the key/value head kept in the row's cache. One warp.
 template <typename KT>
-__global__ void __launch_bounds__(kRopeWarps * 32) rope_keep_kernel(const __grid_constant__ RopeArgs a) {
-  pdl_trigger();  // the attention kernel after it may be scheduled now (it waits for this one)
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x;
-  const int unit = blockIdx.y * kRopeWarps + warp;
-  const int units = a.heads + a.gate_heads + 2 * a.kv_heads;
-  if (unit >= units) return;
+__device__ __forceinline__ void rope_keep_head(const RopeArgs& a, int row, int unit, int lane,
+                                               const float* head) {
   const bool is_query = unit < a.heads;
   if (!is_query && unit < a.heads + a.gate_heads) return;
   const int kunit = unit - a.gate_heads;  // the cache's numbering: query heads, then kv heads
@@ -71,7 +69,6 @@ __global__ void __launch_bounds__(kRopeWarps * 32) rope_keep_kernel(const __grid
   if (!is_query && !a.keep) return;
   const int d = a.head_dim, half = d / 2;
   const int rd = a.rotary_dim > 0 ? a.rotary_dim : d, rhalf = rd / 2;
-  const float* head = a.qkv + int64_t(row) * a.qkv_stride + int64_t(unit) * d;
 
   // Each lane holds the pairs p = lane, lane + 32, ... (up to 4 pairs: head_dim <= 256). Pair p
   // < rotary_dim/2 is the rotated pair (p, p + rotary_dim/2) by halves or (2p, 2p + 1)
@@ -157,6 +154,17 @@ __global__ void __launch_bounds__(kRopeWarps * 32) rope_keep_kernel(const __grid
     target[lo[j]] = to_kv<KT>(x[j]);
     target[hi[j]] = to_kv<KT>(y[j]);
   }
+}
+
+template <typename KT>
+__global__ void __launch_bounds__(kRopeWarps * 32) rope_keep_kernel(const __grid_constant__ RopeArgs a) {
+  pdl_trigger();  // the attention kernel after it may be scheduled now (it waits for this one)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x;
+  const int unit = blockIdx.y * kRopeWarps + warp;
+  if (unit >= a.heads + a.gate_heads + 2 * a.kv_heads) return;
+  rope_keep_head<KT>(a, row, unit, lane,
+                     a.qkv + int64_t(row) * a.qkv_stride + int64_t(unit) * a.head_dim);
 }
 
 }  // namespace fa

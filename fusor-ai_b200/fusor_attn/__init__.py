@@ -70,6 +70,16 @@ class _HeadNorm(C.Structure):
     _fields_ = [("q_norm", C.c_void_p), ("k_norm", C.c_void_p), ("eps", C.c_float)]
 
 
+class _Linear(C.Structure):
+    _fields_ = [("weight", C.c_void_p), ("weight_stride", C.c_int64), ("bias", C.c_void_p),
+                ("inputs", C.c_int32), ("outputs", C.c_int32)]
+
+
+def _linear(weight, bias=None):
+    """A device f32 weight matrix (outputs x inputs, rows weight.stride(0) apart) and bias."""
+    return _Linear(_dptr(weight), weight.stride(0), _dptr(bias), weight.shape[1], weight.shape[0])
+
+
 class _Operand(C.Structure):
     _fields_ = [("values", C.c_void_p), ("stride", C.c_int64), ("offset", C.c_int64)]
 
@@ -116,6 +126,10 @@ SIGNATURES = {
     "fa_attention_host": (C.c_int, [_P, _I32, _P, _I32, _P, _P, _P, _I64, _P, _I64, _P]),
     "fa_attention_batch": (C.c_int, [_P, _P, _I32, _I32, _I32, _P, _P, _P, _I64, _P, _I64, _P]),
     "fa_attention_input_batch": (C.c_int, [_P, _P, _I32, _I32, _I32, _P, _P, _P, _I64, _P, _I64, _P]),
+    "fa_attention_input_projected": (C.c_int, [_P, _I32, _P, _I32, _P, _P, _P, _P, _I64, _P, _P,
+                                               _I64, _P]),
+    "fa_attention_input_projected_batch": (C.c_int, [_P, _P, _I32, _I32, _I32, _P, _P, _P, _P,
+                                                     _I64, _P, _I64, _P]),
     "fa_attend_batch": (C.c_int, [_P, _P, _I32, _I32, _P, _I64, _P, _I64, _P]),
     "fa_attend_partial": (C.c_int, [_P, _I32, _P, _I32, _I32, _P, _P]),
     "fa_attend_static": (C.c_int, [_P, _I32, _P, _P, _I64, _P, _I64, _P]),
@@ -325,6 +339,19 @@ class KvCache:
                                         _dptr(angles), nm, _dptr(qkv), qkv.stride(0),
                                         _dptr(q_out), _stream(stream)))
 
+    def attention_input_projected(self, layer: int, span: Span, x, weight, bias=None,
+                                  angles=None, rope: int = ROPE_HALF, norm=None, q_out=None,
+                                  qkv_out=None, stream=None):
+        """Stack::attention_input (layer.rs:175-209) whole: the qkv projection of the span's
+        input rows x (f32 weight: outputs x inputs, optional bias) fused with head norm, RoPE
+        and keep; the rotated queries into q_out, the projected rows into qkv_out."""
+        sp = span.c()
+        lin = _linear(weight, bias)
+        _check(lib().fa_attention_input_projected(
+            self._h, layer, C.byref(sp), rope if angles is not None else ROPE_NONE,
+            _dptr(angles), _norm(norm), C.byref(lin), _dptr(x), x.stride(0), _dptr(q_out),
+            _dptr(qkv_out), 0 if qkv_out is None else qkv_out.stride(0), _stream(stream)))
+
     def attend(self, layer: int, span: Span, q, out, stream=None):
         """KvCache::attend (transformer.rs:182-219) of rotated queries."""
         sp = span.c()
@@ -409,6 +436,16 @@ class Batch:
         _check(lib().fa_attention_input_batch(
             self.handles, self.spans, self.n, layer, rope if angles is not None else ROPE_NONE,
             _dptr(angles), _norm(norm), _dptr(qkv), qkv.stride(0), _dptr(q_out),
+            0 if q_out is None else q_out.stride(0), _stream(stream)))
+
+    def attention_input_projected(self, layer: int, x, weight, bias=None, q_out=None,
+                                  angles=None, rope: int = ROPE_HALF, norm=None, stream=None):
+        """The qkv projection of each sequence's input row (x row i) fused with head norm,
+        RoPE and keep into its own cache; the rotated queries into q_out."""
+        lin = _linear(weight, bias)
+        _check(lib().fa_attention_input_projected_batch(
+            self.handles, self.spans, self.n, layer, rope if angles is not None else ROPE_NONE,
+            _dptr(angles), _norm(norm), C.byref(lin), _dptr(x), x.stride(0), _dptr(q_out),
             0 if q_out is None else q_out.stride(0), _stream(stream)))
 
     def attend(self, layer: int, q, out, stream=None):

@@ -178,6 +178,39 @@ int fa_attention_input(fa_kvcache* cache, int32_t layer, const fa_span* span, in
                        const float* angles, const fa_head_norm* norm, const float* qkv,
                        int64_t qkv_stride, float* q_out, void* stream);
 
+/* The layer's qkv Linear (crates/kernels/src/linear.rs: the matrix, outputs x inputs, and the
+ * optional bias) with f32 weights, on the device. */
+typedef struct fa_linear {
+  const float* weight;   /* output c's inputs at weight + c * weight_stride */
+  int64_t weight_stride; /* elements, >= inputs; a multiple of 4 */
+  const float* bias;     /* outputs values, or NULL */
+  int32_t inputs;        /* the hidden width, a multiple of 4 */
+  int32_t outputs;       /* (heads + 2 kv_heads) x head_dim */
+} fa_linear;
+
+/* The whole of Stack::attention_input (layer.rs:175-209) on the device: the qkv projection
+ * (project_quads, linear.rs:52-71: qkv = x . W^T + b for f32 weights) of each of span->rows rows
+ * of x (f32, x_stride elements apart, 16-byte aligned), fused in one kernel with what
+ * fa_attention_input does after it: head norm, RoPE of the query and key heads, keep of the key
+ * and value heads at position first + row, the rotated queries into q_out (rows x heads x
+ * head_dim f32; may be NULL). The projected rows themselves (before head norm and RoPE) go to
+ * qkv_out (qkv_out_stride apart) when it is not NULL. Sums in f32, in another order than the
+ * reference's quad kernels (within float rounding of them). */
+int fa_attention_input_projected(fa_kvcache* cache, int32_t layer, const fa_span* span,
+                                 int32_t rope, const float* angles, const fa_head_norm* norm,
+                                 const fa_linear* qkv, const float* x, int64_t x_stride,
+                                 float* q_out, float* qkv_out, int64_t qkv_out_stride,
+                                 void* stream);
+
+/* The same for one decode row of each of `batch` sequences (their own caches, as in
+ * fa_attention_input_batch): x row i is sequence i's input, kept at spans[i].first; the rotated
+ * queries into q_out (batch rows, q_out_stride apart; may be NULL). */
+int fa_attention_input_projected_batch(fa_kvcache* const* caches, const fa_span* spans,
+                                       int32_t batch, int32_t layer, int32_t rope,
+                                       const float* angles, const fa_head_norm* norm,
+                                       const fa_linear* qkv, const float* x, int64_t x_stride,
+                                       float* q_out, int64_t q_out_stride, void* stream);
+
 /* The query half of fa_attention_input without a cache: head-norm (optional) and RoPE of the
  * `heads` query heads of each row of qkv into q_out (rows x q_out_stride f32). The ranks of a
  * KV-range-sharded decode that do not hold the new position rotate the query with this. */

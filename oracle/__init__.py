@@ -299,6 +299,17 @@ def attend_int8(heads, kv_heads, head_dim, q, k, v, fast=False) -> np.ndarray:
     return out
 
 
+def project(x: np.ndarray, weight: np.ndarray, bias=None) -> np.ndarray:
+    """Linear::project_quads for f32 weights (crates/kernels/src/linear.rs:52-71, the matmul of
+    crates/kernels/src/matmul.rs over an f32 matrix): out[r][c] = x[r] . weight[c] + bias[c],
+    summed here in f64 and rounded once to f32 (the reference's f32 quad sums are within float
+    rounding of it; the order of its additions is the backend's)."""
+    out = np.asarray(x, np.float64) @ np.asarray(weight, np.float64).T
+    if bias is not None:
+        out += np.asarray(bias, np.float64)
+    return out.astype(np.float32)
+
+
 def release():
     lib().oracle_team_release()
 
