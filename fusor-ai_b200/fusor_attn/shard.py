@@ -70,7 +70,8 @@ class ShardedDecode:
         self.out = torch.zeros((self.heads, self.head_dim), device="cuda")
         self.owner = self.lo <= self.position < self.hi
 
-    def step(self, qkv, angles, rope, dist=None):
+    def rotate(self, qkv, angles, rope):
+        """The query rotated on every rank; the new row kept on the rank holding its position."""
         import fusor_attn as fa
         if self.owner:
             # keep the new row at its slot in this shard; the rotated query comes back with it
@@ -78,10 +79,22 @@ class ShardedDecode:
             self.cache.attention_input(0, span, qkv, angles, rope, q_out=self.q)
         else:
             fa.rotate_queries(self.heads, self.head_dim, qkv, self.q, angles, rope)
+
+    def attend_local(self):
+        """This rank's key range into per-head (max, sum, o)."""
         self.cache.attend_partial(0, self.q, 0, self.hi - self.lo, self.partials)
+
+    def gather_merge(self, dist=None):
+        """Every rank's partials over NCCL, merged into `out`."""
+        import fusor_attn as fa
         if dist is not None and self.world > 1:
             dist.all_gather_into_tensor(self.gathered, self.partials, group=self.group)
         else:
             self.gathered[0].copy_(self.partials)
         fa.merge_partials(self.gathered, self.out)
         return self.out
+
+    def step(self, qkv, angles, rope, dist=None):
+        self.rotate(qkv, angles, rope)
+        self.attend_local()
+        return self.gather_merge(dist)
