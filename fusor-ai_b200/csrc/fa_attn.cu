@@ -1400,9 +1400,10 @@ int fa_attend_batch(fa_kvcache* const* caches, const fa_span* spans, int32_t bat
   const int64_t want = target_units(c0->dev);
   int64_t chunk_keys = (total_keys * base.kv_groups + want - 1) / want;
   // at least FA_DECODE_MIN_CHUNK_TILES tiles a chunk: a small batch (a GPU's share of C3 over 8
-  // GPUs) otherwise splits into chunks too short for their fixed costs
+  // GPUs) otherwise splits into chunks too short for their fixed costs (measured on B200, 8 of
+  // C3's sequences: 49.6 us with 32-tile chunks, 52.7 with 8; 64 sequences: no change)
 #ifndef FA_DECODE_MIN_CHUNK_TILES
-#define FA_DECODE_MIN_CHUNK_TILES 8
+#define FA_DECODE_MIN_CHUNK_TILES 32
 #endif
   chunk_keys = std::max<int64_t>(int64_t(tile) * FA_DECODE_MIN_CHUNK_TILES,
                                  (chunk_keys + tile - 1) / tile * tile);
