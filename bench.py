@@ -322,6 +322,47 @@ class ProjectedInput(Workload):
         return float(self.bytes)
 
 
+class DitPrologue(Workload):
+    """The query/key prologue of C5's DiT block (Wan's normalize_and_rotate, wan_dit/block.rs:
+    109-140): 32760 tokens of f32 qkv (12 heads x 128), whole-row RMSNorm of the query and key
+    rows, interleaved RoPE by each token's angles, written as the bf16 operand rows the
+    full-mask attention reads. HBM-bound: 604 MB read (+ 16.8 MB of angles), 302 MB written."""
+
+    def __init__(self, torch, fa):
+        self.torch, self.fa, self.name = torch, fa, "prologue"
+        self.kernel = "prologue_kernel"
+        self.heads, self.d, self.n = 12, 128, 32760
+        hidden = self.heads * self.d
+        gen = torch.Generator("cuda").manual_seed(11)
+        self.qkv = torch.randn((self.n, 3 * hidden), device="cuda", generator=gen)
+        self.out = torch.empty((self.n, 3 * hidden), device="cuda", dtype=torch.bfloat16)
+        self.q_norm = 1.0 + 0.1 * torch.randn((hidden,), device="cuda", generator=gen)
+        self.k_norm = 1.0 + 0.1 * torch.randn((hidden,), device="cuda", generator=gen)
+        self.angles = torch.rand((self.n, self.d), device="cuda", generator=gen)
+        self.tokens = self.n
+        self.launches_per_step = 1
+        self.graphs = True
+        self.h_qkv = self.qkv.cpu().pin_memory()
+        self.h_out = torch.empty_like(self.out, device="cpu").pin_memory()
+        self.h2d = self.h_qkv.numel() * 4
+        self.d2h = self.h_out.numel() * 2
+        self.bytes = self.qkv.numel() * 4 + self.out.numel() * 2 + self.angles.numel() * 4
+
+    def phases(self):
+        return (lambda: None,
+                lambda: self.fa.normalize_and_rotate(self.heads, self.d, self.qkv, self.out,
+                                                     self.fa.NORM_ROW, self.q_norm, self.k_norm,
+                                                     1e-6, self.angles, self.fa.ROPE_INTERLEAVED))
+
+    def e2e_step(self):
+        self.qkv.copy_(self.h_qkv, non_blocking=True)
+        self.phases()[1]()
+        self.h_out.copy_(self.out, non_blocking=True)
+
+    def algorithmic(self):
+        return float(self.bytes)
+
+
 class C2Prefill(Workload):
     """C2: 512 rows from position 0, causal, 14/2 heads, d64; the cache written by the pass."""
 
@@ -648,6 +689,8 @@ def run_ours(args):
             return C2Prefill(torch, fa)
         if name == "proj":
             return ProjectedInput(torch, fa)
+        if name == "prologue":
+            return DitPrologue(torch, fa)
         raise SystemExit(f"unknown config {name}")
 
     w = build(args.config)
@@ -678,7 +721,7 @@ def run_ours(args):
     torch.cuda.empty_cache()
     if args.config == "c3" and not args.no_extras and args.sequences == C3_SEQS:
         extras = {}
-        names = ("c1", "c2", "c3bf16", "c4", "c5", "proj") if world == 1 else ("c4", "c5")
+        names = ("c1", "c2", "c3bf16", "c4", "c5", "proj", "prologue") if world == 1 else ("c4", "c5")
         for name in names:
             x = build(name)
             xs = min(steps, 50 if name == "c5" else 200)
@@ -727,6 +770,9 @@ def config_of(name, world):
                "head_dim": 128},
         "c5": {"workload": "C5 DiT full-mask self-attention", "tokens": 32760, "heads": 12,
                "head_dim": 128, "dtype": "bf16 in, f32 accumulate, bf16 out", "mask": "full"},
+        "prologue": {"workload": "C5's DiT query/key prologue (RMSNorm + 3-D RoPE, bf16 out)",
+                     "tokens": 32760, "heads": 12, "head_dim": 128, "norm": "whole row",
+                     "rope": "interleaved"},
         "proj": {"workload": "attention input with its qkv projection (fused), one decode row",
                  "heads": 32, "kv_heads": 8, "head_dim": 128, "hidden": 4096,
                  "weights": "f32 6144 x 4096 + bias", "position": 4096},
@@ -738,8 +784,9 @@ def config_of(name, world):
         "c4": f"KV range over {world} GPU(s), NCCL all-gather of (max, sum, o)" if world > 1 else "1 GPU",
         "c5": f"query rows in whole 256-row pairs over {world} GPU(s), all heads, no collective",
     }.get(name, f"replicas x{world}")
-    c["l2"] = "inputs larger than L2" if name in ("c3", "c3bf16", "c4", "c5") else "L2 flushed between steps"
-    if name in ("c1", "c2", "c3", "c3bf16", "proj") or (name == "c4" and world > 1):
+    c["l2"] = ("inputs larger than L2" if name in ("c3", "c3bf16", "c4", "c5", "prologue")
+               else "L2 flushed between steps")
+    if name in ("c1", "c2", "c3", "c3bf16", "proj", "prologue") or (name == "c4" and world > 1):
         c["launch"] = "the step's calls replayed as captured CUDA graphs"
     return c
 
@@ -807,7 +854,8 @@ def main():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", default="c3", choices=["c1", "c2", "c3", "c3bf16", "c4", "c5", "proj"])
+    ap.add_argument("--config", default="c3",
+                    choices=["c1", "c2", "c3", "c3bf16", "c4", "c5", "proj", "prologue"])
     ap.add_argument("--sequences", type=int, default=C3_SEQS,
                     help="C3 sequences (a smaller batch for profiling captures)")
     ap.add_argument("--no-extras", action="store_true")

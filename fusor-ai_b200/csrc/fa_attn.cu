@@ -1792,6 +1792,9 @@ int fa_normalize_and_rotate(const fa_prologue* prologue, const float* qkv, int64
   a.angles = p.angles;
   a.out = out;
   a.out_stride = out_stride;
+  Device* dev = nullptr;
+  if (int rc = device_state(device, &dev)) return rc;
+  a.err = dev->err;
   const cudaError_t e = fa::launch_prologue(a, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "prologue launch");
   return FA_OK;

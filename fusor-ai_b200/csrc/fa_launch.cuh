@@ -97,6 +97,7 @@ struct PrologueArgs {
   const float* angles;  // row t at angles + t*head_dim: cosines then sines
   void* out;            // row t at out + t*out_stride elements, laid out as qkv
   int64_t out_stride;
+  unsigned* err;        // the device error word (a wait that gave up)
 };
 cudaError_t launch_prologue(const PrologueArgs& args, cudaStream_t stream);
 

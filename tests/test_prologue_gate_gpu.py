@@ -47,15 +47,19 @@ def bf16_close(got, want):
 # ---- the DiT query/key prologue ---------------------------------------------------------------
 
 @pytest.mark.parametrize("case", ["wan_bf16", "wan_f32", "wan_in_place", "mmdit_head_half",
-                                  "unaligned"])
+                                  "unaligned", "d128_head_half", "d128_20_heads"])
 def test_prologue_matches_the_oracle(torch, case):
-    heads, d = (3, 128) if case.startswith("wan") else (4, 64)
+    """Head_dim 128 with at most 16 heads and aligned rows runs the register-resident kernel
+    (the wan cases, d128_head_half); the rest the general one."""
+    heads, d = {"d128_head_half": (5, 128), "d128_20_heads": (20, 128)}.get(
+        case, (3, 128) if case.startswith("wan") else (4, 64))
     frames, rows, cols = 3, 5, 7
     positions = video_positions(frames, rows, cols)
     tokens, width = len(positions), heads * d
-    norm = fa.NORM_HEAD if case == "mmdit_head_half" else fa.NORM_ROW
-    rope = fa.ROPE_HALF if case == "mmdit_head_half" else fa.ROPE_INTERLEAVED
-    rotated = 70 if case == "mmdit_head_half" else tokens
+    head_half = case in ("mmdit_head_half", "d128_head_half")
+    norm = fa.NORM_HEAD if head_half else fa.NORM_ROW
+    rope = fa.ROPE_HALF if head_half else fa.ROPE_INTERLEAVED
+    rotated = 70 if head_half else tokens
     stride = 3 * width + (1 if case == "unaligned" else 0)
     qkv = normal(901, (tokens, stride))
     wn = width if norm == fa.NORM_ROW else d
