@@ -158,6 +158,8 @@ struct SplitWork {
 };
 std::mutex g_split_mutex;
 std::map<std::pair<int, cudaStream_t>, SplitWork> g_split_work;
+// The same for the f32 full-mask calls that run on the split-KV kernel (queries, partials).
+std::map<std::pair<int, cudaStream_t>, SplitWork> g_full_work;
 constexpr size_t kMaxSplitBytes = size_t(512) << 20;
 
 }  // namespace
@@ -1639,10 +1641,8 @@ int fa_attend_full(const fa_call* call, void* out, int64_t out_stride, void* str
   if (k.out_dtype != FA_F32)
     return fail(FA_ERR_UNSUPPORTED, "bf16 output needs the tensor-core path (head_dim 64/128, "
                                     "16-byte aligned rows)");
-  // A call-local workspace, kept per device and grown on demand.
-  static Buffer work[64];
-  static Buffer counters[64];
-  static int counters_epoch[64];
+  // A call-local workspace, kept per (device, stream) and grown on demand: calls on one stream
+  // run in order and share it, calls on different streams do not.
   const int rows = k.images * k.queries;
   fa_kvcache view;  // the call viewed as a cache for the planner
   view.layers = 1;
@@ -1657,14 +1657,18 @@ int fa_attend_full(const fa_call* call, void* out, int64_t out_stride, void* str
   const size_t q_bytes = align_up(size_t(rows) * width * 4, 256);
   const size_t o_bytes = align_up(size_t(rows) * p.chunks * k.heads * k.head_dim * 4, 256);
   const size_t ml_bytes = align_up(size_t(rows) * p.chunks * k.heads * 2 * 4, 256);
-  if (int rc = work[device].ensure(q_bytes + o_bytes + ml_bytes, s)) return rc;
+  std::unique_lock<std::mutex> lock(g_split_mutex);
+  SplitWork& fw = g_full_work[{device, s}];
+  if (int rc = fw.partials.ensure(q_bytes + o_bytes + ml_bytes, s)) return rc;
   const size_t counter_bytes = size_t(rows) * p.kv_groups * sizeof(int);
-  if (counter_bytes > counters[device].bytes || counters_epoch[device] != dev->epoch.load()) {
-    if (int rc = counters[device].ensure(counter_bytes, s)) return rc;
-    FA_CUDA(cudaMemsetAsync(counters[device].ptr, 0, counters[device].bytes, s), "counters");
-    counters_epoch[device] = dev->epoch.load();
+  if (counter_bytes > fw.counters.bytes || fw.counters_epoch != dev->epoch.load()) {
+    if (int rc = fw.counters.ensure(counter_bytes, s)) return rc;
+    FA_CUDA(cudaMemsetAsync(fw.counters.ptr, 0, fw.counters.bytes, s), "counters");
+    fw.counters_epoch = dev->epoch.load();
   }
-  unsigned char* base = static_cast<unsigned char*>(work[device].ptr);
+  unsigned char* base = static_cast<unsigned char*>(fw.partials.ptr);
+  int* counter_base = static_cast<int*>(fw.counters.ptr);
+  lock.unlock();
   float* q = reinterpret_cast<float*>(base);
   cudaError_t e = fa::launch_prepare_queries(k.dtype, k.query.values, k.query.stride, k.query.offset,
                                              rows, k.heads, k.head_dim, query_scale(k.head_dim), q, s);
@@ -1684,7 +1688,7 @@ int fa_attend_full(const fa_call* call, void* out, int64_t out_stride, void* str
   args.c.out_stride = out_stride;
   args.c.part_o = reinterpret_cast<float*>(base + q_bytes);
   args.c.part_ml = reinterpret_cast<float*>(base + q_bytes + o_bytes);
-  args.c.counters = static_cast<int*>(counters[device].ptr);
+  args.c.counters = counter_base;
   args.k = static_cast<const unsigned char*>(k.key.values) + k.key.offset * esize;
   args.v = static_cast<const unsigned char*>(k.value.values) + k.value.offset * esize;
   args.capacity = INT_MAX;

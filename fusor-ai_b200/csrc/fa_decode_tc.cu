@@ -10,14 +10,9 @@ namespace {
 
 template <int kG>
 cudaError_t launch_g(const DtcArgs& args, int grid, cudaStream_t stream) {
-  static bool configured = false;  // per instantiation, per process
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(decode_tc_kernel<kG>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         int(kDtcSmemBytes));
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static std::atomic<bool> configured[64];  // per instantiation, per device
+  cudaError_t e = smem_limit_once(decode_tc_kernel<kG>, int(kDtcSmemBytes), configured);
+  if (e != cudaSuccess) return e;
   return launch_pdl(decode_tc_kernel<kG>, dim3(grid), dim3(kDtcThreads), kDtcSmemBytes, stream,
                     args);
 }

@@ -61,13 +61,9 @@ cudaError_t launch_t(const FmhaLaunch& l, cudaStream_t stream) {
                 bf16 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
     return cudaErrorInvalidValue;
   auto kernel = fmha_kernel<T, D>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           int(S::kSmemBytes));
-    if (err != cudaSuccess) return err;
-    configured = true;
-  }
+  static std::atomic<bool> configured[64];  // per instantiation, per device
+  cudaError_t err = smem_limit_once(kernel, int(S::kSmemBytes), configured);
+  if (err != cudaSuccess) return err;
   const dim3 grid(l.args.images * l.args.q_tiles, l.args.heads);
   return launch_pdl(kernel, grid, dim3(kFmhaThreads), S::kSmemBytes, stream, qm, km, vm, l.args);
 }
@@ -85,13 +81,9 @@ cudaError_t launch_bf16_pairs(const FmhaLaunch& l, cudaStream_t stream) {
                 S::kBlock, S::BN))
     return cudaErrorInvalidValue;
   auto kernel = fmha2_kernel<D>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           int(S::kSmemBytes));
-    if (err != cudaSuccess) return err;
-    configured = true;
-  }
+  static std::atomic<bool> configured[64];  // per instantiation, per device
+  cudaError_t err = smem_limit_once(kernel, int(S::kSmemBytes), configured);
+  if (err != cudaSuccess) return err;
   const int64_t units = int64_t(l.args.images) * ((l.args.q_tiles + 1) / 2) * l.args.heads;
   int64_t grid = units;
   if (l.args.splits > 1) {

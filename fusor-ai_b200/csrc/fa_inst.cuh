@@ -11,13 +11,9 @@ template <int D, typename KT, int G, bool BATCH, typename Args>
 cudaError_t launch_one(const Args& args, int grid, cudaStream_t stream) {
   auto kernel = attend_kernel<D, KT, G, BATCH, Args>;
   constexpr size_t smem = DecodeShape<D, KT, G>::kSmemBytes;
-  static bool configured = false;  // per instantiation, per process
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         int(smem));
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static std::atomic<bool> configured[64];  // per instantiation, per device
+  cudaError_t e = smem_limit_once(kernel, int(smem), configured);
+  if (e != cudaSuccess) return e;
   return launch_pdl_cluster(kernel, dim3(grid), dim3(kDecodeThreads), smem, stream,
                             args.c.cluster > 1 ? args.c.cluster : 1, args);
 }

@@ -4,6 +4,7 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <utility>
 
 #include "fa_decode.cuh"
@@ -36,6 +37,20 @@ cudaError_t launch_pdl_cluster(void (*kernel)(Params...), dim3 grid, dim3 block,
     cfg.numAttrs = 2;
   }
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// Raises `kernel`'s dynamic shared-memory limit to `bytes` on the current device, once per device
+// (the attribute is per device): `done` is the caller's table of flags, one per device.
+template <typename... Params>
+cudaError_t smem_limit_once(void (*kernel)(Params...), int bytes, std::atomic<bool> (&done)[64]) {
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return e;
+  if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
+  if (done[device].load(std::memory_order_acquire)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done[device].store(true, std::memory_order_release);
+  return e;
 }
 
 template <typename... Params, typename... Args>

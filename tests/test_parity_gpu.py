@@ -377,6 +377,36 @@ def test_full_mask_images_and_gqa(torch):
     assert max_abs(out.cpu().numpy(), want) <= TOL_F32
 
 
+@pytest.mark.parametrize("case", ["head_dim_32", "unaligned_queries"])
+def test_full_mask_on_the_split_kv_kernel(torch, case):
+    """f32 full-mask calls the tensor cores do not take (head_dim 32; a query stride of no
+    16-byte rows) run on the split-KV kernel with its per-(device, stream) workspace: the oracle's
+    output, and the same bits from a call on another stream."""
+    d = 32 if case == "head_dim_32" else 64
+    heads, kv, images, queries, keys = 6, 2, 2, 70, 90
+    qs = heads * d + (1 if case == "unaligned_queries" else 0)
+    q = normal(621, (images * queries, qs))
+    k = normal(622, (images * keys, kv * d))
+    v = normal(623, (images * keys, kv * d))
+    tq, tk, tv = dev(torch, q), dev(torch, k), dev(torch, v)
+    out = torch.zeros((images * queries, heads * d), device="cuda")
+    fa.attend_full(heads, kv, d, images, queries, keys, fa.Operand(tq, qs), fa.Operand(tk, kv * d),
+                   fa.Operand(tv, kv * d), out)
+    side = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    out2 = torch.zeros_like(out)
+    fa.attend_full(heads, kv, d, images, queries, keys, fa.Operand(tq, qs), fa.Operand(tk, kv * d),
+                   fa.Operand(tv, kv * d), out2, stream=side)
+    torch.cuda.synchronize()
+    fa.device_status()
+    want = oracle.attend_call(heads, kv, d, images, queries, keys, q, qs, 0, k, kv * d, 0, v,
+                              kv * d, 0)
+    got = out.cpu().numpy()
+    print(compare(f"split-KV full mask {case}", got, want))
+    assert max_abs(got, want) <= TOL_F32
+    assert torch.equal(out, out2)
+
+
 @pytest.mark.parametrize("dtype", [fa.F32, fa.BF16])
 @pytest.mark.parametrize("head_dim", [64, 128])
 @pytest.mark.parametrize("mask_name", ["causal", "window", "full", "groups"])
