@@ -407,6 +407,47 @@ class C2Prefill(Workload):
         return self.flops
 
 
+class LongPrefill(Workload):
+    """A long causal prefill at C3's model shape (32/8 heads x 128, RoPE base 1e6): 8192 rows
+    from position 0 over a bf16 cache, through the whole attention phase (fa_attention: RoPE +
+    keep with bf16 operand queries, then the tensor-core attention). FLOPs 4 x d x heads x the
+    visible keys of every row (0.55 TFLOP); the step's time, RoPE and keep included."""
+
+    def __init__(self, torch, fa):
+        self.torch, self.fa, self.name = torch, fa, "prefill"
+        self.kernel = "fmha2_kernel"
+        rows, heads, kv, d = 8192, 32, 8, 128
+        shape = fa.Shape(1, heads, kv, d)
+        self.cache = fa.KvCache(shape, rows, fa.BF16)
+        gen = torch.Generator("cuda").manual_seed(13)
+        self.span = fa.Span(rows, 0, fa.Mask.causal())
+        self.qkv = torch.randn((rows, shape.qkv), device="cuda", generator=gen)
+        self.angles = torch.from_numpy(fa.rotary_angles(fa.Rotation(base=1e6), d, range(rows))).cuda()
+        self.out = torch.zeros((rows, shape.width), device="cuda")
+        self.tokens = rows
+        self.bound = "tensor"
+        self.launches_per_step = 2
+        self.graphs = True
+        self.h_qkv = self.qkv.cpu().pin_memory()
+        self.h_out = torch.zeros_like(self.out, device="cpu").pin_memory()
+        self.h2d = self.h_qkv.numel() * 4
+        self.d2h = self.h_out.numel() * 4
+        self.flops = 4.0 * heads * d * rows * (rows + 1) / 2
+
+    def phases(self):
+        return (lambda: None,
+                lambda: self.cache.attention(0, self.span, self.qkv, self.out, self.angles,
+                                             self.fa.ROPE_HALF))
+
+    def e2e_step(self):
+        self.qkv.copy_(self.h_qkv, non_blocking=True)
+        self.phases()[1]()
+        self.h_out.copy_(self.out, non_blocking=True)
+
+    def algorithmic(self):
+        return self.flops
+
+
 class C4Sharded(Workload):
     """C4 over `world` GPUs: each rank holds a contiguous range of the 131073 key positions in
     its own cache; a step rotates the query everywhere, keeps the new row on its owner, attends
@@ -691,6 +732,8 @@ def run_ours(args):
             return ProjectedInput(torch, fa)
         if name == "prologue":
             return DitPrologue(torch, fa)
+        if name == "prefill":
+            return LongPrefill(torch, fa)
         raise SystemExit(f"unknown config {name}")
 
     w = build(args.config)
@@ -721,7 +764,8 @@ def run_ours(args):
     torch.cuda.empty_cache()
     if args.config == "c3" and not args.no_extras and args.sequences == C3_SEQS:
         extras = {}
-        names = ("c1", "c2", "c3bf16", "c4", "c5", "proj", "prologue") if world == 1 else ("c4", "c5")
+        names = (("c1", "c2", "c3bf16", "c4", "c5", "prefill", "proj", "prologue") if world == 1
+                 else ("c4", "c5"))
         for name in names:
             x = build(name)
             xs = min(steps, 50 if name == "c5" else 200)
@@ -770,6 +814,9 @@ def config_of(name, world):
                "head_dim": 128},
         "c5": {"workload": "C5 DiT full-mask self-attention", "tokens": 32760, "heads": 12,
                "head_dim": 128, "dtype": "bf16 in, f32 accumulate, bf16 out", "mask": "full"},
+        "prefill": {"workload": "long causal prefill at C3's model shape, bf16 cache",
+                    "rows": 8192, "heads": 32, "kv_heads": 8, "head_dim": 128, "mask": "causal",
+                    "path": "fa_attention (RoPE + keep, then attention)"},
         "prologue": {"workload": "C5's DiT query/key prologue (RMSNorm + 3-D RoPE, bf16 out)",
                      "tokens": 32760, "heads": 12, "head_dim": 128, "norm": "whole row",
                      "rope": "interleaved"},
@@ -784,9 +831,9 @@ def config_of(name, world):
         "c4": f"KV range over {world} GPU(s), NCCL all-gather of (max, sum, o)" if world > 1 else "1 GPU",
         "c5": f"query rows in whole 256-row pairs over {world} GPU(s), all heads, no collective",
     }.get(name, f"replicas x{world}")
-    c["l2"] = ("inputs larger than L2" if name in ("c3", "c3bf16", "c4", "c5", "prologue")
+    c["l2"] = ("inputs larger than L2" if name in ("c3", "c3bf16", "c4", "c5", "prologue", "prefill")
                else "L2 flushed between steps")
-    if name in ("c1", "c2", "c3", "c3bf16", "proj", "prologue") or (name == "c4" and world > 1):
+    if name in ("c1", "c2", "c3", "c3bf16", "proj", "prologue", "prefill") or (name == "c4" and world > 1):
         c["launch"] = "the step's calls replayed as captured CUDA graphs"
     return c
 
@@ -855,7 +902,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="c3",
-                    choices=["c1", "c2", "c3", "c3bf16", "c4", "c5", "proj", "prologue"])
+                    choices=["c1", "c2", "c3", "c3bf16", "c4", "c5", "prefill", "proj", "prologue"])
     ap.add_argument("--sequences", type=int, default=C3_SEQS,
                     help="C3 sequences (a smaller batch for profiling captures)")
     ap.add_argument("--no-extras", action="store_true")

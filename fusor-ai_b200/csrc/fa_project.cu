@@ -172,7 +172,11 @@ __global__ void __launch_bounds__(kProjectThreads)
 template <typename KT, int NR>
 cudaError_t launch_nr(const ProjectArgs& p, const RopeArgs& r, size_t smem, cudaStream_t stream) {
   auto kernel = project_keep_kernel<KT, NR>;
-  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  // the host's plans stay within 200 KB of shared memory; the limit is raised to that once
+  constexpr int kMaxSmem = 200 * 1024;
+  if (smem > size_t(kMaxSmem)) return cudaErrorInvalidValue;
+  static std::atomic<bool> configured[64];  // per instantiation, per device
+  cudaError_t e = smem_limit_once(kernel, kMaxSmem, configured);
   if (e != cudaSuccess) return e;
   const int units = r.heads + 2 * r.kv_heads;
   const dim3 grid(unsigned(units), unsigned((p.rows + p.row_block - 1) / p.row_block),

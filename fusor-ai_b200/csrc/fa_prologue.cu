@@ -370,9 +370,11 @@ cudaError_t launch_prologue(const PrologueArgs& a, cudaStream_t stream) {
   if (rows128) {
     // two rows in flight per warp; persistent CTAs, as many as fit on every SM
     const size_t smem = size_t(kStreamWarps) * 2 * a.heads * 128 * sizeof(float);
+    // the limit raised once per device to what kRowHeads heads need
+    constexpr int kMaxSmem = kStreamWarps * 2 * kRowHeads * 128 * int(sizeof(float));
+    static std::atomic<bool> configured_bf16[64], configured_f32[64];
     auto kernel = a.out_bf16 ? prologue_stream_kernel<__nv_bfloat16> : prologue_stream_kernel<float>;
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         int(smem));
+    cudaError_t e = smem_limit_once(kernel, kMaxSmem, a.out_bf16 ? configured_bf16 : configured_f32);
     if (e != cudaSuccess) return e;
     int per_sm = 0, sms = 0, device = 0;
     if ((e = cudaGetDevice(&device)) != cudaSuccess) return e;
