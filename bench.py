@@ -409,9 +409,9 @@ class C2Prefill(Workload):
 
 class LongPrefill(Workload):
     """A long causal prefill at C3's model shape (32/8 heads x 128, RoPE base 1e6): 8192 rows
-    from position 0 over a bf16 cache, through the whole attention phase (fa_attention: RoPE +
-    keep with bf16 operand queries, then the tensor-core attention). FLOPs 4 x d x heads x the
-    visible keys of every row (0.55 TFLOP); the step's time, RoPE and keep included."""
+    from position 0 over a bf16 cache: RoPE + keep (fa_attention_input), then the attention
+    (fa_attend: the queries to bf16 operand rows and the tensor-core attention). FLOPs 4 x d x
+    heads x the visible keys of every row (0.55 TFLOP) over the attend call's time."""
 
     def __init__(self, torch, fa):
         self.torch, self.fa, self.name = torch, fa, "prefill"
@@ -423,10 +423,11 @@ class LongPrefill(Workload):
         self.span = fa.Span(rows, 0, fa.Mask.causal())
         self.qkv = torch.randn((rows, shape.qkv), device="cuda", generator=gen)
         self.angles = torch.from_numpy(fa.rotary_angles(fa.Rotation(base=1e6), d, range(rows))).cuda()
+        self.q = torch.zeros((rows, shape.width), device="cuda")
         self.out = torch.zeros((rows, shape.width), device="cuda")
         self.tokens = rows
         self.bound = "tensor"
-        self.launches_per_step = 2
+        self.launches_per_step = 3
         self.graphs = True
         self.h_qkv = self.qkv.cpu().pin_memory()
         self.h_out = torch.zeros_like(self.out, device="cpu").pin_memory()
@@ -435,9 +436,28 @@ class LongPrefill(Workload):
         self.flops = 4.0 * heads * d * rows * (rows + 1) / 2
 
     def phases(self):
+        # the step as a user runs it: fa_attention (RoPE + keep writing bf16 operand queries,
+        # then the tensor-core attention)
         return (lambda: None,
                 lambda: self.cache.attention(0, self.span, self.qkv, self.out, self.angles,
                                              self.fa.ROPE_HALF))
+
+    def capture(self):
+        """The step graph (fa_attention), and for the roofline the attention alone: fa_attend
+        over f32 queries that fa_attention_input rotated once beforehand (its own bf16
+        conversion of the queries included)."""
+        torch = self.torch
+        self._step_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self._step_graph, capture_error_mode="relaxed"):
+            self.phases()[1]()
+        self.cache.attention_input(0, self.span, self.qkv, self.angles, self.fa.ROPE_HALF,
+                                   q_out=self.q)
+        self.cache.attend(0, self.span, self.q, self.out)  # sizes its workspace before capture
+        torch.cuda.synchronize()
+        self._kernel_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self._kernel_graph, capture_error_mode="relaxed"):
+            self.cache.attend(0, self.span, self.q, self.out)
+        torch.cuda.synchronize()
 
     def e2e_step(self):
         self.qkv.copy_(self.h_qkv, non_blocking=True)
@@ -748,7 +768,8 @@ def run_ours(args):
         "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": steps,
         "warmup": warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
         "scaling": "strong" if w.sharded else "weak", "vs_baseline": None,
-        "dtype": {"c3bf16": "bf16-kv/f32", "c5": "bf16/f32-acc"}.get(args.config, "f32"),
+        "dtype": {"c3bf16": "bf16-kv/f32", "c5": "bf16/f32-acc", "prefill": "bf16-kv/f32",
+                  "prologue": "f32-in/bf16-out"}.get(args.config, "f32"),
         "data": "synthetic N(0,1) (seeded), random keys/values of the config's shape",
         "config": config_of(args.config, world),
         "roofline": roofline(w, kern_ms, peaks),
@@ -816,7 +837,7 @@ def config_of(name, world):
                "head_dim": 128, "dtype": "bf16 in, f32 accumulate, bf16 out", "mask": "full"},
         "prefill": {"workload": "long causal prefill at C3's model shape, bf16 cache",
                     "rows": 8192, "heads": 32, "kv_heads": 8, "head_dim": 128, "mask": "causal",
-                    "path": "fa_attention (RoPE + keep, then attention)"},
+                    "path": "fa_attention (step); roofline over an fa_attend call alone"},
         "prologue": {"workload": "C5's DiT query/key prologue (RMSNorm + 3-D RoPE, bf16 out)",
                      "tokens": 32760, "heads": 12, "head_dim": 128, "norm": "whole row",
                      "rope": "interleaved"},
