@@ -166,6 +166,10 @@ class Workload:
         """Bytes (hbm) or FLOPs (tensor) of one launch of the dominant kernel on this rank."""
         raise NotImplementedError
 
+    def close(self):
+        """Releases what the workload holds beyond device tensors (every rank, in step)."""
+        self._step_graph = self._kernel_graph = None
+
 
 class C3Decode(Workload):
     def __init__(self, torch, fa, rank, world, dtype, sequences=C3_SEQS):
@@ -471,7 +475,8 @@ class LongPrefill(Workload):
 class C4Sharded(Workload):
     """C4 over `world` GPUs: each rank holds a contiguous range of the 131073 key positions in
     its own cache; a step rotates the query everywhere, keeps the new row on its owner, attends
-    the local range into per-head (max, sum, o), all-gathers those over NCCL and merges them."""
+    the local range into per-head (max, sum, o), and one kernel stores those into every rank's
+    exchange buffer over NVLink peer memory, waits for every rank's and merges them."""
 
     def __init__(self, torch, fa, rank, world, dist):
         from fusor_attn.shard import ShardedDecode, kv_shards
@@ -490,7 +495,8 @@ class C4Sharded(Workload):
         gen0 = torch.Generator("cuda").manual_seed(7)
         self.qkv = torch.randn((1, shape.qkv), device="cuda", generator=gen0)
         self.angles = torch.from_numpy(fa.rotary_angles(fa.Rotation(base=1e6), d, [position])).cuda()
-        self.decode = ShardedDecode(self.cache, heads, d, lo, hi, position, world)
+        self.decode = ShardedDecode(self.cache, heads, d, lo, hi, position, world,
+                                    exchange="peer")
         self.tokens = 1
         self.launches_per_step = 3
         # a step is tens of microseconds on the GPU, less than its calls' host time: the whole
@@ -532,6 +538,10 @@ class C4Sharded(Workload):
 
     def algorithmic(self):
         return float(self.bytes)
+
+    def close(self):
+        super().close()  # the graphs that hold the exchange go first
+        self.decode.close(self.dist)
 
 
 class C5Full(Workload):
@@ -780,7 +790,7 @@ def run_ours(args):
         "gpu_launches": w.launches_per_step * steps,
         "clocks": sampler.report(),
     }
-    w._step_graph = w._kernel_graph = None
+    w.close()
     del w
     torch.cuda.empty_cache()
     if args.config == "c3" and not args.no_extras and args.sequences == C3_SEQS:
@@ -802,7 +812,7 @@ def run_ours(args):
             if name == "c5":
                 entry["tflops"] = round(6.594e12 / (ms_x * 1e-3) / 1e12, 2)
             extras[name] = entry
-            x._step_graph = x._kernel_graph = None  # graphs holding NCCL calls go before the group
+            x.close()  # graphs holding collectives and peer buffers go before the group
             del x
             torch.cuda.empty_cache()
         line["configs"] = extras
@@ -849,7 +859,8 @@ def config_of(name, world):
     c["parallelism"] = {
         "c3": f"sequences over {world} GPU(s), no collective",
         "c3bf16": f"sequences over {world} GPU(s), no collective",
-        "c4": f"KV range over {world} GPU(s), NCCL all-gather of (max, sum, o)" if world > 1 else "1 GPU",
+        "c4": (f"KV range over {world} GPU(s); (max, sum, o) exchanged over NVLink peer memory "
+               "by one kernel (P2P stores, flags) that merges" if world > 1 else "1 GPU"),
         "c5": f"query rows in whole 256-row pairs over {world} GPU(s), all heads, no collective",
     }.get(name, f"replicas x{world}")
     c["l2"] = ("inputs larger than L2" if name in ("c3", "c3bf16", "c4", "c5", "prologue", "prefill")

@@ -22,6 +22,7 @@
 #include "fa_launch.cuh"
 #include "fa_decode_tc.h"
 #include "fa_relpos.h"
+#include "fa_peer.h"
 
 namespace {
 
@@ -1543,6 +1544,86 @@ int fa_merge_partials(const float* partials, int32_t shards, int32_t heads, int3
   cudaError_t e = fa::launch_merge_partials(partials, shards, heads, head_dim, out,
                                             static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "merge launch");
+  return FA_OK;
+}
+
+int fa_peer_buffer_bytes(int32_t world, int32_t heads, int32_t head_dim, uint64_t* bytes) {
+  if (bytes == nullptr) return fail(FA_ERR_ARG, "null bytes");
+  if (world < 1 || world > fa::kMaxPeers || heads < 1 || head_dim < 1 || head_dim > 1024)
+    return fail(FA_ERR_ARG, "world %d (1..%d), heads %d, head_dim %d", world, fa::kMaxPeers,
+                heads, head_dim);
+  *bytes = fa::peer_buffer_bytes(world, heads, head_dim);
+  return FA_OK;
+}
+
+int fa_peer_alloc(uint64_t bytes, void** ptr, fa_ipc_handle* handle) {
+  if (ptr == nullptr || handle == nullptr || bytes < uint64_t(fa::kPeerHeaderBytes))
+    return fail(FA_ERR_ARG, "null argument or a buffer below its header");
+  void* p = nullptr;
+  FA_CUDA(cudaMalloc(&p, bytes), "cudaMalloc(peer buffer)");
+  cudaError_t e = cudaMemset(p, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "peer buffer");
+  }
+  static_assert(sizeof(h) == sizeof(handle->bytes), "a CUDA IPC handle is 64 bytes");
+  std::memcpy(handle->bytes, &h, sizeof(h));
+  *ptr = p;
+  return FA_OK;
+}
+
+int fa_peer_open(const fa_ipc_handle* handle, void** ptr) {
+  if (handle == nullptr || ptr == nullptr) return fail(FA_ERR_ARG, "null argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle->bytes, sizeof(h));
+  FA_CUDA(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+  return FA_OK;
+}
+
+int fa_peer_close(void* ptr) {
+  if (ptr == nullptr) return FA_OK;
+  FA_CUDA(cudaIpcCloseMemHandle(ptr), "cudaIpcCloseMemHandle");
+  return FA_OK;
+}
+
+int fa_peer_free(void* ptr) {
+  if (ptr == nullptr) return FA_OK;
+  FA_CUDA(cudaFree(ptr), "cudaFree(peer buffer)");
+  return FA_OK;
+}
+
+int fa_exchange_merge(void* const* buffers, uint64_t buffer_bytes, int32_t rank, int32_t world,
+                      int32_t heads, int32_t head_dim, const float* partials, float* out,
+                      void* stream) {
+  uint64_t need = 0;
+  if (int rc = fa_peer_buffer_bytes(world, heads, head_dim, &need)) return rc;
+  if (buffers == nullptr || partials == nullptr || out == nullptr)
+    return fail(FA_ERR_ARG, "null argument");
+  if (rank < 0 || rank >= world) return fail(FA_ERR_ARG, "rank %d of %d", rank, world);
+  if (buffer_bytes < need)
+    return fail(FA_ERR_SHAPE, "exchange buffers of %llu bytes, %llu needed",
+                (unsigned long long)buffer_bytes, (unsigned long long)need);
+  const int device = current_device();
+  FA_PTR(partials, device);
+  FA_PTR(out, device);
+  fa::PeerMergeArgs a{};
+  for (int r = 0; r < world; ++r) {
+    if (buffers[r] == nullptr) return fail(FA_ERR_ARG, "no buffer for rank %d", r);
+    a.bufs[r] = static_cast<unsigned char*>(buffers[r]);
+  }
+  Device* dev = nullptr;
+  if (int rc = device_state(device, &dev)) return rc;
+  a.rank = rank;
+  a.world = world;
+  a.heads = heads;
+  a.head_dim = head_dim;
+  a.partials = partials;
+  a.out = out;
+  a.err = dev->err;
+  cudaError_t e = fa::launch_peer_merge(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "exchange launch");
   return FA_OK;
 }
 

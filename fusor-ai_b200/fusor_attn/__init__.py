@@ -126,6 +126,12 @@ SIGNATURES = {
     "fa_attention_host": (C.c_int, [_P, _I32, _P, _I32, _P, _P, _P, _I64, _P, _I64, _P]),
     "fa_attention_batch": (C.c_int, [_P, _P, _I32, _I32, _I32, _P, _P, _P, _I64, _P, _I64, _P]),
     "fa_attention_input_batch": (C.c_int, [_P, _P, _I32, _I32, _I32, _P, _P, _P, _I64, _P, _I64, _P]),
+    "fa_peer_buffer_bytes": (C.c_int, [_I32, _I32, _I32, C.POINTER(C.c_uint64)]),
+    "fa_peer_alloc": (C.c_int, [C.c_uint64, C.POINTER(_P), _P]),
+    "fa_peer_open": (C.c_int, [_P, C.POINTER(_P)]),
+    "fa_peer_close": (C.c_int, [_P]),
+    "fa_peer_free": (C.c_int, [_P]),
+    "fa_exchange_merge": (C.c_int, [_P, C.c_uint64, _I32, _I32, _I32, _I32, _P, _P, _P]),
     "fa_attention_input_projected": (C.c_int, [_P, _I32, _P, _I32, _P, _P, _P, _P, _I64, _P, _P,
                                                _I64, _P]),
     "fa_attention_input_projected_batch": (C.c_int, [_P, _P, _I32, _I32, _I32, _P, _P, _P, _P,
@@ -525,6 +531,54 @@ def normalize_and_rotate(heads: int, head_dim: int, qkv, out, norm: int = NORM_R
     dt = F32 if out.dtype == torch.float32 else BF16
     _check(lib().fa_normalize_and_rotate(C.byref(p), _dptr(qkv), qkv.stride(0), _dptr(out),
                                          out.stride(0), dt, _stream(stream)))
+
+
+class PeerExchange:
+    """This rank's exchange buffer for fa_exchange_merge and the mappings of the other ranks'
+    (CUDA IPC handles swapped over `group`, a torch.distributed process group of one process per
+    GPU of a box)."""
+
+    def __init__(self, heads: int, head_dim: int, group=None):
+        import torch.distributed as dist
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        self.heads, self.head_dim = heads, head_dim
+        nbytes = C.c_uint64()
+        _check(lib().fa_peer_buffer_bytes(self.world, heads, head_dim, C.byref(nbytes)))
+        self.bytes = nbytes.value
+        own = C.c_void_p()
+        handle = (C.c_ubyte * 64)()
+        _check(lib().fa_peer_alloc(self.bytes, C.byref(own), handle))
+        self.own = own
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.mapped = []
+        ptrs = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                ptrs.append(own.value)
+                continue
+            p = C.c_void_p()
+            _check(lib().fa_peer_open((C.c_ubyte * 64).from_buffer_copy(h), C.byref(p)))
+            self.mapped.append(p)
+            ptrs.append(p.value)
+        self.buffers = (C.c_void_p * self.world)(*ptrs)
+
+    def merge(self, partials, out, stream=None):
+        """This rank's (max, sum, o) partials (heads x (head_dim + 2) f32) exchanged with every
+        rank's and merged into out (heads x head_dim f32)."""
+        _check(lib().fa_exchange_merge(self.buffers, self.bytes, self.rank, self.world,
+                                       self.heads, self.head_dim, _dptr(partials), _dptr(out),
+                                       _stream(stream)))
+
+    def close(self):
+        """Unmaps the other ranks' buffers and frees this one's (after every rank's last merge:
+        a barrier of the group first)."""
+        for p in self.mapped:
+            lib().fa_peer_close(p)
+        self.mapped = []
+        if self.own:
+            lib().fa_peer_free(self.own)
+            self.own = None
 
 
 def device_status(stream=None):

@@ -5,8 +5,10 @@ plumbing, a collective only where the path has a real exchange step.
   collective (`shard_sequences`).
 - One long context (split-KV decode): each rank holds a contiguous range of key positions in
   its own KvCache (`kv_shards`); every rank attends its range and produces per-head
-  (max, sum, partial output) triples, which one all-gather over NCCL brings to every rank for
-  the log-sum-exp merge (`ShardedDecode`).
+  (max, sum, partial output) triples, which reach every rank for the log-sum-exp merge
+  (`ShardedDecode`): stored straight into every rank's buffer over NVLink peer memory by one
+  small kernel that then merges (`exchange="peer"`), or by an NCCL all-gather and the merge
+  kernel (`exchange="nccl"`).
 - Full-mask attention: contiguous runs of 256-query pairs (all heads) split evenly over ranks,
   every rank reading the K/V locally and making one call (`query_row_shards`), no collective.
 
@@ -61,6 +63,7 @@ class ShardedDecode:
     position: int          # the new row's position
     world: int
     group: object = None   # torch.distributed process group (None: the default group)
+    exchange: str = "nccl"  # "peer": fa_exchange_merge over NVLink peer memory
 
     def __post_init__(self):
         import torch
@@ -69,6 +72,7 @@ class ShardedDecode:
         self.gathered = torch.zeros((self.world, self.heads, self.head_dim + 2), device="cuda")
         self.out = torch.zeros((self.heads, self.head_dim), device="cuda")
         self.owner = self.lo <= self.position < self.hi
+        self.peers = None  # the PeerExchange, made by the first exchange (a collective step)
 
     def rotate(self, qkv, angles, rope):
         """The query rotated on every rank; the new row kept on the rank holding its position."""
@@ -85,14 +89,29 @@ class ShardedDecode:
         self.cache.attend_partial(0, self.q, 0, self.hi - self.lo, self.partials)
 
     def gather_merge(self, dist=None):
-        """Every rank's partials over NCCL, merged into `out`."""
+        """Every rank's partials merged into `out`: over peer memory, or over NCCL."""
         import fusor_attn as fa
+        if dist is not None and self.world > 1 and self.exchange == "peer":
+            if self.peers is None:
+                self.peers = fa.PeerExchange(self.heads, self.head_dim, self.group)
+            self.peers.merge(self.partials, self.out)
+            return self.out
         if dist is not None and self.world > 1:
             dist.all_gather_into_tensor(self.gathered, self.partials, group=self.group)
         else:
             self.gathered[0].copy_(self.partials)
         fa.merge_partials(self.gathered, self.out)
         return self.out
+
+    def close(self, dist=None):
+        """Releases the peer buffers (every rank, after its last step)."""
+        if self.peers is not None:
+            import torch
+            torch.cuda.synchronize()
+            if dist is not None:
+                dist.barrier(group=self.group)
+            self.peers.close()
+            self.peers = None
 
     def step(self, qkv, angles, rope, dist=None):
         self.rotate(qkv, angles, rope)

@@ -276,6 +276,29 @@ int fa_attend_partial(fa_kvcache* cache, int32_t layer, const float* q, int32_t 
 int fa_merge_partials(const float* partials, int32_t shards, int32_t heads, int32_t head_dim,
                       float* out, void* stream);
 
+/* The exchange of a KV-range-sharded decode over NVLink peer memory (one process per GPU of a
+ * box), in place of an all-gather of the partials and fa_merge_partials. Each rank allocates one
+ * exchange buffer of fa_peer_buffer_bytes (fa_peer_alloc: zeroed, with its CUDA IPC handle),
+ * the ranks swap the handles (any host channel: a process group's all-gather of objects), and
+ * each maps the others' (fa_peer_open). fa_exchange_merge then stores this rank's partials in
+ * every rank's buffer, raises its flag there, waits for every rank's flag in its own (bounded:
+ * FA_ERR_TIMEOUT from fa_device_status after about a second), and merges into out (heads x
+ * head_dim f32) with fa_merge_partials' arithmetic. Every rank calls it once per step, in the
+ * same order; the step count lives in the buffer, so a CUDA graph of the step can be replayed. */
+typedef struct fa_ipc_handle {
+  unsigned char bytes[64];
+} fa_ipc_handle;
+int fa_peer_buffer_bytes(int32_t world, int32_t heads, int32_t head_dim, uint64_t* bytes);
+int fa_peer_alloc(uint64_t bytes, void** ptr, fa_ipc_handle* handle);
+int fa_peer_open(const fa_ipc_handle* handle, void** ptr);
+int fa_peer_close(void* ptr); /* a mapping made by fa_peer_open */
+int fa_peer_free(void* ptr);  /* a buffer made by fa_peer_alloc */
+/* buffers: world pointers, this rank's own at [rank] and the mappings of the others'; every
+ * buffer of buffer_bytes. partials: this rank's heads x (head_dim + 2) f32 (fa_attend_partial). */
+int fa_exchange_merge(void* const* buffers, uint64_t buffer_bytes, int32_t rank, int32_t world,
+                      int32_t heads, int32_t head_dim, const float* partials, float* out,
+                      void* stream);
+
 /* blocks::attention::attend (attention.rs:79-95) and dit::Within::attend (dit.rs:135-166): full
  * (non-causal) softmax attention of every query over every key of its image, scores scaled by
  * 1/sqrt(head_dim), into out (images*queries rows of out_stride elements, heads x head_dim
