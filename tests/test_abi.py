@@ -138,3 +138,21 @@ def test_capabilities():
     flags, dims = fa.capabilities()
     assert flags & 1 and flags & 2
     assert dims == [16, 32, 64, 128, 256]
+
+
+def test_peer_exchange_buffer_size_and_arguments():
+    """fa_peer_buffer_bytes: a 256-byte header (the step counter and the flags), then two halves
+    of world x heads x (head_dim + 2) f32 partials; worlds past the 8 GPUs of a box, and a
+    fa_exchange_merge whose buffers are smaller than that, are refused before any launch."""
+    lib = fa.lib()
+    n = C.c_uint64()
+    assert lib.fa_peer_buffer_bytes(8, 16, 128, C.byref(n)) == fa.OK
+    assert n.value == 256 + 2 * 8 * 16 * 130 * 4
+    assert lib.fa_peer_buffer_bytes(9, 16, 128, C.byref(n)) == fa.ERR_ARG
+    assert lib.fa_peer_buffer_bytes(0, 16, 128, C.byref(n)) == fa.ERR_ARG
+    bufs = (C.c_void_p * 2)(1, 2)
+    rc = lib.fa_exchange_merge(bufs, 256, 0, 2, 16, 128, C.c_void_p(16), C.c_void_p(16), None)
+    assert rc == fa.ERR_SHAPE
+    assert b"exchange buffers" in lib.fa_last_error()
+    rc = lib.fa_exchange_merge(bufs, 1 << 20, 2, 2, 16, 128, C.c_void_p(16), C.c_void_p(16), None)
+    assert rc == fa.ERR_ARG
