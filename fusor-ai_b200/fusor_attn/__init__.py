@@ -536,32 +536,38 @@ def normalize_and_rotate(heads: int, head_dim: int, qkv, out, norm: int = NORM_R
 class PeerExchange:
     """This rank's exchange buffer for fa_exchange_merge and the mappings of the other ranks'
     (CUDA IPC handles swapped over `group`, a torch.distributed process group of one process per
-    GPU of a box)."""
+    GPU of a box). Every rank takes part in the swap even when its own allocation failed; `ok`
+    says whether this rank has every buffer (the ranks agree on it before the first merge)."""
 
     def __init__(self, heads: int, head_dim: int, group=None):
         import torch.distributed as dist
         self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
         self.heads, self.head_dim = heads, head_dim
+        self.own, self.mapped, self.buffers, self.ok = None, [], None, False
         nbytes = C.c_uint64()
         _check(lib().fa_peer_buffer_bytes(self.world, heads, head_dim, C.byref(nbytes)))
         self.bytes = nbytes.value
+        mine = None
         own = C.c_void_p()
         handle = (C.c_ubyte * 64)()
-        _check(lib().fa_peer_alloc(self.bytes, C.byref(own), handle))
-        self.own = own
+        if lib().fa_peer_alloc(self.bytes, C.byref(own), handle) == OK:
+            self.own, mine = own, bytes(handle)
         handles = [None] * self.world
-        dist.all_gather_object(handles, bytes(handle), group=group)
-        self.mapped = []
+        dist.all_gather_object(handles, mine, group=group)  # every rank, allocated or not
+        if self.own is None or any(h is None for h in handles):
+            return
         ptrs = []
         for r, h in enumerate(handles):
             if r == self.rank:
-                ptrs.append(own.value)
+                ptrs.append(self.own.value)
                 continue
             p = C.c_void_p()
-            _check(lib().fa_peer_open((C.c_ubyte * 64).from_buffer_copy(h), C.byref(p)))
+            if lib().fa_peer_open((C.c_ubyte * 64).from_buffer_copy(h), C.byref(p)) != OK:
+                return
             self.mapped.append(p)
             ptrs.append(p.value)
         self.buffers = (C.c_void_p * self.world)(*ptrs)
+        self.ok = True
 
     def merge(self, partials, out, stream=None):
         """This rank's (max, sum, o) partials (heads x (head_dim + 2) f32) exchanged with every

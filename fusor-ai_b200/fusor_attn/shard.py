@@ -91,9 +91,9 @@ class ShardedDecode:
     def gather_merge(self, dist=None):
         """Every rank's partials merged into `out`: over peer memory, or over NCCL."""
         import fusor_attn as fa
-        if dist is not None and self.world > 1 and self.exchange == "peer":
-            if self.peers is None:
-                self.peers = fa.PeerExchange(self.heads, self.head_dim, self.group)
+        if dist is not None and self.world > 1 and self.exchange == "peer" and self.peers is None:
+            self.peers = self._open_peers(dist)
+        if self.peers is not None:
             self.peers.merge(self.partials, self.out)
             return self.out
         if dist is not None and self.world > 1:
@@ -102,6 +102,21 @@ class ShardedDecode:
             self.gathered[0].copy_(self.partials)
         fa.merge_partials(self.gathered, self.out)
         return self.out
+
+    def _open_peers(self, dist):
+        """The peer exchange, if every rank could map every other's buffer; otherwise (a box
+        without peer access, say) every rank agrees to use NCCL instead."""
+        import torch
+
+        import fusor_attn as fa
+        peers = fa.PeerExchange(self.heads, self.head_dim, self.group)
+        flag = torch.tensor([1 if peers.ok else 0], device="cuda", dtype=torch.int32)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=self.group)
+        if int(flag.item()) == 1:
+            return peers
+        peers.close()
+        self.exchange = "nccl"
+        return None
 
     def close(self, dist=None):
         """Releases the peer buffers (every rank, after its last step)."""
