@@ -110,7 +110,8 @@ class ShardedDecode:
 
         import fusor_attn as fa
         peers = fa.PeerExchange(self.heads, self.head_dim, self.group)
-        flag = torch.tensor([1 if peers.ok else 0], device="cuda", dtype=torch.int32)
+        device = "cuda" if dist.get_backend(self.group) == "nccl" else "cpu"
+        flag = torch.tensor([1 if peers.ok else 0], device=device, dtype=torch.int32)
         dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=self.group)
         if int(flag.item()) == 1:
             return peers

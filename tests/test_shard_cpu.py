@@ -4,6 +4,7 @@ partial format of fa_attend_partial (base-2 max, sum, unnormalised output), repr
 oracle's whole-context attention."""
 import os
 import socket
+import types
 
 import numpy as np
 import pytest
@@ -109,3 +110,54 @@ def test_kv_range_split_over_gloo_ranks_matches_the_oracle(world):
             assert p.exitcode == 0
         for r in range(world):
             assert np.abs(result[r] - want).max() < 1e-5
+
+
+class _FakeExchange:
+    """Stands in for fa.PeerExchange: rank 1 cannot map the other ranks' buffers."""
+
+    closed = False
+
+    def __init__(self, heads, head_dim, group=None):
+        import torch.distributed as dist
+        self.ok = dist.get_rank(group) != 1
+
+    def close(self):
+        _FakeExchange.closed = True
+
+
+def _agree_rank(rank, world, port, result):
+    import torch.distributed as dist
+
+    import fusor_attn as fa
+    from fusor_attn.shard import ShardedDecode
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        fa.PeerExchange = _FakeExchange
+        decode = types.SimpleNamespace(heads=4, head_dim=32, group=None, exchange="peer")
+        peers = ShardedDecode._open_peers(decode, dist)
+        result[rank] = (peers is None, decode.exchange, _FakeExchange.closed)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_exchange_falls_back_to_nccl_on_every_rank_when_one_cannot_map():
+    """The set-up of the peer exchange is collective: when one rank could not map the others'
+    buffers, every rank goes on with NCCL and releases what it had set up."""
+    import torch.multiprocessing as mp
+    world = 3
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as manager:
+        result = manager.dict()
+        port = free_port()
+        procs = [ctx.Process(target=_agree_rank, args=(r, world, port, result)) for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(120)
+            assert p.exitcode == 0
+        for r in range(world):
+            none, exchange, closed = result[r]
+            assert none and exchange == "nccl"
+            assert closed  # every rank releases what it holds (a failed rank its own buffer)
