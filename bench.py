@@ -500,7 +500,7 @@ class C4Sharded(Workload):
         self.tokens = 1
         self.launches_per_step = 3
         # a step is tens of microseconds on the GPU, less than its calls' host time: the whole
-        # step (the NCCL all-gather included) is replayed as one captured CUDA graph
+        # step (the exchange of the partials included) is replayed as one captured CUDA graph
         self.graphs = True
         self.bytes = (hi - lo) * kv * d * 2 * 4
         self.h_qkv = self.qkv.cpu().pin_memory()
@@ -510,7 +510,7 @@ class C4Sharded(Workload):
         self.d2h = self.h_out.numel() * 4
 
     def capture(self):
-        """The step (rotate, attend the local range, all-gather, merge) as one CUDA graph, and
+        """The step (rotate, attend the local range, exchange and merge) as one CUDA graph, and
         the local attend alone as another (the dominant kernel's timing). Every rank captures
         the same collectives in the same order, after warm-up has created the communicator."""
         torch = self.torch
