@@ -90,3 +90,57 @@ def test_peer_exchange_matches_the_nccl_all_gather(world):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     mp.spawn(_rank, args=(world, _free_port()), nprocs=world, join=True)
+
+
+def test_exchange_wait_gives_up_on_a_rank_that_never_publishes():
+    """One process, one GPU: rank 0 of a 2-rank exchange whose rank 1 never runs (its buffer is
+    a second local allocation that nothing else writes). The kernel's wait on rank 1's flag runs
+    out after about a second; the host reads ERR_TIMEOUT from fa_device_status, the rank's own
+    partials are still merged, and the context stays usable (a 1-rank exchange right after it
+    succeeds with a clean status)."""
+    import ctypes as C
+    import time
+
+    import torch
+
+    import fusor_attn as fa
+    assert torch.cuda.is_available()
+    lib = fa.lib()
+    heads, d, world = 4, 64, 2
+    nbytes = C.c_uint64()
+    assert lib.fa_peer_buffer_bytes(world, heads, d, C.byref(nbytes)) == fa.OK
+    owned = []
+    for _ in range(world):
+        p, handle = C.c_void_p(), (C.c_ubyte * 64)()
+        assert lib.fa_peer_alloc(nbytes.value, C.byref(p), handle) == fa.OK
+        owned.append(p)
+    try:
+        buffers = (C.c_void_p * world)(*(p.value for p in owned))
+        gen = torch.Generator("cuda").manual_seed(5)
+        partials = torch.empty((heads, d + 2), device="cuda")
+        partials[:, 0] = torch.rand((heads,), device="cuda", generator=gen) * 4 - 2  # max (log2)
+        partials[:, 1] = torch.rand((heads,), device="cuda", generator=gen) * 2 + 1  # sum
+        partials[:, 2:] = torch.randn((heads, d), device="cuda", generator=gen)
+        want = partials[:, 2:] / partials[:, 1:2]
+        out = torch.zeros((heads, d), device="cuda")
+        stream = fa._stream(None)
+        start = time.monotonic()
+        assert lib.fa_exchange_merge(buffers, nbytes.value, 0, world, heads, d,
+                                     fa._dptr(partials), fa._dptr(out), stream) == fa.OK
+        with pytest.raises(fa.FaError) as err:
+            fa.device_status()
+        waited = time.monotonic() - start
+        assert err.value.code == fa.ERR_TIMEOUT
+        assert 0.2 < waited < 30.0, f"the wait gave up after {waited:.2f} s"
+        # rank 1's slot is still zero (max 0, sum 0): the merge is rank 0's partials alone
+        assert torch.allclose(out, want, rtol=1e-6, atol=1e-6)
+        # the context is usable and the error word was cleared: a 1-rank exchange on buffer 0
+        out.zero_()
+        assert lib.fa_exchange_merge(buffers, nbytes.value, 0, 1, heads, d, fa._dptr(partials),
+                                     fa._dptr(out), stream) == fa.OK
+        fa.device_status()
+        assert torch.allclose(out, want, rtol=1e-6, atol=1e-6)
+    finally:
+        torch.cuda.synchronize()
+        for p in owned:
+            lib.fa_peer_free(p)
