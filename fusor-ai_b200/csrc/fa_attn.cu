@@ -294,6 +294,45 @@ struct Plan {
 #ifndef FA_SPAN_MIN_CHUNK_TILES
 #define FA_SPAN_MIN_CHUNK_TILES 16
 #endif
+
+int attend_resident_d(int head_dim, const fa::AttendLaunch& l) {
+  switch (head_dim) {
+    case 16: return fa::attend_resident<16>(l);
+    case 32: return fa::attend_resident<32>(l);
+    case 64: return fa::attend_resident<64>(l);
+    case 128: return fa::attend_resident<128>(l);
+    case 256: return fa::attend_resident<256>(l);
+    default: return 0;
+  }
+}
+
+// The chunk count, at most p.chunks, that streams a span's keys in the least time when the CTAs
+// run in waves of the SMs' resident slots: a last wave that is mostly empty streams at a fraction
+// of the rate (fewer loads in flight per SM) for as long as a full one, so the cost of c chunks
+// is waves(c) / c (waves times each chunk's share of the keys); the largest count of least cost.
+// A GPU's share of C4 over 2 GPUs (65537 keys, 8 KV heads, 444 slots): 128 chunks = 2.3 waves
+// -> 111 chunks, 2 waves; over 4 GPUs 64 -> 55 chunks, one wave.
+int whole_waves(const fa_kvcache* c, int rows, const Plan& p) {
+  fa::AttendLaunch l{};
+  l.kt = c->dtype == FA_F32 ? fa::kKtF32 : fa::kKtBf16;
+  l.g = p.g;
+  l.batch = false;
+  const int resident = attend_resident_d(c->head_dim, l);
+  if (resident <= 0) return p.chunks;
+  const int64_t slots = int64_t(c->dev->sms) * resident;
+  const int64_t per_chunk = int64_t(rows) * p.kv_groups;
+  auto cost = [&](int ch) { return double((per_chunk * ch + slots - 1) / slots) / ch; };
+  int best = p.chunks;
+  double best_cost = cost(best);
+  for (int ch = p.chunks - 1; ch >= 1; --ch) {
+    if (cost(ch) < best_cost * (1.0 - 1e-9)) {
+      best_cost = cost(ch);
+      best = ch;
+    }
+  }
+  return best;
+}
+
 Plan plan_span(const fa_kvcache* c, int rows, int max_keys, bool split_small = true) {
   Plan p;
   const int group = c->heads / c->kv_heads;
@@ -325,6 +364,7 @@ Plan plan_span(const fa_kvcache* c, int rows, int max_keys, bool split_small = t
     // on B200 for one row over 16384 keys of 8 f32 KV heads (a GPU's share of C4 over 8 GPUs):
     // 37 vs 63 us against 3.5-tile chunks; 131073 keys keep their 148 chunks.
     p.chunks = std::min(p.chunks, std::max(1, max_chunks / FA_SPAN_MIN_CHUNK_TILES));
+    p.chunks = whole_waves(c, rows, p);
   }
   return p;
 }

@@ -35,12 +35,53 @@ cudaError_t launch_kt(const AttendLaunch& l, cudaStream_t stream) {
   }
 }
 
+template <int D, typename KT, int G, bool BATCH, typename Args>
+int resident_one() {
+  auto kernel = attend_kernel<D, KT, G, BATCH, Args>;
+  constexpr size_t smem = DecodeShape<D, KT, G>::kSmemBytes;
+  static std::atomic<int> cached[64];         // per instantiation, per device; 0: not asked yet
+  static std::atomic<bool> configured[64];
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64) return 0;
+  int n = cached[device].load(std::memory_order_acquire);
+  if (n > 0) return n;
+  if (smem_limit_once(kernel, int(smem), configured) != cudaSuccess) return 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kDecodeThreads, smem) !=
+      cudaSuccess)
+    return 0;
+  cached[device].store(n, std::memory_order_release);
+  return n;
+}
+
+template <int D, typename KT, int G>
+int resident_g(const AttendLaunch& l) {
+  return l.batch ? resident_one<D, KT, G, true, BatchArgs>()
+                 : resident_one<D, KT, G, false, SpanArgs>();
+}
+
+template <int D, typename KT>
+int resident_kt(const AttendLaunch& l) {
+  switch (l.g) {
+    case 1: return resident_g<D, KT, 1>(l);
+    case 2: return resident_g<D, KT, 2>(l);
+    case 4: return resident_g<D, KT, 4>(l);
+    case 8: return resident_g<D, KT, 8>(l);
+    default: return 0;
+  }
+}
+
 }  // namespace
 
 template <>
 cudaError_t launch_attend<FA_HEAD_DIM>(const AttendLaunch& l, cudaStream_t stream) {
   return l.kt == kKtF32 ? launch_kt<FA_HEAD_DIM, float>(l, stream)
                         : launch_kt<FA_HEAD_DIM, __nv_bfloat16>(l, stream);
+}
+
+template <>
+int attend_resident<FA_HEAD_DIM>(const AttendLaunch& l) {
+  return l.kt == kKtF32 ? resident_kt<FA_HEAD_DIM, float>(l)
+                        : resident_kt<FA_HEAD_DIM, __nv_bfloat16>(l);
 }
 
 }  // namespace fa

@@ -75,6 +75,12 @@ struct AttendLaunch {
 template <int D>
 cudaError_t launch_attend(const AttendLaunch& launch, cudaStream_t stream);
 
+// CTAs of the launch's instantiation that one SM holds at once (its shared memory and
+// registers, cudaOccupancyMaxActiveBlocksPerMultiprocessor on the current device; asked once per
+// device), or 0 if the runtime could not say.
+template <int D>
+int attend_resident(const AttendLaunch& launch);
+
 // Keys per pipeline tile of an instantiation (the chunking granularity).
 inline int tile_keys(int head_dim, int kt) {
   return kTileBytes / (head_dim * (kt == kKtF32 ? 4 : 2));
