@@ -665,6 +665,12 @@ int attend_rows_tc(fa_kvcache* c, int layer, const fa_span* span, const std::vec
   a.out_stride = out_stride;
   a.out_bf16 = 0;
   a.err = c->dev->err;
+  // A causal span whose rows see from a few keys to several times as many runs its heaviest
+  // pairs first across heads, when the K/V it reads fits well inside L2 (every head's pairs run
+  // at once in that order). Measured on B200: an 8192-row causal prefill from position 0 (32/8
+  // heads x 128, bf16 cache).
+  const double kv_bytes = 2.0 * c->kv_heads * double(a.end) * c->head_dim * c->elem();
+  a.pair_major = a.kind == FA_MASK_CAUSAL && span->first < span->rows && kv_bytes <= 48e6;
   fa::FmhaLaunch l{c->dtype == FA_BF16 ? 1 : 0, c->head_dim, q, uint64_t(span->rows),
                    uint64_t(c->heads), uint64_t(q_stride), uint64_t(c->head_dim), c->keys,
                    c->values, uint64_t(c->capacity), uint64_t(c->layers) * c->kv_heads,

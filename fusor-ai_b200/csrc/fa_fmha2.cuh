@@ -14,7 +14,8 @@
 // A query tile takes part in the KV tiles its rows see (the union of their key runs); the other
 // tile's barriers count only its own participating tiles.
 // Schedule (FmhaArgs::whole_units / splits): a 1-D grid over the units (query head, pair of query
-// tiles), head-major. The leading units run whole; with splits > 1 each later unit runs as that
+// tiles), head-major (pair-major, heaviest pairs first, for a causal prefill whose K/V fits in
+// L2: FmhaArgs::pair_major). The leading units run whole; with splits > 1 each later unit runs as that
 // many consecutive CTAs, each over an equal share of the pair's KV tiles, so that the last waves
 // of a call whose units do not fill the SMs evenly are cut into shorter pieces. A piece writes
 // its rows' (max, sum, unnormalised O) partials; the last piece of the unit to finish (an
@@ -125,6 +126,17 @@ __device__ __forceinline__ Fmha2Unit fmha2_unit(const FmhaArgs& a, uint32_t cta)
     u.piece = p % a.splits;
     u.n_pieces = a.splits;
     unit = whole + u.tail_unit;
+  }
+  if (a.pair_major && a.splits <= 1) {
+    // A pair's keys grow with its rows (a causal prefill from the cache's start), so the units
+    // run heaviest first across every head and image (longest-processing-time order: the last
+    // wave holds the lightest pairs). Every head's K/V is then read at once: the host asks for
+    // this order only when that fits in L2.
+    u.head = unit % a.heads;
+    const int rest = unit / a.heads;
+    u.image = rest % a.images;
+    u.r0 = (pairs - 1 - rest / a.images) * 256;
+    return u;
   }
   u.head = unit / per_head;
   const int pair_id = per_head - 1 - unit % per_head;  // heavier (later, for causal masks) first

@@ -35,6 +35,8 @@ struct FmhaArgs {
   // the counter back to zero.
   int whole_units;
   int splits;
+  // 1: without splits, units run pair-major, the heaviest pairs of every head first
+  int pair_major;
   float* part_o;
   float* part_ml;
   int* counters;

@@ -434,6 +434,25 @@ def test_prefill_on_tensor_cores_every_mask(torch, dtype, head_dim, mask_name):
                            f"rows {sorted(set(bad[:, 0].tolist()))[:40]}, heads {sorted(set(bad[:, 1].tolist()))}")
 
 
+@pytest.mark.parametrize("first,rows", [(0, 1000), (37, 700)])
+def test_causal_prefill_over_several_pairs(torch, first, rows):
+    """A causal prefill of several 256-row pairs over a bf16 cache, GQA 8/2, ragged last tile:
+    its units run heaviest pair first across the heads (the K/V fits in L2). Every row of
+    every head against the oracle."""
+    shape = fa.Shape(1, 8, 2, 128)
+    pair = Pair(shape, first + rows + 8, fa.BF16, filled=first, seed=9)
+    qkv = normal(91, (rows, shape.qkv))
+    angles = fa.rotary_angles(fa.Rotation(base=1e6), 128, range(first, first + rows))
+    span = fa.Span(rows, first, fa.Mask.causal())
+    out = torch.zeros((rows, shape.width), device="cuda")
+    pair.gpu.attention(0, span, dev(torch, qkv), out, dev(torch, angles), fa.ROPE_HALF)
+    fa.device_status()
+    want = pair.oracle_attention(0, span, qkv, angles, fa.ROPE_HALF)
+    got = out.cpu().numpy()
+    print(compare(f"causal prefill {rows} rows from {first}, bf16", got, want))
+    assert max_abs(got, want) <= TOL_BF16
+
+
 def test_tensor_core_and_split_kv_paths_agree(torch):
     """The same rows through fa_attend on the tensor cores (64 rows) and through the split-KV
     kernel (one row at a time) give the same attention within the f32 bar."""
