@@ -125,6 +125,8 @@ SIGNATURES = {
     "fa_attention": (C.c_int, [_P, _I32, _P, _I32, _P, _P, _P, _I64, _P, _I64, _P]),
     "fa_attention_host": (C.c_int, [_P, _I32, _P, _I32, _P, _P, _P, _I64, _P, _I64, _P]),
     "fa_attention_batch": (C.c_int, [_P, _P, _I32, _I32, _I32, _P, _P, _P, _I64, _P, _I64, _P]),
+    "fa_attention_batch_host": (C.c_int, [_P, _P, _I32, _I32, _I32, _P, _P, _P, _I64, _P, _I64,
+                                          _P]),
     "fa_attention_input_batch": (C.c_int, [_P, _P, _I32, _I32, _I32, _P, _P, _P, _I64, _P, _I64, _P]),
     "fa_peer_buffer_bytes": (C.c_int, [_I32, _I32, _I32, C.POINTER(C.c_uint64)]),
     "fa_peer_alloc": (C.c_int, [C.c_uint64, C.POINTER(_P), _P]),
@@ -464,6 +466,19 @@ class Batch:
                                         rope if angles is not None else ROPE_NONE, _dptr(angles),
                                         _norm(norm), _dptr(qkv), qkv.stride(0), _dptr(out),
                                         out.stride(0), _stream(stream)))
+
+    def attention_host(self, layer: int, qkv, out, angles=None, rope: int = ROPE_HALF, norm=None,
+                       stream=None):
+        """attention() over HOST tensors (qkv, angles and out in CPU memory, pinned for the
+        copies to overlap the attention): returns when out holds every sequence's row."""
+        for t in (qkv, out) + ((angles,) if angles is not None else ()):
+            if t.device.type != "cpu" or t.stride(-1) != 1:
+                raise ValueError("host tensors with unit stride along a row")
+        _check(lib().fa_attention_batch_host(self.handles, self.spans, self.n, layer,
+                                             rope if angles is not None else ROPE_NONE,
+                                             _dptr(angles), _norm(norm), _dptr(qkv),
+                                             qkv.stride(0), _dptr(out), out.stride(0),
+                                             _stream(stream)))
 
 
 def rotate_queries(heads: int, head_dim: int, qkv, q_out, angles=None, rope: int = ROPE_HALF,

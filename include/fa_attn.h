@@ -248,6 +248,16 @@ int fa_attention_batch(fa_kvcache* const* caches, const fa_span* spans, int32_t 
                        const fa_head_norm* norm, const float* qkv, int64_t qkv_stride,
                        float* out, int64_t out_stride, void* stream);
 
+/* fa_attention_batch with HOST qkv, angles and out (the batched form of fa_attention_host):
+ * returns when `out` holds every sequence's row. A batch of 16 or more runs as two groups of
+ * sequences of about equal key counts, each its own launch: the second group's rows are copied
+ * in, and the first group's outputs copied out, on a copy stream while the other group attends.
+ * Pinned host memory lets the copies overlap; pageable memory still works. */
+int fa_attention_batch_host(fa_kvcache* const* caches, const fa_span* spans, int32_t batch,
+                            int32_t layer, int32_t rope, const float* angles_host,
+                            const fa_head_norm* norm, const float* qkv_host, int64_t qkv_stride,
+                            float* out_host, int64_t out_stride, void* stream);
+
 /* fa_attention_batch's first half: RoPE + keep of each sequence's row into its own cache, the
  * rotated queries into q_out (batch rows, q_out_stride apart; may be NULL). */
 int fa_attention_input_batch(fa_kvcache* const* caches, const fa_span* spans, int32_t batch,

@@ -244,6 +244,35 @@ def test_config3_batched_decode_sample(torch, dtype):
         assert max_abs(got[i:i + 1], want) <= tol, compare(f"C3 seq {i}", got[i:i + 1], want)
 
 
+@pytest.mark.parametrize("batch,pinned", [(40, True), (5, False)])
+def test_config3_batch_from_host_memory(torch, batch, pinned):
+    """fa_attention_batch_host: the rows and angles in host memory (pinned, or pageable); 40
+    sequences run as two groups whose copies overlap the other group's attention, 5 as one
+    launch on the caller's stream. Every sequence against the oracle, and against the
+    device-memory batch call over the same caches within f32 rounding."""
+    shape = fa.Shape(1, 32, 8, 128)
+    lengths = [int(n) // 8 for n in c3_lengths(seed=303, n=batch)]
+    pairs = [Pair(shape, n + 1, filled=n, seed=330 + i) for i, n in enumerate(lengths)]
+    qkv = normal(304, (batch, shape.qkv))
+    angles = fa.rotary_angles(fa.Rotation(base=1e6), 128, lengths)
+    spans = [fa.Span(1, n, fa.Mask.causal()) for n in lengths]
+    b = fa.Batch([p.gpu for p in pairs], spans)
+    h_qkv, h_angles = torch.from_numpy(qkv), torch.from_numpy(angles)
+    h_out = torch.zeros((batch, shape.width))
+    if pinned:
+        h_qkv, h_angles, h_out = h_qkv.pin_memory(), h_angles.pin_memory(), h_out.pin_memory()
+    b.attention_host(0, h_qkv, h_out, h_angles, fa.ROPE_HALF)
+    fa.device_status()
+    got = h_out.numpy()
+    for i, (p, span) in enumerate(zip(pairs, spans)):
+        want = p.oracle_attention(0, span, qkv[i:i + 1], angles[i:i + 1], fa.ROPE_HALF)
+        assert max_abs(got[i:i + 1], want) <= TOL_F32, compare(f"host batch seq {i}", got[i:i + 1], want)
+    # the same step from device memory (the kept rows are written again with the same values)
+    out = torch.zeros((batch, shape.width), device="cuda")
+    b.attention(0, dev(torch, qkv), out, dev(torch, angles), fa.ROPE_HALF)
+    assert float((out.cpu() - h_out).abs().max()) <= 1e-5
+
+
 def test_config3_batch_equals_one_call_per_sequence(torch):
     """Batching is invisible: each sequence alone gives the same output (full C3 shape, a
     quarter of the sequences to keep host memory small). Over a bf16 cache the batch decodes on
