@@ -271,11 +271,13 @@ __device__ __forceinline__ void merge_chunk_partials(const float* part_o, const 
   const int64_t base = int64_t(part_base) * heads + h0;  // slot of (chunk 0, head h0)
   for (int h = warp; h < g; h += kThreads / 32) {
     float mm = -INFINITY;
+#pragma unroll 8
     for (int ch = lane; ch < chunks; ch += 32)
       mm = fmaxf(mm, __ldcg(&part_ml[2 * (base + int64_t(ch) * heads + h)]));
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, off));
     float ll = 0.0f;
+#pragma unroll 8
     for (int ch = lane; ch < chunks; ch += 32) {
       const int64_t slot = base + int64_t(ch) * heads + h;
       const float cm = __ldcg(&part_ml[2 * slot]);
@@ -303,7 +305,9 @@ __device__ __forceinline__ void merge_chunk_partials(const float* part_o, const 
       wts[k * G + h] = cm == -INFINITY ? 0.0f : exp2_approx(cm - merge_m[h]);
     }
     named_sync(bar, kThreads);
-#pragma unroll 4
+    // the loads of 16 chunks in flight per thread (the partials are in L2: each trip is its
+    // latency, and a row split 222 ways otherwise took 56 trips at the end of the launch)
+#pragma unroll 16
     for (int k = 0; k < nb; ++k) {
       const float* po = part_o + (base + int64_t(cb + k) * heads) * D;
 #pragma unroll
