@@ -32,6 +32,38 @@ __global__ void prepare_queries_kernel(const T* values, int64_t stride, int64_t 
   }
 }
 
+// The same over f32 rows whose elements start on 16-byte boundaries (values, offset and stride,
+// and q_out): eight consecutive elements of a row per step of a thread, two 16-byte loads and
+// one 16-byte (bf16) or two (f32) stores, the row found by one division per eight elements.
+template <typename O>
+__global__ void prepare_queries_vec_kernel(const float* values, int64_t stride, int64_t offset,
+                                           int rows, int64_t width, float scale, O* q_out) {
+  const int64_t per_row = width / 8;
+  const int64_t total = int64_t(rows) * per_row;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = i / per_row, c = (i - r * per_row) * 8;
+    const float4* src = reinterpret_cast<const float4*>(values + r * stride + offset + c);
+    float4 a = __ldcs(src), b = __ldcs(src + 1);
+    a = make_float4(a.x * scale, a.y * scale, a.z * scale, a.w * scale);
+    b = make_float4(b.x * scale, b.y * scale, b.z * scale, b.w * scale);
+    if constexpr (sizeof(O) == 2) {
+      const __nv_bfloat162 p0 = __floats2bfloat162_rn(a.x, a.y), p1 = __floats2bfloat162_rn(a.z, a.w);
+      const __nv_bfloat162 p2 = __floats2bfloat162_rn(b.x, b.y), p3 = __floats2bfloat162_rn(b.z, b.w);
+      uint4 w;
+      w.x = *reinterpret_cast<const uint32_t*>(&p0);
+      w.y = *reinterpret_cast<const uint32_t*>(&p1);
+      w.z = *reinterpret_cast<const uint32_t*>(&p2);
+      w.w = *reinterpret_cast<const uint32_t*>(&p3);
+      *reinterpret_cast<uint4*>(q_out + r * width + c) = w;
+    } else {
+      float4* dst = reinterpret_cast<float4*>(q_out + r * width + c);
+      dst[0] = a;
+      dst[1] = b;
+    }
+  }
+}
+
 // out[h][e] = sum_s 2^(m_s - M) o_s[e] / sum_s 2^(m_s - M) l_s over the shards' partials.
 __global__ void merge_partials_kernel(const float* partials, int shards, int heads, int head_dim,
                                       float* out) {
@@ -68,6 +100,17 @@ cudaError_t launch_prepare_queries(int dtype, const void* values, int64_t stride
   if (total == 0) return cudaSuccess;
   const int blocks = int(std::min<int64_t>((total + 255) / 256, 148 * 16));
   auto* qb = reinterpret_cast<__nv_bfloat16*>(q_out);
+  const int64_t width = int64_t(heads) * head_dim;
+  if (dtype == 0 && width % 8 == 0 && reinterpret_cast<uintptr_t>(values) % 16 == 0 &&
+      offset % 4 == 0 && stride % 4 == 0 && reinterpret_cast<uintptr_t>(q_out) % 16 == 0) {
+    auto* v = static_cast<const float*>(values);
+    const int vblocks = int(std::min<int64_t>((total / 8 + 255) / 256, 148 * 16));
+    if (out_bf16)
+      prepare_queries_vec_kernel<<<vblocks, 256, 0, stream>>>(v, stride, offset, rows, width, scale, qb);
+    else
+      prepare_queries_vec_kernel<<<vblocks, 256, 0, stream>>>(v, stride, offset, rows, width, scale, q_out);
+    return cudaGetLastError();
+  }
   if (dtype == 0) {
     auto* v = static_cast<const float*>(values);
     if (out_bf16)

@@ -482,6 +482,27 @@ def test_causal_prefill_over_several_pairs(torch, first, rows):
     assert max_abs(got, want) <= TOL_BF16
 
 
+@pytest.mark.parametrize("rows", [300, 1030])
+def test_attend_over_f32_queries_equals_attention_on_a_bf16_cache(torch, rows):
+    """The reference's plugin split (keep, then attend over f32 queries) on a bf16 cache: fa_attend
+    converts the rotated f32 queries to bf16 operand rows before the tensor-core attention, and
+    gives fa_attention's output bit for bit (there the RoPE kernel writes the bf16 queries):
+    both round the same rotated values to nearest."""
+    shape = fa.Shape(1, 8, 2, 128)
+    cache = fa.KvCache(shape, rows, fa.BF16)
+    qkv = dev(torch, normal(95, (rows, shape.qkv)))
+    angles = dev(torch, fa.rotary_angles(fa.Rotation(base=1e6), 128, range(rows)))
+    span = fa.Span(rows, 0, fa.Mask.causal())
+    whole = torch.zeros((rows, shape.width), device="cuda")
+    cache.attention(0, span, qkv, whole, angles, fa.ROPE_HALF)
+    q = torch.zeros((rows, shape.width), device="cuda")
+    cache.attention_input(0, span, qkv, angles, fa.ROPE_HALF, q_out=q)
+    split = torch.zeros_like(whole)
+    cache.attend(0, span, q, split)
+    fa.device_status()
+    assert torch.equal(whole, split)
+
+
 def test_tensor_core_and_split_kv_paths_agree(torch):
     """The same rows through fa_attend on the tensor cores (64 rows) and through the split-KV
     kernel (one row at a time) give the same attention within the f32 bar."""
