@@ -167,4 +167,100 @@ __global__ void __launch_bounds__(kRopeWarps * 32) rope_keep_kernel(const __grid
                      a.qkv + int64_t(row) * a.qkv_stride + int64_t(unit) * a.head_dim);
 }
 
+// head_dim 128 with the whole head rotated, no gate heads and no head norm, over 16-byte aligned
+// rows: lane l holds elements 4l .. 4l + 3 of a head (one float4). RoPE by halves pairs element
+// e with e + 64, which lane l + 16 holds (one shuffle); interleaved RoPE pairs neighbours within
+// the float4. The arithmetic is rope_keep_head's, element for element (each product rounded,
+// then the difference or sum), so the rows kept and the queries are the same bits. (A head norm
+// would add its sum of squares in another order than rope_keep_head, which the fused projection
+// shares: those calls stay on rope_keep_kernel.) A warp takes R rows of one head unit, all their
+// loads issued before the first row is rotated.
+template <typename KT>
+__device__ __forceinline__ void store4(KT* p, float4 v);
+template <>
+__device__ __forceinline__ void store4<float>(float* p, float4 v) {
+  *reinterpret_cast<float4*>(p) = v;
+}
+template <>
+__device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16* p, float4 v) {
+  const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+  uint2 w;
+  w.x = *reinterpret_cast<const uint32_t*>(&a);
+  w.y = *reinterpret_cast<const uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(p) = w;
+}
+
+__device__ __forceinline__ float4 shfl_xor4(float4 v, int mask) {
+  return make_float4(__shfl_xor_sync(0xffffffffu, v.x, mask), __shfl_xor_sync(0xffffffffu, v.y, mask),
+                     __shfl_xor_sync(0xffffffffu, v.z, mask), __shfl_xor_sync(0xffffffffu, v.w, mask));
+}
+
+template <typename KT, int R>
+__global__ void __launch_bounds__(kRopeWarps * 32) rope_keep128_kernel(const __grid_constant__ RopeArgs a) {
+  pdl_trigger();  // the attention kernel after it may be scheduled now (it waits for this one)
+  constexpr int D = 128;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int unit = blockIdx.y * kRopeWarps + warp;
+  if (unit >= a.heads + 2 * a.kv_heads) return;
+  const int row0 = blockIdx.x * R;
+  const bool is_query = unit < a.heads, is_key = !is_query && unit < a.heads + a.kv_heads;
+  if (!is_query && !a.keep) return;
+  float4 v[R];
+#pragma unroll
+  for (int i = 0; i < R; ++i) {
+    v[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (row0 + i < a.n_rows)
+      v[i] = __ldcs(reinterpret_cast<const float4*>(a.qkv + int64_t(row0 + i) * a.qkv_stride +
+                                                     int64_t(unit) * D) + lane);
+  }
+#pragma unroll
+  for (int i = 0; i < R; ++i) {
+    const int row = row0 + i;
+    if (row >= a.n_rows) break;  // warp-uniform
+    float4 x = v[i];
+    if (is_query || is_key) {
+      if (a.rope == 1) {
+        // pair (e, e + 64): lanes 0-15 hold the first elements, lanes 16-31 their partners
+        const float* cs = a.angles + int64_t(row) * D;
+        const float4 c = reinterpret_cast<const float4*>(cs)[lane & 15];
+        const float4 s = reinterpret_cast<const float4*>(cs + 64)[lane & 15];
+        const float4 o = shfl_xor4(x, 16);
+        if (lane < 16) {
+          x = make_float4(__fsub_rn(__fmul_rn(x.x, c.x), __fmul_rn(o.x, s.x)),
+                          __fsub_rn(__fmul_rn(x.y, c.y), __fmul_rn(o.y, s.y)),
+                          __fsub_rn(__fmul_rn(x.z, c.z), __fmul_rn(o.z, s.z)),
+                          __fsub_rn(__fmul_rn(x.w, c.w), __fmul_rn(o.w, s.w)));
+        } else {
+          x = make_float4(__fadd_rn(__fmul_rn(x.x, c.x), __fmul_rn(o.x, s.x)),
+                          __fadd_rn(__fmul_rn(x.y, c.y), __fmul_rn(o.y, s.y)),
+                          __fadd_rn(__fmul_rn(x.z, c.z), __fmul_rn(o.z, s.z)),
+                          __fadd_rn(__fmul_rn(x.w, c.w), __fmul_rn(o.w, s.w)));
+        }
+      } else if (a.rope != 0) {
+        // pairs (2p, 2p + 1) for p = 2l, 2l + 1: cosines and sines p of the row's table
+        const float* cs = a.angles + int64_t(row) * D;
+        const float2 c = reinterpret_cast<const float2*>(cs)[lane];
+        const float2 s = reinterpret_cast<const float2*>(cs + 64)[lane];
+        x = make_float4(__fsub_rn(__fmul_rn(x.x, c.x), __fmul_rn(x.y, s.x)),
+                        __fadd_rn(__fmul_rn(x.y, c.x), __fmul_rn(x.x, s.x)),
+                        __fsub_rn(__fmul_rn(x.z, c.y), __fmul_rn(x.w, s.y)),
+                        __fadd_rn(__fmul_rn(x.w, c.y), __fmul_rn(x.z, s.y)));
+      }
+    }
+    if (is_query) {
+      if (a.q_out == nullptr) continue;
+      const int64_t at = int64_t(row) * a.q_out_stride + int64_t(unit) * D + 4 * lane;
+      const float4 q = make_float4(x.x * a.q_scale, x.y * a.q_scale, x.z * a.q_scale, x.w * a.q_scale);
+      if (a.q_out_bf16) store4<__nv_bfloat16>(reinterpret_cast<__nv_bfloat16*>(a.q_out) + at, q);
+      else store4<float>(a.q_out + at, q);
+      continue;
+    }
+    const KeepRow& kr = a.keep_rows[a.batch ? row : 0];
+    const int position = a.batch ? kr.position : a.first + row;
+    const int kv = (unit - a.heads) % a.kv_heads;
+    const int64_t at = (int64_t(kv) * kr.capacity + position % kr.capacity) * D + 4 * lane;
+    store4<KT>(static_cast<KT*>(is_key ? kr.k : kr.v) + at, x);
+  }
+}
+
 }  // namespace fa

@@ -85,7 +85,43 @@ __global__ void merge_partials_kernel(const float* partials, int shards, int hea
 
 }  // namespace
 
+namespace {
+
+bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
+// Whether rope_keep128_kernel takes the call: head_dim 128, the whole head rotated, no gate
+// heads, no head norm, and every row and table it reads or writes on a 16-byte boundary.
+bool rope128_fits(const RopeArgs& a) {
+  if (a.head_dim != 128 || a.gate_heads != 0 || (a.rotary_dim != 0 && a.rotary_dim != 128))
+    return false;
+  if (a.q_norm != nullptr || a.k_norm != nullptr) return false;
+  if (!aligned16(a.qkv) || a.qkv_stride % 4 != 0) return false;
+  if (a.rope != 0 && !aligned16(a.angles)) return false;
+  if (a.q_out != nullptr && (!aligned16(a.q_out) || a.q_out_stride % 4 != 0)) return false;
+  return true;
+}
+
+template <typename KT>
+cudaError_t launch_rope128(const RopeArgs& a, cudaStream_t stream) {
+  const int units = a.heads + 2 * a.kv_heads;
+  const unsigned ygrid = unsigned((units + kRopeWarps - 1) / kRopeWarps);
+  // long spans: four rows per warp (more loads in flight per warp, a quarter of the blocks)
+  if (a.n_rows >= 1024) {
+    constexpr int R = 4;
+    rope_keep128_kernel<KT, R><<<dim3(unsigned((a.n_rows + R - 1) / R), ygrid), kRopeWarps * 32, 0,
+                                 stream>>>(a);
+  } else {
+    rope_keep128_kernel<KT, 1><<<dim3(unsigned(a.n_rows), ygrid), kRopeWarps * 32, 0, stream>>>(a);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace
+
 cudaError_t launch_rope(int kt, const RopeArgs& args, cudaStream_t stream) {
+  if (rope128_fits(args))
+    return kt == kKtF32 ? launch_rope128<float>(args, stream)
+                        : launch_rope128<__nv_bfloat16>(args, stream);
   const int units = args.heads + args.gate_heads + 2 * args.kv_heads;
   const dim3 grid(args.n_rows, (units + kRopeWarps - 1) / kRopeWarps);
   if (kt == kKtF32) rope_keep_kernel<float><<<grid, kRopeWarps * 32, 0, stream>>>(args);

@@ -92,13 +92,43 @@ def test_the_cache_holds_the_reference_keys_bit_for_bit(torch):
     assert (v.cpu().numpy().view(np.uint32) == pair.cpu.values.view(np.uint32)).all()
 
 
-def test_head_norms_and_interleaved_rope(torch):
-    shape = fa.Shape(1, 8, 2, 64)
+@pytest.mark.parametrize("rope", [fa.ROPE_HALF, fa.ROPE_INTERLEAVED])
+@pytest.mark.parametrize("dtype", [fa.F32, fa.BF16])
+@pytest.mark.parametrize("rows", [3, 1100])
+def test_head_dim_128_rotation_and_keep_bit_for_bit(torch, rope, dtype, rows):
+    """RoPE + keep at head_dim 128 (a lane holds four consecutive elements; a warp takes four
+    rows of a long span): the rotated queries and the kept keys and values equal the oracle's
+    bit for bit (a bf16 cache holds them rounded to nearest)."""
+    shape = fa.Shape(2, 8, 2, 128)
+    pair = Pair(shape, rows, dtype)
+    qkv = normal(61, (rows, shape.qkv))
+    angles = fa.rotary_angles(fa.Rotation(base=1e6), 128, range(rows))
+    span = fa.Span(rows, 0, fa.Mask.causal())
+    q = torch.zeros((rows, shape.width), device="cuda")
+    pair.gpu.attention_input(1, span, dev(torch, qkv), dev(torch, angles), rope, q_out=q)
+    fa.device_status()
+    want_q = qkv.copy()
+    pair.cpu.attention_input(1, rows, 0, rope, angles, want_q, want_q.shape[1])
+    got_q = np.ascontiguousarray(q.cpu().numpy())
+    want_q = np.ascontiguousarray(want_q[:, :shape.width])
+    assert (got_q.view(np.uint32) == want_q.view(np.uint32)).all()
+    k, v = pair.gpu.copy_rows()
+    k, v = k.float().cpu().numpy(), v.float().cpu().numpy()
+    wk, wv = pair.cpu.keys, pair.cpu.values
+    if dtype == fa.BF16:
+        wk, wv = round_bf16(wk), round_bf16(wv)
+    assert (k.view(np.uint32) == np.ascontiguousarray(wk).view(np.uint32)).all()
+    assert (v.view(np.uint32) == np.ascontiguousarray(wv).view(np.uint32)).all()
+
+
+@pytest.mark.parametrize("head_dim", [64, 128])
+def test_head_norms_and_interleaved_rope(torch, head_dim):
+    shape = fa.Shape(1, 8, 2, head_dim)
     pair = Pair(shape, 300, filled=200, seed=5)
     qkv = normal(12, (3, shape.qkv))
-    qn = 1.0 + 0.2 * normal(13, (64,))
-    kn = 1.0 + 0.2 * normal(14, (64,))
-    angles = fa.rotary_angles(fa.Rotation(base=1e4), 64, range(200, 203))
+    qn = 1.0 + 0.2 * normal(13, (head_dim,))
+    kn = 1.0 + 0.2 * normal(14, (head_dim,))
+    angles = fa.rotary_angles(fa.Rotation(base=1e4), head_dim, range(200, 203))
     span = fa.Span(3, 200, fa.Mask.causal())
     out = torch.zeros((3, shape.width), device="cuda")
     pair.gpu.attention(0, span, dev(torch, qkv), out, dev(torch, angles), fa.ROPE_INTERLEAVED,
