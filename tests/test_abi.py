@@ -156,3 +156,18 @@ def test_peer_exchange_buffer_size_and_arguments():
     assert b"exchange buffers" in lib.fa_last_error()
     rc = lib.fa_exchange_merge(bufs, 1 << 20, 2, 2, 16, 128, C.c_void_p(16), C.c_void_p(16), None)
     assert rc == fa.ERR_ARG
+
+
+def test_batch_host_call_refuses_bad_arguments_before_any_copy():
+    """fa_attention_batch_host checks its arguments on the host: no caches or spans, and a batch
+    past 1024 sequences, are refused with ERR_ARG before any copy or launch."""
+    lib = fa.lib()
+    rc = lib.fa_attention_batch_host(None, None, 1, 0, fa.ROPE_NONE, None, None, None, 0, None, 0,
+                                     None)
+    assert rc == fa.ERR_ARG
+    assert b"null caches or spans" in lib.fa_last_error()
+    caches = (C.c_void_p * 1)(None)
+    spans = (fa._Span * 1)()
+    rc = lib.fa_attention_batch_host(caches, spans, 1025, 0, fa.ROPE_NONE, None, None, None, 0,
+                                     None, 0, None)
+    assert rc == fa.ERR_ARG
