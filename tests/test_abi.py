@@ -171,3 +171,53 @@ def test_batch_host_call_refuses_bad_arguments_before_any_copy():
     rc = lib.fa_attention_batch_host(caches, spans, 1025, 0, fa.ROPE_NONE, None, None, None, 0,
                                      None, 0, None)
     assert rc == fa.ERR_ARG
+
+
+def _strip_c_comments(text):
+    return re.sub(r"//[^\n]*", "", re.sub(r"/\*.*?\*/", "", text, flags=re.S))
+
+
+def _rust_ffi_block():
+    text = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    blocks = re.findall(r"```rust\n(.*?)```", text, re.S)
+    ffi = [b for b in blocks if 'extern "C"' in b]
+    assert len(ffi) == 1
+    return ffi[0]
+
+
+def test_rust_binding_declares_every_entry_point_with_its_arity():
+    """The Rust extern block a maintainer would add to fusor-ai names each entry point the
+    header declares, once, with the header's parameter count (no stale or missing lines)."""
+    header = _strip_c_comments(open(HEADER).read())
+    want = {}
+    for name, params in re.findall(r"\b(fa_\w+)\s*\(([^;{]*?)\)\s*;", header, re.S):
+        params = " ".join(params.split())
+        want[name] = 0 if params in ("", "void") else params.count(",") + 1
+    assert set(want) == set(declared_entry_points())
+    got = {}
+    for name, params in re.findall(r"pub fn (fa_\w+)\((.*?)\)\s*(?:->[^;]*)?;",
+                                   _rust_ffi_block(), re.S):
+        assert name not in got, name
+        params = " ".join(params.split())
+        got[name] = 0 if not params else params.count(":")
+    assert got == want
+
+
+def test_rust_structs_mirror_the_header_structs():
+    """Each #[repr(C)] struct of the Rust binding has the C struct's fields in the same order."""
+    header = _strip_c_comments(open(HEADER).read())
+    c_fields = {}
+    for body, name in re.findall(r"typedef struct\s*\w*\s*\{(.*?)\}\s*(\w+)\s*;", header, re.S):
+        fields = [re.sub(r"\[.*?\]", "", d).split()[-1].lstrip("*")
+                  for d in body.split(";") if d.strip()]
+        c_fields[name] = fields
+    rust = _rust_ffi_block()
+    seen = 0
+    for rname, body in re.findall(r"#\[repr\(C\)\] pub struct (\w+) \{(.*?)\}", rust, re.S):
+        if rname == "FaKvCache":
+            continue
+        cname = "fa_" + re.sub(r"(?<!^)([A-Z])", r"_\1", rname[2:]).lower()
+        fields = [f.split(":")[0].replace("pub", "").strip() for f in body.split(",") if f.strip()]
+        assert fields == c_fields[cname], rname
+        seen += 1
+    assert seen == len(c_fields)
