@@ -8,8 +8,9 @@ hot path over the batch: RoPE + keep of each sequence's new row, then attention 
 over its cache. `value` is tokens/s of the whole job (64 tokens per step); with N GPUs the
 sequences are split across ranks by total length with no collective (total work fixed).
 
-Other configurations (`--config c1|c2|c3bf16|c4`) run the same way; at N=1 the default run adds
-c1, c2, c3bf16 and c4 under "configs" in the same line.
+Other configurations (`--config c1|c2|c3bf16|c4|c5|prefill|proj|prologue`) run the same way; the
+default run adds them under "configs" in the same line. `--cpu-baselines` (1 GPU) also times the
+host restatement of the reference's CPU path for C1, C2, C4 and a slice of C5, beside each.
 
 `--impl reference` times the reference's CPU path (the oracle's C++ restatement of fusor-ai's
 f32 attention, split over the host's threads as its thread team splits heads) on the same
@@ -737,6 +738,78 @@ def cpu_baseline_c3(threads: int, budget_s: float = 20.0):
                   f"one forward call each, heads split over the thread team; mean of {passes} passes"}
 
 
+def _mean_seconds(call, budget_s):
+    """One warm-up call, then the mean of up to 20 calls within about budget_s (the shape of
+    harness::bench::time: a warm-up, then the mean of N calls)."""
+    call()
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        call()
+        n += 1
+        if time.perf_counter() - t0 > budget_s or n >= 20:
+            break
+    return (time.perf_counter() - t0) / n, n
+
+
+def cpu_baselines_other(threads: int, budget_s: float = 4.0):
+    """The oracle's C++ restatement of the reference's CPU path timed on the host for C1, C2 and
+    C4 (whole configs: RoPE and keep of the span, then the team-split attend) and for a slice of
+    C5's f32 full-mask attention (12 heads x 16 query rows against all 32760 keys, scaled to the
+    whole call by the query count), seeded N(0,1) inputs. Returns {config: cpu_baseline}."""
+    import oracle
+    rng = np.random.default_rng(11)
+    out = {}
+
+    def decode_or_prefill(name, heads, kv, d, first, rows):
+        cache = oracle.Cache(1, heads, kv, d, first + rows)
+        rng.standard_normal(cache.keys.shape, dtype=np.float32, out=cache.keys)
+        rng.standard_normal(cache.values.shape, dtype=np.float32, out=cache.values)
+        stride = (heads + 2 * kv) * d
+        qkv0 = rng.standard_normal((rows, stride), dtype=np.float32)
+        angles = oracle.angles_table(oracle.ROT_SEQUENCE, 1e6, d, range(first, first + rows))
+        mask = oracle.Mask.causal()
+
+        def call():
+            qkv = qkv0.copy()
+            cache.attention_input(0, rows, first, 1, angles, qkv, stride)
+            cache.attend(0, rows, first, mask, qkv, stride, threads=threads)
+
+        t, n = _mean_seconds(call, budget_s)
+        out[name] = {"value": round(rows / t, 3), "unit": "tokens/s", "cores": threads,
+                     "kind": "port", "ms_per_call": round(t * 1e3, 3),
+                     "sample": f"the whole config: RoPE + keep of {rows} row(s) at position "
+                               f"{first}, then the attend with heads split over the thread team; "
+                               f"mean of {n} calls"}
+        del cache
+
+    decode_or_prefill("c1", 14, 2, 64, 1024, 1)
+    decode_or_prefill("c2", 14, 2, 64, 0, 512)
+    decode_or_prefill("c4", 16, 8, 128, 131072, 1)
+
+    tokens, heads, d, sampled = 32760, 12, 128, 16
+    width = heads * d
+    k = rng.standard_normal((tokens, width), dtype=np.float32)
+    v = rng.standard_normal((tokens, width), dtype=np.float32)
+    q = rng.standard_normal((sampled, width), dtype=np.float32)
+    res = np.zeros((sampled, width), np.float32)
+
+    def slice_call():
+        oracle.attend_call(heads, heads, d, 1, sampled, tokens, q, width, 0, k, width, 0,
+                           v, width, 0, query_range=(0, sampled), threads=threads, out=res)
+
+    t, n = _mean_seconds(slice_call, budget_s)
+    whole = t * tokens / sampled
+    out["c5"] = {"value": round(tokens / whole, 3), "unit": "tokens/s", "cores": threads,
+                 "kind": "port", "tflops": round(6.594e12 / whole / 1e12, 5),
+                 "ms_per_call": round(whole * 1e3, 1),
+                 "sample": f"f32 full mask (dit::Within, ops::attend): {heads} heads x {sampled} "
+                           f"query rows against all {tokens} keys, mean of {n} calls, scaled "
+                           f"linearly by {tokens}/{sampled} to the whole call"}
+    oracle.release()
+    return out
+
+
 def host_threads():
     try:
         return len(os.sched_getaffinity(0))
@@ -844,6 +917,10 @@ def run_ours(args):
         v, meta = cpu_baseline_c3(threads)
         line["cpu_baseline"] = {"value": round(v, 3), "unit": "tokens/s", "cores": threads,
                                 "kind": "port", **meta}
+        if args.cpu_baselines and "configs" in line:
+            for name, base in cpu_baselines_other(threads).items():
+                if name in line["configs"]:
+                    line["configs"][name]["cpu_baseline"] = base
     fa.device_status()
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -961,6 +1038,8 @@ def main():
                     help="C3 sequences (a smaller batch for profiling captures)")
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-baselines", action="store_true",
+                    help="also time the host restatement for C1, C2, C4 and a C5 slice (1 GPU)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
