@@ -1553,7 +1553,22 @@ int fa_attention_batch_host(fa_kvcache* const* caches, const fa_span* spans, int
   if (int rc = c0->io.ensure(staging, s)) return rc;
   float* qkv_dev = static_cast<float*>(c0->io.ptr);
   float* angles_dev = qkv_dev + size_t(batch) * units;
+  // A pinned output that this device can address (mapped host memory) takes the attention
+  // kernels' stores directly, each row over PCIe as it is merged, during the kernel: no copy of
+  // the outputs after the last group. Pageable output goes through device staging and a copy.
   float* out_dev = angles_dev + size_t(batch) * d;
+  int64_t out_dev_stride = width;
+  bool out_mapped = false;
+  {
+    cudaPointerAttributes attr;
+    if (cudaPointerGetAttributes(&attr, out_host) != cudaSuccess) {
+      cudaGetLastError();
+    } else if (attr.type == cudaMemoryTypeHost && attr.devicePointer != nullptr) {
+      out_dev = static_cast<float*>(attr.devicePointer);
+      out_dev_stride = out_stride;
+      out_mapped = true;
+    }
+  }
   // Two groups of consecutive sequences of about equal key counts once the batch is large
   // enough for each group's launch to fill the SMs (each group's keys are chunked over the whole
   // GPU). Measured on B200 with C3's 64 sequences (f32 caches, pinned memory, per step): one
@@ -1568,10 +1583,11 @@ int fa_attention_batch_host(fa_kvcache* const* caches, const fa_span* spans, int
                               cudaMemcpyHostToDevice, s), "angles to device");
     if (int rc = fa_attention_batch(caches, spans, batch, layer, rope,
                                     rope != FA_ROPE_NONE ? angles_dev : nullptr, norm, qkv_dev,
-                                    units, out_dev, width, stream))
+                                    units, out_dev, out_dev_stride, stream))
       return rc;
-    FA_CUDA(cudaMemcpy2DAsync(out_host, out_stride * 4, out_dev, width * 4, width * 4, batch,
-                              cudaMemcpyDeviceToHost, s), "out to host");
+    if (!out_mapped)
+      FA_CUDA(cudaMemcpy2DAsync(out_host, out_stride * 4, out_dev, width * 4, width * 4, batch,
+                                cudaMemcpyDeviceToHost, s), "out to host");
     FA_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
     return FA_OK;
   }
@@ -1616,11 +1632,16 @@ int fa_attention_batch_host(fa_kvcache* const* caches, const fa_span* spans, int
     if (int rc = fa_attention_batch(caches + b0, spans + b0, n, layer, rope,
                                     rope != FA_ROPE_NONE ? angles_dev + size_t(b0) * d : nullptr,
                                     norm, qkv_dev + size_t(b0) * units, units,
-                                    out_dev + size_t(b0) * width, width, stream)) {
+                                    out_dev + b0 * out_dev_stride, out_dev_stride, stream)) {
       cudaStreamSynchronize(cs);
       return rc;
     }
     FA_CUDA(cudaEventRecord(done[g], s), "attention event");
+  }
+  if (out_mapped) {
+    // the caller's stream ran every group after its rows arrived: its end is the call's end
+    FA_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+    return FA_OK;
   }
   for (int g = 0; g < groups; ++g) {
     const int b0 = bounds[g], n = bounds[g + 1] - bounds[g];

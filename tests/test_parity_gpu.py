@@ -274,12 +274,15 @@ def test_config3_batched_decode_sample(torch, dtype):
         assert max_abs(got[i:i + 1], want) <= tol, compare(f"C3 seq {i}", got[i:i + 1], want)
 
 
-@pytest.mark.parametrize("batch,pinned", [(40, True), (5, False)])
-def test_config3_batch_from_host_memory(torch, batch, pinned):
+@pytest.mark.parametrize("batch,pinned,pad", [(40, True, 0), (5, False, 0), (5, True, 64),
+                                               (40, False, 64)])
+def test_config3_batch_from_host_memory(torch, batch, pinned, pad):
     """fa_attention_batch_host: the rows and angles in host memory (pinned, or pageable); 40
     sequences run as two groups whose copies overlap the other group's attention, 5 as one
-    launch on the caller's stream. Every sequence against the oracle, and against the
-    device-memory batch call over the same caches within f32 rounding."""
+    launch on the caller's stream. A pinned output takes the kernels' stores directly (mapped
+    host memory), a pageable one a copy; `pad` columns past each output row stay untouched.
+    Every sequence against the oracle, and against the device-memory batch call over the same
+    caches within f32 rounding."""
     shape = fa.Shape(1, 32, 8, 128)
     lengths = [int(n) // 8 for n in c3_lengths(seed=303, n=batch)]
     pairs = [Pair(shape, n + 1, filled=n, seed=330 + i) for i, n in enumerate(lengths)]
@@ -288,12 +291,14 @@ def test_config3_batch_from_host_memory(torch, batch, pinned):
     spans = [fa.Span(1, n, fa.Mask.causal()) for n in lengths]
     b = fa.Batch([p.gpu for p in pairs], spans)
     h_qkv, h_angles = torch.from_numpy(qkv), torch.from_numpy(angles)
-    h_out = torch.zeros((batch, shape.width))
+    h_rows = torch.full((batch, shape.width + pad), 7.0)
     if pinned:
-        h_qkv, h_angles, h_out = h_qkv.pin_memory(), h_angles.pin_memory(), h_out.pin_memory()
+        h_qkv, h_angles, h_rows = h_qkv.pin_memory(), h_angles.pin_memory(), h_rows.pin_memory()
+    h_out = h_rows[:, :shape.width]
     b.attention_host(0, h_qkv, h_out, h_angles, fa.ROPE_HALF)
     fa.device_status()
     got = h_out.numpy()
+    assert bool((h_rows[:, shape.width:] == 7.0).all())
     for i, (p, span) in enumerate(zip(pairs, spans)):
         want = p.oracle_attention(0, span, qkv[i:i + 1], angles[i:i + 1], fa.ROPE_HALF)
         assert max_abs(got[i:i + 1], want) <= TOL_F32, compare(f"host batch seq {i}", got[i:i + 1], want)
