@@ -34,6 +34,9 @@ import numpy as np  # noqa: E402
 
 C3_SEQS, C3_HEADS, C3_KV, C3_D = 64, 32, 8, 128
 L2_BYTES = 126 * 1024 * 1024
+# Parity bars (the tests' own): max abs error on the attention output with f32 I/O, and on the
+# bf16-compute paths (bf16 queries and probabilities on the tensor cores).
+TOL_F32, TOL_BF16 = 2e-3, 5e-3
 
 
 def c3_lengths():
@@ -131,8 +134,13 @@ class Workload:
     launches_per_step = 0
     flush_l2 = False
     graphs = False         # latency-bound steps: the step replayed as one captured CUDA graph
+    e2e_ran = False        # time_e2e ran this workload's public-API step
     _step_graph = None
     _kernel_graph = None
+
+    def parity(self, threads):
+        """The timed launch's output against the oracle on this rank (after the timing)."""
+        return None
 
     def phases(self):
         """The step's two calls (before and after the dominant kernel's event)."""
@@ -187,10 +195,12 @@ class C3Decode(Workload):
         self.lengths = [int(lengths[i]) for i in mine]
         shape = fa.Shape(1, C3_HEADS, C3_KV, C3_D)
         self.shape = shape
-        gen = torch.Generator("cuda").manual_seed(1000 + rank)
+        # every sequence's keys and values from its own seed, and the batch's qkv rows from one:
+        # the job is the same whatever the number of GPUs it is split over
         tdt = torch.float32 if dtype == fa.F32 else torch.bfloat16
         self.caches = []
-        for n in self.lengths:
+        for i, n in zip(mine, self.lengths):
+            gen = torch.Generator("cuda").manual_seed(1000 + int(i))
             c = fa.KvCache(shape, n + 1, dtype)
             k = torch.randn((1, C3_KV, n, C3_D), device="cuda", generator=gen).to(tdt)
             v = torch.randn((1, C3_KV, n, C3_D), device="cuda", generator=gen).to(tdt)
@@ -200,7 +210,10 @@ class C3Decode(Workload):
         spans = [fa.Span(1, n, fa.Mask.causal()) for n in self.lengths]
         self.batch = fa.Batch(self.caches, spans)
         b = len(self.caches)
-        self.qkv = torch.randn((b, shape.qkv), device="cuda", generator=gen)
+        gen = torch.Generator("cuda").manual_seed(999)
+        qkv_all = torch.randn((len(lengths), shape.qkv), device="cuda", generator=gen)
+        self.qkv = qkv_all[list(mine)].contiguous()
+        del qkv_all
         self.angles = torch.from_numpy(
             fa.rotary_angles(fa.Rotation(base=1e6), C3_D, self.lengths)).cuda()
         self.q = torch.zeros((b, shape.width), device="cuda")
@@ -231,6 +244,36 @@ class C3Decode(Workload):
         # attention; returns with h_out filled
         self.batch.attention_host(0, self.h_qkv, self.h_out, self.h_angles, self.fa.ROPE_HALF)
 
+    def parity(self, threads):
+        """Every sequence of this rank: the oracle's RoPE + keep of the row into a host copy of
+        the sequence's cache, then its attend, against the timed launch's output row; and the
+        end-to-end call's host output against the device output."""
+        import oracle
+        torch, fa = self.torch, self.fa
+        out = self.out.cpu().numpy()
+        qkv = self.qkv.cpu().numpy()
+        angles = self.angles.cpu().numpy()
+        bf16 = self.dtype == fa.BF16
+        wants = []
+        for j, (c, n) in enumerate(zip(self.caches, self.lengths)):
+            k, v = c.copy_rows(n)
+            oc = oracle.Cache(1, C3_HEADS, C3_KV, C3_D, n + 1)
+            oc.keys[:, :, :n] = k.float().cpu().numpy()
+            oc.values[:, :, :n] = v.float().cpu().numpy()
+            del k, v
+            q = qkv[j:j + 1].copy()
+            oc.attention_input(0, 1, n, fa.ROPE_HALF, angles[j:j + 1], q, q.shape[1])
+            if bf16:  # a bf16 cache keeps the new row rounded to nearest
+                oc.keys[0, :, n] = round_bf16(torch, oc.keys[0, :, n])
+                oc.values[0, :, n] = round_bf16(torch, oc.values[0, :, n])
+            wants.append(oc.attend(0, 1, n, oracle.Mask.causal(), q, q.shape[1], threads=threads))
+        want = np.concatenate(wants) if wants else np.zeros_like(out)
+        p = parity_result(out, want, TOL_BF16 if bf16 else TOL_F32,
+                          f"{len(self.lengths)} sequences, every head")
+        if self.e2e_ran and out.size:
+            p["e2e_vs_device_max_abs"] = sci(np.abs(self.h_out.numpy() - out).max())
+        return p
+
     def algorithmic(self):
         return float(self.bytes)
 
@@ -242,14 +285,12 @@ class SingleDecode(Workload):
         self.torch, self.fa, self.name = torch, fa, name
         shape = fa.Shape(1, heads, kv, d)
         self.shape = shape
+        self.position = position
         self.cache = fa.KvCache(shape, position + 1)
-        gen = torch.Generator("cuda").manual_seed(7)
-        k = torch.randn((1, kv, position, d), device="cuda", generator=gen)
-        v = torch.randn((1, kv, position, d), device="cuda", generator=gen)
+        k, v, self.qkv = decode_inputs(torch, shape, position)
         self.cache.put_rows(k, v)
         del k, v
         self.span = fa.Span(1, position, fa.Mask.causal())
-        self.qkv = torch.randn((1, shape.qkv), device="cuda", generator=gen)
         self.angles = torch.from_numpy(fa.rotary_angles(fa.Rotation(base=1e6), d, [position])).cuda()
         self.q = torch.zeros((1, shape.width), device="cuda")
         self.out = torch.zeros((1, shape.width), device="cuda")
@@ -277,8 +318,43 @@ class SingleDecode(Workload):
         self.cache.attention(0, self.span, self.d_qkv, self.out, self.d_angles, self.fa.ROPE_HALF)
         self.h_out.copy_(self.out, non_blocking=True)
 
+    def parity(self, threads):
+        """The whole decode: the oracle's RoPE + keep and attend over a host copy of the cache's
+        `position` seeded rows, against the timed output."""
+        k, v = self.cache.copy_rows(self.position)
+        want = oracle_decode(self.fa, self.shape, self.position, k.cpu().numpy(), v.cpu().numpy(),
+                             self.qkv.cpu().numpy(), self.angles.cpu().numpy(), threads)
+        p = parity_result(self.out.cpu().numpy(), want, TOL_F32,
+                          f"the decode row, {self.position + 1} keys, every head")
+        if self.e2e_ran:
+            p["e2e_vs_device_max_abs"] = sci(np.abs(self.h_out.numpy() - self.out.cpu().numpy()).max())
+        return p
+
     def algorithmic(self):
         return float(self.bytes)
+
+
+def decode_inputs(torch, shape, position):
+    """C1's and C4's seeded inputs: the cache's `position` keys and values, then the new row's
+    qkv, from one generator (the same on every rank, whatever the number of GPUs)."""
+    gen = torch.Generator("cuda").manual_seed(7)
+    dims = (1, shape.kv_heads, position, shape.head_dim)
+    k = torch.randn(dims, device="cuda", generator=gen)
+    v = torch.randn(dims, device="cuda", generator=gen)
+    qkv = torch.randn((1, shape.qkv), device="cuda", generator=gen)
+    return k, v, qkv
+
+
+def oracle_decode(fa, shape, position, keys, values, qkv, angles, threads):
+    """The reference's attention phase of one decode row at `position` on the host: the
+    oracle's RoPE + keep into a copy of the cache, then its team-split attend."""
+    import oracle
+    oc = oracle.Cache(1, shape.heads, shape.kv_heads, shape.head_dim, position + 1)
+    oc.keys[:, :, :position] = keys
+    oc.values[:, :, :position] = values
+    q = np.ascontiguousarray(qkv, np.float32).copy()
+    oc.attention_input(0, 1, position, fa.ROPE_HALF, angles, q, q.shape[1])
+    return oc.attend(0, 1, position, oracle.Mask.causal(), q, q.shape[1], threads=threads)
 
 
 class ProjectedInput(Workload):
@@ -322,6 +398,29 @@ class ProjectedInput(Workload):
         self.phases()[1]()
         self.h_q.copy_(self.q, non_blocking=True)
 
+    def parity(self, threads):
+        """The rotated queries of the timed launch against the oracle's projection (f64 sums
+        rounded to f32) followed by its RoPE + keep; and the kept key and value rows. The
+        projection's sums run in another order than the host's, so the bar is relative to the
+        magnitude of the projected values (2e-5, the projection tests' bar)."""
+        import oracle
+        fa = self.fa
+        qkv = oracle.project(self.x.cpu().numpy(), self.weight.cpu().numpy(),
+                             self.bias.cpu().numpy())
+        scale = max(1.0, float(np.abs(qkv).max()))
+        position = self.span.first
+        shape = self.cache.shape
+        oc = oracle.Cache(1, shape.heads, shape.kv_heads, shape.head_dim, position + 1)
+        oc.attention_input(0, 1, position, fa.ROPE_HALF, self.angles.cpu().numpy(), qkv,
+                           qkv.shape[1])
+        k, v = self.cache.copy_rows(position + 1)
+        got = np.concatenate([self.q.cpu().numpy().ravel(), k[0, :, position].cpu().numpy().ravel(),
+                              v[0, :, position].cpu().numpy().ravel()])
+        want = np.concatenate([qkv[0, :shape.width], oc.keys[0, :, position].ravel(),
+                               oc.values[0, :, position].ravel()])
+        return parity_result(got, want, 2e-5 * scale,
+                             "the rotated queries and the kept key and value rows")
+
     def algorithmic(self):
         return float(self.bytes)
 
@@ -362,6 +461,24 @@ class DitPrologue(Workload):
         self.qkv.copy_(self.h_qkv, non_blocking=True)
         self.phases()[1]()
         self.h_out.copy_(self.out, non_blocking=True)
+
+    def parity(self, threads):
+        """Every 32nd token (1024 of them) against the oracle's prologue (f32), as the distance
+        from the oracle's value rounded to bf16 relative to that value: at most one bf16 step
+        (2^-7 relative) where the f32 value lies within rounding noise of a rounding boundary."""
+        import oracle
+        torch, fa = self.torch, self.fa
+        idx = np.arange(0, self.n, 32)
+        qkv = self.qkv.cpu().numpy()[idx]
+        angles = self.angles.cpu().numpy()[idx]
+        want = oracle.qk_prologue(len(idx), self.heads, self.d, fa.NORM_ROW, fa.ROPE_INTERLEAVED,
+                                  len(idx), angles, self.q_norm.cpu().numpy(),
+                                  self.k_norm.cpu().numpy(), 1e-6, qkv)
+        got = self.out.float().cpu().numpy()[idx]
+        rel = np.abs(got - round_bf16(torch, want)) / np.maximum(np.abs(want), 1e-30)
+        worst = float(rel.max())
+        return {"max_rel_to_bf16": sci(worst), "tol": 2.0 ** -7, "ok": bool(worst <= 2.0 ** -7),
+                "checked": f"{len(idx)} of {self.n} tokens, queries, keys and values"}
 
     def algorithmic(self):
         return float(self.bytes)
@@ -406,6 +523,21 @@ class C2Prefill(Workload):
         self.d_angles.copy_(self.h_angles, non_blocking=True)
         self.cache.attention(0, self.span, self.d_qkv, self.out, self.d_angles, self.fa.ROPE_HALF)
         self.h_out.copy_(self.out, non_blocking=True)
+
+    def parity(self, threads):
+        """All 512 rows: the oracle's RoPE + keep of the span into an empty cache, then its
+        causal attend, against the timed output."""
+        import oracle
+        fa = self.fa
+        oc = oracle.Cache(1, 14, 2, 64, 512)
+        q = self.qkv.cpu().numpy().copy()
+        oc.attention_input(0, 512, 0, fa.ROPE_HALF, self.angles.cpu().numpy(), q, q.shape[1])
+        want = oc.attend(0, 512, 0, oracle.Mask.causal(), q, q.shape[1], threads=threads)
+        out = self.out.cpu().numpy()
+        p = parity_result(out, want, TOL_F32, "all 512 rows, every head")
+        if self.e2e_ran:
+            p["e2e_vs_device_max_abs"] = sci(np.abs(self.h_out.numpy() - out).max())
+        return p
 
     def algorithmic(self):
         return self.flops
@@ -468,6 +600,27 @@ class LongPrefill(Workload):
         self.phases()[1]()
         self.h_out.copy_(self.out, non_blocking=True)
 
+    def parity(self, threads):
+        """Sampled rows (the first and last 16, and 32 spread between) against the oracle: its
+        RoPE + keep of all 8192 rows into a host cache (the kept rows rounded to bf16, as this
+        cache holds them), then its causal attend of each sampled row. A bf16-compute path: the
+        queries and probabilities are bf16 on the tensor cores."""
+        import oracle
+        torch, fa = self.torch, self.fa
+        rows, heads, kv, d = 8192, 32, 8, 128
+        oc = oracle.Cache(1, heads, kv, d, rows)
+        q = self.qkv.cpu().numpy().copy()
+        oc.attention_input(0, rows, 0, fa.ROPE_HALF, self.angles.cpu().numpy(), q, q.shape[1])
+        oc.keys[:] = round_bf16(torch, oc.keys)
+        oc.values[:] = round_bf16(torch, oc.values)
+        sample = sorted(set(range(16)) | set(range(rows - 16, rows)) |
+                        set(np.linspace(16, rows - 17, 32).astype(int).tolist()))
+        out = self.out.cpu().numpy()
+        want = np.concatenate([oc.attend(0, 1, r, oracle.Mask.causal(), q[r:r + 1], q.shape[1],
+                                         threads=threads) for r in sample])
+        return parity_result(out[sample], want, TOL_BF16,
+                             f"{len(sample)} of {rows} rows, every head")
+
     def algorithmic(self):
         return self.flops
 
@@ -485,15 +638,13 @@ class C4Sharded(Workload):
         heads, kv, d, position = 16, 8, 128, 131072
         lo, hi = kv_shards(position + 1, world)[rank]
         shape = fa.Shape(1, heads, kv, d)
+        self.shape, self.position, self.rank = shape, position, rank
         self.cache = fa.KvCache(shape, hi - lo)
-        gen = torch.Generator("cuda").manual_seed(40 + rank)
+        # the 1-GPU decode's inputs (one seeded stream), this rank's range of positions kept
+        k, v, self.qkv = decode_inputs(torch, shape, position)
         filled = min(hi, position) - lo  # the new row's slot is kept by the step
-        k = torch.randn((1, kv, filled, d), device="cuda", generator=gen)
-        v = torch.randn((1, kv, filled, d), device="cuda", generator=gen)
-        self.cache.put_rows(k, v)
+        self.cache.put_rows(k[:, :, lo:lo + filled].contiguous(), v[:, :, lo:lo + filled].contiguous())
         del k, v
-        gen0 = torch.Generator("cuda").manual_seed(7)
-        self.qkv = torch.randn((1, shape.qkv), device="cuda", generator=gen0)
         self.angles = torch.from_numpy(fa.rotary_angles(fa.Rotation(base=1e6), d, [position])).cuda()
         self.decode = ShardedDecode(self.cache, heads, d, lo, hi, position, world,
                                     exchange="peer")
@@ -535,6 +686,62 @@ class C4Sharded(Workload):
         self.angles.copy_(self.h_angles, non_blocking=True)
         out = self.decode.step(self.qkv, self.angles, self.fa.ROPE_HALF, self.dist)
         self.h_out.copy_(out, non_blocking=True)
+
+    def phases_us(self, steps):
+        """The step's three phases timed apart (each captured as its own CUDA graph and replayed
+        `steps` times back to back between two events; the max over ranks, in microseconds): the
+        query's RoPE (+ the keep on the owner), the local range's attention, and the exchange of
+        the partials with the merge (which includes any wait for a slower rank)."""
+        torch, fa, dist = self.torch, self.fa, self.dist
+        calls = (("rotate_keep", lambda: self.decode.rotate(self.qkv, self.angles, fa.ROPE_HALF)),
+                 ("attend_local", self.decode.attend_local),
+                 ("exchange_merge", lambda: self.decode.gather_merge(dist)))
+        out = {}
+        for name, call in calls:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, capture_error_mode="relaxed"):
+                call()
+            g.replay()
+            torch.cuda.synchronize()
+            dist.barrier()
+            start = torch.cuda.Event(enable_timing=True)
+            end = torch.cuda.Event(enable_timing=True)
+            start.record()
+            for _ in range(steps):
+                g.replay()
+            end.record()
+            torch.cuda.synchronize()
+            t = torch.tensor([start.elapsed_time(end) * 1e3 / steps], device="cuda",
+                             dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            out[name] = round(float(t[0]), 2)
+            del g  # a graph holding the exchange goes before the peer buffers
+        self.decode.recover(dist)
+        return out
+
+    def parity(self, threads):
+        """The merged output of the timed steps: rank 0 against the oracle's decode of the whole
+        131073-key context (the seeded inputs made again on its device), and every rank's merged
+        output against rank 0's (they merge the same partials in the same order: equal bits)."""
+        torch, dist = self.torch, self.dist
+        out = self.decode.out.reshape(1, -1).clone()
+        first = out.clone()
+        dist.broadcast(first, 0)
+        same = bool(torch.equal(out, first))
+        p = {"checked": "the merged decode row on rank 0, every head; every rank's merged row "
+                        "against rank 0's"}
+        if self.rank == 0:
+            k, v, _ = decode_inputs(torch, self.shape, self.position)
+            want = oracle_decode(self.fa, self.shape, self.position, k.cpu().numpy(),
+                                 v.cpu().numpy(), self.qkv.cpu().numpy(),
+                                 self.angles.cpu().numpy(), threads)
+            del k, v
+            p.update(parity_result(out.cpu().numpy(), want, TOL_F32, p["checked"]))
+        p["ranks_agree"] = same
+        if self.e2e_ran:
+            p["e2e_vs_device_max_abs"] = sci(np.abs(self.h_out.numpy().reshape(1, -1)
+                                                    - out.cpu().numpy()).max())
+        return p
 
     def algorithmic(self):
         return float(self.bytes)
@@ -586,6 +793,44 @@ class C5Full(Workload):
         self.qkv.copy_(self.h_qkv, non_blocking=True)
         self.step()
         self.h_out[self.lo:self.hi].copy_(self.out[self.lo:self.hi], non_blocking=True)
+
+    def sample_rows(self):
+        """This rank's checked query rows: its first and last 32 and 64 spread between (every
+        head of each), so that whole units, the last wave's split units and the ragged last
+        query tile are all sampled."""
+        lo, hi = self.lo, self.hi
+        if hi <= lo:
+            return []
+        spread = np.linspace(lo, hi - 1, 64).astype(int).tolist()
+        return sorted(set(range(lo, min(lo + 32, hi))) | set(range(max(hi - 32, lo), hi)) | set(spread))
+
+    def parity(self, threads):
+        """Sampled query rows of this rank's share of the timed call (bf16 output) against the
+        oracle's f32 full-mask attention over the same bf16 queries, keys and values (every one of
+        the 32760 keys)."""
+        import oracle
+        rows = self.sample_rows()
+        if not rows:
+            return {"checked": "no rows on this rank", "ok": True}
+        qkv = self.qkv.float().cpu().numpy()
+        hidden = self.heads * self.d
+        want = np.zeros((self.n, hidden), np.float32)
+        runs, start = [], rows[0]
+        for a, b in zip(rows, rows[1:] + [None]):
+            if b != a + 1:
+                runs.append((start, a + 1))
+                start = b
+        for qb, qe in runs:
+            oracle.attend_call(self.heads, self.heads, self.d, 1, self.n, self.n, qkv, self.stride,
+                               0, qkv, self.stride, hidden, qkv, self.stride, 2 * hidden,
+                               query_range=(qb, qe), threads=threads, out=want)
+        got = self.out.float().cpu().numpy()[rows]
+        p = parity_result(got, want[rows], TOL_BF16,
+                          f"{len(rows)} of this rank's {self.hi - self.lo} query rows, every head")
+        if self.e2e_ran:
+            p["e2e_vs_device_max_abs"] = sci(np.abs(self.h_out[self.lo:self.hi].float().numpy()
+                                                    - self.out[self.lo:self.hi].float().cpu().numpy()).max())
+        return p
 
     def algorithmic(self):
         return self.flops
@@ -657,6 +902,7 @@ def time_e2e(torch, dist, w: Workload, steps: int, warmup: int):
     memory, the attention, D2H of the output, synchronized. Returns the mean over the steps
     (the reported value) and the median step, each the max over ranks. The warm-up is at least
     20 steps: the first host-memory calls of a process page in and grow their staging."""
+    w.e2e_ran = True
     for _ in range(max(warmup, 20)):
         w.e2e_step()
     torch.cuda.synchronize()
@@ -683,6 +929,55 @@ class _null:
 
     def __exit__(self, *a):
         return False
+
+
+# ---------------------------------------------------------------------------------------------
+# parity of the timed outputs: the oracle (oracle/, test infrastructure) is the checker here,
+# run after the timed region on the host; it is never what is timed
+# ---------------------------------------------------------------------------------------------
+
+def sci(x) -> float | str:
+    """A JSON-safe figure with 3 significant digits ("non-finite" for NaN or infinity)."""
+    x = float(x)
+    return float(f"{x:.3e}") if np.isfinite(x) else "non-finite"
+
+
+def round_bf16(torch, a):
+    """f32 values rounded to the nearest bf16 (ties to even), as f32: ops::round_bf16."""
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(torch.bfloat16).float().numpy()
+
+
+def parity_result(got, want, tol, checked):
+    """harness::parity's figures (max abs, relative L2) of `got` against the oracle's `want`."""
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    if got.size == 0:
+        return {"max_abs": 0.0, "rel_l2": 0.0, "tol": tol, "ok": True, "checked": checked}
+    diff = got - want
+    err = float(np.abs(diff).max())
+    rel = float(np.sqrt((diff ** 2).sum() / max((want ** 2).sum(), 1e-300)))
+    return {"max_abs": sci(err), "rel_l2": sci(rel), "tol": tol,
+            "ok": bool(np.isfinite(err) and err <= tol), "checked": checked}
+
+
+def merge_parity(dist, p):
+    """Every rank's parity of its share, gathered to one figure: the worst max abs and relative
+    L2, the ranks' checked counts side by side, ok only if every rank's is."""
+    if dist is None or p is None:
+        return p
+    parts = [None] * dist.get_world_size()
+    dist.all_gather_object(parts, p)
+    merged = {"ok": all(bool(q.get("ok", False)) for q in parts),
+              "per_rank_checked": [q.get("checked") for q in parts]}
+    for key in ("max_abs", "rel_l2", "max_rel_to_bf16", "e2e_vs_device_max_abs"):
+        vals = [q[key] for q in parts if key in q]
+        if vals:
+            merged[key] = "non-finite" if any(isinstance(v, str) for v in vals) else max(vals)
+    for key in ("tol", "ranks_agree"):
+        vals = [q[key] for q in parts if key in q]
+        if vals:
+            merged[key] = vals[0] if key == "tol" else all(vals)
+    return merged
 
 
 def roofline(w: Workload, kern_ms: float, peaks):
@@ -817,6 +1112,44 @@ def host_threads():
         return os.cpu_count() or 1
 
 
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def harness_pool(cores: int) -> int:
+    """harness::threads' default pool (crates/harness/src/lib.rs:35-43): min(8, cores - 2), at
+    least 1 -- the thread team the reference's own benches run on."""
+    return max(1, min(8, cores - 2))
+
+
+def cpu_baseline_both():
+    """C3's CPU baseline timed twice: at the reference harness's own pool size and at every host
+    thread the team can use (its head split caps it at the 32 query heads); `value` is the
+    latter, as the reference arm runs. The host is named, since the figure moves with it."""
+    cores = host_threads()
+    pool = harness_pool(cores)
+    everything = min(cores, C3_HEADS)
+    v_pool, meta = cpu_baseline_c3(pool)
+    v_all, meta_all = cpu_baseline_c3(everything) if everything != pool else (v_pool, meta)
+    return {"value": round(v_all, 3), "unit": "tokens/s", "cores": everything, "kind": "port",
+            "sample": meta_all["sample"], "cpu_model": cpu_model(), "nproc": cores,
+            "harness_pool": {"value": round(v_pool, 3), "cores": pool,
+                             "rule": "min(8, cores - 2), harness::threads"}}
+
+
+def summary_entry(ms, roof, parity):
+    err = None
+    if parity is not None:
+        err = parity.get("max_abs", parity.get("max_rel_to_bf16"))
+    return [round(ms, 4), roof["frac"], err]
+
+
 def run_ours(args):
     import torch
     import torch.distributed as distmod
@@ -859,11 +1192,20 @@ def run_ours(args):
             return LongPrefill(torch, fa)
         raise SystemExit(f"unknown config {name}")
 
+    # the oracle's threads for the parity checks: the host's, shared by the ranks
+    check_threads = max(1, min(host_threads() // world, C3_HEADS))
+
+    def check(x):
+        if args.no_parity:
+            return None
+        return merge_parity(dist, x.parity(check_threads))
+
     w = build(args.config)
     sampler = ClockSampler(torch, local)
     ms, kern_ms = time_workload(torch, dist, w, steps, warmup, sampler)
     fa.device_status()
     e2e_ms, e2e_median_ms = time_e2e(torch, dist, w, min(steps, 200), warmup)
+    parity = check(w)
     job_tokens = w.tokens if w.sharded else w.tokens * world
     value = job_tokens / (ms * 1e-3)
     line = {
@@ -885,6 +1227,9 @@ def run_ours(args):
         "gpu_launches": w.launches_per_step * steps,
         "clocks": sampler.report(),
     }
+    if parity is not None:
+        line["parity"] = parity
+    summary = {args.config: summary_entry(ms, line["roofline"], parity)}
     w.close()
     del w
     torch.cuda.empty_cache()
@@ -906,22 +1251,29 @@ def run_ours(args):
                 entry["launch"] = "each call of the step replayed as a captured CUDA graph"
             if name == "c5":
                 entry["tflops"] = round(6.594e12 / (ms_x * 1e-3) / 1e12, 2)
+            if hasattr(x, "phases_us"):
+                entry["phases_us"] = x.phases_us(xs)
+            px = check(x)
+            if px is not None:
+                entry["parity"] = px
             extras[name] = entry
+            summary[name] = summary_entry(ms_x, entry["roofline"], px)
             x.close()  # graphs holding collectives and peer buffers go before the group
             del x
             torch.cuda.empty_cache()
         line["configs"] = extras
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config.startswith("c3") \
             and args.sequences == C3_SEQS:
-        threads = min(host_threads(), C3_HEADS)
-        v, meta = cpu_baseline_c3(threads)
-        line["cpu_baseline"] = {"value": round(v, 3), "unit": "tokens/s", "cores": threads,
-                                "kind": "port", **meta}
+        line["cpu_baseline"] = cpu_baseline_both()
         if args.cpu_baselines and "configs" in line:
+            threads = min(host_threads(), C3_HEADS)
             for name, base in cpu_baselines_other(threads).items():
                 if name in line["configs"]:
                     line["configs"][name]["cpu_baseline"] = base
     fa.device_status()
+    # last, so that a reader of the line's tail sees every config: [ms per step, roofline
+    # fraction, parity (max abs error against the oracle, or the prologue's relative bf16 step)]
+    line["summary"] = summary
     if rank == 0:
         print(json.dumps(line), flush=True)
     if dist is not None:
@@ -1011,14 +1363,19 @@ def run_reference(args):
     value = len(sample) / (ms * 1e-3)
     sample_desc = (f"each step {len(sample)} of the 64 C3 sequences (every 8th by length), one "
                    f"forward call each, heads split over {threads} threads")
+    config = config_of("c3", 1)
+    config.pop("launch", None)
+    config["parallelism"] = f"the host's thread team ({threads} threads), no GPU"
+
     print(json.dumps({
         "impl": "reference", "metric": "c3 attention tokens/s (decode attn HBM GB/s & prefill TFLOP/s as roofline)",
         "value": round(value, 3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1)",
-        "config": config_of("c3", 1),
+        "config": config,
         "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads,
-                         "kind": "port", "sample": sample_desc},
+                         "kind": "port", "sample": sample_desc, "cpu_model": cpu_model(),
+                         "nproc": host_threads()},
         "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
         "note": "fusor-ai is Rust and no Rust toolchain exists here: the oracle's C++ restatement "
@@ -1038,6 +1395,8 @@ def main():
                     help="C3 sequences (a smaller batch for profiling captures)")
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the oracle's check of the timed outputs (profiling runs)")
     ap.add_argument("--cpu-baselines", action="store_true",
                     help="also time the host restatement for C1, C2, C4 and a C5 slice (1 GPU)")
     args = ap.parse_args()

@@ -1633,6 +1633,9 @@ int fa_attention_batch_host(fa_kvcache* const* caches, const fa_span* spans, int
                                     rope != FA_ROPE_NONE ? angles_dev + size_t(b0) * d : nullptr,
                                     norm, qkv_dev + size_t(b0) * units, units,
                                     out_dev + b0 * out_dev_stride, out_dev_stride, stream)) {
+      // earlier groups' kernels may still be storing into the caller's (mapped) output, and
+      // their copies may be in flight: both end before the call returns its error
+      cudaStreamSynchronize(s);
       cudaStreamSynchronize(cs);
       return rc;
     }
@@ -1770,6 +1773,15 @@ int fa_peer_close(void* ptr) {
 int fa_peer_free(void* ptr) {
   if (ptr == nullptr) return FA_OK;
   FA_CUDA(cudaFree(ptr), "cudaFree(peer buffer)");
+  return FA_OK;
+}
+
+int fa_peer_reset(void* own_buffer, void* stream) {
+  if (own_buffer == nullptr) return fail(FA_ERR_ARG, "null buffer");
+  FA_PTR(own_buffer, current_device());
+  auto s = static_cast<cudaStream_t>(stream);
+  FA_CUDA(cudaMemsetAsync(own_buffer, 0, fa::kPeerHeaderBytes, s), "clear exchange header");
+  FA_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
   return FA_OK;
 }
 
@@ -2207,10 +2219,15 @@ static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBy
 
 // The array's device address, per device; in host code g_static_scratch names a host-side
 // stand-in, not device memory, so it is looked up once per device with that device current.
-unsigned char* g_static_scratch_addr[64];
+constexpr int kStaticScratchDevices = 64;
+unsigned char* g_static_scratch_addr[kStaticScratchDevices];
 std::mutex g_static_scratch_mutex;
 
+// Called with `device` current (the caller's DeviceGuard).
 int static_scratch_address(int device, unsigned char** out) {
+  if (device < 0 || device >= kStaticScratchDevices)
+    return fail(FA_ERR_ARG, "device %d: fa_attend_static serves devices 0..%d", device,
+                kStaticScratchDevices - 1);
   std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
   if (g_static_scratch_addr[device] == nullptr) {
     void* p = nullptr;

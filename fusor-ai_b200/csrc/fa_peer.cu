@@ -3,8 +3,12 @@
 // (max, sum, o) partials straight into every rank's gather buffer (CUDA IPC mappings: P2P stores
 // over NVLink / NVSwitch), raises its flag in each (a system-scope release after a system
 // fence), waits until every rank's flag in its own buffer carries this step's sequence number
-// (a system-scope acquire, bounded: after about a second it records kErrTimeout and merges what
-// it has), and merges the ranks' partials in rank order with the merge kernel's arithmetic.
+// (a system-scope acquire, bounded: after about a second it records kErrTimeout), and merges the
+// partials of the ranks whose flag carries it, in rank order, with the merge kernel's
+// arithmetic. A rank whose flag never came is left out of the merge (its slot holds partials of
+// an earlier step): the output is then incomplete and the error word says so. The ranks' step
+// counters have diverged by then, so every later step would wait in vain: the host resets every
+// rank's header together (fa_peer_reset on each rank between two barriers) before the next.
 //
 // Buffer of each rank (fa_peer_buffer_bytes): a 256-byte header (the step counter at 0, the
 // flags [2][kMaxPeers] at 128), then the partials [2][world][heads][head_dim + 2] f32. Steps
@@ -35,12 +39,14 @@ constexpr int kPeerThreads = 256;
 
 __global__ void __launch_bounds__(kPeerThreads) peer_merge_kernel(const PeerMergeArgs a) {
   __shared__ unsigned s_seq;
+  __shared__ unsigned s_missing;  // ranks whose flag did not arrive in time (bit per rank)
   const int pitch = a.heads * (a.head_dim + 2);  // floats of one rank's partials
   unsigned char* mine = a.bufs[a.rank];
   if (threadIdx.x == 0) {
     unsigned* counter = reinterpret_cast<unsigned*>(mine);
     s_seq = *counter + 1;  // this rank's kernels of this exchange run one at a time (one stream)
     *counter = s_seq;
+    s_missing = 0u;
   }
   __syncthreads();
   const unsigned seq = s_seq;
@@ -67,6 +73,7 @@ __global__ void __launch_bounds__(kPeerThreads) peer_merge_kernel(const PeerMerg
       while (load_acquire_sys(flag) != seq) {
         if (clock64() - start > kWaitCycles) {
           atomicOr(a.err, kErrTimeout);
+          atomicOr(&s_missing, 1u << threadIdx.x);
           break;
         }
       }
@@ -79,12 +86,15 @@ __global__ void __launch_bounds__(kPeerThreads) peer_merge_kernel(const PeerMerg
   const float* data = reinterpret_cast<const float*>(mine + kPeerHeaderBytes) +
                       int64_t(half) * a.world * pitch;
   const int d = a.head_dim;
+  const unsigned missing = s_missing;
   for (int idx = threadIdx.x; idx < a.heads * d; idx += kPeerThreads) {
     const int h = idx / d, e = idx % d;
     float mm = -INFINITY;
-    for (int s = 0; s < a.world; ++s) mm = fmaxf(mm, __ldcg(data + int64_t(s) * pitch + h * (d + 2)));
+    for (int s = 0; s < a.world; ++s)
+      if (!(missing >> s & 1u)) mm = fmaxf(mm, __ldcg(data + int64_t(s) * pitch + h * (d + 2)));
     float ll = 0.0f, oo = 0.0f;
     for (int s = 0; s < a.world; ++s) {
+      if (missing >> s & 1u) continue;
       const float* p = data + int64_t(s) * pitch + h * (d + 2);
       const float m = __ldcg(p);
       const float f = m == -INFINITY ? 0.0f : exp2f(m - mm);

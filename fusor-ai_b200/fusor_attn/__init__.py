@@ -134,6 +134,7 @@ SIGNATURES = {
     "fa_peer_close": (C.c_int, [_P]),
     "fa_peer_free": (C.c_int, [_P]),
     "fa_exchange_merge": (C.c_int, [_P, C.c_uint64, _I32, _I32, _I32, _I32, _P, _P, _P]),
+    "fa_peer_reset": (C.c_int, [_P, _P]),
     "fa_attention_input_projected": (C.c_int, [_P, _I32, _P, _I32, _P, _P, _P, _P, _I64, _P, _P,
                                                _I64, _P]),
     "fa_attention_input_projected_batch": (C.c_int, [_P, _P, _I32, _I32, _I32, _P, _P, _P, _P,
@@ -590,6 +591,30 @@ class PeerExchange:
         _check(lib().fa_exchange_merge(self.buffers, self.bytes, self.rank, self.world,
                                        self.heads, self.head_dim, _dptr(partials), _dptr(out),
                                        _stream(stream)))
+
+    def recover(self, group=None):
+        """Checks the exchanges so far on every rank and, if any rank's gave up waiting (its
+        output was incomplete: FA_ERR_TIMEOUT), brings the ranks' step counters back in line:
+        every rank clears its own buffer's header between two barriers. Collective: every rank
+        of the group calls it at the same point. Returns whether any rank had timed out."""
+        import torch
+        import torch.distributed as dist
+        timed_out = 0
+        try:
+            device_status()
+        except FaError as e:
+            if e.code != ERR_TIMEOUT:
+                raise
+            timed_out = 1
+        device = "cuda" if dist.get_backend(group) == "nccl" else "cpu"
+        flag = torch.tensor([timed_out], device=device, dtype=torch.int32)
+        dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=group)
+        if int(flag.item()) == 0:
+            return False
+        dist.barrier(group=group)
+        _check(lib().fa_peer_reset(self.own, _stream()))
+        dist.barrier(group=group)
+        return True
 
     def close(self):
         """Unmaps the other ranks' buffers and frees this one's (after every rank's last merge:

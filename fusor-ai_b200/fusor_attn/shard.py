@@ -119,6 +119,17 @@ class ShardedDecode:
         self.exchange = "nccl"
         return None
 
+    def recover(self, dist=None):
+        """After a run of steps, on every rank at the same point: whether any rank's peer
+        exchange gave up waiting for another (its merged output was then incomplete), the
+        exchange made ready again if so (every rank's step counter and flags cleared together).
+        With the NCCL exchange a rank that fails raises from the collective itself."""
+        if self.peers is None or dist is None:
+            import fusor_attn as fa
+            fa.device_status()
+            return False
+        return self.peers.recover(self.group)
+
     def close(self, dist=None):
         """Releases the peer buffers (every rank, after its last step)."""
         if self.peers is not None:

@@ -308,6 +308,12 @@ int fa_peer_free(void* ptr);  /* a buffer made by fa_peer_alloc */
 int fa_exchange_merge(void* const* buffers, uint64_t buffer_bytes, int32_t rank, int32_t world,
                       int32_t heads, int32_t head_dim, const float* partials, float* out,
                       void* stream);
+/* After an exchange that gave up on a rank (FA_ERR_TIMEOUT), the ranks' step counters differ and
+ * every later exchange would wait in vain: each rank synchronizes its device, the ranks meet at a
+ * barrier, each clears its own buffer's step counter and flags with fa_peer_reset (which returns
+ * once they are clear), and they meet at a second barrier before the next exchange. There is no
+ * counterpart in the reference (one process, no exchange); it is this exchange's recovery. */
+int fa_peer_reset(void* own_buffer, void* stream);
 
 /* blocks::attention::attend (attention.rs:79-95) and dit::Within::attend (dit.rs:135-166): full
  * (non-causal) softmax attention of every query over every key of its image, scores scaled by

@@ -13,7 +13,7 @@ the fusor-ai sources are mounted; the fixtures travel, this script's input does 
    222-278), with inputs from the tests' LCG (support/mod.rs:33-44, seed 2) and the output of the
    tests' f64 reference attention (support/mod.rs:471-512), restated here in numpy.
 
-Usage: python tests/golden/make_golden.py [/path/to/fusor-ai]
+Usage: python tests/golden/make_golden.py <root of the fusor-ai source tree>
 """
 from __future__ import annotations
 
@@ -205,7 +205,9 @@ def decoder_attention() -> dict:
 
 
 def main():
-    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: make_golden.py <root of the fusor-ai source tree>")
+    root = sys.argv[1]
     kats = {
         "rotary": rotary_kats(root),
         "round_bf16": bf16_kats(root),

@@ -11,8 +11,9 @@ import oracle
 # Parity bar on the attention output with f32 I/O.
 TOL_F32 = 2e-3
 # bf16-compute paths (bf16 queries and probabilities on the tensor cores) are reported
-# separately; their bar here is about five bf16 rounding steps of an output of magnitude 1.
-TOL_BF16 = 2e-2
+# separately; their bar is a little above the 2-4e-3 worst cases seen on these tests (a bf16
+# rounding step of an output of magnitude 1 is 4e-3), so that a regression shows.
+TOL_BF16 = 5e-3
 
 
 def relative_l2(ours, reference) -> float:

@@ -178,11 +178,11 @@ def _strip_c_comments(text):
 
 
 def _rust_ffi_block():
-    text = open(os.path.join(ROOT, "INTEGRATION.md")).read()
-    blocks = re.findall(r"```rust\n(.*?)```", text, re.S)
-    ffi = [b for b in blocks if 'extern "C"' in b]
-    assert len(ffi) == 1
-    return ffi[0]
+    """The Rust binding's source (rust/fusor-cuda-attn/src/ffi.rs): its structs and its one
+    extern block."""
+    text = open(os.path.join(ROOT, "rust", "fusor-cuda-attn", "src", "ffi.rs")).read()
+    assert text.count('extern "C"') == 1
+    return text
 
 
 def test_rust_binding_declares_every_entry_point_with_its_arity():
