@@ -34,9 +34,10 @@ import numpy as np  # noqa: E402
 
 C3_SEQS, C3_HEADS, C3_KV, C3_D = 64, 32, 8, 128
 L2_BYTES = 126 * 1024 * 1024
-# Parity bars (the tests' own): max abs error on the attention output with f32 I/O, and on the
-# bf16-compute paths (bf16 queries and probabilities on the tensor cores).
-TOL_F32, TOL_BF16 = 2e-3, 5e-3
+# Parity bars (the tests' own): max abs error on the attention output with f32 I/O; the
+# bf16-compute paths (bf16 queries and probabilities on the tensor cores) are held to a max abs
+# error and a relative L2 error.
+TOL_F32, TOL_BF16, REL_BF16 = 2e-3, 1e-2, 5e-3
 
 
 def c3_lengths():
@@ -269,7 +270,8 @@ class C3Decode(Workload):
             wants.append(oc.attend(0, 1, n, oracle.Mask.causal(), q, q.shape[1], threads=threads))
         want = np.concatenate(wants) if wants else np.zeros_like(out)
         p = parity_result(out, want, TOL_BF16 if bf16 else TOL_F32,
-                          f"{len(self.lengths)} sequences, every head")
+                          f"{len(self.lengths)} sequences, every head",
+                          REL_BF16 if bf16 else None)
         if self.e2e_ran and out.size:
             p["e2e_vs_device_max_abs"] = sci(np.abs(self.h_out.numpy() - out).max())
         return p
@@ -463,9 +465,11 @@ class DitPrologue(Workload):
         self.h_out.copy_(self.out, non_blocking=True)
 
     def parity(self, threads):
-        """Every 32nd token (1024 of them) against the oracle's prologue (f32), as the distance
-        from the oracle's value rounded to bf16 relative to that value: at most one bf16 step
-        (2^-7 relative) where the f32 value lies within rounding noise of a rounding boundary."""
+        """Every 32nd token (1024 of them) against the oracle's prologue (f32): each bf16 output
+        within half a bf16 step of the oracle's f32 value (2^-8 of its magnitude: the output's
+        own rounding) plus 1e-5 (the f32 arithmetic's difference, which decides the rounding of
+        a value near a rounding boundary, and dominates for values near zero). `worst` is the
+        largest ratio of an error to that bound."""
         import oracle
         torch, fa = self.torch, self.fa
         idx = np.arange(0, self.n, 32)
@@ -475,9 +479,10 @@ class DitPrologue(Workload):
                                   len(idx), angles, self.q_norm.cpu().numpy(),
                                   self.k_norm.cpu().numpy(), 1e-6, qkv)
         got = self.out.float().cpu().numpy()[idx]
-        rel = np.abs(got - round_bf16(torch, want)) / np.maximum(np.abs(want), 1e-30)
-        worst = float(rel.max())
-        return {"max_rel_to_bf16": sci(worst), "tol": 2.0 ** -7, "ok": bool(worst <= 2.0 ** -7),
+        err = np.abs(got.astype(np.float64) - want)
+        worst = float((err / (np.abs(want) * 2.0 ** -8 + 1e-5)).max())
+        return {"max_abs": sci(err.max()), "worst": sci(worst), "tol": 1.0,
+                "ok": bool(np.isfinite(worst) and worst <= 1.0),
                 "checked": f"{len(idx)} of {self.n} tokens, queries, keys and values"}
 
     def algorithmic(self):
@@ -619,7 +624,7 @@ class LongPrefill(Workload):
         want = np.concatenate([oc.attend(0, 1, r, oracle.Mask.causal(), q[r:r + 1], q.shape[1],
                                          threads=threads) for r in sample])
         return parity_result(out[sample], want, TOL_BF16,
-                             f"{len(sample)} of {rows} rows, every head")
+                             f"{len(sample)} of {rows} rows, every head", REL_BF16)
 
     def algorithmic(self):
         return self.flops
@@ -826,7 +831,8 @@ class C5Full(Workload):
                                query_range=(qb, qe), threads=threads, out=want)
         got = self.out.float().cpu().numpy()[rows]
         p = parity_result(got, want[rows], TOL_BF16,
-                          f"{len(rows)} of this rank's {self.hi - self.lo} query rows, every head")
+                          f"{len(rows)} of this rank's {self.hi - self.lo} query rows, every head",
+                          REL_BF16)
         if self.e2e_ran:
             p["e2e_vs_device_max_abs"] = sci(np.abs(self.h_out[self.lo:self.hi].float().numpy()
                                                     - self.out[self.lo:self.hi].float().cpu().numpy()).max())
@@ -947,8 +953,9 @@ def round_bf16(torch, a):
     return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(torch.bfloat16).float().numpy()
 
 
-def parity_result(got, want, tol, checked):
-    """harness::parity's figures (max abs, relative L2) of `got` against the oracle's `want`."""
+def parity_result(got, want, tol, checked, rel_tol=None):
+    """harness::parity's figures (max abs, relative L2) of `got` against the oracle's `want`,
+    within the max abs bar `tol` (and the relative L2 bar `rel_tol` of a bf16-compute path)."""
     got = np.asarray(got, np.float64)
     want = np.asarray(want, np.float64)
     if got.size == 0:
@@ -956,8 +963,11 @@ def parity_result(got, want, tol, checked):
     diff = got - want
     err = float(np.abs(diff).max())
     rel = float(np.sqrt((diff ** 2).sum() / max((want ** 2).sum(), 1e-300)))
-    return {"max_abs": sci(err), "rel_l2": sci(rel), "tol": tol,
-            "ok": bool(np.isfinite(err) and err <= tol), "checked": checked}
+    ok = bool(np.isfinite(err) and err <= tol and (rel_tol is None or rel <= rel_tol))
+    out = {"max_abs": sci(err), "rel_l2": sci(rel), "tol": tol, "ok": ok, "checked": checked}
+    if rel_tol is not None:
+        out["rel_tol"] = rel_tol
+    return out
 
 
 def merge_parity(dist, p):
@@ -969,11 +979,11 @@ def merge_parity(dist, p):
     dist.all_gather_object(parts, p)
     merged = {"ok": all(bool(q.get("ok", False)) for q in parts),
               "per_rank_checked": [q.get("checked") for q in parts]}
-    for key in ("max_abs", "rel_l2", "max_rel_to_bf16", "e2e_vs_device_max_abs"):
+    for key in ("max_abs", "rel_l2", "worst", "e2e_vs_device_max_abs"):
         vals = [q[key] for q in parts if key in q]
         if vals:
             merged[key] = "non-finite" if any(isinstance(v, str) for v in vals) else max(vals)
-    for key in ("tol", "ranks_agree"):
+    for key in ("tol", "rel_tol", "ranks_agree"):
         vals = [q[key] for q in parts if key in q]
         if vals:
             merged[key] = vals[0] if key == "tol" else all(vals)
@@ -1146,7 +1156,7 @@ def cpu_baseline_both():
 def summary_entry(ms, roof, parity):
     err = None
     if parity is not None:
-        err = parity.get("max_abs", parity.get("max_rel_to_bf16"))
+        err = parity.get("max_abs")
     return [round(ms, 4), roof["frac"], err]
 
 
@@ -1272,7 +1282,7 @@ def run_ours(args):
                     line["configs"][name]["cpu_baseline"] = base
     fa.device_status()
     # last, so that a reader of the line's tail sees every config: [ms per step, roofline
-    # fraction, parity (max abs error against the oracle, or the prologue's relative bf16 step)]
+    # fraction, parity (max abs error against the oracle)]
     line["summary"] = summary
     if rank == 0:
         print(json.dumps(line), flush=True)

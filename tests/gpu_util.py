@@ -11,9 +11,19 @@ import oracle
 # Parity bar on the attention output with f32 I/O.
 TOL_F32 = 2e-3
 # bf16-compute paths (bf16 queries and probabilities on the tensor cores) are reported
-# separately; their bar is a little above the 2-4e-3 worst cases seen on these tests (a bf16
-# rounding step of an output of magnitude 1 is 4e-3), so that a regression shows.
-TOL_BF16 = 5e-3
+# separately and held to two bars: a max abs error a little above the worst seen on these tests
+# (7.3e-3: a query rounded to bf16 moves a score of magnitude 4 by about 8e-3 relative, and a
+# peaked softmax carries that into the output), and a relative L2 error twice the worst seen
+# (2.4e-3), which is what shows a regression: every bf16 path sits at 1.3-2.4e-3.
+TOL_BF16 = 1e-2
+REL_BF16 = 5e-3
+
+
+def parity_ok(ours, reference, bf16: bool) -> bool:
+    """Within the f32 bar, or within both bf16-compute bars."""
+    if bf16:
+        return max_abs(ours, reference) <= TOL_BF16 and relative_l2(ours, reference) <= REL_BF16
+    return max_abs(ours, reference) <= TOL_F32
 
 
 def relative_l2(ours, reference) -> float:

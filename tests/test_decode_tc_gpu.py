@@ -6,7 +6,7 @@ import numpy as np
 import pytest
 
 import fusor_attn as fa
-from gpu_util import TOL_BF16, Pair, compare, max_abs, normal
+from gpu_util import Pair, compare, max_abs, normal, parity_ok
 
 pytestmark = pytest.mark.gpu
 
@@ -39,7 +39,8 @@ def run_batch(torch, shape, positions, masks, capacity=None, seed=0):
         want = p.oracle_attention(0, span, qkv[i:i + 1], angles[i:i + 1], fa.ROPE_HALF, threads=4)
         err = max_abs(got[i:i + 1], want)
         worst = max(worst, err)
-        assert err <= TOL_BF16, compare(f"row {i} position {positions[i]}", got[i:i + 1], want)
+        assert parity_ok(got[i:i + 1], want, True), compare(f"row {i} position {positions[i]}",
+                                                             got[i:i + 1], want)
     return worst
 
 

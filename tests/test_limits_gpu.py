@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 
 import fusor_attn as fa
-from gpu_util import TOL_BF16, TOL_F32, compare, max_abs
+from gpu_util import compare, parity_ok
 
 pytestmark = pytest.mark.gpu
 
@@ -63,5 +63,5 @@ def test_decode_over_a_cache_past_two_billion_elements(torch, dtype):
     g, w = got.cpu().numpy(), want.cpu().numpy()
     print(compare(f"{CAPACITY}-row decode {'f32' if dtype == fa.F32 else 'bf16'}", g, w))
     rel = float(np.sqrt(((g - w) ** 2).sum() / (w ** 2).sum()))
-    assert max_abs(g, w) <= (TOL_F32 if dtype == fa.F32 else TOL_BF16)
+    assert parity_ok(g, w, dtype == fa.BF16)
     assert rel <= (1e-4 if dtype == fa.F32 else 2e-2)

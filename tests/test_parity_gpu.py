@@ -12,7 +12,8 @@ import pytest
 
 import fusor_attn as fa
 import oracle
-from gpu_util import TOL_BF16, TOL_F32, Pair, compare, max_abs, normal, relative_l2, round_bf16
+from gpu_util import (TOL_BF16, TOL_F32, Pair, compare, max_abs, normal, parity_ok, relative_l2,
+                      round_bf16)
 
 pytestmark = pytest.mark.gpu
 
@@ -153,8 +154,7 @@ def test_every_head_dim_and_storage(torch, dtype, head_dim):
     want = pair.oracle_attention(0, span, qkv, angles, fa.ROPE_HALF)
     got = out.cpu().numpy()
     # a bf16 cache of head_dim 128 decodes on the tensor cores (bf16 queries and probabilities)
-    tol = TOL_BF16 if dtype == fa.BF16 and head_dim == 128 else TOL_F32
-    assert max_abs(got, want) <= tol, compare(f"d{head_dim}", got, want)
+    assert parity_ok(got, want, dtype == fa.BF16 and head_dim == 128), compare(f"d{head_dim}", got, want)
 
 
 def test_window_ring_wraps_and_groups(torch):
@@ -270,8 +270,7 @@ def test_config3_batched_decode_sample(torch, dtype):
     for i, (p, span) in enumerate(zip(pairs, spans)):
         want = p.oracle_attention(0, span, qkv[i:i + 1], angles[i:i + 1], fa.ROPE_HALF)
         # a bf16 cache decodes on the tensor cores (bf16 queries and probabilities)
-        tol = TOL_F32 if dtype == fa.F32 else TOL_BF16
-        assert max_abs(got[i:i + 1], want) <= tol, compare(f"C3 seq {i}", got[i:i + 1], want)
+        assert parity_ok(got[i:i + 1], want, dtype == fa.BF16), compare(f"C3 seq {i}", got[i:i + 1], want)
 
 
 @pytest.mark.parametrize("batch,pinned,pad", [(40, True, 0), (5, False, 0), (5, True, 64),
@@ -402,7 +401,7 @@ def test_config5_full_mask_sample(torch, dtype):
                            qkv, stride, 2 * hidden, query_range=qr, threads=8, out=want)
     rows = np.r_[0:128, n - 128:n]
     print(compare(f"C5 sample {dtype}", got[rows], want[rows]))
-    assert max_abs(got[rows], want[rows]) <= (TOL_F32 if dtype == "f32" else TOL_BF16)
+    assert parity_ok(got[rows], want[rows], dtype == "bf16")
 
 
 def test_bf16_tensor_cores_beat_the_reference_int8_approximation(torch):
@@ -496,6 +495,7 @@ def test_prefill_on_tensor_cores_every_mask(torch, dtype, head_dim, mask_name):
     bad = np.argwhere(err > tol)
     assert len(bad) == 0, (f"{len(bad)} (row, head) pairs over {tol}: first {bad[:12].tolist()}, "
                            f"rows {sorted(set(bad[:, 0].tolist()))[:40]}, heads {sorted(set(bad[:, 1].tolist()))}")
+    assert parity_ok(got, want, dtype == fa.BF16)
 
 
 @pytest.mark.parametrize("first,rows", [(0, 1000), (37, 700)])
@@ -514,7 +514,7 @@ def test_causal_prefill_over_several_pairs(torch, first, rows):
     want = pair.oracle_attention(0, span, qkv, angles, fa.ROPE_HALF)
     got = out.cpu().numpy()
     print(compare(f"causal prefill {rows} rows from {first}, bf16", got, want))
-    assert max_abs(got, want) <= TOL_BF16
+    assert parity_ok(got, want, True)
 
 
 @pytest.mark.parametrize("rows", [300, 1030])

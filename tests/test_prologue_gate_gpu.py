@@ -8,7 +8,7 @@ import pytest
 
 import fusor_attn as fa
 import oracle
-from gpu_util import TOL_BF16, TOL_F32, Pair, compare, max_abs, normal, round_bf16
+from gpu_util import Pair, compare, max_abs, normal, parity_ok, round_bf16
 
 pytestmark = pytest.mark.gpu
 
@@ -122,7 +122,7 @@ def test_wan_self_attention_prologue_then_full_mask(torch, dtype):
                               width, prepared, s, 2 * width)
     got = out.cpu().numpy()
     print(compare(f"wan self-attention {dtype}", got, want))
-    assert max_abs(got, want) <= (TOL_F32 if dtype == "f32" else TOL_BF16)
+    assert parity_ok(got, want, dtype == "bf16")
 
 
 # ---- the hybrid blocks' gated attention -------------------------------------------------------
@@ -159,8 +159,7 @@ def test_gated_attention_matches_the_oracle(torch, gate, head_dim, rotary_dim, r
     want = oracle.gate(rows, shape.heads, shape.kv_heads, head_dim, gate, q, attended)
     got = out.cpu().numpy()
     print(compare(f"gated g{gate} d{head_dim}/{rotary_dim} rows {rows}", got, want))
-    tol = TOL_F32 if dtype == fa.F32 else TOL_BF16
-    assert max_abs(got, want) <= tol
+    assert parity_ok(got, want, dtype == fa.BF16)
 
 
 def test_gated_attention_argument_errors(torch):

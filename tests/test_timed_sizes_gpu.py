@@ -22,7 +22,7 @@ import pytest
 import fusor_attn as fa
 import oracle
 from fusor_attn.shard import query_row_shards, shard_sequences
-from gpu_util import TOL_BF16, TOL_F32, compare, max_abs, round_bf16
+from gpu_util import TOL_F32, compare, max_abs, parity_ok, round_bf16
 
 pytestmark = pytest.mark.gpu
 
@@ -88,8 +88,8 @@ def test_c3_every_sequence_of_the_timed_batch(torch, dtype):
             oc.keys[0, :, n] = round_bf16(oc.keys[0, :, n])
             oc.values[0, :, n] = round_bf16(oc.values[0, :, n])
         want = oc.attend(0, 1, n, oracle.Mask.causal(), q, q.shape[1], threads=threads())
-        tol = TOL_F32 if dtype == fa.F32 else TOL_BF16
-        assert max_abs(got[i:i + 1], want) <= tol, compare(f"C3 sequence {i} ({n} keys)", got[i:i + 1], want)
+        assert parity_ok(got[i:i + 1], want, dtype == fa.BF16), compare(
+            f"C3 sequence {i} ({n} keys)", got[i:i + 1], want)
         worst = max(worst, max_abs(got[i:i + 1], want))
     print(f"C3 {'f32' if dtype == fa.F32 else 'bf16'}: 64 sequences, max abs {worst:.2e}")
 
@@ -180,7 +180,7 @@ def test_c5_whole_call_against_the_oracle(torch):
                            threads=threads(), out=want)
     rows = np.r_[0:256, C5_N - 256:C5_N]
     print(compare("C5 edge pairs, every head", got[rows], want[rows]))
-    assert max_abs(got[rows], want[rows]) <= TOL_BF16
+    assert parity_ok(got[rows], want[rows], True)
     pairs = (C5_N + 255) // 256
     units = C5_HEADS * pairs
     tail_units = range(units // 148 * 148, units)  # head-major: the last ones are head 11's
@@ -201,14 +201,15 @@ def test_c5_whole_call_against_the_oracle(torch):
     cols = slice(11 * D, 12 * D)
     print(compare(f"C5 head 11, {len(split_rows)} rows of the split units",
                   got[split_rows, cols], want11[split_rows, cols]))
-    assert max_abs(got[split_rows, cols], want11[split_rows, cols]) <= TOL_BF16
+    assert parity_ok(got[split_rows, cols], want11[split_rows, cols], True)
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_c5_row_shares_equal_the_whole_call(torch, world):
     """Each rank's query rows as its own call (the multi-GPU run's per-rank call) give the whole
-    call's rows: the shares' schedules split other units into key pieces, so they agree within
-    one bf16 step of the output."""
+    call's rows within the bf16-compute bars: the shares' schedules cut other units into key
+    pieces, whose probabilities are rounded to bf16 against their own running maxima, so the two
+    differ at the level each differs from the f32 oracle (about 2e-4 here), not bit for bit."""
     qkv, hidden, stride = c5_inputs(torch)
     whole = torch.zeros((C5_N, hidden), device="cuda", dtype=torch.bfloat16)
     c5_call(torch, qkv, hidden, stride, 0, C5_N, whole)
@@ -217,8 +218,6 @@ def test_c5_row_shares_equal_the_whole_call(torch, world):
         if hi > lo:
             c5_call(torch, qkv, hidden, stride, lo, hi, parts)
     fa.device_status()
-    a, b = parts.float(), whole.float()
-    step = b.abs() * 2.0 ** -7 + 1e-6
-    worst = float(((a - b).abs() / step).max())
-    print(f"C5 over {world} shares: worst difference {worst:.2f} bf16 steps")
-    assert worst <= 1.0
+    a, b = parts.float().cpu().numpy(), whole.float().cpu().numpy()
+    print(compare(f"C5 over {world} shares against the whole call", a, b))
+    assert parity_ok(a, b, True)
