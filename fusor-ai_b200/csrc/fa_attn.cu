@@ -90,18 +90,21 @@ struct DeviceGuard {
   }
 };
 
-// A grow-only device buffer.
+// A grow-only device buffer. An outgrown allocation is kept, not freed, until the buffer is
+// released: a CUDA graph captured while it was current still reads and writes it on every
+// replay (freeing it would leave such a graph writing freed memory), and so may kernels still in
+// flight on another stream. Growth is by half again, so the kept allocations add up to at most
+// twice the current one.
 struct Buffer {
   void* ptr = nullptr;
   size_t bytes = 0;
+  std::vector<void*> outgrown;
   int ensure(size_t want, cudaStream_t stream) {
+    (void)stream;
     if (want <= bytes) return FA_OK;
-    if (ptr != nullptr) {
-      FA_CUDA(cudaStreamSynchronize(stream), "cudaStreamSynchronize(workspace growth)");
-      cudaFree(ptr);
-      ptr = nullptr;
-      bytes = 0;
-    }
+    if (ptr != nullptr) outgrown.push_back(ptr);
+    ptr = nullptr;
+    bytes = 0;
     const size_t size = std::max<size_t>(want + want / 2, 1 << 16);
     FA_CUDA(cudaMalloc(&ptr, size), "cudaMalloc(workspace)");
     bytes = size;
@@ -109,6 +112,8 @@ struct Buffer {
   }
   void release() {
     if (ptr != nullptr) cudaFree(ptr);
+    for (void* p : outgrown) cudaFree(p);
+    outgrown.clear();
     ptr = nullptr;
     bytes = 0;
   }
@@ -454,7 +459,10 @@ bool decode_on_tensor_cores(fa_kvcache* const* caches, const std::vector<fa::Run
 
 // The chunking of a tensor-core decode: chunks of a common length (a multiple of 128 keys), about
 // FA_DTC_UNITS (row, KV head, chunk) units per CTA (measured best: 1, the fewest unit ends and
-// chunk merges; the schedule balances whole rows), at most kDtcMaxUnits a launch.
+// chunk merges; the schedule balances whole rows), at most kDtcMaxUnits a launch. Measured on
+// B200 over a GPU's share of C3 (bf16) at 1, 2, 4 and 8 GPUs, 1..8 units a CTA: 1 is fastest at
+// 64, 32 and 16 sequences (181 / 101 / 62 us; 8 units: 224 / 139 / 102 us) and within 2 % of 2
+// units at 8 sequences (43.6 vs 42.9 us).
 #ifndef FA_DTC_UNITS
 #define FA_DTC_UNITS 1
 #endif
@@ -1194,6 +1202,54 @@ int check_batch(fa_kvcache* const* caches, const fa_span* spans, int32_t batch, 
   return FA_OK;
 }
 
+// The chunk length, in tiles, of a batch decode on the split-KV kernel: the one of least
+// modelled time among 8..64 tiles. The CTAs run in waves of the SMs' resident slots, the units of
+// a length spread evenly over them. A wave is bound both by its bytes at the HBM rate (a) and by
+// its longest chunk at one CTA's own streaming rate, two stages of K and V in flight (b); the two
+// overlap only in part, so a wave takes cbrt(a^3 + b^3), and a launch 10 us more. Fitted on B200
+// to a GPU's share of C3 at 1, 2, 4 and 8 GPUs (64, 32, 16 and 8 sequences, f32, head_dim 128;
+// sixteen fixed lengths of 16..64 tiles each, three repetitions): 6.9 TB/s, 32.8 GB/s per CTA
+// (one 32 KB tile a microsecond); it predicts the 64 timings within 6 % (rms) and its choice runs
+// within 3 % of the fastest length at every size. The fixed floor of 32 tiles it replaces left
+// 16 sequences in 1.37 waves, 115 us against 97 us; lengths whose last wave is barely begun
+// (1.05, 1.14 and 2.25 waves) are the slowest.
+int batch_chunk_tiles(const fa_kvcache* c0, const Plan& base, const std::vector<fa::Runs>& runs,
+                      int batch, int tile, int kt) {
+  constexpr int kMinTiles = 8, kMaxTiles = 64;
+  constexpr double kHbmTilesPerUs = 210.0;  // the whole GPU, reading (32 KB tiles)
+  constexpr double kCtaTilesPerUs = 1.0;    // one CTA
+  fa::AttendLaunch probe{kt, base.g, true, nullptr, nullptr, 0};
+  const int resident = attend_resident_d(c0->head_dim, probe);
+  const int64_t slots = int64_t(std::max(c0->dev->sms, 1)) * std::max(resident, 1);
+  int64_t longest = 1, keys_total = 0;
+  for (int i = 0; i < batch; ++i) {
+    const int64_t n = runs[i].n0 + runs[i].n1;
+    longest = std::max(longest, n);
+    keys_total += n;
+  }
+  const double tiles_total = double(keys_total) * base.kv_groups / tile;
+  const int top = int(std::min<int64_t>(kMaxTiles, std::max<int64_t>(kMinTiles, (longest + tile - 1) / tile)));
+  int best = top;
+  double best_us = 1e300;
+  for (int t = top; t >= kMinTiles; --t) {  // ties go to the longer chunk: fewer partials
+    const int64_t keys = int64_t(t) * tile;
+    int64_t units = 0;
+    for (int i = 0; i < batch; ++i)
+      units += std::max<int64_t>(1, (runs[i].n0 + runs[i].n1 + keys - 1) / keys);
+    units *= base.kv_groups;
+    const double per_unit = tiles_total / double(units);
+    const double b3 = std::pow(t / kCtaTilesPerUs, 3.0);
+    auto wave = [&](int64_t n) { return std::cbrt(std::pow(n * per_unit / kHbmTilesPerUs, 3.0) + b3); };
+    const int64_t full = units / slots, rest = units % slots;
+    const double us = double(full) * wave(slots) + (rest > 0 ? wave(rest) : 0.0);
+    if (us < best_us * (1.0 - 1e-9)) {
+      best_us = us;
+      best = t;
+    }
+  }
+  return best;
+}
+
 }  // namespace
 
 namespace {
@@ -1452,17 +1508,9 @@ int fa_attend_batch(fa_kvcache* const* caches, const fa_span* spans, int32_t bat
   if (decode_on_tensor_cores(caches, runs, batch))
     return attend_batch_tc(caches, runs, batch, layer, q, q_stride, out, out_stride, s);
   const Plan base = plan_span(c0, 1, 1, false);
-  const int tile = fa::tile_keys(c0->head_dim, c0->dtype == FA_F32 ? fa::kKtF32 : fa::kKtBf16);
-  const int64_t want = target_units(c0->dev);
-  int64_t chunk_keys = (total_keys * base.kv_groups + want - 1) / want;
-  // at least FA_DECODE_MIN_CHUNK_TILES tiles a chunk: a small batch (a GPU's share of C3 over 8
-  // GPUs) otherwise splits into chunks too short for their fixed costs (measured on B200, 8 of
-  // C3's sequences: 49.6 us with 32-tile chunks, 52.7 with 8; 64 sequences: no change)
-#ifndef FA_DECODE_MIN_CHUNK_TILES
-#define FA_DECODE_MIN_CHUNK_TILES 32
-#endif
-  chunk_keys = std::max<int64_t>(int64_t(tile) * FA_DECODE_MIN_CHUNK_TILES,
-                                 (chunk_keys + tile - 1) / tile * tile);
+  const int kt = c0->dtype == FA_F32 ? fa::kKtF32 : fa::kKtBf16;
+  const int tile = fa::tile_keys(c0->head_dim, kt);
+  const int64_t chunk_keys = int64_t(tile) * batch_chunk_tiles(c0, base, runs, batch, tile, kt);
   // Chunks and partial slots of every row, then one launch per kMaxBatchRows rows.
   std::vector<int> chunks(batch), part_base(batch);
   int64_t slots = 0;
@@ -1475,7 +1523,6 @@ int fa_attend_batch(fa_kvcache* const* caches, const fa_span* spans, int32_t bat
   Work w;
   if (int rc = ensure_work(c0, 0, size_t(slots) * c0->heads, 0, s, &w)) return rc;
   if (int rc = ensure_counters(c0, size_t(batch) * base.kv_groups, s)) return rc;
-  const int kt = c0->dtype == FA_F32 ? fa::kKtF32 : fa::kKtBf16;
   for (int first = 0; first < batch; first += fa::kMaxBatchRows) {
     const int n = std::min(batch - first, fa::kMaxBatchRows);
     fa::BatchArgs ba{};
