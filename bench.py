@@ -630,6 +630,103 @@ class LongPrefill(Workload):
         return self.flops
 
 
+class GatedPrefill256(Workload):
+    """A long prefill of Qwen3.5's gated attention layer (models/qwen3-5/model/src/model.rs:
+    60-75): 8 query heads over 2 KV heads of 256, 64 of each head's dimensions rotated by
+    interleaved multimodal RoPE (base 1e7, sections [11, 11, 10]), head RMSNorm, an elementwise
+    sigmoid gate; 8192 rows from position 0 over a bf16 cache. The step is fa_gated_attention
+    (norm, RoPE and keep, the head_dim-256 tensor-core attention, the gate); the roofline times the
+    attention alone (fa_attend over the rotated queries). FLOPs 4 x 256 x 8 x the visible keys of
+    every row (0.275 TFLOP)."""
+
+    def __init__(self, torch, fa):
+        self.torch, self.fa, self.name = torch, fa, "qwen35"
+        self.kernel = "fmha_kernel"
+        rows, heads, kv, d = 8192, 8, 2, 256
+        self.rows, self.heads, self.kv, self.d = rows, heads, kv, d
+        shape = fa.Shape(1, heads, kv, d)
+        self.shape = shape
+        self.cache = fa.KvCache(shape, rows, fa.BF16)
+        gen = torch.Generator("cuda").manual_seed(17)
+        self.width = (2 * heads + 2 * kv) * d  # query, gate, key and value heads
+        self.qkv = torch.randn((rows, self.width), device="cuda", generator=gen)
+        self.q_norm = 1.0 + 0.1 * torch.randn((d,), device="cuda", generator=gen)
+        self.k_norm = 1.0 + 0.1 * torch.randn((d,), device="cuda", generator=gen)
+        rot = fa.Rotation(fa.ROT_MULTIMODAL_INTERLEAVED, (11, 11, 10), 1e7)
+        self.angles = torch.from_numpy(fa.rotary_angles(rot, 64, range(rows))).cuda()
+        self.span = fa.Span(rows, 0, fa.Mask.causal())
+        self.out = torch.zeros((rows, shape.width), device="cuda")
+        self.q = torch.zeros((rows, shape.width), device="cuda")
+        self.tokens = rows
+        self.bound = "tensor"
+        self.launches_per_step = 4
+        self.graphs = True
+        self.h_qkv = self.qkv.cpu().pin_memory()
+        self.h_out = torch.zeros_like(self.out, device="cpu").pin_memory()
+        self.h2d = self.h_qkv.numel() * 4
+        self.d2h = self.h_out.numel() * 4
+        self.flops = 4.0 * heads * d * rows * (rows + 1) / 2
+
+    def gated(self):
+        fa = self.fa
+        self.cache.gated_attention(0, self.span, self.qkv, self.out, fa.GATE_ELEMENTWISE, 64,
+                                   self.angles, norm=(self.q_norm, self.k_norm, 1e-6))
+
+    def phases(self):
+        return (lambda: None, self.gated)
+
+    def capture(self):
+        """The step graph (fa_gated_attention), and for the roofline the attention alone: fa_attend
+        over the rows' query heads (f32, converted to bf16 operand rows by the call, as the
+        step's own queries are; their values do not change the work)."""
+        torch = self.torch
+        self._step_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self._step_graph, capture_error_mode="relaxed"):
+            self.gated()
+        self.q.copy_(self.qkv[:, :self.shape.width])
+        self.cache.attend(0, self.span, self.q, self.out)  # sizes its workspace before capture
+        torch.cuda.synchronize()
+        self._kernel_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self._kernel_graph, capture_error_mode="relaxed"):
+            self.cache.attend(0, self.span, self.q, self.out)
+        torch.cuda.synchronize()
+
+    def e2e_step(self):
+        self.qkv.copy_(self.h_qkv, non_blocking=True)
+        self.gated()
+        self.h_out.copy_(self.out, non_blocking=True)
+
+    def parity(self, threads):
+        """Sampled rows of the gated layer's output (the first and last 16, 32 spread between)
+        against the oracle: its norm, partial RoPE and keep of all 8192 rows into a host cache
+        (the kept rows rounded to bf16, as this cache holds them), its causal attend of each
+        sampled row, and the gate. A bf16-compute path."""
+        import oracle
+        torch, fa = self.torch, self.fa
+        self.gated()  # the timed kernel graph overwrote the output with the attention alone
+        torch.cuda.synchronize()
+        rows, heads, kv, d = self.rows, self.heads, self.kv, self.d
+        oc = oracle.Cache(1, heads, kv, d, rows)
+        q = self.qkv.cpu().numpy().copy()
+        angles = self.angles.cpu().numpy()
+        oc.gated_input(0, rows, 0, fa.GATE_ELEMENTWISE, 64, angles, q, self.width,
+                       self.q_norm.cpu().numpy(), self.k_norm.cpu().numpy(), 1e-6)
+        oc.keys[:] = round_bf16(torch, oc.keys)
+        oc.values[:] = round_bf16(torch, oc.values)
+        sample = sorted(set(range(16)) | set(range(rows - 16, rows)) |
+                        set(np.linspace(16, rows - 17, 32).astype(int).tolist()))
+        got = self.out.cpu().numpy()[sample]
+        want = []
+        for r in sample:
+            att = oc.attend(0, 1, r, oracle.Mask.causal(), q[r:r + 1], self.width, threads=threads)
+            want.append(oracle.gate(1, heads, kv, d, fa.GATE_ELEMENTWISE, q[r:r + 1], att))
+        return parity_result(got, np.concatenate(want), TOL_BF16,
+                             f"{len(sample)} of {rows} rows, every head", REL_BF16)
+
+    def algorithmic(self):
+        return self.flops
+
+
 class C4Sharded(Workload):
     """C4 over `world` GPUs: each rank holds a contiguous range of the 131073 key positions in
     its own cache; a step rotates the query everywhere, keeps the new row on its owner, attends
@@ -1200,6 +1297,8 @@ def run_ours(args):
             return DitPrologue(torch, fa)
         if name == "prefill":
             return LongPrefill(torch, fa)
+        if name == "qwen35":
+            return GatedPrefill256(torch, fa)
         raise SystemExit(f"unknown config {name}")
 
     # the oracle's threads for the parity checks: the host's, shared by the ranks
@@ -1224,6 +1323,7 @@ def run_ours(args):
         "warmup": warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
         "scaling": "strong" if w.sharded else "weak", "vs_baseline": None,
         "dtype": {"c3bf16": "bf16-kv/f32", "c5": "bf16/f32-acc", "prefill": "bf16-kv/f32",
+                  "qwen35": "bf16-kv/f32",
                   "prologue": "f32-in/bf16-out"}.get(args.config, "f32"),
         "data": "synthetic N(0,1) (seeded), random keys/values of the config's shape",
         "config": config_of(args.config, world),
@@ -1245,8 +1345,8 @@ def run_ours(args):
     torch.cuda.empty_cache()
     if args.config == "c3" and not args.no_extras and args.sequences == C3_SEQS:
         extras = {}
-        names = (("c1", "c2", "c3bf16", "c4", "c5", "prefill", "proj", "prologue") if world == 1
-                 else ("c4", "c5"))
+        names = (("c1", "c2", "c3bf16", "c4", "c5", "prefill", "qwen35", "proj", "prologue")
+                 if world == 1 else ("c4", "c5"))
         for name in names:
             x = build(name)
             xs = min(steps, 50 if name == "c5" else 200)
@@ -1309,6 +1409,11 @@ def config_of(name, world):
         "prefill": {"workload": "long causal prefill at C3's model shape, bf16 cache",
                     "rows": 8192, "heads": 32, "kv_heads": 8, "head_dim": 128, "mask": "causal",
                     "path": "fa_attention (step); roofline over an fa_attend call alone"},
+        "qwen35": {"workload": "Qwen3.5 gated attention layer, long prefill, bf16 cache",
+                   "rows": 8192, "heads": 8, "kv_heads": 2, "head_dim": 256, "rotary_dim": 64,
+                   "rotation": "MultimodalInterleaved [11, 11, 10], base 1e7", "gate": "elementwise",
+                   "head_norm": "rms", "mask": "causal",
+                   "path": "fa_gated_attention (step); roofline over an fa_attend call alone"},
         "prologue": {"workload": "C5's DiT query/key prologue (RMSNorm + 3-D RoPE, bf16 out)",
                      "tokens": 32760, "heads": 12, "head_dim": 128, "norm": "whole row",
                      "rope": "interleaved"},
@@ -1324,9 +1429,11 @@ def config_of(name, world):
                "by one kernel (P2P stores, flags) that merges" if world > 1 else "1 GPU"),
         "c5": f"query rows in whole 256-row pairs over {world} GPU(s), all heads, no collective",
     }.get(name, f"replicas x{world}")
-    c["l2"] = ("inputs larger than L2" if name in ("c3", "c3bf16", "c4", "c5", "prologue", "prefill")
+    c["l2"] = ("inputs larger than L2" if name in ("c3", "c3bf16", "c4", "c5", "prologue", "prefill",
+                                                   "qwen35")
                else "L2 flushed between steps (clean lines left)")
-    if name in ("c1", "c2", "c3", "c3bf16", "proj", "prologue", "prefill") or (name == "c4" and world > 1):
+    if name in ("c1", "c2", "c3", "c3bf16", "proj", "prologue", "prefill", "qwen35") or \
+            (name == "c4" and world > 1):
         c["launch"] = "the step's calls replayed as captured CUDA graphs"
     return c
 
@@ -1400,7 +1507,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="c3",
-                    choices=["c1", "c2", "c3", "c3bf16", "c4", "c5", "prefill", "proj", "prologue"])
+                    choices=["c1", "c2", "c3", "c3bf16", "c4", "c5", "prefill", "qwen35", "proj",
+                             "prologue"])
     ap.add_argument("--sequences", type=int, default=C3_SEQS,
                     help="C3 sequences (a smaller batch for profiling captures)")
     ap.add_argument("--no-extras", action="store_true")

@@ -1920,7 +1920,7 @@ int fa_attend_full(const fa_call* call, void* out, int64_t out_stride, void* str
     a.out_stride = out_stride;
     a.out_bf16 = k.out_dtype == FA_BF16 ? 1 : 0;
     a.err = dev->err;
-    if (fa::fmha_splits_supported(k.dtype == FA_BF16)) {
+    if (fa::fmha_splits_supported(k.dtype == FA_BF16, k.head_dim)) {
       const int64_t units = int64_t(k.images) * ((a.q_tiles + 1) / 2) * k.heads;
       int64_t whole = units;
       int splits = 1;

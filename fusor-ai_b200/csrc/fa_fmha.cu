@@ -106,21 +106,22 @@ bool encode_cache_map_bf16(void* map, const void* base, uint64_t rows, uint64_t 
 }
 
 bool fmha_supported(int dtype_bf16, int head_dim) {
-  (void)dtype_bf16;
-  return (head_dim == 64 || head_dim == 128) && encode_fn() != nullptr;
+  const bool dim = head_dim == 64 || head_dim == 128 || (head_dim == 256 && dtype_bf16);
+  return dim && encode_fn() != nullptr;
 }
 
-bool fmha_splits_supported(int dtype_bf16) {
+bool fmha_splits_supported(int dtype_bf16, int head_dim) {
 #ifdef FA_FMHA_ONE_TILE
   (void)dtype_bf16;
+  (void)head_dim;
   return false;
 #else
-  return dtype_bf16 != 0;
+  return dtype_bf16 != 0 && head_dim != 256;  // head_dim 256 runs one query tile per CTA
 #endif
 }
 
 int fmha_block_n(int dtype_bf16, int head_dim) {
-  return (!dtype_bf16 && head_dim == 128) ? 64 : 128;
+  return (head_dim == 256 || (!dtype_bf16 && head_dim == 128)) ? 64 : 128;
 }
 
 cudaError_t launch_fmha(const FmhaLaunch& l, cudaStream_t stream) {
@@ -132,6 +133,8 @@ cudaError_t launch_fmha(const FmhaLaunch& l, cudaStream_t stream) {
     if (l.head_dim == 64) return launch_bf16_pairs<64>(l, stream);
     if (l.head_dim == 128) return launch_bf16_pairs<128>(l, stream);
 #endif
+    // two query tiles of head_dim 256 (S and O for each) do not fit in TMEM's 512 columns
+    if (l.head_dim == 256) return launch_t<__nv_bfloat16, 256>(l, stream);
   } else {
     if (l.head_dim == 64) return launch_t<float, 64>(l, stream);
     if (l.head_dim == 128) return launch_t<float, 128>(l, stream);

@@ -26,11 +26,13 @@
 
 namespace fa {
 
+// head_dim 256 (bf16 only): 64-key tiles, so that Q (64 KB) and two stages of K and V (32 KB
+// each) fit in shared memory, and two S buffers of 64 columns beside O's 256 in TMEM.
 template <typename T, int D>
 struct FmhaShape {
   static constexpr bool kTf32 = sizeof(T) == 4;
   static constexpr int BM = 128;                               // query rows per CTA
-  static constexpr int BN = (kTf32 && D == 128) ? 64 : 128;    // keys per KV tile
+  static constexpr int BN = (D == 256 || (kTf32 && D == 128)) ? 64 : 128;  // keys per KV tile
   static constexpr int kElem = int(sizeof(T));
   static constexpr int kBlock = 128 / kElem;                   // elements per swizzled 128 B row
   static constexpr int kDBlocks = D / kBlock;
@@ -47,6 +49,8 @@ struct FmhaShape {
   static constexpr size_t kSmemBytes = kSmemUsed > 122880 ? kSmemUsed : 122880;
   static_assert(D % kBlock == 0, "head_dim a multiple of the swizzle block");
   static_assert(BN % 32 == 0 && D % 32 == 0, "TMEM loads of 32 columns");
+  static_assert(kOCol + D <= 512 && 2 * kSCols <= kOCol, "two S buffers and O in 512 columns");
+  static_assert(kSmemUsed <= 227 * 1024, "shared memory of one CTA");
 };
 
 constexpr int kFmhaThreads = 256;

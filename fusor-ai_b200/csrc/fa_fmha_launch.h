@@ -49,7 +49,7 @@ constexpr int kFmhaMaxSplits = 8;
 // rows and z its query heads; K/V rows are key positions and z (layer x) KV heads.
 struct FmhaLaunch {
   int bf16;      // operands bf16 (kind::f16) or f32 (kind::tf32)
-  int head_dim;  // 64 or 128
+  int head_dim;  // 64 or 128, or 256 for bf16
   const void* q;
   uint64_t q_rows, q_heads;
   uint64_t q_row_stride, q_head_stride;  // elements
@@ -62,7 +62,7 @@ struct FmhaLaunch {
 
 bool fmha_supported(int dtype_bf16, int head_dim);
 // Whether launch_fmha honours FmhaArgs::splits for these operands (the two-tile bf16 kernel).
-bool fmha_splits_supported(int dtype_bf16);
+bool fmha_splits_supported(int dtype_bf16, int head_dim);
 // A TMA map (written to the 128 bytes at `map`, 64-byte aligned) over a bf16 cache's keys or
 // values: [z][rows][128] elements, z_stride_bytes apart, 64 x 128 boxes, 128-byte swizzle (the
 // tensor-core decode's K and V tiles).

@@ -471,11 +471,13 @@ def test_full_mask_on_the_split_kv_kernel(torch, case):
 
 
 @pytest.mark.parametrize("dtype", [fa.F32, fa.BF16])
-@pytest.mark.parametrize("head_dim", [64, 128])
+@pytest.mark.parametrize("head_dim", [64, 128, 256])
 @pytest.mark.parametrize("mask_name", ["causal", "window", "full", "groups"])
 def test_prefill_on_tensor_cores_every_mask(torch, dtype, head_dim, mask_name):
     """Spans of >= 64 rows run on the tcgen05 kernel: every mask, a cache already holding keys
-    (first > 0), GQA 12/4, a row count that is not a multiple of the 128-row tile."""
+    (first > 0), GQA 12/4, a row count that is not a multiple of the 128-row tile. head_dim 256
+    runs on the tensor cores over a bf16 cache (one query tile per CTA, 64-key tiles), on the
+    split-KV kernel over an f32 cache."""
     shape = fa.Shape(1, 12, 4, head_dim)
     first, rows = 150, 200
     mask = {"causal": fa.Mask.causal(), "window": fa.Mask.window_of(97), "full": fa.Mask.full(),
