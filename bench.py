@@ -552,14 +552,23 @@ class LongPrefill(Workload):
     """A long causal prefill at C3's model shape (32/8 heads x 128, RoPE base 1e6): 8192 rows
     from position 0 over a bf16 cache: RoPE + keep (fa_attention_input), then the attention
     (fa_attend: the queries to bf16 operand rows and the tensor-core attention). FLOPs 4 x d x
-    heads x the visible keys of every row (0.55 TFLOP) over the attend call's time."""
+    heads x the visible keys of every row (0.55 TFLOP) over the attend call's time.
+    `prefill_f32`: the same over an f32 cache, the reference's own cache type (transformer.rs:
+    134-162), on the tf32 tensor-core kernel (f32 queries, keys and values rounded to tf32 on the
+    way in, f32 accumulation); its roofline is against half the bf16 peak, the tensor cores' tf32
+    rate (1.1 of 2.25 PFLOP/s nominal, dense)."""
 
-    def __init__(self, torch, fa):
-        self.torch, self.fa, self.name = torch, fa, "prefill"
-        self.kernel = "fmha2_kernel"
+    def __init__(self, torch, fa, dtype=None):
+        dtype = fa.BF16 if dtype is None else dtype
+        self.torch, self.fa = torch, fa
+        self.dtype = dtype
+        self.name = "prefill" if dtype == fa.BF16 else "prefill_f32"
+        self.kernel = "fmha2_kernel" if dtype == fa.BF16 else "fmha_kernel"
+        if dtype == fa.F32:
+            self.peak_scale = 0.5
         rows, heads, kv, d = 8192, 32, 8, 128
         shape = fa.Shape(1, heads, kv, d)
-        self.cache = fa.KvCache(shape, rows, fa.BF16)
+        self.cache = fa.KvCache(shape, rows, dtype)
         gen = torch.Generator("cuda").manual_seed(13)
         self.span = fa.Span(rows, 0, fa.Mask.causal())
         self.qkv = torch.randn((rows, shape.qkv), device="cuda", generator=gen)
@@ -616,15 +625,18 @@ class LongPrefill(Workload):
         oc = oracle.Cache(1, heads, kv, d, rows)
         q = self.qkv.cpu().numpy().copy()
         oc.attention_input(0, rows, 0, fa.ROPE_HALF, self.angles.cpu().numpy(), q, q.shape[1])
-        oc.keys[:] = round_bf16(torch, oc.keys)
-        oc.values[:] = round_bf16(torch, oc.values)
+        bf16 = self.dtype == fa.BF16
+        if bf16:
+            oc.keys[:] = round_bf16(torch, oc.keys)
+            oc.values[:] = round_bf16(torch, oc.values)
         sample = sorted(set(range(16)) | set(range(rows - 16, rows)) |
                         set(np.linspace(16, rows - 17, 32).astype(int).tolist()))
         out = self.out.cpu().numpy()
         want = np.concatenate([oc.attend(0, 1, r, oracle.Mask.causal(), q[r:r + 1], q.shape[1],
                                          threads=threads) for r in sample])
-        return parity_result(out[sample], want, TOL_BF16,
-                             f"{len(sample)} of {rows} rows, every head", REL_BF16)
+        return parity_result(out[sample], want, TOL_BF16 if bf16 else TOL_F32,
+                             f"{len(sample)} of {rows} rows, every head",
+                             REL_BF16 if bf16 else None)
 
     def algorithmic(self):
         return self.flops
@@ -1095,6 +1107,9 @@ def roofline(w: Workload, kern_ms: float, peaks):
     else:
         achieved = w.algorithmic() / (kern_ms * 1e-3) / 1e12
         peak, unit = tflops, "TFLOP/s"
+        scale = getattr(w, "peak_scale", 1.0)
+        if scale != 1.0:  # tf32: half the bf16 rate
+            peak, kind = peak * scale, f"{kind} bf16 x {scale} (tf32)"
     return {"bound": w.bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
             "frac": round(achieved / peak, 4), "peak_source": kind,
             "traffic": profile_traffic(w.name), "kernel": getattr(w, "kernel", "attend_kernel"),
@@ -1297,6 +1312,8 @@ def run_ours(args):
             return DitPrologue(torch, fa)
         if name == "prefill":
             return LongPrefill(torch, fa)
+        if name == "prefill_f32":
+            return LongPrefill(torch, fa, fa.F32)
         if name == "qwen35":
             return GatedPrefill256(torch, fa)
         raise SystemExit(f"unknown config {name}")
@@ -1323,7 +1340,7 @@ def run_ours(args):
         "warmup": warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
         "scaling": "strong" if w.sharded else "weak", "vs_baseline": None,
         "dtype": {"c3bf16": "bf16-kv/f32", "c5": "bf16/f32-acc", "prefill": "bf16-kv/f32",
-                  "qwen35": "bf16-kv/f32",
+                  "qwen35": "bf16-kv/f32", "prefill_f32": "f32 (tf32 tensor cores)",
                   "prologue": "f32-in/bf16-out"}.get(args.config, "f32"),
         "data": "synthetic N(0,1) (seeded), random keys/values of the config's shape",
         "config": config_of(args.config, world),
@@ -1345,8 +1362,8 @@ def run_ours(args):
     torch.cuda.empty_cache()
     if args.config == "c3" and not args.no_extras and args.sequences == C3_SEQS:
         extras = {}
-        names = (("c1", "c2", "c3bf16", "c4", "c5", "prefill", "qwen35", "proj", "prologue")
-                 if world == 1 else ("c4", "c5"))
+        names = (("c1", "c2", "c3bf16", "c4", "c5", "prefill", "prefill_f32", "qwen35", "proj",
+                  "prologue") if world == 1 else ("c4", "c5"))
         for name in names:
             x = build(name)
             xs = min(steps, 50 if name == "c5" else 200)
@@ -1409,6 +1426,10 @@ def config_of(name, world):
         "prefill": {"workload": "long causal prefill at C3's model shape, bf16 cache",
                     "rows": 8192, "heads": 32, "kv_heads": 8, "head_dim": 128, "mask": "causal",
                     "path": "fa_attention (step); roofline over an fa_attend call alone"},
+        "prefill_f32": {"workload": "long causal prefill at C3's model shape, f32 cache (tf32)",
+                        "rows": 8192, "heads": 32, "kv_heads": 8, "head_dim": 128,
+                        "mask": "causal",
+                        "path": "fa_attention (step); roofline over an fa_attend call alone"},
         "qwen35": {"workload": "Qwen3.5 gated attention layer, long prefill, bf16 cache",
                    "rows": 8192, "heads": 8, "kv_heads": 2, "head_dim": 256, "rotary_dim": 64,
                    "rotation": "MultimodalInterleaved [11, 11, 10], base 1e7", "gate": "elementwise",
@@ -1430,9 +1451,9 @@ def config_of(name, world):
         "c5": f"query rows in whole 256-row pairs over {world} GPU(s), all heads, no collective",
     }.get(name, f"replicas x{world}")
     c["l2"] = ("inputs larger than L2" if name in ("c3", "c3bf16", "c4", "c5", "prologue", "prefill",
-                                                   "qwen35")
+                                                   "prefill_f32", "qwen35")
                else "L2 flushed between steps (clean lines left)")
-    if name in ("c1", "c2", "c3", "c3bf16", "proj", "prologue", "prefill", "qwen35") or \
+    if name in ("c1", "c2", "c3", "c3bf16", "proj", "prologue", "prefill", "prefill_f32", "qwen35") or \
             (name == "c4" and world > 1):
         c["launch"] = "the step's calls replayed as captured CUDA graphs"
     return c
@@ -1507,8 +1528,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="c3",
-                    choices=["c1", "c2", "c3", "c3bf16", "c4", "c5", "prefill", "qwen35", "proj",
-                             "prologue"])
+                    choices=["c1", "c2", "c3", "c3bf16", "c4", "c5", "prefill", "prefill_f32",
+                             "qwen35", "proj", "prologue"])
     ap.add_argument("--sequences", type=int, default=C3_SEQS,
                     help="C3 sequences (a smaller batch for profiling captures)")
     ap.add_argument("--no-extras", action="store_true")

@@ -1192,11 +1192,11 @@ int check_batch(fa_kvcache* const* caches, const fa_span* spans, int32_t batch, 
         c->layers != c0->layers || c->dtype != c0->dtype || c->device != c0->device)
       return fail(FA_ERR_SHAPE, "sequence %d's cache differs in shape from the first", i);
     if (spans[i].rows != 1) return fail(FA_ERR_ARG, "batched spans are one row (decode)");
-    if (spans[i].mask.kind == FA_MASK_GROUPS)
-      return fail(FA_ERR_UNSUPPORTED, "Groups masks in a batched decode");
     if (int rc = check_span(c, &spans[i], &ends)) return rc;
-    (*runs)[i] = fa::mask_runs(spans[i].mask.kind, spans[i].mask.window, 0, 0, nullptr,
-                               spans[i].first, spans[i].first + 1);
+    // Mask::keys of the row: under Groups the state's run and the row's own group (two runs,
+    // which decode on the CUDA cores)
+    (*runs)[i] = fa::mask_runs(spans[i].mask.kind, spans[i].mask.window, spans[i].mask.state,
+                               int(ends.size()), ends.data(), spans[i].first, spans[i].first + 1);
     *total_keys += (*runs)[i].n0 + (*runs)[i].n1;
   }
   return FA_OK;

@@ -240,9 +240,10 @@ int fa_attention_host(fa_kvcache* cache, int32_t layer, const fa_span* span, int
 
 /* One decode step (Span rows = 1) of `batch` independent sequences, each with its own cache
  * (all of one shape and device), in one launch: sequence i's row is row i of qkv (qkv_stride
- * apart) at spans[i].first under spans[i].mask, angles row i (device, batch x head_dim; NULL
- * for FA_ROPE_NONE), output row i of out. The reference runs one Transformer::forward per
- * sequence (models/ming/model/src/session.rs:268-282); batch <= 1024. */
+ * apart) at spans[i].first under spans[i].mask (any kind; a Groups mask's last end is the row's
+ * position + 1), angles row i (device, batch x head_dim; NULL for FA_ROPE_NONE), output row i
+ * of out. The reference runs one Transformer::forward per sequence
+ * (models/ming/model/src/session.rs:268-282); batch <= 1024. */
 int fa_attention_batch(fa_kvcache* const* caches, const fa_span* spans, int32_t batch,
                        int32_t layer, int32_t rope, const float* angles,
                        const fa_head_norm* norm, const float* qkv, int64_t qkv_stride,

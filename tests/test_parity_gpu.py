@@ -180,6 +180,31 @@ def test_window_ring_wraps_and_groups(torch):
     assert max_abs(out.cpu().numpy(), want) <= TOL_F32
 
 
+@pytest.mark.parametrize("dtype", [fa.F32, fa.BF16])
+def test_batched_decode_under_groups_masks(torch, dtype):
+    """One-row spans under Mask::Groups in one batch (Mask::keys, transformer.rs:119-126: the
+    state's run and the row's own group, or every key before the state), beside causal and
+    window rows; each against the oracle (two key runs decode on the CUDA cores, in f32)."""
+    shape = fa.Shape(1, 8, 2, 128)
+    cases = [(700, fa.Mask.groups(300, [650, 701])),   # the state, then its own group
+             (90, fa.Mask.groups(91, [91])),           # before the state: every key
+             (400, fa.Mask.groups(0, [380, 401])),     # no state: its own group alone
+             (512, fa.Mask.causal()),
+             (1000, fa.Mask.window_of(333))]
+    pairs = [Pair(shape, n + 1, dtype, filled=n, seed=140 + i) for i, (n, _) in enumerate(cases)]
+    qkv = normal(141, (len(cases), shape.qkv))
+    angles = fa.rotary_angles(fa.Rotation(base=1e6), 128, [n for n, _ in cases])
+    spans = [fa.Span(1, n, m) for n, m in cases]
+    out = torch.zeros((len(cases), shape.width), device="cuda")
+    fa.attention_batch([p.gpu for p in pairs], spans, 0, dev(torch, qkv), out, dev(torch, angles),
+                       fa.ROPE_HALF)
+    fa.device_status()
+    got = out.cpu().numpy()
+    for i, (p, span) in enumerate(zip(pairs, spans)):
+        want = p.oracle_attention(0, span, qkv[i:i + 1], angles[i:i + 1], fa.ROPE_HALF)
+        assert max_abs(got[i:i + 1], want) <= TOL_F32, compare(f"groups batch row {i}", got[i:i + 1], want)
+
+
 def test_capacity_and_span_errors(torch):
     shape = fa.Shape(1, 4, 2, 16)
     cache = fa.KvCache(shape, 8)

@@ -221,3 +221,41 @@ def test_c5_row_shares_equal_the_whole_call(torch, world):
     a, b = parts.float().cpu().numpy(), whole.float().cpu().numpy()
     print(compare(f"C5 over {world} shares against the whole call", a, b))
     assert parity_ok(a, b, True)
+
+
+def test_f32_cache_long_prefill_on_tf32_against_f32_cores(torch):
+    """The bench's f32-cache prefill (8192 rows from position 0, 32/8 heads x 128, causal) on the
+    tf32 tensor-core kernel, every row against the same attention on the split-KV kernel's f32
+    arithmetic (queries given with a row stride the tensor path's TMA cannot take), which the
+    oracle matches within 1e-6; and sampled rows against the oracle itself."""
+    rows, heads, kv = 8192, 32, 8
+    shape = fa.Shape(1, heads, kv, D)
+    cache = fa.KvCache(shape, rows)
+    gen = torch.Generator("cuda").manual_seed(13)
+    qkv = torch.randn((rows, shape.qkv), device="cuda", generator=gen)
+    angles = torch.from_numpy(fa.rotary_angles(fa.Rotation(base=1e6), D, range(rows))).cuda()
+    span = fa.Span(rows, 0, fa.Mask.causal())
+    q = torch.zeros((rows, shape.width), device="cuda")
+    cache.attention_input(0, span, qkv, angles, fa.ROPE_HALF, q_out=q)
+    tc = torch.zeros((rows, shape.width), device="cuda")
+    cache.attend(0, span, q, tc)
+    q_odd = torch.zeros((rows, shape.width + 1), device="cuda")
+    q_odd[:, :shape.width] = q
+    cores = torch.zeros_like(tc)
+    cache.attend(0, span, q_odd[:, :shape.width], cores)
+    fa.device_status()
+    err = (tc - cores).abs()
+    worst_rows = err.max(dim=1).values
+    print(f"f32 prefill 8192 rows, tf32 tensor cores vs f32 cores: max abs {float(err.max()):.2e}, "
+          f"rows over 1e-3: {int((worst_rows > 1e-3).sum())}, worst row {int(worst_rows.argmax())}")
+    assert float(err.max()) <= TOL_F32
+    # the f32 cores against the oracle on a few rows, the worst one among them
+    k, v = cache.copy_rows(rows)
+    oc = oracle.Cache(1, heads, kv, D, rows)
+    oc.keys[:] = k.cpu().numpy()
+    oc.values[:] = v.cpu().numpy()
+    qh = q.cpu().numpy()
+    for r in sorted({0, 1, 7, 100, rows - 1, int(worst_rows.argmax())}):
+        want = oc.attend(0, 1, r, oracle.Mask.causal(), qh[r:r + 1], qh.shape[1], threads=threads())
+        assert max_abs(cores.cpu().numpy()[r:r + 1], want) <= 1e-5
+        assert max_abs(tc.cpu().numpy()[r:r + 1], want) <= TOL_F32
