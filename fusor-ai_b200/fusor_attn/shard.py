@@ -17,6 +17,7 @@ of its one-call semantics, checked against the single-GPU result by the tests.
 """
 from __future__ import annotations
 
+import time
 from dataclasses import dataclass
 
 
@@ -46,6 +47,37 @@ def query_row_shards(rows: int, world: int, pair: int = 256):
             for r in range(world)]
 
 
+def _abort(group=None):
+    """Aborts the process group (its communicator released, every rank's pending collective on
+    it ended with an error); best effort: the group may already be gone."""
+    try:
+        from torch.distributed import distributed_c10d as c10d
+        c10d._abort_process_group(group)
+    except Exception:  # noqa: BLE001 - the error raised to the caller is the exchange's
+        pass
+
+
+def wait_or_abort(work, timeout_s: float, what: str, group=None):
+    """Waits on the host for this rank's asynchronous collective `work`, at most `timeout_s`, so
+    that a rank that left or stalls cannot hold the others for the process group's own timeout
+    (minutes). Past the limit the group is aborted and FaError(ERR_TIMEOUT) raised; a collective
+    that ended with an error (a peer that exited) raises the same after the abort. The
+    reference's analogue is a cancelled job (crates/bundle/src/engine.rs:13-14)."""
+    import fusor_attn as fa
+    deadline = time.monotonic() + timeout_s
+    while not work.is_completed():
+        if time.monotonic() > deadline:
+            _abort(group)
+            raise fa.FaError(fa.ERR_TIMEOUT, f"{what}: no progress in {timeout_s:g} s; the process "
+                                             "group was aborted")
+        time.sleep(50e-6)
+    try:
+        work.wait()
+    except Exception as e:  # noqa: BLE001 - re-raised as the exchange's status
+        _abort(group)
+        raise fa.FaError(fa.ERR_TIMEOUT, f"{what} failed ({e}); the process group was aborted") from e
+
+
 @dataclass
 class ShardedDecode:
     """One decode row over a context split by key position across the ranks of `group`.
@@ -64,6 +96,7 @@ class ShardedDecode:
     world: int
     group: object = None   # torch.distributed process group (None: the default group)
     exchange: str = "nccl"  # "peer": fa_exchange_merge over NVLink peer memory
+    timeout_s: float = 10.0  # the NCCL exchange's host-side watchdog (eager steps)
 
     def __post_init__(self):
         import torch
@@ -97,7 +130,15 @@ class ShardedDecode:
             self.peers.merge(self.partials, self.out)
             return self.out
         if dist is not None and self.world > 1:
-            dist.all_gather_into_tensor(self.gathered, self.partials, group=self.group)
+            import torch
+            # Eager steps wait for the all-gather on the host under the watchdog; a step being
+            # captured into a CUDA graph cannot wait on the host (its replay is bounded by the
+            # process group's own timeout).
+            eager = not torch.cuda.is_current_stream_capturing()
+            work = dist.all_gather_into_tensor(self.gathered, self.partials, group=self.group,
+                                               async_op=eager)
+            if eager:
+                wait_or_abort(work, self.timeout_s, "the partials' all-gather", self.group)
         else:
             self.gathered[0].copy_(self.partials)
         fa.merge_partials(self.gathered, self.out)

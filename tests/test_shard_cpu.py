@@ -161,3 +161,63 @@ def test_peer_exchange_falls_back_to_nccl_on_every_rank_when_one_cannot_map():
             none, exchange, closed = result[r]
             assert none and exchange == "nccl"
             assert closed  # every rank releases what it holds (a failed rank its own buffer)
+
+
+def _watchdog_rank(rank, world, port, mode, result):
+    import datetime
+    import time as _time
+
+    import torch
+    import torch.distributed as dist
+
+    import fusor_attn as fa
+    from fusor_attn.shard import wait_or_abort
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    mine = torch.full((3,), float(rank))
+    out = torch.zeros(3 * world)
+    wait_or_abort(dist.all_gather_into_tensor(out, mine, async_op=True), 5.0, "step 1")
+    ok = out.tolist() == [float(r) for r in range(world) for _ in range(3)]
+    if rank == world - 1:
+        # this rank leaves between steps (none of its collectives in flight), at once or after
+        # stalling longer than the others' watchdog
+        if mode == "stalls":
+            _time.sleep(4.0)
+        result[rank] = ("left", ok)
+        os._exit(0)
+    start = _time.monotonic()
+    try:
+        wait_or_abort(dist.all_gather_into_tensor(out, mine, async_op=True), 1.5, "step 2")
+        result[rank] = ("no error", ok, _time.monotonic() - start)
+    except fa.FaError as e:
+        result[rank] = (e.code, ok, _time.monotonic() - start)
+    os._exit(0)
+
+
+@pytest.mark.parametrize("mode", ["exits", "stalls"])
+def test_exchange_watchdog_ends_a_step_whose_rank_left(mode):
+    """The NCCL exchange's host-side watchdog (wait_or_abort), on gloo ranks: after a step every
+    rank completes, the last rank leaves (at once, or after stalling past the others' 1.5 s
+    limit); the other ranks' next collective ends with FaError(ERR_TIMEOUT) and an aborted group,
+    within seconds instead of the process group's 60 s timeout."""
+    import torch.multiprocessing as mp
+
+    import fusor_attn as fa
+    world = 3
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as manager:
+        result = manager.dict()
+        port = free_port()
+        procs = [ctx.Process(target=_watchdog_rank, args=(r, world, port, mode, result))
+                 for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(120)
+            assert p.exitcode == 0
+        assert result[world - 1] == ("left", True)
+        for r in range(world - 1):
+            code, ok, waited = result[r]
+            assert ok and code == fa.ERR_TIMEOUT, result[r]
+            assert waited < 30.0, result[r]
