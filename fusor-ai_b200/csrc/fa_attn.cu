@@ -1203,21 +1203,23 @@ int check_batch(fa_kvcache* const* caches, const fa_span* spans, int32_t batch, 
 }
 
 // The chunk length, in tiles, of a batch decode on the split-KV kernel: the one of least
-// modelled time among 8..64 tiles. The CTAs run in waves of the SMs' resident slots, the units of
-// a length spread evenly over them. A wave is bound both by its bytes at the HBM rate (a) and by
-// its longest chunk at one CTA's own streaming rate, two stages of K and V in flight (b); the two
-// overlap only in part, so a wave takes cbrt(a^3 + b^3), and a launch 10 us more. Fitted on B200
-// to a GPU's share of C3 at 1, 2, 4 and 8 GPUs (64, 32, 16 and 8 sequences, f32, head_dim 128;
-// sixteen fixed lengths of 16..64 tiles each, three repetitions): 6.9 TB/s, 32.8 GB/s per CTA
-// (one 32 KB tile a microsecond); it predicts the 64 timings within 6 % (rms) and its choice runs
-// within 3 % of the fastest length at every size. The fixed floor of 32 tiles it replaces left
-// 16 sequences in 1.37 waves, 115 us against 97 us; lengths whose last wave is barely begun
-// (1.05, 1.14 and 2.25 waves) are the slowest.
+// modelled time among 16..64 tiles. The CTAs run in waves of the SMs' resident slots, the units
+// of a length spread evenly over them. A wave is bound both by its bytes at the HBM rate (a) and
+// by its longest chunk at one CTA's own streaming rate, two stages of K and V in flight (b); the
+// two overlap only in part, so a wave takes cbrt(a^3 + b^3), plus 2 us. Fitted on B200 to a
+// GPU's share of C3 at 1, 2, 4 and 8 GPUs (64, 32, 16 and 8 sequences, f32, head_dim 128;
+// lengths of 8..64 tiles): 6.9 TB/s, 32.8 GB/s per CTA (one 32 KB tile a microsecond). Against
+// eight lengths timed in interleaved rounds on one GPU, its choice (63, 46, 47 and 22 tiles) runs
+// within 2 % of the fastest at every size; the fixed floor of 32 tiles it replaces left 16
+// sequences in 1.37 waves (114 us against 95 us), and lengths whose last wave is barely begun
+// (1.05, 1.14 and 2.25 waves) are the slowest. Below 16 tiles the CTAs' fixed costs dominate
+// (9 tiles: 367 us for 64 sequences, against 340-346 us for 22-63).
 int batch_chunk_tiles(const fa_kvcache* c0, const Plan& base, const std::vector<fa::Runs>& runs,
                       int batch, int tile, int kt) {
-  constexpr int kMinTiles = 8, kMaxTiles = 64;
+  constexpr int kMinTiles = 16, kMaxTiles = 64;
   constexpr double kHbmTilesPerUs = 210.0;  // the whole GPU, reading (32 KB tiles)
   constexpr double kCtaTilesPerUs = 1.0;    // one CTA
+  constexpr double kWaveUs = 2.0;
   fa::AttendLaunch probe{kt, base.g, true, nullptr, nullptr, 0};
   const int resident = attend_resident_d(c0->head_dim, probe);
   const int64_t slots = int64_t(std::max(c0->dev->sms, 1)) * std::max(resident, 1);
@@ -1239,7 +1241,9 @@ int batch_chunk_tiles(const fa_kvcache* c0, const Plan& base, const std::vector<
     units *= base.kv_groups;
     const double per_unit = tiles_total / double(units);
     const double b3 = std::pow(t / kCtaTilesPerUs, 3.0);
-    auto wave = [&](int64_t n) { return std::cbrt(std::pow(n * per_unit / kHbmTilesPerUs, 3.0) + b3); };
+    auto wave = [&](int64_t n) {
+      return std::cbrt(std::pow(n * per_unit / kHbmTilesPerUs, 3.0) + b3) + kWaveUs;
+    };
     const int64_t full = units / slots, rest = units % slots;
     const double us = double(full) * wave(slots) + (rest > 0 ? wave(rest) : 0.0);
     if (us < best_us * (1.0 - 1e-9)) {
