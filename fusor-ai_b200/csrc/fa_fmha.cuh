@@ -307,10 +307,19 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
                           (kp >= runs.b0 && kp + BN <= runs.b0 + runs.n0) ||
                           (kp >= runs.b1 && kp + BN <= runs.b1 + runs.n1);
       if (!all_in) mask_scores<BN>(runs, kp, s);
-      float mx = -INFINITY;
+      // the tile's max in four independent chains of three-input maxima (the chain is on the
+      // critical path of every tile: one dependent maximum per key took a quarter of it)
+      static_assert(BN % 8 == 0, "the max chains take 8 keys a step");
+      float mx0 = fmax3(s[0], s[1], -INFINITY), mx1 = fmax3(s[2], s[3], -INFINITY);
+      float mx2 = fmax3(s[4], s[5], -INFINITY), mx3 = fmax3(s[6], s[7], -INFINITY);
 #pragma unroll
-      for (int c = 0; c < BN; ++c) mx = fmaxf(mx, s[c]);
-      const float m_tile = mx * a.scale_log2;  // -inf stays -inf
+      for (int c = 8; c < BN; c += 8) {
+        mx0 = fmax3(mx0, s[c], s[c + 1]);
+        mx1 = fmax3(mx1, s[c + 2], s[c + 3]);
+        mx2 = fmax3(mx2, s[c + 4], s[c + 5]);
+        mx3 = fmax3(mx3, s[c + 6], s[c + 7]);
+      }
+      const float m_tile = fmax3(mx0, mx1, fmaxf(mx2, mx3)) * a.scale_log2;  // -inf stays -inf
       // Lazy rescale: move the reference max only when the tile's max exceeds it by 2^8 (the
       // first finite max just sets it: nothing has accumulated for the row yet).
       float alpha = 1.0f;
@@ -339,26 +348,36 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
       const float ms = m_used == -INFINITY ? 0.0f : m_used;
       float sum = 0.0f;
       if constexpr (kTf32) {
+        float sums[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // independent chains
 #pragma unroll
         for (int c = 0; c < BN; ++c) {
           const float p = exp2_approx(fmaf(s[c], a.scale_log2, -ms));
-          sum += p;
+          sums[c & 3] += p;
           sreg[c] = tc::round_tf32(p);
         }
+        sum = (sums[0] + sums[1]) + (sums[2] + sums[3]);
 #pragma unroll
         for (int c = 0; c < BN / 32; ++c)
           tc::tmem_st32(lane_base + b * S::kSCols + c * 32,
                         *reinterpret_cast<const uint32_t(*)[32]>(&sreg[c * 32]));
       } else {
         // pairs of probabilities packed in place: sreg[c / 2] is written only after s[c] and
-        // s[c + 1] are read
+        // s[c + 1] are read; paired FFMA/FADD, the sums in two independent chains
+        const float2 scale2 = make_float2(a.scale_log2, a.scale_log2);
+        const float2 neg2 = make_float2(-ms, -ms);
+        float2 sum2a = make_float2(0.0f, 0.0f), sum2b = make_float2(0.0f, 0.0f);
 #pragma unroll
-        for (int c = 0; c < BN; c += 2) {
-          const float p0 = exp2_approx(fmaf(s[c], a.scale_log2, -ms));
-          const float p1 = exp2_approx(fmaf(s[c + 1], a.scale_log2, -ms));
-          sum += p0 + p1;
-          sreg[c / 2] = tc::pack_bf16(p0, p1);
+        for (int c = 0; c < BN; c += 4) {
+          const float2 x0 = __ffma2_rn(make_float2(s[c], s[c + 1]), scale2, neg2);
+          const float2 x1 = __ffma2_rn(make_float2(s[c + 2], s[c + 3]), scale2, neg2);
+          const float2 p0 = make_float2(exp2_approx(x0.x), exp2_approx(x0.y));
+          const float2 p1 = make_float2(exp2_approx(x1.x), exp2_approx(x1.y));
+          sum2a = __fadd2_rn(sum2a, p0);
+          sum2b = __fadd2_rn(sum2b, p1);
+          sreg[c / 2] = tc::pack_bf16(p0.x, p0.y);
+          sreg[c / 2 + 1] = tc::pack_bf16(p1.x, p1.y);
         }
+        sum = (sum2a.x + sum2a.y) + (sum2b.x + sum2b.y);
 #pragma unroll
         for (int c = 0; c < BN / 64; ++c)
           tc::tmem_st32(lane_base + b * S::kSCols + c * 32,
