@@ -14,7 +14,8 @@
 //               by more than 2^8, FA4's trick), writes P back into the S buffer (bf16 pairs, or
 //               tf32) and finally normalises O and stores it.
 // The MMA order S_0, S_1, PV_0, S_2, PV_1, ... keeps the tensor core on S_{j+1} while the
-// softmax works on S_j.
+// softmax works on S_j (the lookahead and the buffer and stage counts are parameters of the
+// shape: FmhaShape).
 //
 // T = __nv_bfloat16 runs kind::f16 (bf16 operands, f32 accumulation); T = float runs kind::tf32
 // on f32 data (the f32-I/O path).
@@ -37,19 +38,25 @@ struct FmhaShape {
   static constexpr int kBlock = 128 / kElem;                   // elements per swizzled 128 B row
   static constexpr int kDBlocks = D / kBlock;
   static constexpr int kKStep = 32 / kElem;                    // elements per MMA K step
-  static constexpr int kStages = 2;
+  // S (P) buffers in TMEM, S products ahead of P.V, K and V tiles in shared memory. Measured on
+  // B200 over 64-key tiles (the Qwen3.5 prefill at head_dim 256, the f32 prefill on tf32): three
+  // S buffers with three K stages, or a third K or V stage alone, ran 1-2 % slower than this.
+  static constexpr int kSBufs = 2;
+  static constexpr int kLookahead = kSBufs - 1;
+  static constexpr int kKStages = 2;
+  static constexpr int kVStages = 2;
   static constexpr int kQBytes = BM * D * kElem;
   static constexpr int kKVBytes = BN * D * kElem;
   static constexpr int kSCols = BN;                            // TMEM columns of one S buffer
   static constexpr int kOCol = 256;                            // TMEM column of O
   static constexpr int kPCols = kTf32 ? BN : BN / 2;           // TMEM columns of P
-  static constexpr size_t kSmemUsed =
-      size_t(kQBytes) + size_t(kStages) * 2 * kKVBytes + 1024 /* alignment */ + 256 /* bars */;
+  static constexpr size_t kSmemUsed = size_t(kQBytes) + size_t(kKStages + kVStages) * kKVBytes +
+                                      1024 /* alignment */ + 256 /* bars */;
   // At least 120 KB so that one CTA holds an SM: each CTA allocates all 512 TMEM columns.
   static constexpr size_t kSmemBytes = kSmemUsed > 122880 ? kSmemUsed : 122880;
   static_assert(D % kBlock == 0, "head_dim a multiple of the swizzle block");
   static_assert(BN % 32 == 0 && D % 32 == 0, "TMEM loads of 32 columns");
-  static_assert(kOCol + D <= 512 && 2 * kSCols <= kOCol, "two S buffers and O in 512 columns");
+  static_assert(kOCol + D <= 512 && kSBufs * kSCols <= kOCol, "the S buffers and O in 512 columns");
   static_assert(kSmemUsed <= 227 * 1024, "shared memory of one CTA");
 };
 
@@ -102,25 +109,26 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
   // 1024-byte alignment for the 128-byte swizzle atoms.
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int NB = S::kSBufs, L = S::kLookahead, KS = S::kKStages, VS = S::kVStages;
   unsigned char* sQ = smem;
   unsigned char* sK = sQ + S::kQBytes;
-  unsigned char* sV = sK + S::kStages * S::kKVBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + S::kStages * S::kKVBytes);
+  unsigned char* sV = sK + KS * S::kKVBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + VS * S::kKVBytes);
   uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
-  uint64_t* k_empty = k_full + S::kStages;
-  uint64_t* v_full = k_empty + S::kStages;
-  uint64_t* v_empty = v_full + S::kStages;
-  uint64_t* s_full = v_empty + S::kStages;  // [2]
-  uint64_t* p_full = s_full + 2;            // [2]
-  uint64_t* o_done = p_full + 2;
-  uint64_t* o_final = o_done + 1;  // the last P.V product has completed
+  uint64_t* k_full = bars + 1;       // [KS]
+  uint64_t* k_empty = k_full + KS;   // [KS]
+  uint64_t* v_full = k_empty + KS;   // [VS]
+  uint64_t* v_empty = v_full + VS;   // [VS]
+  uint64_t* s_full = v_empty + VS;   // [NB]
+  uint64_t* p_full = s_full + NB;    // [NB]
+  uint64_t* o_done = p_full + NB;    // [NB]: P.V of tile j completes phase j / NB of o_done[j % NB]
+  uint64_t* o_final = o_done + NB;   // the last P.V product has completed
   uint64_t* mma_drained = o_final + 1;
   // tf32: Q, K and V tiles rounded to tf32 in place by warps 2-3 before the MMA reads them
   uint64_t* q_conv = mma_drained + 1;
-  uint64_t* k_conv = q_conv + 1;
-  uint64_t* v_conv = k_conv + S::kStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(v_conv + S::kStages);
+  uint64_t* k_conv = q_conv + 1;     // [KS]
+  uint64_t* v_conv = k_conv + KS;    // [VS]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(v_conv + VS);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int head = blockIdx.y;
@@ -145,24 +153,24 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < S::kStages; ++s) {
-      mbar_init(&k_full[s], 1);
-      mbar_init(&k_empty[s], 1);
-      mbar_init(&v_full[s], 1);
-      mbar_init(&v_empty[s], 1);
+    for (int st = 0; st < KS; ++st) {
+      mbar_init(&k_full[st], 1);
+      mbar_init(&k_empty[st], 1);
+      mbar_init(&k_conv[st], kConvThreads);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int st = 0; st < VS; ++st) {
+      mbar_init(&v_full[st], 1);
+      mbar_init(&v_empty[st], 1);
+      mbar_init(&v_conv[st], kConvThreads);
+    }
+    for (int b = 0; b < NB; ++b) {
       mbar_init(&s_full[b], 1);
       mbar_init(&p_full[b], 128);
+      mbar_init(&o_done[b], 1);
     }
-    mbar_init(o_done, 1);
     mbar_init(o_final, 1);
     mbar_init(mma_drained, 1);
     mbar_init(q_conv, kConvThreads);
-    for (int st = 0; st < S::kStages; ++st) {
-      mbar_init(&k_conv[st], kConvThreads);
-      mbar_init(&v_conv[st], kConvThreads);
-    }
     mbar_fence_init();
   }
   if (warp == 1) tc::tmem_alloc(tmem_slot, 512);
@@ -183,30 +191,40 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
         tc::tma_load_3d(sQ + db * BM * 128, &q_map, db * S::kBlock, qy, head, q_full);
       const int kz = a.kv_layer_base + kv;
       const int ky0 = image * a.kv_row_base_per_image;
-      int issued = 0;
-      for (int j = 0; j < n_tiles; ++j) {
-        const int st = j % S::kStages;
-        const uint32_t ph = ((j / S::kStages) & 1) ^ 1;
-        const int ky = ky0 + (t0 + j) * BN;
-        if (!mbar_wait(&k_empty[st], ph, a.err)) break;
+      // In the order the MMAs take them: K_0 .. K_L, then V_j and K_{j+L+1} for each j.
+      auto load_k = [&](int j) {
+        const int st = j % KS;
+        if (!mbar_wait(&k_empty[st], ((j / KS) & 1) ^ 1, a.err)) return false;
         mbar_arrive_expect_tx(&k_full[st], S::kKVBytes);
         for (int db = 0; db < S::kDBlocks; ++db)
-          tc::tma_load_3d(sK + st * S::kKVBytes + db * BN * 128, &k_map, db * S::kBlock, ky, kz,
-                          &k_full[st]);
-        if (!mbar_wait(&v_empty[st], ph, a.err)) break;
+          tc::tma_load_3d(sK + st * S::kKVBytes + db * BN * 128, &k_map, db * S::kBlock,
+                          ky0 + (t0 + j) * BN, kz, &k_full[st]);
+        return true;
+      };
+      auto load_v = [&](int j) {
+        const int st = j % VS;
+        if (!mbar_wait(&v_empty[st], ((j / VS) & 1) ^ 1, a.err)) return false;
         mbar_arrive_expect_tx(&v_full[st], S::kKVBytes);
         for (int db = 0; db < S::kDBlocks; ++db)
-          tc::tma_load_3d(sV + st * S::kKVBytes + db * BN * 128, &v_map, db * S::kBlock, ky, kz,
-                          &v_full[st]);
-        issued = j + 1;
+          tc::tma_load_3d(sV + st * S::kKVBytes + db * BN * 128, &v_map, db * S::kBlock,
+                          ky0 + (t0 + j) * BN, kz, &v_full[st]);
+        return true;
+      };
+      int k_issued = 0, v_issued = 0;
+      bool ok = true;
+      for (int j = 0; ok && j <= L && j < n_tiles; ++j)
+        if ((ok = load_k(j))) k_issued = j + 1;
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        if ((ok = load_v(j))) v_issued = j + 1;
+        if (ok && j + L + 1 < n_tiles && (ok = load_k(j + L + 1))) k_issued = j + L + 2;
       }
       // The loads still in flight land before the CTA may exit (they have, unless a wait gave
       // up: every full barrier of the last stages completes once its bytes arrive).
       mbar_wait(q_full, 0, a.err);
-      for (int j = max(0, issued - S::kStages); j < issued; ++j) {
-        mbar_wait(&k_full[j % S::kStages], (j / S::kStages) & 1, a.err);
-        mbar_wait(&v_full[j % S::kStages], (j / S::kStages) & 1, a.err);
-      }
+      for (int j = max(0, k_issued - KS); j < k_issued; ++j)
+        mbar_wait(&k_full[j % KS], (j / KS) & 1, a.err);
+      for (int j = max(0, v_issued - VS); j < v_issued; ++j)
+        mbar_wait(&v_full[j % VS], (j / VS) & 1, a.err);
     }
   } else if (warp == 1) {
     // ---- MMA issuer ----------------------------------------------------------------------
@@ -214,10 +232,10 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
       const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV);
       bool ok = mbar_wait(kTf32 ? q_conv : q_full, 0, a.err);
       auto issue_pv = [&](int j) {
-        const int st = j % S::kStages;
-        const int b = j & 1;
-        if (!mbar_wait(&p_full[b], (j >> 1) & 1, a.err)) return false;
-        if (!mbar_wait(kTf32 ? &v_conv[st] : &v_full[st], (j / S::kStages) & 1, a.err)) return false;
+        const int st = j % VS;
+        const int b = j % NB;
+        if (!mbar_wait(&p_full[b], (j / NB) & 1, a.err)) return false;
+        if (!mbar_wait(kTf32 ? &v_conv[st] : &v_full[st], (j / VS) & 1, a.err)) return false;
         tc::fence_after_sync();
         const uint32_t p_tmem = tmem + uint32_t(b * S::kSCols);
 #pragma unroll
@@ -233,28 +251,32 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
           tc::mma_ts<kTf32>(tmem + S::kOCol, p_tmem + k * 8, vd, kIdescPV,
                             (j > 0 || k > 0) ? 1u : 0u);
         }
-        tc::commit(o_done);
+        tc::commit(&o_done[b]);
         tc::commit(&v_empty[st]);
         return true;
       };
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        const int st = j % S::kStages;
-        const int b = j & 1;
-        if (!mbar_wait(kTf32 ? &k_conv[st] : &k_full[st], (j / S::kStages) & 1, a.err)) { ok = false; break; }
-        tc::fence_after_sync();
+      // S_t into buffer t % NB, which held P_{t-NB}: its P.V was issued the step before (the
+      // tensor core runs one thread's MMAs in issue order).
+      for (int t = 0; ok && t < n_tiles + L; ++t) {
+        if (t < n_tiles) {
+          const int st = t % KS;
+          const int b = t % NB;
+          if (!mbar_wait(kTf32 ? &k_conv[st] : &k_full[st], (t / KS) & 1, a.err)) { ok = false; break; }
+          tc::fence_after_sync();
 #pragma unroll
-        for (int k = 0; k < D / S::kKStep; ++k) {
-          const int db = k / (128 / 32), koff = (k % (128 / 32)) * 32;
-          const uint64_t qd = tc::smem_desc_sw128(q_base + db * BM * 128 + koff, 16, 1024);
-          const uint64_t kd =
-              tc::smem_desc_sw128(k_base + st * S::kKVBytes + db * BN * 128 + koff, 16, 1024);
-          tc::mma_ss<kTf32>(tmem + b * S::kSCols, qd, kd, kIdescQK, k > 0 ? 1u : 0u);
+          for (int k = 0; k < D / S::kKStep; ++k) {
+            const int db = k / (128 / 32), koff = (k % (128 / 32)) * 32;
+            const uint64_t qd = tc::smem_desc_sw128(q_base + db * BM * 128 + koff, 16, 1024);
+            const uint64_t kd =
+                tc::smem_desc_sw128(k_base + st * S::kKVBytes + db * BN * 128 + koff, 16, 1024);
+            tc::mma_ss<kTf32>(tmem + b * S::kSCols, qd, kd, kIdescQK, k > 0 ? 1u : 0u);
+          }
+          tc::commit(&s_full[b]);
+          tc::commit(&k_empty[st]);
         }
-        tc::commit(&s_full[b]);
-        tc::commit(&k_empty[st]);
-        if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+        if (t >= L && !issue_pv(t - L)) { ok = false; break; }
       }
-      if (ok && n_tiles > 0 && issue_pv(n_tiles - 1)) tc::commit(o_final);
+      if (ok && n_tiles > 0) tc::commit(o_final);
       // Every MMA this thread issued has completed before the CTA may free TMEM.
       tc::commit(mma_drained);
       mbar_wait(mma_drained, 0, a.err);
@@ -272,13 +294,20 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
         mbar_arrive(conv);
         return true;
       };
-      if (convert(q_full, q_conv, 0, sQ, S::kQBytes)) {
-        for (int j = 0; j < n_tiles; ++j) {
-          const int st = j % S::kStages;
-          const uint32_t ph = (j / S::kStages) & 1;
-          if (!convert(&k_full[st], &k_conv[st], ph, sK + st * S::kKVBytes, S::kKVBytes)) break;
-          if (!convert(&v_full[st], &v_conv[st], ph, sV + st * S::kKVBytes, S::kKVBytes)) break;
-        }
+      // in the producer's order: K_0 .. K_L, then V_j and K_{j+L+1}
+      auto conv_k = [&](int j) {
+        return convert(&k_full[j % KS], &k_conv[j % KS], (j / KS) & 1, sK + (j % KS) * S::kKVBytes,
+                       S::kKVBytes);
+      };
+      auto conv_v = [&](int j) {
+        return convert(&v_full[j % VS], &v_conv[j % VS], (j / VS) & 1, sV + (j % VS) * S::kKVBytes,
+                       S::kKVBytes);
+      };
+      bool ok = convert(q_full, q_conv, 0, sQ, S::kQBytes);
+      for (int j = 0; ok && j <= L && j < n_tiles; ++j) ok = conv_k(j);
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        ok = conv_v(j);
+        if (ok && j + L + 1 < n_tiles) ok = conv_k(j + L + 1);
       }
     }
   } else if (warp >= 4) {
@@ -291,10 +320,10 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
     float m_used = -INFINITY, l_sum = 0.0f;
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
-      const int b = j & 1;
+      const int b = j % NB;
       const int kp = (t0 + j) * BN;  // first key position of the tile
       // Every decision before a whole-warp tcgen05 instruction is made warp-uniform.
-      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[b], (j >> 1) & 1, a.err))) { ok = false; break; }
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[b], (j / NB) & 1, a.err))) { ok = false; break; }
       tc::fence_after_sync();
       uint32_t sreg[BN];
       if constexpr (BN == 128) tc::tmem_ld128_wait(lane_base + b * S::kSCols, sreg);
@@ -331,9 +360,14 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
         // O holds PV of tiles < j: wait for PV_{j-1}, then rescale the warp's rows.
         l_sum *= alpha;
         // A parity wait names only the current or the previous phase of a barrier. Here it is
-        // unambiguous: S_j has completed (its commit tracks every earlier MMA, PV_{j-2} among
-        // them), so o_done is in the phase of PV_{j-1} or just past it.
-        if (!__all_sync(0xffffffffu, mbar_wait(o_done, (j - 1) & 1, a.err))) { ok = false; break; }
+        // unambiguous: S_j has completed, and its commit tracks every MMA issued before it,
+        // P.V_{j-NB} among them; the barrier of P.V_{j-1}, o_done[(j-1) % NB], was last
+        // completed by P.V_{j-1-NB}, so its phase (j-1) / NB is P.V_{j-1}'s own.
+        const int jb = (j - 1) % NB;
+        if (!__all_sync(0xffffffffu, mbar_wait(&o_done[jb], ((j - 1) / NB) & 1, a.err))) {
+          ok = false;
+          break;
+        }
         tc::fence_after_sync();
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
