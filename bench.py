@@ -843,7 +843,7 @@ class C4Sharded(Workload):
         dist.broadcast(first, 0)
         same = bool(torch.equal(out, first))
         p = {"checked": "the merged decode row on rank 0, every head; every rank's merged row "
-                        "against rank 0's"}
+                        "against rank 0's", "ok": same}
         if self.rank == 0:
             k, v, _ = decode_inputs(torch, self.shape, self.position)
             want = oracle_decode(self.fa, self.shape, self.position, k.cpu().numpy(),
@@ -851,6 +851,7 @@ class C4Sharded(Workload):
                                  self.angles.cpu().numpy(), threads)
             del k, v
             p.update(parity_result(out.cpu().numpy(), want, TOL_F32, p["checked"]))
+            p["ok"] = p["ok"] and same
         p["ranks_agree"] = same
         if self.e2e_ran:
             p["e2e_vs_device_max_abs"] = sci(np.abs(self.h_out.numpy().reshape(1, -1)
@@ -1092,10 +1093,13 @@ def merge_parity(dist, p):
         vals = [q[key] for q in parts if key in q]
         if vals:
             merged[key] = "non-finite" if any(isinstance(v, str) for v in vals) else max(vals)
-    for key in ("tol", "rel_tol", "ranks_agree"):
+    for key in ("tol", "rel_tol"):
         vals = [q[key] for q in parts if key in q]
         if vals:
-            merged[key] = vals[0] if key == "tol" else all(vals)
+            merged[key] = vals[0]
+    vals = [q["ranks_agree"] for q in parts if "ranks_agree" in q]
+    if vals:
+        merged["ranks_agree"] = all(vals)
     return merged
 
 

@@ -1827,11 +1827,13 @@ int fa_peer_free(void* ptr) {
   return FA_OK;
 }
 
-int fa_peer_reset(void* own_buffer, void* stream) {
+int fa_peer_reset(void* own_buffer, uint64_t buffer_bytes, void* stream) {
   if (own_buffer == nullptr) return fail(FA_ERR_ARG, "null buffer");
+  if (buffer_bytes < uint64_t(fa::kPeerHeaderBytes)) return fail(FA_ERR_ARG, "a buffer below its header");
   FA_PTR(own_buffer, current_device());
   auto s = static_cast<cudaStream_t>(stream);
-  FA_CUDA(cudaMemsetAsync(own_buffer, 0, fa::kPeerHeaderBytes, s), "clear exchange header");
+  // the step counter and every stamped word: no word of an earlier step can match a new one
+  FA_CUDA(cudaMemsetAsync(own_buffer, 0, buffer_bytes, s), "clear exchange buffer");
   FA_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
   return FA_OK;
 }

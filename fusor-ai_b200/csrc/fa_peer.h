@@ -7,8 +7,7 @@
 namespace fa {
 
 constexpr int kMaxPeers = 8;            // ranks of one box
-constexpr int kPeerHeaderBytes = 256;   // the step counter, then the flags
-constexpr int kPeerFlagsOffset = 128;   // flags [2][kMaxPeers] of u32
+constexpr int kPeerHeaderBytes = 256;   // the step counter, then the stamped words
 
 struct PeerMergeArgs {
   unsigned char* bufs[kMaxPeers];  // every rank's buffer as mapped in this process

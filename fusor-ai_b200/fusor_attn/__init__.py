@@ -134,7 +134,7 @@ SIGNATURES = {
     "fa_peer_close": (C.c_int, [_P]),
     "fa_peer_free": (C.c_int, [_P]),
     "fa_exchange_merge": (C.c_int, [_P, C.c_uint64, _I32, _I32, _I32, _I32, _P, _P, _P]),
-    "fa_peer_reset": (C.c_int, [_P, _P]),
+    "fa_peer_reset": (C.c_int, [_P, C.c_uint64, _P]),
     "fa_attention_input_projected": (C.c_int, [_P, _I32, _P, _I32, _P, _P, _P, _P, _I64, _P, _P,
                                                _I64, _P]),
     "fa_attention_input_projected_batch": (C.c_int, [_P, _P, _I32, _I32, _I32, _P, _P, _P, _P,
@@ -612,7 +612,7 @@ class PeerExchange:
         if int(flag.item()) == 0:
             return False
         dist.barrier(group=group)
-        _check(lib().fa_peer_reset(self.own, _stream()))
+        _check(lib().fa_peer_reset(self.own, self.bytes, _stream()))
         dist.barrier(group=group)
         return True
 

@@ -292,10 +292,11 @@ int fa_merge_partials(const float* partials, int32_t shards, int32_t heads, int3
  * exchange buffer of fa_peer_buffer_bytes (fa_peer_alloc: zeroed, with its CUDA IPC handle),
  * the ranks swap the handles (any host channel: a process group's all-gather of objects), and
  * each maps the others' (fa_peer_open). fa_exchange_merge then stores this rank's partials in
- * every rank's buffer, raises its flag there, waits for every rank's flag in its own (bounded:
- * FA_ERR_TIMEOUT from fa_device_status after about a second), and merges into out (heads x
- * head_dim f32) with fa_merge_partials' arithmetic. Every rank calls it once per step, in the
- * same order; the step count lives in the buffer, so a CUDA graph of the step can be replayed. */
+ * every rank's buffer, each value a 64-bit word stamped with the step, waits until every rank's
+ * words of the step are in its own (bounded: FA_ERR_TIMEOUT from fa_device_status after about a
+ * second, the late rank left out of the merge), and merges into out (heads x head_dim f32) with
+ * fa_merge_partials' arithmetic. Every rank calls it once per step, in the same order; the step
+ * count lives in the buffer, so a CUDA graph of the step can be replayed. */
 typedef struct fa_ipc_handle {
   unsigned char bytes[64];
 } fa_ipc_handle;
@@ -311,10 +312,11 @@ int fa_exchange_merge(void* const* buffers, uint64_t buffer_bytes, int32_t rank,
                       void* stream);
 /* After an exchange that gave up on a rank (FA_ERR_TIMEOUT), the ranks' step counters differ and
  * every later exchange would wait in vain: each rank synchronizes its device, the ranks meet at a
- * barrier, each clears its own buffer's step counter and flags with fa_peer_reset (which returns
- * once they are clear), and they meet at a second barrier before the next exchange. There is no
- * counterpart in the reference (one process, no exchange); it is this exchange's recovery. */
-int fa_peer_reset(void* own_buffer, void* stream);
+ * barrier, each clears its own buffer (buffer_bytes: its step counter and every stamped word)
+ * with fa_peer_reset, which returns once it is clear, and they meet at a second barrier before
+ * the next exchange. There is no counterpart in the reference (one process, no exchange); it is
+ * this exchange's recovery. */
+int fa_peer_reset(void* own_buffer, uint64_t buffer_bytes, void* stream);
 
 /* blocks::attention::attend (attention.rs:79-95) and dit::Within::attend (dit.rs:135-166): full
  * (non-causal) softmax attention of every query over every key of its image, scores scaled by

@@ -110,7 +110,7 @@ unsafe extern "C" {
     pub fn fa_exchange_merge(buffers: *const *mut c_void, buffer_bytes: u64, rank: i32, world: i32,
                              heads: i32, head_dim: i32, partials: *const f32, out: *mut f32,
                              stream: *mut c_void) -> i32;
-    pub fn fa_peer_reset(own_buffer: *mut c_void, stream: *mut c_void) -> i32;
+    pub fn fa_peer_reset(own_buffer: *mut c_void, buffer_bytes: u64, stream: *mut c_void) -> i32;
 
     // full-mask attention (DiT, conformer) and its prologue
     pub fn fa_attend_full(call: *const FaCall, out: *mut c_void, out_stride: i64,

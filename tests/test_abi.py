@@ -141,13 +141,14 @@ def test_capabilities():
 
 
 def test_peer_exchange_buffer_size_and_arguments():
-    """fa_peer_buffer_bytes: a 256-byte header (the step counter and the flags), then two halves
-    of world x heads x (head_dim + 2) f32 partials; worlds past the 8 GPUs of a box, and a
+    """fa_peer_buffer_bytes: a 256-byte header (the step counter), then two halves of world x
+    heads x (head_dim + 2) partials, each value a 64-bit word (its step stamp and its f32 bits);
+    worlds past the 8 GPUs of a box, and a
     fa_exchange_merge whose buffers are smaller than that, are refused before any launch."""
     lib = fa.lib()
     n = C.c_uint64()
     assert lib.fa_peer_buffer_bytes(8, 16, 128, C.byref(n)) == fa.OK
-    assert n.value == 256 + 2 * 8 * 16 * 130 * 4
+    assert n.value == 256 + 2 * 8 * 16 * 130 * 8  # 64-bit stamped words
     assert lib.fa_peer_buffer_bytes(9, 16, 128, C.byref(n)) == fa.ERR_ARG
     assert lib.fa_peer_buffer_bytes(0, 16, 128, C.byref(n)) == fa.ERR_ARG
     bufs = (C.c_void_p * 2)(1, 2)

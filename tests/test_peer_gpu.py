@@ -147,12 +147,12 @@ def test_exchange_wait_gives_up_on_a_rank_that_never_publishes():
 
 
 def test_exchange_leaves_out_a_late_rank_and_resumes_after_a_reset():
-    """One process, one GPU, rank 0 of a 2-rank exchange. (1) Rank 1's slot holds partials of an
-    earlier step (planted, with a dominant max) but its flag never carries this step: the wait
-    gives up, and the merge leaves rank 1 out instead of merging the stale partials. (2) After
-    fa_peer_reset of the buffer the step counter starts again: with rank 1's partials and flag
-    for step 1 in place beforehand (as rank 1's own kernel would have stored them), the next
-    exchange waits for nothing and merges both ranks."""
+    """One process, one GPU, rank 0 of a 2-rank exchange. (1) Rank 1's slot holds words of an
+    earlier step (planted, with a dominant max) that never carry this step's stamp: the wait gives
+    up, and the merge leaves rank 1 out instead of merging the stale partials. (2) After
+    fa_peer_reset the step counter starts again: with rank 1's words for step 1 in place
+    beforehand (as rank 1's own kernel would have stored them), the next exchange waits for
+    nothing and merges both ranks."""
     import ctypes as C
 
     import torch
@@ -160,48 +160,47 @@ def test_exchange_leaves_out_a_late_rank_and_resumes_after_a_reset():
     import fusor_attn as fa
     assert torch.cuda.is_available()
     lib = fa.lib()
-    heads, d, world, max_peers = 4, 64, 2, 8
+    heads, d, world = 4, 64, 2
     pitch = heads * (d + 2)
     nbytes = C.c_uint64()
     assert lib.fa_peer_buffer_bytes(world, heads, d, C.byref(nbytes)) == fa.OK
     own, handle = C.c_void_p(), (C.c_ubyte * 64)()
     assert lib.fa_peer_alloc(nbytes.value, C.byref(own), handle) == fa.OK
     try:
-        # the buffer viewed as floats: header (64 words), then [half][rank][heads][d + 2]
-        view = _float_view(torch, own.value, int(nbytes.value) // 4)
+        # the buffer as 64-bit words: the 256-byte header, then [half][rank][heads][d + 2]
+        words = _view(torch, own.value, int(nbytes.value) // 8, "<i8")
         gen = torch.Generator("cuda").manual_seed(9)
 
-        def partials_of(seed_shift):
+        def partials_of(shift):
             p = torch.empty((heads, d + 2), device="cuda")
-            p[:, 0] = torch.rand((heads,), device="cuda", generator=gen) * 4 - 2 + seed_shift
+            p[:, 0] = torch.rand((heads,), device="cuda", generator=gen) * 4 - 2 + shift
             p[:, 1] = torch.rand((heads,), device="cuda", generator=gen) * 2 + 1
             p[:, 2:] = torch.randn((heads, d), device="cuda", generator=gen)
             return p
 
-        def slot(half, rank):
-            start = 64 + (half * world + rank) * pitch
-            return view[start:start + pitch].view(heads, d + 2)
+        def plant(half, rank, partials, step):
+            bits = partials.reshape(-1).view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+            start = 32 + (half * world + rank) * pitch
+            words[start:start + pitch] = (step << 32) | bits
 
         mine = partials_of(0.0)
-        stale = partials_of(20.0)  # would dominate every head if merged
-        slot(1, 1).copy_(stale)    # step 1 uses half 1
+        plant(1, 1, partials_of(20.0), 3)  # step 1 uses half 1; these words are of step 3
         out = torch.zeros((heads, d), device="cuda")
-        bufs = (C.c_void_p * world)(own.value, own.value)  # rank 1's buffer: never read here
+        bufs = (C.c_void_p * world)(own.value, own.value)  # rank 1's buffer: written, never read
         stream = fa._stream(None)
+        torch.cuda.synchronize()
         assert lib.fa_exchange_merge(bufs, nbytes.value, 0, world, heads, d, fa._dptr(mine),
                                      fa._dptr(out), stream) == fa.OK
         with pytest.raises(fa.FaError) as err:
             fa.device_status()
         assert err.value.code == fa.ERR_TIMEOUT
         assert torch.allclose(out, mine[:, 2:] / mine[:, 1:2], rtol=1e-6, atol=1e-6)
-        # the reset: counter and flags cleared
-        assert lib.fa_peer_reset(own, stream) == fa.OK
-        assert float(view[:64].abs().max()) == 0.0
-        # rank 1's step-1 publication in place, then rank 0's step 1
+        # the reset: the counter and every word cleared
+        assert lib.fa_peer_reset(own, nbytes.value, stream) == fa.OK
+        assert int(words.abs().max()) == 0
+        # rank 1's step-1 words in place, then rank 0's step 1
         theirs = partials_of(0.5)
-        slot(1, 1).copy_(theirs)
-        flags = view[32:32 + 2 * max_peers].view(torch.int32)
-        flags[1 * max_peers + 1] = 1
+        plant(1, 1, theirs, 1)
         torch.cuda.synchronize()
         out.zero_()
         assert lib.fa_exchange_merge(bufs, nbytes.value, 0, world, heads, d, fa._dptr(mine),
@@ -217,9 +216,9 @@ def test_exchange_leaves_out_a_late_rank_and_resumes_after_a_reset():
         lib.fa_peer_free(own)
 
 
-def _float_view(torch, address, words):
-    """A float32 tensor over `words` words of device memory at `address` (not owned)."""
+def _view(torch, address, count, typestr):
+    """A tensor over `count` elements of device memory at `address` (not owned)."""
     class _Cuda:
-        __cuda_array_interface__ = {"shape": (words,), "typestr": "<f4", "data": (address, False),
+        __cuda_array_interface__ = {"shape": (count,), "typestr": typestr, "data": (address, False),
                                     "version": 3, "strides": None}
     return torch.as_tensor(_Cuda(), device="cuda")
