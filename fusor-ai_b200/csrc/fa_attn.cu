@@ -1782,9 +1782,10 @@ int fa_merge_partials(const float* partials, int32_t shards, int32_t heads, int3
 
 int fa_peer_buffer_bytes(int32_t world, int32_t heads, int32_t head_dim, uint64_t* bytes) {
   if (bytes == nullptr) return fail(FA_ERR_ARG, "null bytes");
-  if (world < 1 || world > fa::kMaxPeers || heads < 1 || head_dim < 1 || head_dim > 1024)
-    return fail(FA_ERR_ARG, "world %d (1..%d), heads %d, head_dim %d", world, fa::kMaxPeers,
-                heads, head_dim);
+  if (world < 1 || world > fa::kMaxPeers || heads < 1 || heads > fa::kMaxPeerHeads ||
+      head_dim < 1 || head_dim > 1024)
+    return fail(FA_ERR_ARG, "world %d (1..%d), heads %d (1..%d), head_dim %d", world,
+                fa::kMaxPeers, heads, fa::kMaxPeerHeads, head_dim);
   *bytes = fa::peer_buffer_bytes(world, heads, head_dim);
   return FA_OK;
 }

@@ -7,7 +7,8 @@
 namespace fa {
 
 constexpr int kMaxPeers = 8;            // ranks of one box
-constexpr int kPeerHeaderBytes = 256;   // the step counter, then the stamped words
+constexpr int kPeerHeaderBytes = 256;   // a step counter per query head, then the stamped words
+constexpr int kMaxPeerHeads = kPeerHeaderBytes / 4;
 
 struct PeerMergeArgs {
   unsigned char* bufs[kMaxPeers];  // every rank's buffer as mapped in this process

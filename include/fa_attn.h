@@ -300,7 +300,7 @@ int fa_merge_partials(const float* partials, int32_t shards, int32_t heads, int3
 typedef struct fa_ipc_handle {
   unsigned char bytes[64];
 } fa_ipc_handle;
-int fa_peer_buffer_bytes(int32_t world, int32_t heads, int32_t head_dim, uint64_t* bytes);
+int fa_peer_buffer_bytes(int32_t world, int32_t heads, int32_t head_dim, uint64_t* bytes);  /* heads <= 64 */
 int fa_peer_alloc(uint64_t bytes, void** ptr, fa_ipc_handle* handle);
 int fa_peer_open(const fa_ipc_handle* handle, void** ptr);
 int fa_peer_close(void* ptr); /* a mapping made by fa_peer_open */
