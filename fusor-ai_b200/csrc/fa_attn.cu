@@ -48,7 +48,21 @@ int cuda_fail(cudaError_t e, const char* what) {
     if (e_ != cudaSuccess) return cuda_fail(e_, what); \
   } while (0)
 
-bool supported_head_dim(int d) { return d == 16 || d == 32 || d == 64 || d == 128 || d == 256; }
+bool exact_head_dim(int d) { return d == 16 || d == 32 || d == 64 || d == 128 || d == 256; }
+
+// Head dims with a kernel: the powers of two 16..256, and between 32 and 256 any whole number of
+// the attention kernels' 16-byte vectors (4 f32 or 8 bf16 elements), which run on the next wider
+// kernel with the lanes past the head idle (kronos' 52, iris' 80).
+bool supported_head_dim(int d, int dtype) {
+  if (exact_head_dim(d)) return true;
+  return d > 32 && d <= 256 && d % (dtype == FA_BF16 ? 8 : 4) == 0;
+}
+
+// The split-KV kernel's D for a head_dim: itself, or the next power of two (PAD).
+int kernel_dim(int d) {
+  if (exact_head_dim(d)) return d;
+  return d <= 64 ? 64 : d <= 128 ? 128 : 256;
+}
 
 // Per-device state: the SM count and the device error word.
 struct Device {
@@ -303,8 +317,10 @@ struct Plan {
 #define FA_SPAN_MIN_CHUNK_TILES 16
 #endif
 
-int attend_resident_d(int head_dim, const fa::AttendLaunch& l) {
-  switch (head_dim) {
+int attend_resident_d(int head_dim, const fa::AttendLaunch& launch) {
+  fa::AttendLaunch l = launch;
+  l.pad = kernel_dim(head_dim) != head_dim;
+  switch (kernel_dim(head_dim)) {
     case 16: return fa::attend_resident<16>(l);
     case 32: return fa::attend_resident<32>(l);
     case 64: return fa::attend_resident<64>(l);
@@ -345,7 +361,7 @@ Plan plan_span(const fa_kvcache* c, int rows, int max_keys, bool split_small = t
   Plan p;
   const int group = c->heads / c->kv_heads;
   p.g = pow2_heads(group);
-  const int tile = fa::tile_keys(c->head_dim, c->dtype == FA_F32 ? fa::kKtF32 : fa::kKtBf16);
+  const int tile = fa::tile_keys(kernel_dim(c->head_dim), c->dtype == FA_F32 ? fa::kKtF32 : fa::kKtBf16);
   const int max_chunks = std::max(1, (max_keys + tile - 1) / tile);
   // A launch too small for a CTA on every SM (a short decode, C1's 1025 keys) splits each KV
   // head's query heads over more CTAs: each re-reads the KV head, from L2 at these sizes.
@@ -388,7 +404,8 @@ int ensure_work(fa_kvcache* c, size_t q_floats, size_t part_slots, size_t unused
                 cudaStream_t stream, Work* w) {
   (void)unused;
   const size_t q_bytes = align_up(q_floats * 4, 256);
-  const size_t o_bytes = align_up(part_slots * c->head_dim * 4, 256);
+  // a chunk's partial output is the kernel's D wide (kernel_dim: a padded head_dim's kernel)
+  const size_t o_bytes = align_up(part_slots * kernel_dim(c->head_dim) * 4, 256);
   const size_t ml_bytes = align_up(part_slots * 2 * 4, 256);
   if (int rc = c->work.ensure(q_bytes + o_bytes + ml_bytes, stream)) return rc;
   unsigned char* base = static_cast<unsigned char*>(c->work.ptr);
@@ -407,10 +424,13 @@ void fill_common(fa::AttendCommon* a, const fa_kvcache* c, const Plan& p) {
   a->key_stride = c->head_dim;
   a->q_scale = query_scale(c->head_dim);
   a->err = c->dev->err;
+  a->dh = c->head_dim;
 }
 
-cudaError_t launch_attend_d(int head_dim, const fa::AttendLaunch& l, cudaStream_t stream) {
-  switch (head_dim) {
+cudaError_t launch_attend_d(int head_dim, const fa::AttendLaunch& launch, cudaStream_t stream) {
+  fa::AttendLaunch l = launch;
+  l.pad = kernel_dim(head_dim) != head_dim;
+  switch (kernel_dim(head_dim)) {
     case 16: return fa::launch_attend<16>(l, stream);
     case 32: return fa::launch_attend<32>(l, stream);
     case 64: return fa::launch_attend<64>(l, stream);
@@ -807,7 +827,7 @@ const char* fa_last_error(void) { return g_last_error.c_str(); }
 int fa_capabilities(int32_t* flags, int32_t* head_dims, int32_t max_head_dims,
                     int32_t* n_head_dims) {
   static const int32_t dims[] = {16, 32, 64, 128, 256};
-  if (flags) *flags = 1 | 2 | (fa::fmha_supported(1, 128) ? 4 : 0);
+  if (flags) *flags = 1 | 2 | (fa::fmha_supported(1, 128) ? 4 : 0) | 8;
   const int n = int(sizeof dims / sizeof dims[0]);
   if (head_dims)
     for (int i = 0; i < n && i < max_head_dims; ++i) head_dims[i] = dims[i];
@@ -824,7 +844,7 @@ int fa_kvcache_create(int32_t layers, int32_t heads, int32_t kv_heads, int32_t h
                 heads, kv_heads, capacity);
   if (heads % kv_heads != 0)
     return fail(FA_ERR_SHAPE, "%d heads over %d KV heads", heads, kv_heads);
-  if (!supported_head_dim(head_dim)) return fail(FA_ERR_UNSUPPORTED, "head_dim %d", head_dim);
+  if (!supported_head_dim(head_dim, dtype)) return fail(FA_ERR_UNSUPPORTED, "head_dim %d", head_dim);
   if (dtype != FA_F32 && dtype != FA_BF16) return fail(FA_ERR_ARG, "dtype %d", dtype);
   Device* dev = nullptr;
   if (int rc = device_state(device, &dev)) return rc;
@@ -1014,7 +1034,7 @@ int fa_rotate_queries(int32_t heads, int32_t head_dim, int32_t rows, int32_t rop
                       const float* angles, const fa_head_norm* norm, const float* qkv,
                       int64_t qkv_stride, float* q_out, int64_t q_out_stride, void* stream) {
   if (heads < 1 || rows < 0) return fail(FA_ERR_ARG, "heads %d rows %d", heads, rows);
-  if (!supported_head_dim(head_dim)) return fail(FA_ERR_UNSUPPORTED, "head_dim %d", head_dim);
+  if (!supported_head_dim(head_dim, FA_F32)) return fail(FA_ERR_UNSUPPORTED, "head_dim %d", head_dim);
   if (int rc = check_rope(rope, angles)) return rc;
   if (rows == 0) return FA_OK;
   if (qkv == nullptr || q_out == nullptr) return fail(FA_ERR_ARG, "null qkv or q_out");
@@ -1299,6 +1319,8 @@ int check_linear(const fa_kvcache* c, const fa_linear* lin, const float* x, int6
   if (lin->inputs < 1 || lin->weight_stride < lin->inputs || x_stride < lin->inputs)
     return fail(FA_ERR_SHAPE, "inputs %d, weight stride %lld, input stride %lld", lin->inputs,
                 (long long)lin->weight_stride, (long long)x_stride);
+  if (c->head_dim % 8 != 0)
+    return fail(FA_ERR_UNSUPPORTED, "the fused projection takes head_dim a multiple of 8");
   if (lin->inputs % 4 || lin->weight_stride % 4 || x_stride % 4 ||
       reinterpret_cast<uintptr_t>(lin->weight) % 16 || reinterpret_cast<uintptr_t>(x) % 16)
     return fail(FA_ERR_UNSUPPORTED, "weight and input rows must start on 16-byte boundaries");
@@ -1513,7 +1535,7 @@ int fa_attend_batch(fa_kvcache* const* caches, const fa_span* spans, int32_t bat
     return attend_batch_tc(caches, runs, batch, layer, q, q_stride, out, out_stride, s);
   const Plan base = plan_span(c0, 1, 1, false);
   const int kt = c0->dtype == FA_F32 ? fa::kKtF32 : fa::kKtBf16;
-  const int tile = fa::tile_keys(c0->head_dim, kt);
+  const int tile = fa::tile_keys(kernel_dim(c0->head_dim), kt);
   const int64_t chunk_keys = int64_t(tile) * batch_chunk_tiles(c0, base, runs, batch, tile, kt);
   // Chunks and partial slots of every row, then one launch per kMaxBatchRows rows.
   std::vector<int> chunks(batch), part_base(batch);
@@ -1878,7 +1900,7 @@ int fa_attend_full(const fa_call* call, void* out, int64_t out_stride, void* str
   if (k.heads < 1 || k.kv_heads < 1 || k.images < 0 || k.queries < 0 || k.keys < 0)
     return fail(FA_ERR_ARG, "call sizes");
   if (k.heads % k.kv_heads != 0) return fail(FA_ERR_SHAPE, "%d heads over %d KV heads", k.heads, k.kv_heads);
-  if (!supported_head_dim(k.head_dim)) return fail(FA_ERR_UNSUPPORTED, "head_dim %d", k.head_dim);
+  if (!supported_head_dim(k.head_dim, k.dtype)) return fail(FA_ERR_UNSUPPORTED, "head_dim %d", k.head_dim);
   if (k.dtype != FA_F32 && k.dtype != FA_BF16) return fail(FA_ERR_ARG, "dtype %d", k.dtype);
   if (k.out_dtype != FA_F32 && k.out_dtype != FA_BF16)
     return fail(FA_ERR_ARG, "output dtype %d", k.out_dtype);
@@ -1981,7 +2003,7 @@ int fa_attend_full(const fa_call* call, void* out, int64_t out_stride, void* str
   view.dev = dev;
   const Plan p = plan_span(&view, rows, k.keys);
   const size_t q_bytes = align_up(size_t(rows) * width * 4, 256);
-  const size_t o_bytes = align_up(size_t(rows) * p.chunks * k.heads * k.head_dim * 4, 256);
+  const size_t o_bytes = align_up(size_t(rows) * p.chunks * k.heads * kernel_dim(k.head_dim) * 4, 256);
   const size_t ml_bytes = align_up(size_t(rows) * p.chunks * k.heads * 2 * 4, 256);
   std::unique_lock<std::mutex> lock(g_split_mutex);
   SplitWork& fw = g_full_work[{device, s}];
@@ -2008,6 +2030,7 @@ int fa_attend_full(const fa_call* call, void* out, int64_t out_stride, void* str
   args.c.key_stride = k.key.stride;
   args.c.q_scale = 1.0f;  // prepare_queries scaled them
   args.c.err = dev->err;
+  args.c.dh = k.head_dim;
   args.c.q = q;
   args.c.q_stride = width;
   args.c.out = static_cast<float*>(out);
@@ -2341,7 +2364,7 @@ extern "C" int fa_attend_static(fa_kvcache* cache, int32_t layer, const fa_span*
   const Plan p = plan_span(cache, span->rows, max_keys);
   const size_t counter_bytes = size_t(span->rows) * p.kv_groups * sizeof(int);
   const size_t slots = size_t(span->rows) * p.chunks * cache->heads;
-  const size_t o_bytes = align_up(slots * cache->head_dim * 4, 256);
+  const size_t o_bytes = align_up(slots * kernel_dim(cache->head_dim) * 4, 256);
   const size_t ml_bytes = align_up(slots * 2 * 4, 256);
   if (counter_bytes > kStaticCounterBytes ||
       o_bytes + ml_bytes > kStaticScratchBytes - kStaticCounterBytes)

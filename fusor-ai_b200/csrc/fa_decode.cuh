@@ -224,6 +224,7 @@ struct AttendCommon {
   int* counters;   // per (row, kv group) arrival counters, zero between launches
   unsigned* err;   // device error word
   int cluster;     // spans: a row's chunks are one thread-block cluster (merged in shared memory)
+  int dh;          // the rows' head_dim: D, or fewer on a kernel of a wider D (PAD)
 };
 
 // One span over one cache: row r at position first + r, keys from the mask.
@@ -325,7 +326,11 @@ __device__ __forceinline__ void merge_chunk_partials(const float* part_o, const 
   }
 }
 
-template <int D, typename KT, int G, bool BATCH, typename Args>
+// PAD: the rows hold dh < D elements (a head_dim between the powers of two, dh a multiple of
+// the 16-byte vectors: 4 for f32, 8 for bf16); they stream and sit in shared memory dh apart, the
+// lanes' vectors past dh are zero, and only elements below dh are written out. The tile stays T
+// rows of the D layout (fewer bytes).
+template <int D, typename KT, int G, bool BATCH, typename Args, bool PAD = false>
 __global__ void __launch_bounds__(kDecodeThreads, (DecodeShape<D, KT, G>::kMinCtas)) attend_kernel(const __grid_constant__ Args args) {
   using S = DecodeShape<D, KT, G>;
   constexpr int E = S::kLaneElems;
@@ -333,6 +338,8 @@ __global__ void __launch_bounds__(kDecodeThreads, (DecodeShape<D, KT, G>::kMinCt
   constexpr int LPK = S::kLanesPerKey;
   constexpr int KPW = S::kKeysPerWarp;
   const AttendCommon& c = args.c;
+  const int RD = PAD ? c.dh : D;  // elements of a row (its stride in the cache and in a tile)
+  const uint32_t row_bytes = uint32_t(RD) * KvElem<KT>::kBytes;
 
   extern __shared__ __align__(128) unsigned char smem[];
   KT* k_tiles = reinterpret_cast<KT*>(smem);
@@ -386,8 +393,8 @@ __global__ void __launch_bounds__(kDecodeThreads, (DecodeShape<D, KT, G>::kMinCt
   const int sg = kvg % c.hgroups;
   const int h0 = kv * c.group + sg * G;
   const int g = min(G, c.group - sg * G);
-  // A batch row's KV heads are its own cache's blocks of capacity x D.
-  const int64_t kv_stride = BATCH ? int64_t(capacity) * D : c.kv_stride;
+  // A batch row's KV heads are its own cache's blocks of capacity x RD.
+  const int64_t kv_stride = BATCH ? int64_t(capacity) * RD : c.kv_stride;
   kbase += kv * kv_stride;
   vbase += kv * kv_stride;
   const int n = runs.n0 + runs.n1;
@@ -419,7 +426,7 @@ __global__ void __launch_bounds__(kDecodeThreads, (DecodeShape<D, KT, G>::kMinCt
         if (!mbar_wait(&empty[s], ((t / kStages) & 1) ^ 1, c.err)) break;
         const int ja = j0 + t * T;
         const int nk = min(T, j1 - ja);
-        mbar_arrive_expect_tx(&full[s], uint32_t(nk) * S::kRowBytes * 2);
+        mbar_arrive_expect_tx(&full[s], uint32_t(nk) * row_bytes * 2);
         KT* kd = k_tiles + size_t(s) * S::kElemsPerTile;
         KT* vd = v_tiles + size_t(s) * S::kElemsPerTile;
         int j = ja, at = 0;
@@ -429,15 +436,15 @@ __global__ void __launch_bounds__(kDecodeThreads, (DecodeShape<D, KT, G>::kMinCt
           else { pos = runs.b1 + (j - runs.n0); left = n - j; }
           const int slot = pos % capacity;
           const int cnt = min(ja + nk - j, min(left, capacity - slot));
-          if (c.key_stride == D) {  // a cache: the run's rows are contiguous
-            const uint32_t bytes = uint32_t(cnt) * S::kRowBytes;
-            bulk_g2s_hint(kd + size_t(at) * D, kbase + int64_t(slot) * D, bytes, &full[s], policy);
-            bulk_g2s_hint(vd + size_t(at) * D, vbase + int64_t(slot) * D, bytes, &full[s], policy);
+          if (c.key_stride == RD) {  // a cache: the run's rows are contiguous
+            const uint32_t bytes = uint32_t(cnt) * row_bytes;
+            bulk_g2s_hint(kd + size_t(at) * RD, kbase + int64_t(slot) * RD, bytes, &full[s], policy);
+            bulk_g2s_hint(vd + size_t(at) * RD, vbase + int64_t(slot) * RD, bytes, &full[s], policy);
           } else {  // strided operand rows: one copy per row
             for (int i = 0; i < cnt; ++i) {
               const int64_t src = int64_t(slot + i) * c.key_stride;
-              bulk_g2s_hint(kd + size_t(at + i) * D, kbase + src, S::kRowBytes, &full[s], policy);
-              bulk_g2s_hint(vd + size_t(at + i) * D, vbase + src, S::kRowBytes, &full[s], policy);
+              bulk_g2s_hint(kd + size_t(at + i) * RD, kbase + src, row_bytes, &full[s], policy);
+              bulk_g2s_hint(vd + size_t(at + i) * RD, vbase + src, row_bytes, &full[s], policy);
             }
           }
           j += cnt;
@@ -479,10 +486,17 @@ __global__ void __launch_bounds__(kDecodeThreads, (DecodeShape<D, KT, G>::kMinCt
   for (int h = 0; h < G; ++h)
 #pragma unroll
     for (int i = 0; i < P; ++i) {
-      const int at = (h0 + h) * D + elem_of<D, KT, E>(sub, 2 * i);
-      q[h][i] = h < g ? make_float2(qrow[at] * c.q_scale, qrow[at + 1] * c.q_scale)
-                      : make_float2(0.0f, 0.0f);
+      const int el = elem_of<D, KT, E>(sub, 2 * i);
+      const int at = (h0 + h) * RD + el;
+      q[h][i] = h < g && (!PAD || el < RD)
+                    ? make_float2(qrow[at] * c.q_scale, qrow[at + 1] * c.q_scale)
+                    : make_float2(0.0f, 0.0f);
     }
+  // PAD: the lane's key vectors past the row (all or none of a vector: RD is a multiple of it)
+  // read as zero, so that whatever the tile holds there cannot reach a score
+  bool lane_valid[P];
+#pragma unroll
+  for (int i = 0; i < P; ++i) lane_valid[i] = !PAD || elem_of<D, KT, E>(sub, 2 * i) < RD;
 
   // m[h], l[h]: every head (per-head path) or m[0], l[0]: the lane's own head (scatter path)
   float m[G], l[G];
@@ -510,7 +524,12 @@ __global__ void __launch_bounds__(kDecodeThreads, (DecodeShape<D, KT, G>::kMinCt
       const bool valid = kr < nk;
       const int rr = valid ? kr : first_key;
       float2 kx[P], vx[P];
-      load_lane<D, KT, E>(kt + size_t(rr) * D, sub, kx);
+      load_lane<D, KT, E>(kt + size_t(rr) * RD, sub, kx);
+      if constexpr (PAD) {
+#pragma unroll
+        for (int i = 0; i < P; ++i)
+          if (!lane_valid[i]) kx[i] = make_float2(0.0f, 0.0f);
+      }
       float part[G];
 #pragma unroll
       for (int h = 0; h < G; ++h) {
@@ -519,7 +538,7 @@ __global__ void __launch_bounds__(kDecodeThreads, (DecodeShape<D, KT, G>::kMinCt
         for (int i = 0; i < P; ++i) a = fma2(q[h][i], kx[i], a);
         part[h] = a.x + a.y;
       }
-      load_lane<D, KT, E>(vt + size_t(rr) * D, sub, vx);
+      load_lane<D, KT, E>(vt + size_t(rr) * RD, sub, vx);
       if constexpr (kScatter) {
 #pragma unroll
         for (int k = 0; k < kLogG; ++k) {
@@ -646,13 +665,14 @@ __global__ void __launch_bounds__(kDecodeThreads, (DecodeShape<D, KT, G>::kMinCt
 
   const int count = g * D;
   float* out_row = c.out != nullptr ? c.out + int64_t(row) * c.out_stride : nullptr;
-  float* part_row = c.partial_out != nullptr ? c.partial_out + int64_t(row) * c.heads * (D + 2) : nullptr;
+  float* part_row = c.partial_out != nullptr ? c.partial_out + int64_t(row) * c.heads * (RD + 2) : nullptr;
   // The row's merged state of head h0 + h: its output, or its (max, sum, o) when partial.
   auto finish = [&](int h, int e, float mm, float ll, float oo) {
+    if (PAD && e >= RD) return;
     if (out_row != nullptr) {
-      out_row[(h0 + h) * D + e] = ll > 0.0f ? oo / ll : 0.0f;
+      out_row[(h0 + h) * RD + e] = ll > 0.0f ? oo / ll : 0.0f;
     } else {
-      float* pr = part_row + (h0 + h) * (D + 2);
+      float* pr = part_row + (h0 + h) * (RD + 2);
       if (e == 0) { pr[0] = mm; pr[1] = ll; }
       pr[2 + e] = oo;
     }

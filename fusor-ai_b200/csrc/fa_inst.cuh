@@ -7,9 +7,9 @@ namespace fa {
 
 namespace {
 
-template <int D, typename KT, int G, bool BATCH, typename Args>
+template <int D, typename KT, int G, bool BATCH, bool PAD, typename Args>
 cudaError_t launch_one(const Args& args, int grid, cudaStream_t stream) {
-  auto kernel = attend_kernel<D, KT, G, BATCH, Args>;
+  auto kernel = attend_kernel<D, KT, G, BATCH, Args, PAD>;
   constexpr size_t smem = DecodeShape<D, KT, G>::kSmemBytes;
   static std::atomic<bool> configured[64];  // per instantiation, per device
   cudaError_t e = smem_limit_once(kernel, int(smem), configured);
@@ -18,10 +18,21 @@ cudaError_t launch_one(const Args& args, int grid, cudaStream_t stream) {
                             args.c.cluster > 1 ? args.c.cluster : 1, args);
 }
 
+// Head dims between the powers of two run on the next wider kernel (PAD); the narrow ones
+// have no wider neighbour worth a second instantiation.
+constexpr bool kPadded(int d) { return d >= 64; }
+
 template <int D, typename KT, int G>
 cudaError_t launch_g(const AttendLaunch& l, cudaStream_t stream) {
-  return l.batch ? launch_one<D, KT, G, true>(*l.rows, l.grid, stream)
-                 : launch_one<D, KT, G, false>(*l.span, l.grid, stream);
+  if constexpr (kPadded(D)) {
+    if (l.pad)
+      return l.batch ? launch_one<D, KT, G, true, true>(*l.rows, l.grid, stream)
+                     : launch_one<D, KT, G, false, true>(*l.span, l.grid, stream);
+  } else if (l.pad) {
+    return cudaErrorInvalidValue;
+  }
+  return l.batch ? launch_one<D, KT, G, true, false>(*l.rows, l.grid, stream)
+                 : launch_one<D, KT, G, false, false>(*l.span, l.grid, stream);
 }
 
 template <int D, typename KT>
@@ -35,9 +46,9 @@ cudaError_t launch_kt(const AttendLaunch& l, cudaStream_t stream) {
   }
 }
 
-template <int D, typename KT, int G, bool BATCH, typename Args>
+template <int D, typename KT, int G, bool BATCH, typename Args, bool PAD>
 int resident_one() {
-  auto kernel = attend_kernel<D, KT, G, BATCH, Args>;
+  auto kernel = attend_kernel<D, KT, G, BATCH, Args, PAD>;
   constexpr size_t smem = DecodeShape<D, KT, G>::kSmemBytes;
   static std::atomic<int> cached[64];         // per instantiation, per device; 0: not asked yet
   static std::atomic<bool> configured[64];
@@ -55,8 +66,13 @@ int resident_one() {
 
 template <int D, typename KT, int G>
 int resident_g(const AttendLaunch& l) {
-  return l.batch ? resident_one<D, KT, G, true, BatchArgs>()
-                 : resident_one<D, KT, G, false, SpanArgs>();
+  if constexpr (kPadded(D)) {
+    if (l.pad)
+      return l.batch ? resident_one<D, KT, G, true, BatchArgs, true>()
+                     : resident_one<D, KT, G, false, SpanArgs, true>();
+  }
+  return l.batch ? resident_one<D, KT, G, true, BatchArgs, false>()
+                 : resident_one<D, KT, G, false, SpanArgs, false>();
 }
 
 template <int D, typename KT>

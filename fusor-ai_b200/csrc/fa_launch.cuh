@@ -70,6 +70,7 @@ struct AttendLaunch {
   const SpanArgs* span;
   const BatchArgs* rows;
   int grid;
+  bool pad = false;         // rows of AttendCommon::dh < D elements (the kernel's PAD form)
 };
 
 template <int D>

@@ -132,7 +132,11 @@ typedef struct fa_kvcache fa_kvcache;
 const char* fa_last_error(void);
 
 /* The build's capabilities: a bitmask of 1 = f32 cache, 2 = bf16 cache, 4 = tcgen05 prefill /
- * full-mask kernels; and the supported head_dim values through *head_dims (may be NULL). */
+ * full-mask kernels, 8 = head dims between the powers of two; and the head_dim values with a
+ * kernel of their own through *head_dims (may be NULL). With flag 8, a head_dim between 32 and
+ * 256 that is a multiple of 4 (f32 rows) or 8 (bf16 rows) runs on the kernel of the next power
+ * of two, the lanes past the head idle (Kronos' 52, Iris' 80); the tensor-core kernels take
+ * 64 and 128, and 256 over bf16. */
 int fa_capabilities(int32_t* flags, int32_t* head_dims, int32_t max_head_dims,
                     int32_t* n_head_dims);
 

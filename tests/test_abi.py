@@ -119,7 +119,10 @@ def test_shape_errors_are_status_codes_not_panics():
     rc = fa.lib().fa_kvcache_create(1, 14, 4, 64, 16, fa.F32, 0, C.byref(h))
     assert rc == fa.ERR_SHAPE
     assert b"14 heads over 4 KV heads" in fa.lib().fa_last_error()
-    assert fa.lib().fa_kvcache_create(1, 4, 2, 48, 16, fa.F32, 0, C.byref(h)) == fa.ERR_UNSUPPORTED
+    # head dims off the kernels' 16-byte vectors, or past 256: no kernel (52 f32 and 80 bf16 have
+    # one, the next wider kernel's; 52 bf16 is not a whole number of 8-element vectors)
+    for d, dtype in ((50, fa.F32), (52, fa.BF16), (260, fa.F32), (24, fa.F32)):
+        assert fa.lib().fa_kvcache_create(1, 4, 2, d, 16, dtype, 0, C.byref(h)) == fa.ERR_UNSUPPORTED
     assert fa.lib().fa_kvcache_create(1, 4, 2, 64, 0, fa.F32, 0, C.byref(h)) == fa.ERR_ARG
     assert fa.lib().fa_kvcache_create(1, 4, 2, 64, 8, 7, 0, C.byref(h)) == fa.ERR_ARG
     assert fa.lib().fa_kvcache_create(1, 4, 2, 64, 8, fa.F32, 0, None) == fa.ERR_ARG
@@ -136,7 +139,7 @@ def test_rotary_argument_errors():
 
 def test_capabilities():
     flags, dims = fa.capabilities()
-    assert flags & 1 and flags & 2
+    assert flags & 1 and flags & 2 and flags & 8  # f32, bf16, head dims between the powers of two
     assert dims == [16, 32, 64, 128, 256]
 
 
