@@ -135,6 +135,21 @@ struct Buffer {
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+// K/V bytes the tensor-core kernels' schedules may keep in L2 at once. Measured on B200 (126 MB
+// of L2 over two dies): an 8192-row causal prefill whose every head's pairs ran at once slowed
+// down past about this much K/V.
+constexpr double kL2KvBudget = 48e6;
+
+// The one-tile kernel's band (FmhaArgs::band_heads): the most whole KV groups whose K/V
+// (kv_bytes_per_head for each KV head) fits the L2 budget together, at least one, and a divisor
+// of the KV heads so that the bands are equal.
+int band_heads(int heads, int kv_heads, double kv_bytes_per_head) {
+  int best = 1;
+  for (int b = 2; b <= kv_heads; ++b)
+    if (kv_heads % b == 0 && b * kv_bytes_per_head <= kL2KvBudget) best = b;
+  return best * (heads / kv_heads);
+}
+
 // The schedule of a bf16 full-mask call's units (query head, pair of 128-row query tiles) over
 // `sms` SMs: the first `whole` units run as one CTA each and every later unit as `splits` pieces
 // over equal shares of its `kv_tiles` key tiles. Units whose count is not a multiple of the SM
@@ -700,8 +715,10 @@ int attend_rows_tc(fa_kvcache* c, int layer, const fa_span* span, const std::vec
   // pairs first across heads, when the K/V it reads fits well inside L2 (every head's pairs run
   // at once in that order). Measured on B200: an 8192-row causal prefill from position 0 (32/8
   // heads x 128, bf16 cache).
-  const double kv_bytes = 2.0 * c->kv_heads * double(a.end) * c->head_dim * c->elem();
-  a.pair_major = a.kind == FA_MASK_CAUSAL && span->first < span->rows && kv_bytes <= 48e6;
+  const double kv_head_bytes = 2.0 * double(a.end) * c->head_dim * c->elem();
+  a.pair_major = a.kind == FA_MASK_CAUSAL && span->first < span->rows &&
+                 c->kv_heads * kv_head_bytes <= kL2KvBudget;
+  a.band_heads = band_heads(c->heads, c->kv_heads, kv_head_bytes);
   fa::FmhaLaunch l{c->dtype == FA_BF16 ? 1 : 0, c->head_dim, q, uint64_t(span->rows),
                    uint64_t(c->heads), uint64_t(q_stride), uint64_t(c->head_dim), c->keys,
                    c->values, uint64_t(c->capacity), uint64_t(c->layers) * c->kv_heads,
@@ -1949,6 +1966,8 @@ int fa_attend_full(const fa_call* call, void* out, int64_t out_stride, void* str
     a.out_stride = out_stride;
     a.out_bf16 = k.out_dtype == FA_BF16 ? 1 : 0;
     a.err = dev->err;
+    a.band_heads = band_heads(k.heads, k.kv_heads,
+                              2.0 * k.images * double(k.keys) * k.head_dim * (k.dtype == FA_BF16 ? 2 : 4));
     if (fa::fmha_splits_supported(k.dtype == FA_BF16, k.head_dim)) {
       const int64_t units = int64_t(k.images) * ((a.q_tiles + 1) / 2) * k.heads;
       int64_t whole = units;

@@ -64,8 +64,12 @@ cudaError_t launch_t(const FmhaLaunch& l, cudaStream_t stream) {
   static std::atomic<bool> configured[64];  // per instantiation, per device
   cudaError_t err = smem_limit_once(kernel, int(S::kSmemBytes), configured);
   if (err != cudaSuccess) return err;
-  const dim3 grid(l.args.images * l.args.q_tiles, l.args.heads);
-  return launch_pdl(kernel, grid, dim3(kFmhaThreads), S::kSmemBytes, stream, qm, km, vm, l.args);
+  const int band = l.args.band_heads > 0 ? l.args.band_heads : l.args.group;
+  if (band % l.args.group || l.args.heads % band) return cudaErrorInvalidValue;
+  const int64_t grid = int64_t(l.args.images) * l.args.q_tiles * l.args.heads;
+  if (grid > 0x7fffffff) return cudaErrorInvalidValue;
+  return launch_pdl(kernel, dim3(unsigned(grid)), dim3(kFmhaThreads), S::kSmemBytes, stream, qm,
+                    km, vm, l.args);
 }
 
 // bf16: two query tiles per CTA (fa_fmha2.cuh).

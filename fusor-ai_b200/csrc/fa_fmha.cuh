@@ -131,10 +131,15 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(v_conv + VS);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int head = blockIdx.y;
+  // The CTA's query head and tile: band by band, each band's heaviest tiles first across its
+  // heads (longest-processing-time order within the band; its K/V stays in L2 meanwhile).
+  const int band_heads = a.band_heads > 0 ? a.band_heads : a.group;
+  const int tiles = a.images * a.q_tiles;
+  const int band = int(blockIdx.x) / (tiles * band_heads);
+  const int in_band = int(blockIdx.x) - band * tiles * band_heads;
+  const int head = band * band_heads + in_band % band_heads;
   const int kv = head / a.group;
-  // heavier (later, for causal masks) tiles first
-  const int tile_id = int(gridDim.x) - 1 - int(blockIdx.x);
+  const int tile_id = tiles - 1 - in_band / band_heads;
   const int image = tile_id / a.q_tiles;
   const int r0 = (tile_id % a.q_tiles) * BM;
   const int r_last = min(r0 + BM, a.rows) - 1;

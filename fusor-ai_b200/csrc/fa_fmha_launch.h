@@ -37,6 +37,10 @@ struct FmhaArgs {
   int splits;
   // 1: without splits, units run pair-major, the heaviest pairs of every head first
   int pair_major;
+  // The one-tile kernel's schedule: a 1-D grid over bands of band_heads query heads (whole KV
+  // groups, consecutive heads), band after band; within a band the query tiles run heaviest
+  // first (later rows, for causal masks), the band's heads fastest. 0: one KV group per band.
+  int band_heads;
   float* part_o;
   float* part_ml;
   int* counters;
