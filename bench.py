@@ -360,26 +360,32 @@ def oracle_decode(fa, shape, position, keys, values, qkv, angles, threads):
 
 
 class ProjectedInput(Workload):
-    """Stack::attention_input of one decode row with its qkv projection on the device
-    (fa_attention_input_projected: projection, RoPE and keep in one kernel), Llama-8B-shaped:
-    32/8 heads x 128, hidden 4096, f32 weights (6144 x 4096, 100.7 MB) and bias, position 4096.
-    Bound by the weight bytes; L2 (126 MB) flushed between steps."""
+    """Stack::attention_input with its qkv projection on the device
+    (fa_attention_input_projected: projection, RoPE and keep), Llama-8B-shaped: 32/8 heads x
+    128, hidden 4096, f32 weights (6144 x 4096, 100.7 MB) and bias, from position 4096. `proj`:
+    one decode row (the fused CUDA-core kernel); `proj64`: 64 rows (a batched decode's or a
+    prefill chunk's rows: the tensor-core projection in three tf32 products, then the RoPE +
+    keep kernel). Roofline against the bytes (weights, input, kept rows, queries); L2 (126 MB)
+    flushed between steps."""
 
-    def __init__(self, torch, fa):
-        self.torch, self.fa, self.name = torch, fa, "proj"
-        self.kernel = "project_keep_kernel"
+    def __init__(self, torch, fa, rows=1):
+        self.torch, self.fa = torch, fa
+        self.name = "proj" if rows == 1 else f"proj{rows}"
+        self.kernel = "project_keep_kernel" if rows < 16 else "project_tc_kernel"
         heads, kv, d, self.hidden, position = 32, 8, 128, 4096, 4096
+        self.rows = rows
         shape = fa.Shape(1, heads, kv, d)
-        self.cache = fa.KvCache(shape, position + 1)
+        self.cache = fa.KvCache(shape, position + rows)
         gen = torch.Generator("cuda").manual_seed(9)
         self.weight = torch.randn((shape.qkv, self.hidden), device="cuda", generator=gen) / 64.0
         self.bias = torch.randn((shape.qkv,), device="cuda", generator=gen)
-        self.x = torch.randn((1, self.hidden), device="cuda", generator=gen)
-        self.span = fa.Span(1, position, fa.Mask.causal())
-        self.angles = torch.from_numpy(fa.rotary_angles(fa.Rotation(base=1e6), d, [position])).cuda()
-        self.q = torch.zeros((1, shape.width), device="cuda")
-        self.tokens = 1
-        self.launches_per_step = 1
+        self.x = torch.randn((rows, self.hidden), device="cuda", generator=gen)
+        self.span = fa.Span(rows, position, fa.Mask.causal())
+        self.angles = torch.from_numpy(fa.rotary_angles(fa.Rotation(base=1e6), d,
+                                                        range(position, position + rows))).cuda()
+        self.q = torch.zeros((rows, shape.width), device="cuda")
+        self.tokens = rows
+        self.launches_per_step = 1 if rows < 16 else 2
         self.flush_l2 = True
         self.graphs = True
         self.h_x = self.x.cpu().pin_memory()
@@ -387,7 +393,7 @@ class ProjectedInput(Workload):
         self.h2d = self.h_x.numel() * 4
         self.d2h = self.h_q.numel() * 4
         self.bytes = (self.weight.numel() + self.bias.numel() + self.x.numel()
-                      + 2 * kv * d + shape.width) * 4
+                      + rows * (2 * kv * d + shape.width)) * 4
 
     def phases(self):
         return (lambda: None,
@@ -410,18 +416,19 @@ class ProjectedInput(Workload):
         qkv = oracle.project(self.x.cpu().numpy(), self.weight.cpu().numpy(),
                              self.bias.cpu().numpy())
         scale = max(1.0, float(np.abs(qkv).max()))
-        position = self.span.first
+        first, rows = self.span.first, self.rows
         shape = self.cache.shape
-        oc = oracle.Cache(1, shape.heads, shape.kv_heads, shape.head_dim, position + 1)
-        oc.attention_input(0, 1, position, fa.ROPE_HALF, self.angles.cpu().numpy(), qkv,
+        oc = oracle.Cache(1, shape.heads, shape.kv_heads, shape.head_dim, first + rows)
+        oc.attention_input(0, rows, first, fa.ROPE_HALF, self.angles.cpu().numpy(), qkv,
                            qkv.shape[1])
-        k, v = self.cache.copy_rows(position + 1)
-        got = np.concatenate([self.q.cpu().numpy().ravel(), k[0, :, position].cpu().numpy().ravel(),
-                              v[0, :, position].cpu().numpy().ravel()])
-        want = np.concatenate([qkv[0, :shape.width], oc.keys[0, :, position].ravel(),
-                               oc.values[0, :, position].ravel()])
+        k, v = self.cache.copy_rows(first + rows)
+        kept = slice(first, first + rows)
+        got = np.concatenate([self.q.cpu().numpy().ravel(), k[0, :, kept].cpu().numpy().ravel(),
+                              v[0, :, kept].cpu().numpy().ravel()])
+        want = np.concatenate([qkv[:, :shape.width].ravel(), oc.keys[0, :, kept].ravel(),
+                               oc.values[0, :, kept].ravel()])
         return parity_result(got, want, 2e-5 * scale,
-                             "the rotated queries and the kept key and value rows")
+                             f"the rotated queries and the kept key and value rows of {rows} row(s)")
 
     def algorithmic(self):
         return float(self.bytes)
@@ -1312,6 +1319,8 @@ def run_ours(args):
             return C2Prefill(torch, fa)
         if name == "proj":
             return ProjectedInput(torch, fa)
+        if name == "proj64":
+            return ProjectedInput(torch, fa, rows=64)
         if name == "prologue":
             return DitPrologue(torch, fa)
         if name == "prefill":
@@ -1367,7 +1376,7 @@ def run_ours(args):
     if args.config == "c3" and not args.no_extras and args.sequences == C3_SEQS:
         extras = {}
         names = (("c1", "c2", "c3bf16", "c4", "c5", "prefill", "prefill_f32", "qwen35", "proj",
-                  "prologue") if world == 1 else ("c4", "c5"))
+                  "proj64", "prologue") if world == 1 else ("c4", "c5"))
         for name in names:
             x = build(name)
             xs = min(steps, 50 if name == "c5" else 200)
@@ -1445,19 +1454,25 @@ def config_of(name, world):
         "proj": {"workload": "attention input with its qkv projection (fused), one decode row",
                  "heads": 32, "kv_heads": 8, "head_dim": 128, "hidden": 4096,
                  "weights": "f32 6144 x 4096 + bias", "position": 4096},
+        "proj64": {"workload": "attention input with its qkv projection, 64 rows (tensor cores, "
+                   "three tf32 products, then RoPE + keep)",
+                   "rows": 64, "heads": 32, "kv_heads": 8, "head_dim": 128, "hidden": 4096,
+                   "weights": "f32 6144 x 4096 + bias", "first": 4096},
     }
     c = dict(cfgs[name])
     c["parallelism"] = {
         "c3": f"sequences over {world} GPU(s), no collective",
         "c3bf16": f"sequences over {world} GPU(s), no collective",
         "c4": (f"KV range over {world} GPU(s); (max, sum, o) exchanged over NVLink peer memory "
-               "by one kernel (P2P stores, flags) that merges" if world > 1 else "1 GPU"),
+               "by one kernel (P2P stores of step-stamped words) that merges" if world > 1
+               else "1 GPU"),
         "c5": f"query rows in whole 256-row pairs over {world} GPU(s), all heads, no collective",
     }.get(name, f"replicas x{world}")
     c["l2"] = ("inputs larger than L2" if name in ("c3", "c3bf16", "c4", "c5", "prologue", "prefill",
                                                    "prefill_f32", "qwen35")
                else "L2 flushed between steps (clean lines left)")
-    if name in ("c1", "c2", "c3", "c3bf16", "proj", "prologue", "prefill", "prefill_f32", "qwen35") or \
+    if name in ("c1", "c2", "c3", "c3bf16", "proj", "proj64", "prologue", "prefill", "prefill_f32",
+                "qwen35") or \
             (name == "c4" and world > 1):
         c["launch"] = "the step's calls replayed as captured CUDA graphs"
     return c
@@ -1533,7 +1548,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="c3",
                     choices=["c1", "c2", "c3", "c3bf16", "c4", "c5", "prefill", "prefill_f32",
-                             "qwen35", "proj", "prologue"])
+                             "qwen35", "proj", "proj64", "prologue"])
     ap.add_argument("--sequences", type=int, default=C3_SEQS,
                     help="C3 sequences (a smaller batch for profiling captures)")
     ap.add_argument("--no-extras", action="store_true")

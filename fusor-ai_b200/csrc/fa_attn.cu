@@ -1347,12 +1347,81 @@ int check_linear(const fa_kvcache* c, const fa_linear* lin, const float* x, int6
   return FA_OK;
 }
 
+// From this many rows the projection runs on the tensor cores (fa_project_tc.cu) and then the
+// RoPE + keep kernel; below it, in the fused CUDA-core kernel, bound by the weight bytes.
+constexpr int kProjectTcRows = 16;
+
+// Splits of the hidden dimension for the tensor-core projection: enough CTAs (one an SM, each
+// holding about 200 KB of shared memory) to fill the SMs once, at most 8, with at least 4
+// k-blocks each.
+int project_tc_splits(int64_t blocks, int k_blocks, int sms) {
+  int64_t s = std::max<int64_t>(1, sms / std::max<int64_t>(blocks, 1));
+  s = std::min<int64_t>(s, 8);
+  s = std::min<int64_t>(s, std::max(1, k_blocks / 4));
+  return int(s);
+}
+
+// The tensor-core projection of `rows` rows into qkv_out (or c0's projection workspace), then the
+// RoPE + keep kernel over them.
+int launch_projection_tc(fa_kvcache* c0, const fa_linear* lin, const float* x, int64_t x_stride,
+                         int rows, const fa::RopeArgs& ra, float* qkv_out, int64_t qkv_out_stride,
+                         cudaStream_t s) {
+  fa::ProjectTcArgs t{};
+  t.x = x;
+  t.x_stride = x_stride;
+  t.weight = lin->weight;
+  t.w_stride = lin->weight_stride;
+  t.bias = lin->bias;
+  t.hidden = lin->inputs;
+  t.outputs = lin->outputs;
+  t.rows = rows;
+  t.k_blocks = (lin->inputs + 31) / 32;
+  t.qkv = qkv_out;
+  t.qkv_stride = qkv_out_stride;
+  t.err = c0->dev->err;
+  const int bn = fa::project_tc_rows_per_tile(rows);
+  const int64_t tiles = int64_t((lin->outputs + 127) / 128) * ((rows + bn - 1) / bn);
+  t.splits = project_tc_splits(tiles, t.k_blocks, c0->dev->sms);
+  // the workspace: the projected rows (when the caller keeps none), then the splits' partials
+  const size_t qkv_bytes = qkv_out ? 0 : align_up(size_t(rows) * lin->outputs * sizeof(float), 256);
+  const size_t part_bytes = t.splits > 1 ? size_t(tiles) * t.splits * bn * 128 * sizeof(float) : 0;
+  if (qkv_bytes + part_bytes > 0) {
+    if (int rc = c0->proj_work.ensure(qkv_bytes + part_bytes, s)) return rc;
+    unsigned char* w = static_cast<unsigned char*>(c0->proj_work.ptr);
+    if (qkv_out == nullptr) {
+      t.qkv = reinterpret_cast<float*>(w);
+      t.qkv_stride = lin->outputs;
+    }
+    t.partials = reinterpret_cast<float*>(w + qkv_bytes);
+  }
+  if (t.splits > 1) {
+    const int epoch = c0->dev->epoch.load();
+    if (size_t(tiles) * sizeof(int) > c0->proj_counters.bytes || c0->proj_epoch != epoch) {
+      if (int rc = c0->proj_counters.ensure(size_t(tiles) * sizeof(int), s)) return rc;
+      FA_CUDA(cudaMemsetAsync(c0->proj_counters.ptr, 0, c0->proj_counters.bytes, s),
+              "clear projection counters");
+      c0->proj_epoch = epoch;
+    }
+    t.counters = static_cast<int*>(c0->proj_counters.ptr);
+  }
+  cudaError_t e = fa::launch_project_tc(t, s);
+  if (e != cudaSuccess) return cuda_fail(e, "tensor-core projection launch");
+  fa::RopeArgs r = ra;
+  r.qkv = t.qkv;
+  r.qkv_stride = t.qkv_stride;
+  e = fa::launch_rope(c0->dtype == FA_F32 ? fa::kKtF32 : fa::kKtBf16, r, s);
+  if (e != cudaSuccess) return cuda_fail(e, "rope launch");
+  return FA_OK;
+}
+
 // One launch of the fused projection over `rows` rows: the RopeArgs say where each row's keys and
 // values go; the partials and counters live in c0's projection workspace.
 int launch_projection(fa_kvcache* c0, const fa_linear* lin, const float* x, int64_t x_stride,
                       int rows, const fa::RopeArgs& ra, float* qkv_out, int64_t qkv_out_stride,
                       cudaStream_t s) {
   if (rows == 0) return FA_OK;
+  if (rows >= kProjectTcRows)
+    return launch_projection_tc(c0, lin, x, x_stride, rows, ra, qkv_out, qkv_out_stride, s);
   const int units = c0->heads + 2 * c0->kv_heads;
   const ProjectPlan plan = plan_project(rows, lin->inputs, units, c0->head_dim, c0->dev->sms);
   fa::ProjectArgs p{};

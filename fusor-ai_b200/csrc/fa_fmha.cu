@@ -109,6 +109,12 @@ bool encode_cache_map_bf16(void* map, const void* base, uint64_t rows, uint64_t 
                   z_stride_bytes, 64, 128);
 }
 
+bool encode_map_f32(void* map, const void* base, uint64_t x, uint64_t y, uint64_t y_stride_bytes,
+                    uint32_t box_x, uint32_t box_y) {
+  return make_map(static_cast<CUtensorMap*>(map), false, base, x, y, 1, y_stride_bytes,
+                  y * y_stride_bytes, box_x, box_y);
+}
+
 bool fmha_supported(int dtype_bf16, int head_dim) {
   const bool dim = head_dim == 64 || head_dim == 128 || (head_dim == 256 && dtype_bf16);
   return dim && encode_fn() != nullptr;

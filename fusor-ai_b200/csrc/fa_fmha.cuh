@@ -234,7 +234,17 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
   } else if (warp == 1) {
     // ---- MMA issuer ----------------------------------------------------------------------
     if (lane == 0) {
-      const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV);
+      // The descriptors differ only in their start address (16-byte units in the low bits;
+      // shared-memory addresses stay below 2^18): built once, offsets added per stage and K step
+      // (the issue of the MMAs is on this thread's critical path).
+      const uint64_t q_desc = tc::smem_desc_sw128(smem_u32(sQ), 16, 1024);
+      const uint64_t k_desc = tc::smem_desc_sw128(smem_u32(sK), 16, 1024);
+      // V is the MN-major B operand: rows of 128 bytes of one head_dim block, blocks BN*128 bytes
+      // apart; bf16 in 8-row 128-byte-swizzle atoms, tf32 in the only MN-major tf32 layout, 4-row
+      // atoms of 32-byte chunks.
+      const uint64_t v_desc =
+          kTf32 ? tc::smem_desc(smem_u32(sV), BN * 128, 512, tc::kSwizzle128BAtom32B)
+                : tc::smem_desc(smem_u32(sV), BN * 128, 1024, tc::kSwizzle128B);
       bool ok = mbar_wait(kTf32 ? q_conv : q_full, 0, a.err);
       auto issue_pv = [&](int j) {
         const int st = j % VS;
@@ -243,19 +253,12 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
         if (!mbar_wait(kTf32 ? &v_conv[st] : &v_full[st], (j / VS) & 1, a.err)) return false;
         tc::fence_after_sync();
         const uint32_t p_tmem = tmem + uint32_t(b * S::kSCols);
+        const uint64_t vd0 = v_desc + uint64_t(st) * uint64_t(S::kKVBytes >> 4);
 #pragma unroll
-        for (int k = 0; k < BN / S::kKStep; ++k) {
-          // V is the MN-major B operand: rows of 128 bytes of one head_dim block, blocks BN*128
-          // bytes apart; bf16 in 8-row 128-byte-swizzle atoms, tf32 in the only MN-major tf32
-          // layout, 4-row atoms of 32-byte chunks.
-          const uint64_t vd = kTf32
-              ? tc::smem_desc(v_base + st * S::kKVBytes + k * S::kKStep * 128, BN * 128, 512,
-                              tc::kSwizzle128BAtom32B)
-              : tc::smem_desc(v_base + st * S::kKVBytes + k * S::kKStep * 128, BN * 128, 1024,
-                              tc::kSwizzle128B);
-          tc::mma_ts<kTf32>(tmem + S::kOCol, p_tmem + k * 8, vd, kIdescPV,
+        for (int k = 0; k < BN / S::kKStep; ++k)
+          tc::mma_ts<kTf32>(tmem + S::kOCol, p_tmem + k * 8,
+                            vd0 + uint64_t((k * S::kKStep * 128) >> 4), kIdescPV,
                             (j > 0 || k > 0) ? 1u : 0u);
-        }
         tc::commit(&o_done[b]);
         tc::commit(&v_empty[st]);
         return true;
@@ -268,13 +271,13 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
           const int b = t % NB;
           if (!mbar_wait(kTf32 ? &k_conv[st] : &k_full[st], (t / KS) & 1, a.err)) { ok = false; break; }
           tc::fence_after_sync();
+          const uint64_t kd0 = k_desc + uint64_t(st) * uint64_t(S::kKVBytes >> 4);
 #pragma unroll
           for (int k = 0; k < D / S::kKStep; ++k) {
             const int db = k / (128 / 32), koff = (k % (128 / 32)) * 32;
-            const uint64_t qd = tc::smem_desc_sw128(q_base + db * BM * 128 + koff, 16, 1024);
-            const uint64_t kd =
-                tc::smem_desc_sw128(k_base + st * S::kKVBytes + db * BN * 128 + koff, 16, 1024);
-            tc::mma_ss<kTf32>(tmem + b * S::kSCols, qd, kd, kIdescQK, k > 0 ? 1u : 0u);
+            tc::mma_ss<kTf32>(tmem + b * S::kSCols, q_desc + uint64_t((db * BM * 128 + koff) >> 4),
+                              kd0 + uint64_t((db * BN * 128 + koff) >> 4), kIdescQK,
+                              k > 0 ? 1u : 0u);
           }
           tc::commit(&s_full[b]);
           tc::commit(&k_empty[st]);

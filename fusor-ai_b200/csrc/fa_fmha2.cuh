@@ -281,19 +281,24 @@ __global__ void __launch_bounds__(kFmha2Threads, 1)
   } else if (warp == 1) {
     // ---- MMA issuer ----------------------------------------------------------------------
     if (lane == 0) {
-      const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV);
+      // The descriptors differ only in their start address (16-byte units in the low bits;
+      // shared-memory addresses stay below 2^18): built once, offsets added per stage and K step
+      // (the issue of the MMAs is on this thread's critical path).
+      const uint64_t q_desc = tc::smem_desc_sw128(smem_u32(sQ), 16, 1024);
+      const uint64_t k_desc = tc::smem_desc_sw128(smem_u32(sK), 16, 1024);
+      const uint64_t v_desc = tc::smem_desc(smem_u32(sV), BN * 128, 1024, tc::kSwizzle128B);
       bool ok = mbar_wait(q_full, 0, a.err);
       int pv_count[2] = {0, 0};
       auto issue_s = [&](int i, int L) {
         const int st = L % S::kStages;
+        const uint64_t qd0 = q_desc + uint64_t(i * S::kQBytes >> 4);
+        const uint64_t kd0 = k_desc + uint64_t(st) * uint64_t(S::kKVBytes >> 4);
 #pragma unroll
         for (int k = 0; k < D / S::kKStep; ++k) {
           const int db = k / 4, koff = (k % 4) * 32;
-          const uint64_t qd =
-              tc::smem_desc_sw128(q_base + i * S::kQBytes + db * BM * 128 + koff, 16, 1024);
-          const uint64_t kd =
-              tc::smem_desc_sw128(k_base + st * S::kKVBytes + db * BN * 128 + koff, 16, 1024);
-          tc::mma_ss<false>(tmem + i * S::kTileCols, qd, kd, kIdescQK, k > 0 ? 1u : 0u);
+          tc::mma_ss<false>(tmem + i * S::kTileCols, qd0 + uint64_t((db * BM * 128 + koff) >> 4),
+                            kd0 + uint64_t((db * BN * 128 + koff) >> 4), kIdescQK,
+                            k > 0 ? 1u : 0u);
         }
         tc::commit(&s_full[i]);
       };
@@ -304,13 +309,12 @@ __global__ void __launch_bounds__(kFmha2Threads, 1)
         if (!mbar_wait(&v_full[st], (L / S::kStages) & 1, a.err)) return false;
         tc::fence_after_sync();
         const uint32_t p_tmem = tmem + i * S::kTileCols;
+        const uint64_t vd0 = v_desc + uint64_t(st) * uint64_t(S::kKVBytes >> 4);
 #pragma unroll
-        for (int k = 0; k < BN / S::kKStep; ++k) {
-          const uint64_t vd = tc::smem_desc(v_base + st * S::kKVBytes + k * S::kKStep * 128,
-                                            BN * 128, 1024, tc::kSwizzle128B);
-          tc::mma_ts<false>(tmem + i * S::kTileCols + 128, p_tmem + k * 8, vd, kIdescPV,
+        for (int k = 0; k < BN / S::kKStep; ++k)
+          tc::mma_ts<false>(tmem + i * S::kTileCols + 128, p_tmem + k * 8,
+                            vd0 + uint64_t((k * S::kKStep * 128) >> 4), kIdescPV,
                             (c > 0 || k > 0) ? 1u : 0u);
-        }
         tc::commit(&o_done[i]);
         pv_count[i] = c + 1;
         return true;

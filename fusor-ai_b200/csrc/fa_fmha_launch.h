@@ -72,6 +72,10 @@ bool fmha_splits_supported(int dtype_bf16, int head_dim);
 // tensor-core decode's K and V tiles).
 bool encode_cache_map_bf16(void* map, const void* base, uint64_t rows, uint64_t z,
                            uint64_t z_stride_bytes);
+// A TMA map over a 2-D f32 array [y][x] (rows y_stride_bytes apart) with box_x x box_y boxes,
+// 128-byte swizzled (box_x = 32), zero fill past the edges.
+bool encode_map_f32(void* map, const void* base, uint64_t x, uint64_t y, uint64_t y_stride_bytes,
+                    uint32_t box_x, uint32_t box_y);
 int fmha_block_n(int dtype_bf16, int head_dim);
 cudaError_t launch_fmha(const FmhaLaunch& launch, cudaStream_t stream);
 

@@ -155,6 +155,27 @@ struct ProjectArgs {
 cudaError_t launch_project(int kt, int nr, const ProjectArgs& p, const RopeArgs& r, size_t smem,
                            cudaStream_t stream);
 
+// The qkv projection of many rows on the tensor cores (fa_project_tc.cu): qkv = x . W^T + b in
+// three tf32 products, the hidden dimension in `splits` ranges.
+struct ProjectTcArgs {
+  const float* x;        // row r at x + r*x_stride: hidden values (16-byte aligned rows)
+  int64_t x_stride;
+  const float* weight;   // output column c at weight + c*w_stride (16-byte aligned rows)
+  int64_t w_stride;
+  const float* bias;     // outputs values, or nullptr
+  int hidden, outputs, rows;
+  int k_blocks;          // (hidden + 31) / 32
+  int splits;            // 1 to 8, at most k_blocks: the CTAs of a tile
+  float* qkv;            // row r at qkv + r*qkv_stride
+  int64_t qkv_stride;
+  float* partials;       // splits > 1: [tile][split][rows per tile][128] floats
+  int* counters;         // splits > 1: one per tile (column block x row tile), zero between launches
+  unsigned* err;
+};
+// Rows per CTA tile (the MMA's N) for `rows` rows: 16, 32 or 64.
+int project_tc_rows_per_tile(int rows);
+cudaError_t launch_project_tc(const ProjectTcArgs& args, cudaStream_t stream);
+
 // The tensor-core decode over bf16 caches (fa_decode_tc.cu): `grid` persistent CTAs.
 struct DtcArgs;
 cudaError_t launch_decode_tc(const DtcArgs& args, int grid, cudaStream_t stream);

@@ -41,6 +41,14 @@ CASES = [
     ("qwen3_norms_interleaved", 8, 2, 128, 1024, 9, 17, fa.ROPE_INTERLEAVED, True, fa.F32),
     ("bf16_cache_no_rope", 4, 4, 32, 256, 2, 5, fa.ROPE_NONE, False, fa.BF16),
     ("llama_dims_decode", 32, 8, 128, 4096, 1, 300, fa.ROPE_HALF, False, fa.F32),
+    # from 16 rows on the tensor cores (three tf32 products), the hidden dimension split over a
+    # cluster: 16 rows (7 splits), a Llama-shaped batch of 64 (3 splits), a hidden dimension that
+    # is not a whole number of 32-value blocks with 40 rows over a bf16 cache, and 300 rows
+    # (three 128-row tiles, the last one ragged)
+    ("qwen2_rows16", 14, 2, 64, 896, 16, 7, fa.ROPE_HALF, False, fa.F32),
+    ("llama_dims_rows64", 32, 8, 128, 4096, 64, 300, fa.ROPE_HALF, False, fa.F32),
+    ("ragged_hidden_rows40_bf16", 8, 2, 128, 900, 40, 3, fa.ROPE_INTERLEAVED, True, fa.BF16),
+    ("rows300", 8, 2, 64, 512, 300, 0, fa.ROPE_HALF, False, fa.F32),
 ]
 
 
@@ -105,16 +113,19 @@ def test_projected_decode_step_matches_the_oracle_phase(torch):
     assert max_abs(got, want) <= TOL_F32
 
 
-def test_projected_batch_keeps_each_sequence_in_its_own_cache(torch):
-    """Twelve sequences' rows in one fused launch: each keeps into its own cache at its own
-    position, as twelve single-sequence fused calls would (projected within float rounding)."""
+@pytest.mark.parametrize("n", [12, 64])
+def test_projected_batch_keeps_each_sequence_in_its_own_cache(torch, n):
+    """A batch of sequences' rows in one projection (12 on the CUDA cores, 64 on the tensor
+    cores): each keeps into its own cache at its own position, as single-sequence calls would
+    (projected within float rounding)."""
     shape = fa.Shape(1, 8, 2, 64)
-    hidden, n = 512, 12
+    hidden = 512
     w, b = layer_weights(90, shape, hidden)
     x = normal(92, (n, hidden))
     positions = [5 + 7 * i for i in range(n)]
+    cap = positions[-1] + 1
     angles = fa.rotary_angles(fa.Rotation(base=1e6), 64, positions)
-    caches = [fa.KvCache(shape, 128) for _ in range(n)]
+    caches = [fa.KvCache(shape, cap) for _ in range(n)]
     spans = [fa.Span(1, p, fa.Mask.causal()) for p in positions]
     batch = fa.Batch(caches, spans)
     q = torch.zeros((n, shape.width), device="cuda")
@@ -124,7 +135,7 @@ def test_projected_batch_keeps_each_sequence_in_its_own_cache(torch):
     fa.device_status()
     qkv = oracle.project(x, w, b)
     for i, (c, p) in enumerate(zip(caches, positions)):
-        cpu = oracle.Cache(1, shape.heads, shape.kv_heads, 64, 128)
+        cpu = oracle.Cache(1, shape.heads, shape.kv_heads, 64, cap)
         qi = qkv[i:i + 1].copy()
         cpu.attention_input(0, 1, p, fa.ROPE_HALF, angles[i:i + 1], qi, qi.shape[1])
         k, v = c.copy_rows()
@@ -132,8 +143,28 @@ def test_projected_batch_keeps_each_sequence_in_its_own_cache(torch):
         assert max_abs(v.cpu().numpy()[0, :, p], cpu.values[0, :, p]) <= 1e-5
         assert max_abs(q.cpu().numpy()[i], qi[0, :shape.width]) <= 1e-5
         # nothing else of the cache was written
-        others = np.delete(np.arange(128), p)
+        others = np.delete(np.arange(cap), p)
         assert not k.cpu().numpy()[0][:, others].any()
+
+
+def test_tensor_core_projection_without_bias(torch):
+    """The tensor-core projection with no bias (32 rows, Qwen3's 16/8 x 128 heads over a 2048
+    hidden dimension): the projected rows against the oracle's."""
+    shape = fa.Shape(1, 16, 8, 128)
+    hidden, rows = 2048, 32
+    w, _ = layer_weights(95, shape, hidden, bias=False)
+    x = normal(96, (rows, hidden))
+    span = fa.Span(rows, 0, fa.Mask.causal())
+    cache = fa.KvCache(shape, rows)
+    qkv = torch.zeros((rows, shape.qkv), device="cuda")
+    cache.attention_input_projected(0, span, dev(torch, x), dev(torch, w), None, rope=fa.ROPE_NONE,
+                                    qkv_out=qkv)
+    torch.cuda.synchronize()
+    fa.device_status()
+    want = oracle.project(x, w, None)
+    got = qkv.cpu().numpy()
+    print(compare("tensor-core projection, no bias", got, want))
+    assert max_abs(got, want) <= 2e-5 * max(1.0, np.abs(want).max())
 
 
 def test_projection_argument_errors(torch):
