@@ -8,7 +8,8 @@ hot path over the batch: RoPE + keep of each sequence's new row, then attention 
 over its cache. `value` is tokens/s of the whole job (64 tokens per step); with N GPUs the
 sequences are split across ranks by total length with no collective (total work fixed).
 
-Other configurations (`--config c1|c2|c3bf16|c4|c5|prefill|proj|prologue`) run the same way; the
+Other configurations (`--config c1|c2|c3bf16|decode256|c4|c5|prefill|prefill_f32|qwen35|proj|
+proj64|prologue`) run the same way; the
 default run adds them under "configs" in the same line. `--cpu-baselines` (1 GPU) also times the
 host restatement of the reference's CPU path for C1, C2, C4 and a slice of C5, beside each.
 
@@ -182,10 +183,16 @@ class Workload:
 
 
 class C3Decode(Workload):
-    def __init__(self, torch, fa, rank, world, dtype, sequences=C3_SEQS):
+    """A batched decode: C3's 64 sequences (lengths U[512, 8192], seed 301) at C3's shape (32/8
+    heads x 128) over an f32 or a bf16 cache; `decode256`: the same sequences at Qwen3.5's gated
+    layers' shape (8/2 heads x 256) over a bf16 cache."""
+
+    def __init__(self, torch, fa, rank, world, dtype, sequences=C3_SEQS, dims=None, name=None):
         self.torch, self.fa = torch, fa
         self.dtype = dtype
-        self.name = "c3" if dtype == fa.F32 else "c3bf16"
+        self.name = name or ("c3" if dtype == fa.F32 else "c3bf16")
+        heads, kv, d = dims or (C3_HEADS, C3_KV, C3_D)
+        self.dims = (heads, kv, d)
         # f32 caches decode on the CUDA cores (split-KV), bf16 caches on the tensor cores
         self.kernel = "attend_kernel" if dtype == fa.F32 else "decode_tc_kernel"
         self.sharded = True
@@ -194,7 +201,7 @@ class C3Decode(Workload):
         mine = shard_sequences(lengths, world)[rank]
         self.tokens = len(lengths)
         self.lengths = [int(lengths[i]) for i in mine]
-        shape = fa.Shape(1, C3_HEADS, C3_KV, C3_D)
+        shape = fa.Shape(1, heads, kv, d)
         self.shape = shape
         # every sequence's keys and values from its own seed, and the batch's qkv rows from one:
         # the job is the same whatever the number of GPUs it is split over
@@ -203,8 +210,8 @@ class C3Decode(Workload):
         for i, n in zip(mine, self.lengths):
             gen = torch.Generator("cuda").manual_seed(1000 + int(i))
             c = fa.KvCache(shape, n + 1, dtype)
-            k = torch.randn((1, C3_KV, n, C3_D), device="cuda", generator=gen).to(tdt)
-            v = torch.randn((1, C3_KV, n, C3_D), device="cuda", generator=gen).to(tdt)
+            k = torch.randn((1, kv, n, d), device="cuda", generator=gen).to(tdt)
+            v = torch.randn((1, kv, n, d), device="cuda", generator=gen).to(tdt)
             c.put_rows(k, v)
             del k, v
             self.caches.append(c)
@@ -216,7 +223,7 @@ class C3Decode(Workload):
         self.qkv = qkv_all[list(mine)].contiguous()
         del qkv_all
         self.angles = torch.from_numpy(
-            fa.rotary_angles(fa.Rotation(base=1e6), C3_D, self.lengths)).cuda()
+            fa.rotary_angles(fa.Rotation(base=1e6), d, self.lengths)).cuda()
         self.q = torch.zeros((b, shape.width), device="cuda")
         self.out = torch.zeros((b, shape.width), device="cuda")
         self.launches_per_step = 2 * ((b + 255) // 256)
@@ -231,7 +238,7 @@ class C3Decode(Workload):
         self.d2h = self.h_out.numel() * 4
         esize = 4 if dtype == fa.F32 else 2
         keys = sum(n + 1 for n in self.lengths)
-        self.bytes = keys * C3_KV * C3_D * 2 * esize + 2 * b * shape.width * 4
+        self.bytes = keys * kv * d * 2 * esize + 2 * b * shape.width * 4
 
     def phases(self):
         return (lambda: self.batch.attention_input(0, self.qkv, self.q, self.angles,
@@ -258,7 +265,7 @@ class C3Decode(Workload):
         wants = []
         for j, (c, n) in enumerate(zip(self.caches, self.lengths)):
             k, v = c.copy_rows(n)
-            oc = oracle.Cache(1, C3_HEADS, C3_KV, C3_D, n + 1)
+            oc = oracle.Cache(1, *self.dims, n + 1)
             oc.keys[:, :, :n] = k.float().cpu().numpy()
             oc.values[:, :, :n] = v.float().cpu().numpy()
             del k, v
@@ -1307,6 +1314,9 @@ def run_ours(args):
         if name in ("c3", "c3bf16"):
             return C3Decode(torch, fa, rank, world, fa.F32 if name == "c3" else fa.BF16,
                             args.sequences)
+        if name == "decode256":
+            return C3Decode(torch, fa, rank, world, fa.BF16, args.sequences, dims=(8, 2, 256),
+                            name="decode256")
         if name == "c1":
             return SingleDecode(torch, fa, "c1", 14, 2, 64, 1024)
         if name == "c4":
@@ -1352,7 +1362,8 @@ def run_ours(args):
         "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": steps,
         "warmup": warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
         "scaling": "strong" if w.sharded else "weak", "vs_baseline": None,
-        "dtype": {"c3bf16": "bf16-kv/f32", "c5": "bf16/f32-acc", "prefill": "bf16-kv/f32",
+        "dtype": {"c3bf16": "bf16-kv/f32", "decode256": "bf16-kv/f32", "c5": "bf16/f32-acc",
+                  "prefill": "bf16-kv/f32",
                   "qwen35": "bf16-kv/f32", "prefill_f32": "f32 (tf32 tensor cores)",
                   "prologue": "f32-in/bf16-out"}.get(args.config, "f32"),
         "data": "synthetic N(0,1) (seeded), random keys/values of the config's shape",
@@ -1375,8 +1386,8 @@ def run_ours(args):
     torch.cuda.empty_cache()
     if args.config == "c3" and not args.no_extras and args.sequences == C3_SEQS:
         extras = {}
-        names = (("c1", "c2", "c3bf16", "c4", "c5", "prefill", "prefill_f32", "qwen35", "proj",
-                  "proj64", "prologue") if world == 1 else ("c4", "c5"))
+        names = (("c1", "c2", "c3bf16", "decode256", "c4", "c5", "prefill", "prefill_f32", "qwen35",
+                  "proj", "proj64", "prologue") if world == 1 else ("c4", "c5"))
         for name in names:
             x = build(name)
             xs = min(steps, 50 if name == "c5" else 200)
@@ -1428,6 +1439,10 @@ def config_of(name, world):
                "kv_dtype": "f32", "rope_base": 1e6},
         "c3bf16": {"workload": "C3 batched GQA decode, bf16 cache", "sequences": 64, "heads": 32,
                    "kv_heads": 8, "head_dim": 128, "kv_dtype": "bf16"},
+        "decode256": {"workload": "C3's 64 sequences at Qwen3.5's gated layers' shape, bf16 cache "
+                      "(tensor-core decode, head_dim 256 in two halves)", "sequences": 64,
+                      "heads": 8, "kv_heads": 2, "head_dim": 256, "kv_dtype": "bf16",
+                      "cache_lengths": "U[512, 8192] seed 301"},
         "c1": {"workload": "C1 Qwen2-0.5B decode", "heads": 14, "kv_heads": 2, "head_dim": 64,
                "position": 1024, "mask": "causal"},
         "c2": {"workload": "C2 Qwen2-0.5B prefill", "rows": 512, "heads": 14, "kv_heads": 2,
@@ -1463,15 +1478,18 @@ def config_of(name, world):
     c["parallelism"] = {
         "c3": f"sequences over {world} GPU(s), no collective",
         "c3bf16": f"sequences over {world} GPU(s), no collective",
+        "decode256": f"sequences over {world} GPU(s), no collective",
         "c4": (f"KV range over {world} GPU(s); (max, sum, o) exchanged over NVLink peer memory "
                "by one kernel (P2P stores of step-stamped words) that merges" if world > 1
                else "1 GPU"),
         "c5": f"query rows in whole 256-row pairs over {world} GPU(s), all heads, no collective",
     }.get(name, f"replicas x{world}")
-    c["l2"] = ("inputs larger than L2" if name in ("c3", "c3bf16", "c4", "c5", "prologue", "prefill",
+    c["l2"] = ("inputs larger than L2" if name in ("c3", "c3bf16", "decode256", "c4", "c5",
+                                                   "prologue", "prefill",
                                                    "prefill_f32", "qwen35")
                else "L2 flushed between steps (clean lines left)")
-    if name in ("c1", "c2", "c3", "c3bf16", "proj", "proj64", "prologue", "prefill", "prefill_f32",
+    if name in ("c1", "c2", "c3", "c3bf16", "decode256", "proj", "proj64", "prologue", "prefill",
+                "prefill_f32",
                 "qwen35") or \
             (name == "c4" and world > 1):
         c["launch"] = "the step's calls replayed as captured CUDA graphs"
@@ -1547,7 +1565,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="c3",
-                    choices=["c1", "c2", "c3", "c3bf16", "c4", "c5", "prefill", "prefill_f32",
+                    choices=["c1", "c2", "c3", "c3bf16", "decode256", "c4", "c5", "prefill",
+                             "prefill_f32",
                              "qwen35", "proj", "proj64", "prologue"])
     ap.add_argument("--sequences", type=int, default=C3_SEQS,
                     help="C3 sequences (a smaller batch for profiling captures)")

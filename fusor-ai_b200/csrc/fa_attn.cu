@@ -471,9 +471,9 @@ Plan plan_for_span(const fa_kvcache* c, const fa_span* span, const std::vector<i
   return plan_span(c, std::max(span->rows, 1), max_keys);
 }
 
-// Whether a batch of one-row decodes runs on the tensor cores: bf16 caches of head_dim 128 with
-// their TMA maps, at most 16 query heads per KV head, and every row's keys one run of cache slots
-// without a ring wrap (a window that wraps, or Groups' two runs, decode on the CUDA cores).
+// Whether a batch of one-row decodes runs on the tensor cores: bf16 caches of head_dim 128 or 256
+// with their TMA maps, at most 16 query heads per KV head, and every row's keys one run of cache
+// slots without a ring wrap (a window that wraps, or Groups' two runs, decode on the CUDA cores).
 #ifndef FA_DECODE_TC
 #define FA_DECODE_TC 1
 #endif
@@ -481,7 +481,8 @@ bool decode_on_tensor_cores(fa_kvcache* const* caches, const std::vector<fa::Run
                             int batch) {
   if (!FA_DECODE_TC) return false;
   const fa_kvcache* c0 = caches[0];
-  if (c0->dtype != FA_BF16 || c0->head_dim != 128 || c0->heads / c0->kv_heads > fa::kDtcN)
+  if (c0->dtype != FA_BF16 || (c0->head_dim != 128 && c0->head_dim != 256) ||
+      c0->heads / c0->kv_heads > fa::kDtcN)
     return false;
   for (int i = 0; i < batch; ++i) {
     const fa_kvcache* c = caches[i];
@@ -622,7 +623,7 @@ int attend_batch_tc(fa_kvcache* const* caches, const std::vector<fa::Runs>& runs
     for (int c = 0; c < ctas; ++c) per_cta[c + 1] += per_cta[c];
     for (int c = 0; c <= ctas; ++c) a.cta_first[c] = uint16_t(per_cta[c]);
     for (int u : sorted) a.order[per_cta[owner[u]]++] = uint16_t(u);
-    cudaError_t e = fa::launch_decode_tc(a, ctas, s);
+    cudaError_t e = fa::launch_decode_tc(a, c0->head_dim, ctas, s);
     if (e != cudaSuccess) return cuda_fail(e, "tensor-core decode launch");
   }
   return FA_OK;
@@ -884,14 +885,14 @@ int fa_kvcache_create(int32_t layers, int32_t heads, int32_t kv_heads, int32_t h
     fa_kvcache_destroy(c);
     return cuda_fail(e, "cache allocation");
   }
-  if (dtype == FA_BF16 && head_dim == 128) {
+  if (dtype == FA_BF16 && (head_dim == 128 || head_dim == 256)) {
     // TMA maps of the keys and values for the tensor-core decode, made once: [layers x kv heads]
-    // [capacity][128] (a cache that cannot have them decodes on the CUDA cores)
+    // [capacity][head_dim] (a cache that cannot have them decodes on the CUDA cores)
     alignas(64) unsigned char maps[256];
-    const uint64_t z_stride = uint64_t(capacity) * 128 * 2;
-    if (fa::encode_cache_map_bf16(maps, c->keys, uint64_t(capacity), uint64_t(layers) * kv_heads,
-                                  z_stride) &&
-        fa::encode_cache_map_bf16(maps + 128, c->values, uint64_t(capacity),
+    const uint64_t z_stride = uint64_t(capacity) * head_dim * 2;
+    if (fa::encode_cache_map_bf16(maps, c->keys, uint64_t(head_dim), uint64_t(capacity),
+                                  uint64_t(layers) * kv_heads, z_stride) &&
+        fa::encode_cache_map_bf16(maps + 128, c->values, uint64_t(head_dim), uint64_t(capacity),
                                   uint64_t(layers) * kv_heads, z_stride)) {
       e = cudaMalloc(&c->tc_maps.ptr, sizeof(maps));
       if (e == cudaSuccess) {

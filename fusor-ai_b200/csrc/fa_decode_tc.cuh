@@ -5,10 +5,12 @@
 // softmax of each key.
 //
 // Transposed so that the keys fill the 128 rows of the MMA: per tile of 128 keys,
-//   S^T (128 keys x 16) = K (128 x 128 head_dim) . Q^T (128 x 16: the KV head's G <= 16 query
+//   S^T (128 keys x 16) = K (128 x D head_dim) . Q^T (D x 16: the KV head's G <= 16 query
 //                        heads, zero-padded),
-//   O^T (128 head_dim x 16) += V^T (128 x 128 keys) . P^T (128 keys x 16),
-// accumulators in TMEM. A persistent CTA per SM walks the (row, KV head, chunk of keys) units;
+//   O^T (D head_dim x 16) += V^T (D x 128 keys) . P^T (128 keys x 16),
+// accumulators in TMEM, D = 128 or 256. The K and V rings hold 128 keys x 128 head_dim entries:
+// a tile of head_dim 256 is two entries of each (its halves), S^T adds up both halves' products
+// and O^T is two 128-row accumulators, so the rings' shared memory is that of head_dim 128. A persistent CTA per SM walks the (row, KV head, chunk of keys) units;
 // warps:
 //   warps 0, 6  TMA producers of the K and of the V tiles (128-byte swizzled boxes of the cache's
 //               own tensor maps, one pair per cache), 3 stages each; plain per-CTA loads only;
@@ -28,9 +30,9 @@
 
 namespace fa {
 
-// Byte offset of element (r, k) of a 16-row x 128-element bf16 operand in the 128-byte swizzled
-// K-major layout the descriptors below read: two 64-element blocks of 16 rows x 128 bytes, the
-// 16-byte chunks of a row XOR-ed with the row index within its 8-row group.
+// Byte offset of element (r, k) of a 16-row bf16 operand in the 128-byte swizzled K-major layout
+// the descriptors below read: 64-element blocks of 16 rows x 128 bytes, the 16-byte chunks of a
+// row XOR-ed with the row index within its 8-row group.
 __device__ __forceinline__ uint32_t dtc_op_offset(int r, int k) {
   const int block = k >> 6, within = k & 63;
   return uint32_t(block * (kDtcN * 128) + r * 128 + ((((within >> 3) ^ (r & 7))) << 4) +
@@ -54,13 +56,19 @@ __device__ __forceinline__ void dtc_unit(const DtcArgs& a, int u, int* row, int*
 }
 
 // kG: the group's query heads rounded up to a power of two (<= kDtcN), the per-head work of the
-// softmax threads.
-template <int kG>
+// softmax threads; D: the head_dim, 128 or 256.
+template <int D, int kG>
 __global__ void __launch_bounds__(kDtcThreads, 1) decode_tc_kernel(const __grid_constant__ DtcArgs a) {
+  static_assert(D == 128 || D == 256, "head_dim");
+  static_assert(dtc_smem_bytes(D) + 1024 <= 227 * 1024, "shared memory");
+  constexpr int kHalves = D / kDtcD;            // ring entries per tile, O^T accumulators
+  constexpr int kQBytes = dtc_q_bytes(D);
   constexpr uint32_t kIdescS = tc::instr_desc_ab(1u, false, false, kDtcN, kDtcKeys);
   constexpr uint32_t kIdescPV = tc::instr_desc_ab(1u, true, false, kDtcN, kDtcD);
   constexpr int kS = 3;            // S^T and P^T buffers
-  constexpr uint32_t kOCol = 48;   // TMEM: S^T 0 | S^T 1 | S^T 2 | O^T, 16 columns each
+  // TMEM: S^T 0 | S^T 1 | S^T 2 | O^T (one 16-column accumulator per 128 head_dim rows)
+  constexpr uint32_t kOCol = 48;
+  constexpr uint32_t kTmemCols = kHalves == 1 ? 64 : 128;
 
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -68,8 +76,8 @@ __global__ void __launch_bounds__(kDtcThreads, 1) decode_tc_kernel(const __grid_
   unsigned char* sK = smem;
   unsigned char* sV = sK + kDtcStages * kDtcTileBytes;
   unsigned char* sQ = sV + kDtcStages * kDtcTileBytes;  // two buffers
-  unsigned char* sP = sQ + 2 * kDtcOpBytes;             // three buffers
-  float* s_merge = reinterpret_cast<float*>(sP + kS * kDtcOpBytes);
+  unsigned char* sP = sQ + 2 * kQBytes;                 // three buffers
+  float* s_merge = reinterpret_cast<float*>(sP + kS * kDtcPBytes);
   uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(s_merge) +
                                                kDtcMergeBytes);
   uint64_t* k_full = bars;
@@ -110,7 +118,7 @@ __global__ void __launch_bounds__(kDtcThreads, 1) decode_tc_kernel(const __grid_
     mbar_init(mma_drained, 1);
     mbar_fence_init();
   }
-  if (warp == 1) tc::tmem_alloc(tmem_slot, 64);
+  if (warp == 1) tc::tmem_alloc(tmem_slot, kTmemCols);
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
@@ -131,13 +139,15 @@ __global__ void __launch_bounds__(kDtcThreads, 1) decode_tc_kernel(const __grid_
         const DtcRow& r = a.rows[row];
         const void* map = keys ? r.kmap : r.vmap;
         const int tiles = (j1 - j0 + kDtcKeys - 1) / kDtcKeys;
-        for (int t = 0; t < tiles; ++t, ++T) {
+        for (int e = 0; e < tiles * kHalves; ++e, ++T) {
+          // ring entry T: head_dim half e % kHalves of the unit's tile e / kHalves
           const int st = T % kDtcStages;
+          const int t = e / kHalves, half = e % kHalves;
           if (!mbar_wait(&empty[st], ((T / kDtcStages) & 1) ^ 1, a.err)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[st], kDtcTileBytes);
           for (int db = 0; db < kDtcD / 64; ++db)
-            tc::tma_load_3d(dst + st * kDtcTileBytes + db * (kDtcKeys * 128), map, db * 64,
-                            r.b0 + j0 + t * kDtcKeys, r.z0 + kv, &full[st]);
+            tc::tma_load_3d(dst + st * kDtcTileBytes + db * (kDtcKeys * 128), map,
+                            half * kDtcD + db * 64, r.b0 + j0 + t * kDtcKeys, r.z0 + kv, &full[st]);
           issued = T + 1;
         }
       }
@@ -152,24 +162,30 @@ __global__ void __launch_bounds__(kDtcThreads, 1) decode_tc_kernel(const __grid_
       const uint32_t q_base = smem_u32(sQ), p_base = smem_u32(sP);
       bool ok = true;
       int T = 0, ui = 0;
-      // O^T += V^T P^T of global tile T2 (`first`: the first of its unit, which overwrites O^T)
+      // O^T += V^T P^T of global tile T2 (`first`: the first of its unit, which overwrites O^T),
+      // one accumulator per head_dim half (V ring entries T2 * kHalves + h)
       auto issue_pv = [&](int T2, bool first) {
-        const int st = T2 % kDtcStages, b = T2 % kS;
+        const int b = T2 % kS;
         if (first && ui > 0 && !mbar_wait(o_free, (ui - 1) & 1, a.err)) return false;
         if (!mbar_wait(&p_full[b], (T2 / kS) & 1, a.err)) return false;
-        if (!mbar_wait(&v_full[st], (T2 / kDtcStages) & 1, a.err)) return false;
-        tc::fence_after_sync();
 #pragma unroll
-        for (int k = 0; k < kDtcKeys / 16; ++k) {
-          // A = V^T: the V tile's rows are keys (the K of this product), 64-element head_dim
-          // blocks kDtcKeys * 128 bytes apart (M-major, 128-byte swizzle)
-          const uint64_t ad = tc::smem_desc(v_base + st * kDtcTileBytes + k * 16 * 128,
-                                            kDtcKeys * 128, 1024, tc::kSwizzle128B);
-          const uint64_t bd = tc::smem_desc_sw128(
-              p_base + b * kDtcOpBytes + (k >> 2) * (kDtcN * 128) + (k & 3) * 32, 16, 1024);
-          tc::mma_ss<false>(tmem + kOCol, ad, bd, kIdescPV, (!first || k > 0) ? 1u : 0u);
+        for (int h = 0; h < kHalves; ++h) {
+          const int E = T2 * kHalves + h, st = E % kDtcStages;
+          if (!mbar_wait(&v_full[st], (E / kDtcStages) & 1, a.err)) return false;
+          tc::fence_after_sync();
+#pragma unroll
+          for (int k = 0; k < kDtcKeys / 16; ++k) {
+            // A = V^T: the V entry's rows are keys (the K of this product), 64-element head_dim
+            // blocks kDtcKeys * 128 bytes apart (M-major, 128-byte swizzle)
+            const uint64_t ad = tc::smem_desc(v_base + st * kDtcTileBytes + k * 16 * 128,
+                                              kDtcKeys * 128, 1024, tc::kSwizzle128B);
+            const uint64_t bd = tc::smem_desc_sw128(
+                p_base + b * kDtcPBytes + (k >> 2) * (kDtcN * 128) + (k & 3) * 32, 16, 1024);
+            tc::mma_ss<false>(tmem + kOCol + 16 * h, ad, bd, kIdescPV,
+                              (!first || k > 0) ? 1u : 0u);
+          }
+          tc::commit(&v_empty[st]);
         }
-        tc::commit(&v_empty[st]);
         tc::commit(&o_done[T2 & 1]);
         return true;
       };
@@ -181,20 +197,26 @@ __global__ void __launch_bounds__(kDtcThreads, 1) decode_tc_kernel(const __grid_
         const int qb = ui & 1;
         if (!mbar_wait(&q_ready[qb], (ui >> 1) & 1, a.err)) { ok = false; break; }
         for (int t = 0; t < tiles; ++t, ++T) {
-          const int st = T % kDtcStages;
-          if (!mbar_wait(&k_full[st], (T / kDtcStages) & 1, a.err)) { ok = false; break; }
-          tc::fence_after_sync();
+          // S^T of tile T over its head_dim halves (K ring entries T * kHalves + h)
 #pragma unroll
-          for (int k = 0; k < kDtcD / 16; ++k) {
-            const int db = k >> 2, koff = (k & 3) * 32;
-            const uint64_t ad = tc::smem_desc_sw128(
-                k_base + st * kDtcTileBytes + db * (kDtcKeys * 128) + koff, 16, 1024);
-            const uint64_t bd = tc::smem_desc_sw128(
-                q_base + qb * kDtcOpBytes + db * (kDtcN * 128) + koff, 16, 1024);
-            tc::mma_ss<false>(tmem + (T % kS) * 16, ad, bd, kIdescS, k > 0 ? 1u : 0u);
+          for (int h = 0; h < kHalves; ++h) {
+            const int E = T * kHalves + h, st = E % kDtcStages;
+            if (!mbar_wait(&k_full[st], (E / kDtcStages) & 1, a.err)) { ok = false; break; }
+            tc::fence_after_sync();
+#pragma unroll
+            for (int k = 0; k < kDtcD / 16; ++k) {
+              const int db = k >> 2, koff = (k & 3) * 32;
+              const uint64_t ad = tc::smem_desc_sw128(
+                  k_base + st * kDtcTileBytes + db * (kDtcKeys * 128) + koff, 16, 1024);
+              const uint64_t bd = tc::smem_desc_sw128(
+                  q_base + qb * kQBytes + (h * 2 + db) * (kDtcN * 128) + koff, 16, 1024);
+              tc::mma_ss<false>(tmem + (T % kS) * 16, ad, bd, kIdescS,
+                                (h > 0 || k > 0) ? 1u : 0u);
+            }
+            tc::commit(&k_empty[st]);
           }
+          if (!ok) break;
           tc::commit(&s_full[T % kS]);
-          tc::commit(&k_empty[st]);
           // the P.V of two tiles back: S^T_{T+1} may then reuse that tile's S^T buffer
           if (t >= 2 && !issue_pv(T - 2, t == 2)) { ok = false; break; }
         }
@@ -216,7 +238,7 @@ __global__ void __launch_bounds__(kDtcThreads, 1) decode_tc_kernel(const __grid_
     const int sw = warp - 2;              // this warp's slot in the cross-warp reductions
     const uint32_t lane_base = tmem + (uint32_t(wq * 32) << 16);
     // Q^T and P^T buffers start zero: the padding rows (heads >= group) stay zero.
-    for (int i = tid; i < (2 + kS) * kDtcOpBytes / 16; i += 128)
+    for (int i = tid; i < (2 * kQBytes + kS * kDtcPBytes) / 16; i += 128)
       reinterpret_cast<uint4*>(sQ)[i] = make_uint4(0, 0, 0, 0);
     named_sync(1, 128);
     const int g = a.group;
@@ -224,10 +246,10 @@ __global__ void __launch_bounds__(kDtcThreads, 1) decode_tc_kernel(const __grid_
     auto write_q = [&](int u, int qb) {
       int row, kv, j0, j1;
       dtc_unit(a, u, &row, &kv, &j0, &j1);
-      const float* qrow = a.q + int64_t(row) * a.q_stride + int64_t(kv * g) * kDtcD;
-      unsigned char* qdst = sQ + qb * kDtcOpBytes;
-      for (int i = tid; i < g * kDtcD; i += 128)
-        *reinterpret_cast<__nv_bfloat16*>(qdst + dtc_op_offset(i / kDtcD, i % kDtcD)) =
+      const float* qrow = a.q + int64_t(row) * a.q_stride + int64_t(kv * g) * D;
+      unsigned char* qdst = sQ + qb * kQBytes;
+      for (int i = tid; i < g * D; i += 128)
+        *reinterpret_cast<__nv_bfloat16*>(qdst + dtc_op_offset(i / D, i % D)) =
             __float2bfloat16_rn(qrow[i]);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       mbar_arrive(&q_ready[qb]);
@@ -314,12 +336,15 @@ __global__ void __launch_bounds__(kDtcThreads, 1) decode_tc_kernel(const __grid_
             ok = __all_sync(0xffffffffu, mbar_wait(&o_done[(T - 1) & 1], ((T - 1) >> 1) & 1, a.err));
             if (ok) {
               tc::fence_after_sync();
-              uint32_t o[16];
-              tc::tmem_ld16_wait(lane_base + kOCol, o);
 #pragma unroll
-              for (int h = 0; h < kG; ++h) o[h] = __float_as_uint(__uint_as_float(o[h]) * alpha[h]);
-              tc::tmem_st16(lane_base + kOCol, o);
-              tc::tmem_wait_st();
+              for (int hf = 0; hf < kHalves; ++hf) {
+                uint32_t o[16];
+                tc::tmem_ld16_wait(lane_base + kOCol + 16 * hf, o);
+#pragma unroll
+                for (int h = 0; h < kG; ++h) o[h] = __float_as_uint(__uint_as_float(o[h]) * alpha[h]);
+                tc::tmem_st16(lane_base + kOCol + 16 * hf, o);
+                tc::tmem_wait_st();
+              }
             }
           }
         }
@@ -331,7 +356,7 @@ __global__ void __launch_bounds__(kDtcThreads, 1) decode_tc_kernel(const __grid_
         }
         // P^T_T into buffer b: the P.V that read it (tile T - 3) completed before S^T_T did
         if (ok) {
-          unsigned char* pb = sP + b * kDtcOpBytes;
+          unsigned char* pb = sP + b * kDtcPBytes;
 #pragma unroll
           for (int h = 0; h < kG; ++h)
             if (h < g)
@@ -355,20 +380,25 @@ __global__ void __launch_bounds__(kDtcThreads, 1) decode_tc_kernel(const __grid_
       for (int h = 0; h < kG; ++h)
         L[h] = (red_sum[0][h] + red_sum[1][h]) + (red_sum[2][h] + red_sum[3][h]);
       ok = __all_sync(0xffffffffu, mbar_wait(o_final, ui & 1, a.err));
-      uint32_t o[16];
+      uint32_t o[kHalves][16];
       if (ok) {
         tc::fence_after_sync();
-        tc::tmem_ld16_wait(lane_base + kOCol, o);
+#pragma unroll
+        for (int hf = 0; hf < kHalves; ++hf) tc::tmem_ld16_wait(lane_base + kOCol + 16 * hf, o[hf]);
         tc::fence_before_sync();
         mbar_arrive(o_free);  // the next unit's first P.V may overwrite O^T
       }
-      const int d = lane_row;
+      // this thread's head_dim elements: lane_row of each 128-row half
       if (r.chunks == 1) {
         if (ok) {
-          float* orow = a.out + int64_t(row) * a.out_stride + int64_t(h0) * kDtcD;
+          float* orow = a.out + int64_t(row) * a.out_stride + int64_t(h0) * D;
 #pragma unroll
-          for (int h = 0; h < kG; ++h)
-            if (h < g) orow[h * kDtcD + d] = L[h] > 0.0f ? __uint_as_float(o[h]) / L[h] : 0.0f;
+          for (int hf = 0; hf < kHalves; ++hf)
+#pragma unroll
+            for (int h = 0; h < kG; ++h)
+              if (h < g)
+                orow[h * D + hf * kDtcD + lane_row] =
+                    L[h] > 0.0f ? __uint_as_float(o[hf][h]) / L[h] : 0.0f;
         }
         continue;
       }
@@ -378,8 +408,10 @@ __global__ void __launch_bounds__(kDtcThreads, 1) decode_tc_kernel(const __grid_
 #pragma unroll
         for (int h = 0; h < kG; ++h) {
           if (h >= g) continue;
-          a.part_o[(slot0 + h) * kDtcD + d] = __uint_as_float(o[h]);
-          if (d == 0) {
+#pragma unroll
+          for (int hf = 0; hf < kHalves; ++hf)
+            a.part_o[(slot0 + h) * D + hf * kDtcD + lane_row] = __uint_as_float(o[hf][h]);
+          if (lane_row == 0) {
             a.part_ml[2 * (slot0 + h)] = m[h];
             a.part_ml[2 * (slot0 + h) + 1] = L[h];
           }
@@ -398,11 +430,11 @@ __global__ void __launch_bounds__(kDtcThreads, 1) decode_tc_kernel(const __grid_
       if (!last_flag) continue;
       __threadfence();
       float* orow = a.out + int64_t(row) * a.out_stride;
-      merge_chunk_partials<kG, kDtcD, 128>(
+      merge_chunk_partials<kG, D, 128>(
           a.part_o, a.part_ml, a.heads, h0, g, r.part_base, r.chunks, s_merge,
           kDtcMergeBytes / (4 * kG), 1, tid,
           [&](int h, int e, float, float ll, float oo) {
-            orow[(h0 + h) * kDtcD + e] = ll > 0.0f ? oo / ll : 0.0f;
+            orow[(h0 + h) * D + e] = ll > 0.0f ? oo / ll : 0.0f;
           });
     }
   }
@@ -412,7 +444,7 @@ __global__ void __launch_bounds__(kDtcThreads, 1) decode_tc_kernel(const __grid_
   __syncthreads();
   if (warp == 1) {
     tc::fence_after_sync();
-    tc::tmem_dealloc(tmem, 64);
+    tc::tmem_dealloc(tmem, kTmemCols);
   }
 }
 

@@ -8,21 +8,25 @@
 
 namespace fa {
 
-constexpr int kDtcD = 128;      // head_dim (the M of O^T)
+constexpr int kDtcD = 128;      // head_dim block of a ring entry (the M of O^T)
 constexpr int kDtcKeys = 128;   // keys per tile (the M of S^T)
 constexpr int kDtcN = 16;       // query heads per KV head, padded (the N of both products)
 constexpr int kDtcStages = 3;
 constexpr int kDtcThreads = 224;
-constexpr int kDtcTileBytes = kDtcKeys * kDtcD * 2;   // one K (or V) tile, bf16
-constexpr int kDtcOpBytes = kDtcN * kDtcD * 2;        // Q^T or one P^T buffer: 16 rows x 256 B
+constexpr int kDtcTileBytes = kDtcKeys * kDtcD * 2;   // one ring entry: 128 keys x 128 head_dim
+constexpr int kDtcPBytes = kDtcN * kDtcKeys * 2;      // one P^T buffer: 16 rows x 256 B
 constexpr int kDtcMergeBytes = 4096;
+// Q^T: 16 rows x head_dim bf16
+__host__ __device__ constexpr int dtc_q_bytes(int head_dim) { return kDtcN * head_dim * 2; }
 // K and V stages, two Q^T buffers, three P^T buffers, the merge's weights
-constexpr size_t kDtcSmemBytes = size_t(2 * kDtcStages) * kDtcTileBytes + 5 * kDtcOpBytes +
-                                 kDtcMergeBytes + 1024 /* alignment */ + 512 /* barriers */;
+__host__ __device__ constexpr size_t dtc_smem_bytes(int head_dim) {
+  return size_t(2 * kDtcStages) * kDtcTileBytes + 2 * size_t(dtc_q_bytes(head_dim)) +
+         3 * size_t(kDtcPBytes) + kDtcMergeBytes + 1024 /* alignment */ + 512 /* barriers */;
+}
 
 // One decode row: its cache's key and value tensor maps (device CUtensorMap, 64-byte aligned:
-// [layers x kv_heads][capacity][128] bf16, 64 x 128 boxes, 128-byte swizzle) and its keys, the
-// cache slots b0 .. b0 + n - 1 (one run, no ring wrap).
+// [layers x kv_heads][capacity][head_dim] bf16, 64 x 128 boxes, 128-byte swizzle) and its keys,
+// the cache slots b0 .. b0 + n - 1 (one run, no ring wrap).
 struct DtcRow {
   const void* kmap;
   const void* vmap;
@@ -40,7 +44,7 @@ struct DtcArgs {
   int heads, kv_heads, group;  // group <= kDtcN
   int n_rows, n_units;
   int chunk_keys;              // a multiple of kDtcKeys
-  const float* q;              // rotated queries, row r at q + r * q_stride (heads x 128, f32)
+  const float* q;              // rotated queries, row r at q + r * q_stride (heads x head_dim, f32)
   int64_t q_stride;
   float scale_log2;            // log2(e) / sqrt(head_dim)
   float* out;

@@ -103,9 +103,9 @@ cudaError_t launch_bf16_pairs(const FmhaLaunch& l, cudaStream_t stream) {
 
 }  // namespace
 
-bool encode_cache_map_bf16(void* map, const void* base, uint64_t rows, uint64_t z,
-                           uint64_t z_stride_bytes) {
-  return make_map(static_cast<CUtensorMap*>(map), true, base, 128, rows, z, 128 * 2,
+bool encode_cache_map_bf16(void* map, const void* base, uint64_t head_dim, uint64_t rows,
+                           uint64_t z, uint64_t z_stride_bytes) {
+  return make_map(static_cast<CUtensorMap*>(map), true, base, head_dim, rows, z, head_dim * 2,
                   z_stride_bytes, 64, 128);
 }
 

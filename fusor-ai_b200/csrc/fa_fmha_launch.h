@@ -68,10 +68,10 @@ bool fmha_supported(int dtype_bf16, int head_dim);
 // Whether launch_fmha honours FmhaArgs::splits for these operands (the two-tile bf16 kernel).
 bool fmha_splits_supported(int dtype_bf16, int head_dim);
 // A TMA map (written to the 128 bytes at `map`, 64-byte aligned) over a bf16 cache's keys or
-// values: [z][rows][128] elements, z_stride_bytes apart, 64 x 128 boxes, 128-byte swizzle (the
-// tensor-core decode's K and V tiles).
-bool encode_cache_map_bf16(void* map, const void* base, uint64_t rows, uint64_t z,
-                           uint64_t z_stride_bytes);
+// values: [z][rows][head_dim] elements, z_stride_bytes apart, 64 x 128 boxes, 128-byte swizzle
+// (the tensor-core decode's K and V tiles).
+bool encode_cache_map_bf16(void* map, const void* base, uint64_t head_dim, uint64_t rows,
+                           uint64_t z, uint64_t z_stride_bytes);
 // A TMA map over a 2-D f32 array [y][x] (rows y_stride_bytes apart) with box_x x box_y boxes,
 // 128-byte swizzled (box_x = 32), zero fill past the edges.
 bool encode_map_f32(void* map, const void* base, uint64_t x, uint64_t y, uint64_t y_stride_bytes,

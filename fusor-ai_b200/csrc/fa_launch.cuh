@@ -176,8 +176,9 @@ struct ProjectTcArgs {
 int project_tc_rows_per_tile(int rows);
 cudaError_t launch_project_tc(const ProjectTcArgs& args, cudaStream_t stream);
 
-// The tensor-core decode over bf16 caches (fa_decode_tc.cu): `grid` persistent CTAs.
+// The tensor-core decode over bf16 caches of head_dim 128 or 256 (fa_decode_tc.cu): `grid`
+// persistent CTAs.
 struct DtcArgs;
-cudaError_t launch_decode_tc(const DtcArgs& args, int grid, cudaStream_t stream);
+cudaError_t launch_decode_tc(const DtcArgs& args, int head_dim, int grid, cudaStream_t stream);
 
 }  // namespace fa

@@ -34,6 +34,8 @@ CASES = [
     # one row over 20000 keys: the keys split into chunks whose partials merge through the array
     ("f32_split", fa.F32, (1, 16, 8, 128), 20001, 20000, fa.Span(1, 19999, fa.Mask.causal())),
     ("bf16_split", fa.BF16, (1, 16, 8, 128), 20001, 20000, fa.Span(1, 19999, fa.Mask.causal())),
+    # head_dim 256 over a bf16 cache: the tensor-core decode's chunk partials in the array
+    ("bf16_d256_split", fa.BF16, (1, 8, 2, 256), 12001, 12000, fa.Span(1, 11999, fa.Mask.causal())),
     # C1's shape: 1025 keys, whose chunks run as one thread-block cluster (merged in shared
     # memory: only the counters come from the array)
     ("f32_cluster", fa.F32, (1, 14, 2, 64), 1025, 1024, fa.Span(1, 1024, fa.Mask.causal())),
@@ -63,7 +65,7 @@ def test_static_scratch_attend_matches_fa_attend_and_the_oracle_on_two_calls(cas
                              fa.ROPE_HALF, q_out=q)
     want_oracle = pair.oracle_attention(0, span, qkv, angles, fa.ROPE_HALF)
     # against fa_attend: the bf16 bar where fa_attend decodes on the tensor cores
-    tc = dtype == fa.BF16 and shape.head_dim == 128
+    tc = dtype == fa.BF16 and shape.head_dim in (128, 256)
     tol_attend = TOL_BF16 if tc else TOL_F32
     for call in range(2):
         if call == 1:  # another query the second time: nothing carries over from the first call
