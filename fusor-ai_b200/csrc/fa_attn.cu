@@ -207,8 +207,9 @@ struct fa_kvcache {
   Buffer work;       // queries and partials
   Buffer staging;    // fa_attention_host's device copies of the host rows
   Buffer counters;   // arrival counters (kept zero between launches)
-  Buffer tc_maps;    // bf16, head_dim 128: TMA maps over the keys and values (tensor-core decode)
-  Buffer proj_work;      // the fused projection's partial sums
+  Buffer tc_maps;    // bf16, head_dim 128 or 256: TMA maps over the keys and values (tensor-core
+                     // decode)
+  Buffer proj_work;      // the projections' partial sums (and the tensor-core one's projected rows)
   Buffer proj_counters;  // and its arrival counters (kept zero between launches)
   Buffer io;             // fa_attention_batch_host's device copies of the host rows
   cudaStream_t copy_stream = nullptr;  // and its copies, beside the caller's stream
