@@ -10,10 +10,12 @@
 //   O^T (D head_dim x 16) += V^T (D x 128 keys) . P^T (128 keys x 16),
 // accumulators in TMEM, D = 128 or 256. The K and V rings hold 128 keys x 128 head_dim entries:
 // a tile of head_dim 256 is two entries of each (its halves), S^T adds up both halves' products
-// and O^T is two 128-row accumulators, so the rings' shared memory is that of head_dim 128. A persistent CTA per SM walks the (row, KV head, chunk of keys) units;
-// warps:
-//   warps 0, 6  TMA producers of the K and of the V tiles (128-byte swizzled boxes of the cache's
-//               own tensor maps, one pair per cache), 3 stages each; plain per-CTA loads only;
+// and O^T is two 128-row accumulators, so the rings' shared memory is that of head_dim 128. A
+// persistent CTA per SM walks the (row, KV head, chunk of keys) units; warps:
+//   warps 0, 6  TMA producers of the K and of the V entries (128-byte swizzled boxes of the
+//               cache's own tensor maps, one pair per cache), 3 entries each; plain per-CTA
+//               loads only;
+//   (a thread of the softmax group below also keeps O^T rows d + 128 at head_dim 256)
 //   warp 1      TMEM owner and MMA issuer (one thread): S^T_t (three S^T buffers), then
 //               O^T += V^T P^T_{t-2}: the softmax has two tiles of slack;
 //   warps 2-5   softmax: thread = key (TMEM lane) of S^T and head_dim row of O^T. Per tile a
