@@ -15,7 +15,6 @@
 //   warps 0, 6  TMA producers of the K and of the V entries (128-byte swizzled boxes of the
 //               cache's own tensor maps, one pair per cache), 3 entries each; plain per-CTA
 //               loads only;
-//   (a thread of the softmax group below also keeps O^T rows d + 128 at head_dim 256)
 //   warp 1      TMEM owner and MMA issuer (one thread): S^T_t (three S^T buffers), then
 //               O^T += V^T P^T_{t-2}: the softmax has two tiles of slack;
 //   warps 2-5   softmax: thread = key (TMEM lane) of S^T and head_dim row of O^T. Per tile a
@@ -23,7 +22,8 @@
 //               one OR-reducing barrier decides; then the heads' maxima over the 128 keys),
 //               P^T as bf16 into shared memory (three buffers); per unit the next unit's Q^T
 //               into shared memory (two buffers, so the MMAs run on across units) and at the
-//               end O^T / L or the unit's partial (max, sum, o) for the chunk merge.
+//               end O^T / L or the unit's partial (max, sum, o) for the chunk merge (at
+//               head_dim 256 a thread keeps O^T rows d and d + 128).
 #pragma once
 
 #include "fa_decode.cuh"
