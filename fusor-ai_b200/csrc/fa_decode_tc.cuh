@@ -13,8 +13,8 @@
 // and O^T is two 128-row accumulators, so the rings' shared memory is that of head_dim 128. A
 // persistent CTA per SM walks the (row, KV head, chunk of keys) units; warps:
 //   warps 0, 6  TMA producers of the K and of the V entries (128-byte swizzled boxes of the
-//               cache's own tensor maps, one pair per cache), 3 entries each; plain per-CTA
-//               loads only;
+//               cache's own tensor maps, one pair per cache), 3 entries each (2 and 4 at
+//               head_dim 256); plain per-CTA loads only;
 //   warp 1      TMEM owner and MMA issuer (one thread): S^T_t (three S^T buffers), then
 //               O^T += V^T P^T_{t-2}: the softmax has two tiles of slack;
 //   warps 2-5   softmax: thread = key (TMEM lane) of S^T and head_dim row of O^T. Per tile a
@@ -64,6 +64,8 @@ __global__ void __launch_bounds__(kDtcThreads, 1) decode_tc_kernel(const __grid_
   static_assert(D == 128 || D == 256, "head_dim");
   static_assert(dtc_smem_bytes(D) + 1024 <= 227 * 1024, "shared memory");
   constexpr int kHalves = D / kDtcD;            // ring entries per tile, O^T accumulators
+  // K and V ring entries (2 * kDtcStages together)
+  constexpr int KS = dtc_k_stages(D), VS = 2 * kDtcStages - KS;
   constexpr int kQBytes = dtc_q_bytes(D);
   constexpr uint32_t kIdescS = tc::instr_desc_ab(1u, false, false, kDtcN, kDtcKeys);
   constexpr uint32_t kIdescPV = tc::instr_desc_ab(1u, true, false, kDtcN, kDtcD);
@@ -76,17 +78,17 @@ __global__ void __launch_bounds__(kDtcThreads, 1) decode_tc_kernel(const __grid_
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* sK = smem;
-  unsigned char* sV = sK + kDtcStages * kDtcTileBytes;
-  unsigned char* sQ = sV + kDtcStages * kDtcTileBytes;  // two buffers
+  unsigned char* sV = sK + KS * kDtcTileBytes;
+  unsigned char* sQ = sV + VS * kDtcTileBytes;  // two buffers
   unsigned char* sP = sQ + 2 * kQBytes;                 // three buffers
   float* s_merge = reinterpret_cast<float*>(sP + kS * kDtcPBytes);
   uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(s_merge) +
                                                kDtcMergeBytes);
   uint64_t* k_full = bars;
-  uint64_t* k_empty = k_full + kDtcStages;
-  uint64_t* v_full = k_empty + kDtcStages;
-  uint64_t* v_empty = v_full + kDtcStages;
-  uint64_t* s_full = v_empty + kDtcStages;  // [kS] S^T buffers
+  uint64_t* k_empty = k_full + KS;
+  uint64_t* v_full = k_empty + KS;
+  uint64_t* v_empty = v_full + VS;
+  uint64_t* s_full = v_empty + VS;  // [kS] S^T buffers
   uint64_t* p_full = s_full + kS;           // [kS] P^T buffers written
   uint64_t* o_done = p_full + kS;           // [2] the P.V products of even / odd tiles
   uint64_t* o_final = o_done + 2;           // a unit's last P.V
@@ -101,9 +103,11 @@ __global__ void __launch_bounds__(kDtcThreads, 1) decode_tc_kernel(const __grid_
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kDtcStages; ++s) {
+    for (int s = 0; s < KS; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < VS; ++s) {
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
@@ -132,6 +136,7 @@ __global__ void __launch_bounds__(kDtcThreads, 1) decode_tc_kernel(const __grid_
       uint64_t* full = keys ? k_full : v_full;
       uint64_t* empty = keys ? k_empty : v_empty;
       unsigned char* dst = keys ? sK : sV;
+      const int stages = keys ? KS : VS;
       pdl_wait();  // the keys and values kept by the kernel before this one
       int T = 0, issued = 0;
       bool ok = true;
@@ -143,9 +148,9 @@ __global__ void __launch_bounds__(kDtcThreads, 1) decode_tc_kernel(const __grid_
         const int tiles = (j1 - j0 + kDtcKeys - 1) / kDtcKeys;
         for (int e = 0; e < tiles * kHalves; ++e, ++T) {
           // ring entry T: head_dim half e % kHalves of the unit's tile e / kHalves
-          const int st = T % kDtcStages;
+          const int st = T % stages;
           const int t = e / kHalves, half = e % kHalves;
-          if (!mbar_wait(&empty[st], ((T / kDtcStages) & 1) ^ 1, a.err)) { ok = false; break; }
+          if (!mbar_wait(&empty[st], ((T / stages) & 1) ^ 1, a.err)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[st], kDtcTileBytes);
           for (int db = 0; db < kDtcD / 64; ++db)
             tc::tma_load_3d(dst + st * kDtcTileBytes + db * (kDtcKeys * 128), map,
@@ -154,8 +159,8 @@ __global__ void __launch_bounds__(kDtcThreads, 1) decode_tc_kernel(const __grid_
         }
       }
       // The loads still in flight land before the CTA may exit.
-      for (int L = max(0, issued - kDtcStages); L < issued; ++L)
-        mbar_wait(&full[L % kDtcStages], (L / kDtcStages) & 1, a.err);
+      for (int L = max(0, issued - stages); L < issued; ++L)
+        mbar_wait(&full[L % stages], (L / stages) & 1, a.err);
     }
   } else if (warp == 1) {
     // ---- MMA issuer ----------------------------------------------------------------------
@@ -172,8 +177,8 @@ __global__ void __launch_bounds__(kDtcThreads, 1) decode_tc_kernel(const __grid_
         if (!mbar_wait(&p_full[b], (T2 / kS) & 1, a.err)) return false;
 #pragma unroll
         for (int h = 0; h < kHalves; ++h) {
-          const int E = T2 * kHalves + h, st = E % kDtcStages;
-          if (!mbar_wait(&v_full[st], (E / kDtcStages) & 1, a.err)) return false;
+          const int E = T2 * kHalves + h, st = E % VS;
+          if (!mbar_wait(&v_full[st], (E / VS) & 1, a.err)) return false;
           tc::fence_after_sync();
 #pragma unroll
           for (int k = 0; k < kDtcKeys / 16; ++k) {
@@ -202,8 +207,8 @@ __global__ void __launch_bounds__(kDtcThreads, 1) decode_tc_kernel(const __grid_
           // S^T of tile T over its head_dim halves (K ring entries T * kHalves + h)
 #pragma unroll
           for (int h = 0; h < kHalves; ++h) {
-            const int E = T * kHalves + h, st = E % kDtcStages;
-            if (!mbar_wait(&k_full[st], (E / kDtcStages) & 1, a.err)) { ok = false; break; }
+            const int E = T * kHalves + h, st = E % KS;
+            if (!mbar_wait(&k_full[st], (E / KS) & 1, a.err)) { ok = false; break; }
             tc::fence_after_sync();
 #pragma unroll
             for (int k = 0; k < kDtcD / 16; ++k) {

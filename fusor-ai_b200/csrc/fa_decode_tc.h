@@ -16,6 +16,12 @@ constexpr int kDtcThreads = 224;
 constexpr int kDtcTileBytes = kDtcKeys * kDtcD * 2;   // one ring entry: 128 keys x 128 head_dim
 constexpr int kDtcPBytes = kDtcN * kDtcKeys * 2;      // one P^T buffer: 16 rows x 256 B
 constexpr int kDtcMergeBytes = 4096;
+// K ring entries, of the 2 x kDtcStages the K and V rings share. At head_dim 256 a tile is two
+// entries of each, and the V ring, whose tiles wait two tiles for their P.V, takes four: measured
+// on B200 (`decode256`), K/V entries 3/3 0.109 ms, 4/2 0.108, 2/4 0.106.
+__host__ __device__ constexpr int dtc_k_stages(int head_dim) {
+  return head_dim == 256 ? 2 : kDtcStages;
+}
 // Q^T: 16 rows x head_dim bf16
 __host__ __device__ constexpr int dtc_q_bytes(int head_dim) { return kDtcN * head_dim * 2; }
 // K and V stages, two Q^T buffers, three P^T buffers, the merge's weights
