@@ -137,6 +137,7 @@ class Workload:
     flush_l2 = False
     graphs = False         # latency-bound steps: the step replayed as one captured CUDA graph
     e2e_ran = False        # time_e2e ran this workload's public-API step
+    e2e_returns_synchronized = False  # e2e_step returns with its host output filled
     _step_graph = None
     _kernel_graph = None
 
@@ -247,9 +248,11 @@ class C3Decode(Workload):
 
     e2e_path = "pinned host rows -> fa_attention_batch_host -> pinned host output"
 
+    e2e_returns_synchronized = True
+
     def e2e_step(self):
-        # fa_attention_batch_host: the copies of groups of sequences overlap the other groups'
-        # attention; returns with h_out filled
+        # fa_attention_batch_host: the copy of the second group of sequences overlaps the first
+        # group's attention; returns with h_out filled
         self.batch.attention_host(0, self.h_qkv, self.h_out, self.h_angles, self.fa.ROPE_HALF)
 
     def parity(self, threads):
@@ -1039,12 +1042,17 @@ def time_e2e(torch, dist, w: Workload, steps: int, warmup: int):
     if dist is not None:
         dist.barrier()
     times = []
+    # a step whose call returns with the host output filled (it synchronizes its own streams)
+    # needs no synchronize after it; every other step gets one
+    sync_each = not w.e2e_returns_synchronized
     t0 = time.perf_counter()
     for _ in range(steps):
         a = time.perf_counter()
         w.e2e_step()
-        torch.cuda.current_stream().synchronize()
+        if sync_each:
+            torch.cuda.current_stream().synchronize()
         times.append(time.perf_counter() - a)
+    torch.cuda.synchronize()
     ms = (time.perf_counter() - t0) * 1e3 / steps
     med = sorted(times)[len(times) // 2] * 1e3
     t = torch.tensor([ms, med], device="cuda", dtype=torch.float64)

@@ -140,6 +140,9 @@ size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 // down past about this much K/V.
 constexpr double kL2KvBudget = 48e6;
 
+// fa_attention_batch_host's groups of sequences (their copies overlap the other group's work).
+constexpr int kMaxHostGroups = 2;
+
 // The one-tile kernel's band (FmhaArgs::band_heads): the most whole KV groups whose K/V
 // (kv_bytes_per_head for each KV head) fits the L2 budget together, at least one, and a divisor
 // of the KV heads so that the bands are equal.
@@ -213,7 +216,9 @@ struct fa_kvcache {
   Buffer proj_counters;  // and its arrival counters (kept zero between launches)
   Buffer io;             // fa_attention_batch_host's device copies of the host rows
   cudaStream_t copy_stream = nullptr;  // and its copies, beside the caller's stream
-  cudaEvent_t io_events[4] = {};       // rows in (2 groups), then attention done (2 groups)
+  cudaStream_t side_stream = nullptr;  // and its odd groups, concurrent with the even ones
+  cudaEvent_t io_events[2 * kMaxHostGroups + 1] = {};  // rows in, attention done (per group),
+                                                       // the side stream's end
   int counters_epoch = 0;
   int proj_epoch = -1;
   size_t elem() const { return dtype == FA_F32 ? 4 : 2; }
@@ -257,6 +262,16 @@ int current_device() {
   int d = 0;
   if (cudaGetDevice(&d) != cudaSuccess) d = 0;
   return d;
+}
+
+// Host rows (`stride` floats apart) to `width`-float device rows: one linear copy when the rows
+// are contiguous (the 2D form's per-row transfers cost more), else a pitched one.
+cudaError_t rows_to_device(float* dst, int64_t width, const float* src, int64_t stride,
+                           int64_t rows, cudaStream_t s) {
+  if (stride == width)
+    return cudaMemcpyAsync(dst, src, size_t(rows * width) * 4, cudaMemcpyHostToDevice, s);
+  return cudaMemcpy2DAsync(dst, size_t(width) * 4, src, size_t(stride) * 4, size_t(width) * 4,
+                           size_t(rows), cudaMemcpyHostToDevice, s);
 }
 
 int ensure_counters(fa_kvcache* c, size_t n, cudaStream_t stream) {
@@ -925,6 +940,7 @@ int fa_kvcache_destroy(fa_kvcache* cache) {
   for (cudaEvent_t& e : cache->io_events)
     if (e != nullptr) cudaEventDestroy(e);
   if (cache->copy_stream != nullptr) cudaStreamDestroy(cache->copy_stream);
+  if (cache->side_stream != nullptr) cudaStreamDestroy(cache->side_stream);
   delete cache;
   return FA_OK;
 }
@@ -1196,8 +1212,7 @@ int fa_attention_host(fa_kvcache* cache, int32_t layer, const fa_span* span, int
   float* qkv_dev = static_cast<float*>(cache->staging.ptr);
   float* angles_dev = qkv_dev + size_t(rows) * units;
   float* out_dev = angles_dev + size_t(rows) * cache->head_dim;
-  FA_CUDA(cudaMemcpy2DAsync(qkv_dev, units * 4, qkv_host, qkv_stride * 4, units * 4, rows,
-                            cudaMemcpyHostToDevice, s), "qkv to device");
+  FA_CUDA(rows_to_device(qkv_dev, units, qkv_host, qkv_stride, rows, s), "qkv to device");
   if (rope != FA_ROPE_NONE)
     FA_CUDA(cudaMemcpyAsync(angles_dev, angles_host, size_t(rows) * cache->head_dim * 4,
                             cudaMemcpyHostToDevice, s), "angles to device");
@@ -1262,26 +1277,31 @@ int batch_chunk_tiles(const fa_kvcache* c0, const Plan& base, const std::vector<
   fa::AttendLaunch probe{kt, base.g, true, nullptr, nullptr, 0};
   const int resident = attend_resident_d(c0->head_dim, probe);
   const int64_t slots = int64_t(std::max(c0->dev->sms, 1)) * std::max(resident, 1);
+  // Each row in tiles, at least one: its chunks of t tiles are ceil(tiles / t) (= ceil(keys /
+  // (t x tile))), in 32-bit arithmetic (a row holds fewer than 2^31 keys). This search runs on
+  // the host before every batch launch: 16 rows x 49 lengths took 7.5 us in 64-bit divisions.
   int64_t longest = 1, keys_total = 0;
+  std::vector<uint32_t> row_tiles(batch);
   for (int i = 0; i < batch; ++i) {
     const int64_t n = runs[i].n0 + runs[i].n1;
     longest = std::max(longest, n);
     keys_total += n;
+    row_tiles[i] = uint32_t(std::max<int64_t>(1, (n + tile - 1) / tile));
   }
   const double tiles_total = double(keys_total) * base.kv_groups / tile;
   const int top = int(std::min<int64_t>(kMaxTiles, std::max<int64_t>(kMinTiles, (longest + tile - 1) / tile)));
   int best = top;
   double best_us = 1e300;
   for (int t = top; t >= kMinTiles; --t) {  // ties go to the longer chunk: fewer partials
-    const int64_t keys = int64_t(t) * tile;
+    const uint32_t ut = uint32_t(t);
     int64_t units = 0;
-    for (int i = 0; i < batch; ++i)
-      units += std::max<int64_t>(1, (runs[i].n0 + runs[i].n1 + keys - 1) / keys);
+    for (int i = 0; i < batch; ++i) units += (row_tiles[i] + ut - 1) / ut;
     units *= base.kv_groups;
     const double per_unit = tiles_total / double(units);
-    const double b3 = std::pow(t / kCtaTilesPerUs, 3.0);
+    const double bt = t / kCtaTilesPerUs, b3 = bt * bt * bt;
     auto wave = [&](int64_t n) {
-      return std::cbrt(std::pow(n * per_unit / kHbmTilesPerUs, 3.0) + b3) + kWaveUs;
+      const double a = n * per_unit / kHbmTilesPerUs;
+      return std::cbrt(a * a * a + b3) + kWaveUs;
     };
     const int64_t full = units / slots, rest = units % slots;
     const double us = double(full) * wave(slots) + (rest > 0 ? wave(rest) : 0.0);
@@ -1730,15 +1750,18 @@ int fa_attention_batch_host(fa_kvcache* const* caches, const fa_span* spans, int
       out_mapped = true;
     }
   }
-  // Two groups of consecutive sequences of about equal key counts once the batch is large
-  // enough for each group's launch to fill the SMs (each group's keys are chunked over the whole
-  // GPU). Measured on B200 with C3's 64 sequences (f32 caches, pinned memory, per step): one
-  // launch with the copies on the caller's stream 0.423 ms, two groups 0.420 ms, four 0.510 ms
-  // (a quarter of C3 is 1.3 waves of chunks: the launches' tails outweigh the copies hidden).
+  // Two groups of consecutive sequences once the batch is large enough for each group's launch
+  // to fill the SMs (each group's keys are chunked over the whole GPU): the first a quarter of
+  // the keys, so that its rows (a quarter of the copy) land soon and the GPU starts on them while
+  // the others' rows arrive; the second group runs on a second stream, concurrent with the
+  // first, so that its launch fills the SMs the first one's last wave leaves idle. Measured on
+  // B200 with C3's 64 sequences (pinned memory, mean per step, f32 / bf16 caches): the groups
+  // one after the other on the caller's stream 0.422 / 0.291 ms; concurrent, halves of the keys
+  // 0.403-0.407 / 0.257-0.279, a quarter first 0.402 / 0.254 (an eighth 0.405-0.416; four
+  // concurrent quarters 0.402 / 0.317).
   const int groups = batch >= 16 ? 2 : 1;
   if (groups == 1) {
-    FA_CUDA(cudaMemcpy2DAsync(qkv_dev, units * 4, qkv_host, qkv_stride * 4, units * 4, batch,
-                              cudaMemcpyHostToDevice, s), "qkv to device");
+    FA_CUDA(rows_to_device(qkv_dev, units, qkv_host, qkv_stride, batch, s), "qkv to device");
     if (rope != FA_ROPE_NONE)
       FA_CUDA(cudaMemcpyAsync(angles_dev, angles_host, size_t(batch) * d * 4,
                               cudaMemcpyHostToDevice, s), "angles to device");
@@ -1752,58 +1775,79 @@ int fa_attention_batch_host(fa_kvcache* const* caches, const fa_span* spans, int
     FA_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
     return FA_OK;
   }
+  static_assert(kMaxHostGroups == 2, "groups");
   if (c0->copy_stream == nullptr)
     FA_CUDA(cudaStreamCreateWithFlags(&c0->copy_stream, cudaStreamNonBlocking), "copy stream");
+  if (c0->side_stream == nullptr)
+    FA_CUDA(cudaStreamCreateWithFlags(&c0->side_stream, cudaStreamNonBlocking), "side stream");
   for (cudaEvent_t& e : c0->io_events)
     if (e == nullptr) FA_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "copy event");
   cudaStream_t cs = c0->copy_stream;
   cudaEvent_t* in_ready = c0->io_events;
-  cudaEvent_t* done = c0->io_events + 2;
-  std::vector<int> bounds(groups + 1, batch);
-  bounds[0] = 0;
+  cudaEvent_t* done = c0->io_events + kMaxHostGroups;
+  cudaEvent_t side_end = c0->io_events[2 * kMaxHostGroups];
+  int bounds[3] = {0, batch, batch};
   {
     int64_t seen = 0;
-    int g = 1;
-    for (int i = 0; i < batch && g < groups; ++i) {
+    for (int i = 0; i + 1 < batch; ++i) {
       seen += runs[i].n0 + runs[i].n1;
-      if (seen * groups >= total_keys * g && i + 1 < batch) bounds[g++] = i + 1;
+      if (seen * 4 >= total_keys) {
+        bounds[1] = i + 1;
+        break;
+      }
     }
-    for (; g < groups; ++g) bounds[g] = batch;  // fewer non-empty groups than asked
   }
-  // The copy stream starts after the caller's earlier work, takes every group's rows in, then
-  // each group's outputs out once that group has attended.
+  // A group's launches use its first cache's workspace, queries and counters: the groups run
+  // concurrently only when those caches are distinct (a batch may name a cache twice).
+  const bool concurrent = bounds[1] == batch || caches[0] != caches[bounds[1]];
+  cudaStream_t side = concurrent ? c0->side_stream : s;
+  // The copy stream and the side stream start after the caller's earlier work; the copy stream
+  // takes each group's rows in, then (unmapped output) each group's outputs out once that group
+  // has attended. The host issues a group's copy and then its launches before the next group's
+  // copy: the first group's launches are the host's share of the call's critical path.
   FA_CUDA(cudaEventRecord(done[0], s), "copy event");
   FA_CUDA(cudaStreamWaitEvent(cs, done[0], 0), "copy stream wait");
-  for (int g = 0; g < groups; ++g) {
+  if (side != s) FA_CUDA(cudaStreamWaitEvent(side, done[0], 0), "side stream wait");
+  int rc = FA_OK;
+  for (int g = 0; g < groups && rc == FA_OK; ++g) {
     const int b0 = bounds[g], n = bounds[g + 1] - bounds[g];
     if (n == 0) continue;
-    FA_CUDA(cudaMemcpy2DAsync(qkv_dev + size_t(b0) * units, units * 4, qkv_host + b0 * qkv_stride,
-                              qkv_stride * 4, units * 4, n, cudaMemcpyHostToDevice, cs),
-            "qkv to device");
-    if (rope != FA_ROPE_NONE)
-      FA_CUDA(cudaMemcpyAsync(angles_dev + size_t(b0) * d, angles_host + int64_t(b0) * d,
-                              size_t(n) * d * 4, cudaMemcpyHostToDevice, cs),
-              "angles to device");
-    FA_CUDA(cudaEventRecord(in_ready[g], cs), "copy event");
-  }
-  for (int g = 0; g < groups; ++g) {
-    const int b0 = bounds[g], n = bounds[g + 1] - bounds[g];
-    if (n == 0) continue;
-    FA_CUDA(cudaStreamWaitEvent(s, in_ready[g], 0), "stream wait");
-    if (int rc = fa_attention_batch(caches + b0, spans + b0, n, layer, rope,
-                                    rope != FA_ROPE_NONE ? angles_dev + size_t(b0) * d : nullptr,
-                                    norm, qkv_dev + size_t(b0) * units, units,
-                                    out_dev + b0 * out_dev_stride, out_dev_stride, stream)) {
-      // earlier groups' kernels may still be storing into the caller's (mapped) output, and
-      // their copies may be in flight: both end before the call returns its error
-      cudaStreamSynchronize(s);
-      cudaStreamSynchronize(cs);
-      return rc;
+    cudaError_t e = rows_to_device(qkv_dev + size_t(b0) * units, units,
+                                   qkv_host + b0 * qkv_stride, qkv_stride, n, cs);
+    if (e == cudaSuccess && rope != FA_ROPE_NONE)
+      e = cudaMemcpyAsync(angles_dev + size_t(b0) * d, angles_host + int64_t(b0) * d,
+                          size_t(n) * d * 4, cudaMemcpyHostToDevice, cs);
+    if (e == cudaSuccess) e = cudaEventRecord(in_ready[g], cs);
+    cudaStream_t gs = g % 2 == 1 ? side : s;
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(gs, in_ready[g], 0);
+    if (e != cudaSuccess) {
+      rc = cuda_fail(e, "rows to device");
+      break;
     }
-    FA_CUDA(cudaEventRecord(done[g], s), "attention event");
+    rc = fa_attention_batch(caches + b0, spans + b0, n, layer, rope,
+                            rope != FA_ROPE_NONE ? angles_dev + size_t(b0) * d : nullptr, norm,
+                            qkv_dev + size_t(b0) * units, units, out_dev + b0 * out_dev_stride,
+                            out_dev_stride, gs);
+    if (rc == FA_OK) {
+      e = cudaEventRecord(done[g], gs);
+      if (e != cudaSuccess) rc = cuda_fail(e, "attention event");
+    }
+  }
+  if (rc != FA_OK) {
+    // earlier groups' kernels may still be storing into the caller's (mapped) output, and
+    // their copies may be in flight: all of them end before the call returns its error
+    cudaStreamSynchronize(s);
+    cudaStreamSynchronize(side);
+    cudaStreamSynchronize(cs);
+    return rc;
+  }
+  // the caller's stream ends after the side stream's groups
+  if (side != s) {
+    FA_CUDA(cudaEventRecord(side_end, side), "side stream event");
+    FA_CUDA(cudaStreamWaitEvent(s, side_end, 0), "stream wait");
   }
   if (out_mapped) {
-    // the caller's stream ran every group after its rows arrived: its end is the call's end
+    // the caller's stream ran (or waited for) every group: its end is the call's end
     FA_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
     return FA_OK;
   }
@@ -1817,6 +1861,7 @@ int fa_attention_batch_host(fa_kvcache* const* caches, const fa_span* spans, int
             "out to host");
   }
   FA_CUDA(cudaStreamSynchronize(cs), "cudaStreamSynchronize");
+  FA_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
   return FA_OK;
 }
 

@@ -177,8 +177,14 @@ def _check(rc: int):
 
 def _stream(stream=None):
     import torch
-    s = stream if stream is not None else torch.cuda.current_stream()
-    return C.c_void_p(s.cuda_stream)
+    if stream is None:
+        # torch's current stream on the current device, as a raw handle: the Stream object
+        # (torch.cuda.current_stream) costs several microseconds per call on a decode step
+        raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+        if raw is not None:
+            return C.c_void_p(raw(torch.cuda.current_device()))
+        stream = torch.cuda.current_stream()
+    return C.c_void_p(stream.cuda_stream)
 
 
 def _dptr(t):
@@ -473,7 +479,7 @@ class Batch:
         """attention() over HOST tensors (qkv, angles and out in CPU memory, pinned for the
         copies to overlap the attention): returns when out holds every sequence's row."""
         for t in (qkv, out) + ((angles,) if angles is not None else ()):
-            if t.device.type != "cpu" or t.stride(-1) != 1:
+            if not t.is_cpu or t.stride(-1) != 1:
                 raise ValueError("host tensors with unit stride along a row")
         _check(lib().fa_attention_batch_host(self.handles, self.spans, self.n, layer,
                                              rope if angles is not None else ROPE_NONE,

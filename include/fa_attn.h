@@ -255,9 +255,11 @@ int fa_attention_batch(fa_kvcache* const* caches, const fa_span* spans, int32_t 
 
 /* fa_attention_batch with HOST qkv, angles and out (the batched form of fa_attention_host):
  * returns when `out` holds every sequence's row. A batch of 16 or more runs as two groups of
- * sequences of about equal key counts, each its own launch: the second group's rows are copied
- * in, and the first group's outputs copied out, on a copy stream while the other group attends.
- * Pinned host memory lets the copies overlap; pageable memory still works. */
+ * consecutive sequences (the first a quarter of the keys), each its own launch: the second
+ * group's rows are copied in on a copy stream while the first group attends, and the second
+ * group runs on a second stream, concurrent with the first. A pinned output is stored into by
+ * the kernels directly (mapped host memory); a pageable one is copied out per group. Pinned
+ * host memory lets the copies overlap; pageable memory still works. */
 int fa_attention_batch_host(fa_kvcache* const* caches, const fa_span* spans, int32_t batch,
                             int32_t layer, int32_t rope, const float* angles_host,
                             const fa_head_norm* norm, const float* qkv_host, int64_t qkv_stride,
