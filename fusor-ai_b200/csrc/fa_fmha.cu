@@ -68,7 +68,7 @@ cudaError_t launch_t(const FmhaLaunch& l, cudaStream_t stream) {
   if (band % l.args.group || l.args.heads % band) return cudaErrorInvalidValue;
   const int64_t grid = int64_t(l.args.images) * l.args.q_tiles * l.args.heads;
   if (grid > 0x7fffffff) return cudaErrorInvalidValue;
-  return launch_pdl(kernel, dim3(unsigned(grid)), dim3(kFmhaThreads), S::kSmemBytes, stream, qm,
+  return launch_pdl(kernel, dim3(unsigned(grid)), dim3(fmha_threads<T, D>()), S::kSmemBytes, stream, qm,
                     km, vm, l.args);
 }
 

@@ -9,6 +9,10 @@
 //               layout; plain per-CTA loads only);
 //   warp 1      TMEM owner and MMA issuer (one thread): S = Q K^T into one of two TMEM
 //               buffers, then O += P V with P read from TMEM (the TS form);
+//   warps 2-3   (tf32) the rounding pass: Q and every K and V tile rounded to tf32 (nearest)
+//               in shared memory between the TMA's landing and the MMA that reads it; at
+//               head_dim 128 also warps 8-11, so that the pass runs on all four of the SM's
+//               schedulers (fmha_threads);
 //   warps 4-7   softmax: thread i owns query row i (TMEM lane i); it loads its S row, masks,
 //               updates the running max lazily (the output is rescaled only when the max grows
 //               by more than 2^8, FA4's trick), writes P back into the S buffer (bf16 pairs, or
@@ -60,12 +64,22 @@ struct FmhaShape {
   static_assert(kSmemUsed <= 227 * 1024, "shared memory of one CTA");
 };
 
-constexpr int kFmhaThreads = 256;
-constexpr int kConvThreads = 64;  // warps 2-3: the tf32 rounding pass
+// Threads of an instantiation: warps 0-1 (TMA, MMA), 2-3 (the tf32 rounding pass), 4-7
+// (softmax), and for the f32 kernel of head_dim 128 warps 8-11 (more of the rounding pass, which
+// is on the critical path of every KV tile: measured on B200 over the 8192-row f32 prefill,
+// 1.618 ms with two rounding warps, 1.401 with four, 1.377 with six). The head_dim-64 f32 kernel
+// keeps 256 threads: it holds 218 registers a thread, above the 168 that 384 threads allow.
+template <typename T, int D>
+__host__ __device__ constexpr int fmha_threads() {
+  return FmhaShape<T, D>::kTf32 && D == 128 ? 384 : 256;
+}
+template <typename T, int D>
+__host__ __device__ constexpr int fmha_conv_threads() { return fmha_threads<T, D>() - 192; }
 
 // Rounds `bytes` of f32 shared memory to tf32 (nearest, ties away) in place, 16 bytes per
 // thread per step, four steps' loads in flight at a time (the pass is on the critical path of
 // every KV tile). The swizzled layout is untouched: the same function of every element.
+template <int kConvThreads>
 __device__ __forceinline__ void round_tile_tf32(unsigned char* tile, int bytes, int tid) {
   float4* v = reinterpret_cast<float4*>(tile);
   const int n = bytes / 16;
@@ -95,7 +109,7 @@ __device__ __forceinline__ void round_tile_tf32(unsigned char* tile, int bytes, 
 
 
 template <typename T, int D>
-__global__ void __launch_bounds__(kFmhaThreads, 1)
+__global__ void __launch_bounds__(fmha_threads<T, D>(), 1)
     fmha_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
                 const __grid_constant__ CUtensorMap v_map, const __grid_constant__ FmhaArgs a) {
   using S = FmhaShape<T, D>;
@@ -124,7 +138,8 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
   uint64_t* o_done = p_full + NB;    // [NB]: P.V of tile j completes phase j / NB of o_done[j % NB]
   uint64_t* o_final = o_done + NB;   // the last P.V product has completed
   uint64_t* mma_drained = o_final + 1;
-  // tf32: Q, K and V tiles rounded to tf32 in place by warps 2-3 before the MMA reads them
+  // tf32: Q, K and V tiles rounded to tf32 in place by the rounding warps before the MMA reads
+  // them
   uint64_t* q_conv = mma_drained + 1;
   uint64_t* k_conv = q_conv + 1;     // [KS]
   uint64_t* v_conv = k_conv + KS;    // [VS]
@@ -161,12 +176,12 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
     for (int st = 0; st < KS; ++st) {
       mbar_init(&k_full[st], 1);
       mbar_init(&k_empty[st], 1);
-      mbar_init(&k_conv[st], kConvThreads);
+      mbar_init(&k_conv[st], fmha_conv_threads<T, D>());
     }
     for (int st = 0; st < VS; ++st) {
       mbar_init(&v_full[st], 1);
       mbar_init(&v_empty[st], 1);
-      mbar_init(&v_conv[st], kConvThreads);
+      mbar_init(&v_conv[st], fmha_conv_threads<T, D>());
     }
     for (int b = 0; b < NB; ++b) {
       mbar_init(&s_full[b], 1);
@@ -175,7 +190,7 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
     }
     mbar_init(o_final, 1);
     mbar_init(mma_drained, 1);
-    mbar_init(q_conv, kConvThreads);
+    mbar_init(q_conv, fmha_conv_threads<T, D>());
     mbar_fence_init();
   }
   if (warp == 1) tc::tmem_alloc(tmem_slot, 512);
@@ -289,14 +304,14 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
       tc::commit(mma_drained);
       mbar_wait(mma_drained, 0, a.err);
     }
-  } else if (warp < 4) {
+  } else if (warp < 4 || warp >= 8) {
     // ---- tf32: round Q, then every K and V tile, to nearest before the MMA reads them -------
     if constexpr (kTf32) {
-      const int tid = threadIdx.x - 64;
+      const int tid = warp < 4 ? int(threadIdx.x) - 64 : int(threadIdx.x) - 192;
       auto convert = [&](uint64_t* full, uint64_t* conv, uint32_t parity, unsigned char* tile,
                          int bytes) {
         if (!mbar_wait(full, parity, a.err)) return false;
-        round_tile_tf32(tile, bytes, tid);
+        round_tile_tf32<fmha_conv_threads<T, D>()>(tile, bytes, tid);
         // generic-proxy writes become visible to the tensor core's async proxy
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         mbar_arrive(conv);
@@ -318,8 +333,8 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
         if (ok && j + L + 1 < n_tiles) ok = conv_k(j + L + 1);
       }
     }
-  } else if (warp >= 4) {
-    // ---- softmax + epilogue ----------------------------------------------------------------
+  } else {
+    // ---- softmax + epilogue (warps 4-7) ----------------------------------------------------
     const int wq = warp - 4;
     const int r = r0 + wq * 32 + lane;  // this thread's query row within the image
     const bool row_valid = r < a.rows;
