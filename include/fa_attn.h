@@ -259,7 +259,9 @@ int fa_attention_batch(fa_kvcache* const* caches, const fa_span* spans, int32_t 
  * group's rows are copied in on a copy stream while the first group attends, and the second
  * group runs on a second stream, concurrent with the first. A pinned output is stored into by
  * the kernels directly (mapped host memory); a pageable one is copied out per group. Pinned
- * host memory lets the copies overlap; pageable memory still works. */
+ * host memory lets the copies overlap; pageable memory still works. The device staging, the
+ * copy stream and the second stream belong to the batch's first cache: two calls whose first
+ * caches are the same run one after the other, not from two host threads at once. */
 int fa_attention_batch_host(fa_kvcache* const* caches, const fa_span* spans, int32_t batch,
                             int32_t layer, int32_t rope, const float* angles_host,
                             const fa_head_norm* norm, const float* qkv_host, int64_t qkv_stride,
